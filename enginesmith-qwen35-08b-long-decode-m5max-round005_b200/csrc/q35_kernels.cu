@@ -1,0 +1,956 @@
+// q35 decode kernels for sm_100a.
+//
+// One decode step (model.rs:228-307, rows == 1) is a chain of launches:
+//   per GDN layer       : qmv[norm|qkv,z,a,b|conv] -> gdn_recur -> qmv[norm-gate|out|+res]
+//   per attention layer : qmv[norm|q,k,v] -> attn (split-K, cluster combine, gate) -> qmv[o|+res]
+//   per layer           : qmv[norm|gate,up|SwiGLU] -> qmv[down|+res]
+//   once                : head (final norm, vocab projection, LSE, greedy)
+// Every launch uses programmatic dependent launch: before griddepcontrol.wait
+// a CTA only issues bulk copies of constant weights and of state written by
+// earlier steps, so the next launch's weight stream overlaps this one's
+// activation-dependent compute.
+#include "q35_kernels.h"
+#include "q35_qmv.cuh"
+
+namespace q35 {
+
+// ---------------------------------------------------------------------------
+// Q4 matvec with fused prologue / epilogue
+// ---------------------------------------------------------------------------
+struct Piece {
+  int seg, row0, count;
+};
+
+__host__ __device__ inline int qmv_pieces(const QmvArgs& a, int cta, Piece* p) {
+  const int u0 = cta * a.units_per_cta;
+  const int u1 = (u0 + a.units_per_cta < a.units) ? u0 + a.units_per_cta : a.units;
+  if (u1 <= u0) return 0;
+  if (a.epi == kEpiSwiglu) {
+    p[0] = {0, u0, u1 - u0};
+    p[1] = {1, u0, u1 - u0};
+    return 2;
+  }
+  int n = 0, off = 0;
+  for (int s = 0; s < a.nseg; ++s) {
+    const int lo = u0 > off ? u0 : off;
+    const int hi = u1 < off + a.seg[s].rows ? u1 : off + a.seg[s].rows;
+    if (lo < hi) p[n++] = {s, lo - off, hi - lo};
+    off += a.seg[s].rows;
+  }
+  return n;
+}
+
+__host__ __device__ inline size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
+
+struct QmvLayout {
+  size_t codes, scl, bia, xq, xsum, xf, pl, vals, red, bar, total;
+};
+__host__ __device__ inline QmvLayout qmv_layout(int K, int rows) {
+  QmvLayout L;
+  const int KW = K / 8, KG = K / 64, nch = K / 512;
+  L.codes = 0;
+  L.scl = L.codes + size_t(rows) * KW * 4;
+  L.bia = L.scl + size_t(rows) * KG * 2;
+  L.xq = align16(L.bia + size_t(rows) * KG * 2);
+  L.xsum = L.xq + size_t(nch) * 8 * 32 * 16;
+  L.xf = L.xsum + size_t(nch) * 32 * 4;
+  L.pl = L.xf + size_t(K) * 4;
+  L.vals = L.pl + size_t(rows) * nch * 32 * 4;
+  L.red = L.vals + size_t(rows) * 4;
+  L.bar = align16(L.red + 64 * 4);
+  L.total = L.bar + 16;
+  return L;
+}
+
+size_t qmv_smem_bytes(const QmvArgs& a) {
+  const int rows = a.epi == kEpiSwiglu ? 2 * a.units_per_cta : a.units_per_cta;
+  return qmv_layout(a.K, rows).total;
+}
+
+// gdn_input.metal:419-431: 4-tap causal conv (tap 3 = current token), BF16
+// boundary, SiLU with the BF16-stepped sigmoid, then the history shift.
+__device__ __forceinline__ void gdn_conv_channel(int c, uint16_t raw, uint16_t* hist,
+                                                 const uint16_t* convw, uint16_t* conv_out) {
+  const uint16_t h0 = hist[c], h1 = hist[kGdnConv + c], h2 = hist[2 * kGdnConv + c];
+  float acc = 0.0f;
+  acc = fmaf(bf2f(h0), bf2f(convw[4 * c + 0]), acc);
+  acc = fmaf(bf2f(h1), bf2f(convw[4 * c + 1]), acc);
+  acc = fmaf(bf2f(h2), bf2f(convw[4 * c + 2]), acc);
+  acc = fmaf(bf2f(raw), bf2f(convw[4 * c + 3]), acc);
+  const float xq = bfr(acc);
+  conv_out[c] = f2bf(__fmul_rn(xq, sigmoid_bf(xq)));
+  hist[c] = h1;
+  hist[kGdnConv + c] = h2;
+  hist[2 * kGdnConv + c] = raw;
+}
+
+// attention.metal:55-70 / the RoPE table: cos/sin of position * inv_freq for
+// the 32 rotary pairs, evaluated in double from the f32 angle.
+__device__ __forceinline__ void rope_pair(uint32_t position, int pair, float* cs) {
+  const float arg = __fmul_rn(-__fdiv_rn(float(pair), 32.0f), 23.253496170043945f);
+  const float inv_freq = (float)exp2((double)arg);
+  const float angle = __fmul_rn(float(position), inv_freq);
+  cs[2 * pair] = (float)cos((double)angle);
+  cs[2 * pair + 1] = (float)sin((double)angle);
+}
+
+__global__ void __launch_bounds__(256) k_qmv(const __grid_constant__ QmvArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int K = a.K, KW = K / 8, KG = K / 64, nch = K / 512;
+  Piece pc[4];
+  const int np = qmv_pieces(a, blockIdx.x, pc);
+  int nrows = 0;
+  for (int i = 0; i < np; ++i) nrows += pc[i].count;
+  const int rows_alloc = a.epi == kEpiSwiglu ? 2 * a.units_per_cta : a.units_per_cta;
+  const QmvLayout L = qmv_layout(K, rows_alloc);
+  uint32_t* codes = reinterpret_cast<uint32_t*>(smem + L.codes);
+  uint16_t* scl = reinterpret_cast<uint16_t*>(smem + L.scl);
+  uint16_t* bia = reinterpret_cast<uint16_t*>(smem + L.bia);
+  float4* xq = reinterpret_cast<float4*>(smem + L.xq);
+  float* xsum = reinterpret_cast<float*>(smem + L.xsum);
+  float* xf = reinterpret_cast<float*>(smem + L.xf);
+  float* pl = reinterpret_cast<float*>(smem + L.pl);
+  float* vals = reinterpret_cast<float*>(smem + L.vals);
+  float* red = reinterpret_cast<float*>(smem + L.red);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.bar);
+
+  // 1. weights: bulk copies issued before the dependency wait.
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (tid == 0 && nrows > 0) {
+    uint32_t bytes = 0;
+    for (int i = 0; i < np; ++i) bytes += uint32_t(pc[i].count) * (KW * 4 + KG * 4);
+    mbar_expect_tx(bar, bytes);
+    int srow = 0;
+    for (int i = 0; i < np; ++i) {
+      const QmvSeg& s = a.seg[pc[i].seg];
+      const int n = pc[i].count;
+      bulk_g2s(codes + size_t(srow) * KW, s.w + size_t(pc[i].row0) * KW, uint32_t(n) * KW * 4, bar);
+      bulk_g2s(scl + size_t(srow) * KG, s.s + size_t(pc[i].row0) * KG, uint32_t(n) * KG * 2, bar);
+      bulk_g2s(bia + size_t(srow) * KG, s.b + size_t(pc[i].row0) * KG, uint32_t(n) * KG * 2, bar);
+      srow += n;
+    }
+  }
+
+  // 2. activations.
+  pdl_wait();
+  pdl_launch();
+  if (a.pro == kProPlain) {
+    for (int k = tid; k < K; k += blockDim.x) xf[k] = bf2f(a.x[k]);
+  } else if (a.pro == kProRms || a.pro == kProEmbedRms) {
+    float v[4];
+    if (a.pro == kProEmbedRms) {
+      // linear.metal:19-23 for the token the step consumes.
+      const uint32_t pos = ld_cg_u32(&a.ctl->pos);
+      uint32_t token = ld_cg_u32(&a.seq[pos]);
+      if (token >= uint32_t(kVocab)) {
+        if (tid == 0) atomicCAS(&a.ctl->err, 0u, kErrToken);
+        token = 0;
+      }
+      const uint32_t word = a.ew[size_t(token) * (kHidden / 8) + tid / 2];
+      const int g = int(token) * (kHidden / 64) + (4 * tid) / 64;
+      const float sc = bf2f(a.es[g]), bs = bf2f(a.eb[g]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int k = 4 * tid + j;
+        const uint32_t q = (word >> (4 * (k % 8))) & 15u;
+        v[j] = bfr(__fadd_rn(__fmul_rn(sc, float(q)), bs));
+      }
+      if (blockIdx.x == 0) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) a.h_out[4 * tid + j] = f2bf(v[j]);
+        if (tid == 0) {
+          a.ctl->pos_step = pos;
+          a.ctl->token_step = token;
+        }
+        if (tid < 32) rope_pair(pos, tid, a.ctl->rope_cs);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = bf2f(a.x[4 * tid + j]);
+    }
+    rms1024(v, a.gain, xf, red);
+  } else {  // kProNormGate: gdn.metal:238-254 for all 16 heads
+    for (int hh = warp; hh < kGdnHeads; hh += 8) {
+      float v[4], ss = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        v[i] = bf2f(a.gy[hh * 128 + 4 * lane + i]);
+        ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+      }
+      ss = warp_sum(ss);
+      const float inv = drsqrtf(__fadd_rn(__fdiv_rn(ss, 128.0f), 1e-6f));
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int d = 4 * lane + i;
+        const float norm = bfr(__fmul_rn(bfr(__fmul_rn(v[i], inv)), bf2f(a.gw[d])));
+        const float gate = bf2f(a.gz[hh * 128 + d]);
+        const float sy = __fdiv_rn(1.0f, __fadd_rn(1.0f, dexpf(fabsf(gate))));
+        const float sig = gate < 0.0f ? sy : __fsub_rn(1.0f, sy);
+        xf[hh * 128 + d] = bfr(__fmul_rn(__fmul_rn(gate, sig), norm));
+      }
+    }
+  }
+  __syncthreads();
+  build_xq(xf, K, xq, xsum);
+  __syncthreads();
+
+  // 3. dot products from shared memory.
+  mbar_wait(bar, 0, a.ctl, kErrQmvWait);
+  const int ngroups = (nrows + 3) / 4;
+  for (int task = warp; task < ngroups * nch; task += 8) {
+    const int g = task / nch, c = task % nch;
+    qmv_chunk_task(codes, scl, bia, nrows, 4 * g, c, K, xq, xsum, pl, lane);
+  }
+  __syncthreads();
+  for (int g = warp; g < ngroups; g += 8) qmv_finish_task(pl, nrows, 4 * g, nch, vals, lane);
+  __syncthreads();
+
+  // 4. epilogue.
+  if (a.epi == kEpiSwiglu) {
+    const int n = pc[0].count;
+    for (int i = tid; i < n; i += blockDim.x)
+      a.seg[0].y[pc[0].row0 + i] = swiglu_bf(bfr(vals[i]), bfr(vals[n + i]));
+    return;
+  }
+  int srow = 0;
+  for (int p = 0; p < np; ++p) {
+    const QmvSeg& s = a.seg[pc[p].seg];
+    for (int i = tid; i < pc[p].count; i += blockDim.x) {
+      const float v = vals[srow + i];
+      const int row = pc[p].row0 + i;
+      if (a.epi == kEpiResAdd) {
+        a.res[row] = f2bf(__fadd_rn(bf2f(a.res[row]), bfr(v)));
+      } else if (a.epi == kEpiGdnConv && pc[p].seg == 0) {
+        gdn_conv_channel(row, f2bf(v), a.hist, a.convw, a.conv_out);
+      } else {
+        s.y[row] = f2bf(v);
+      }
+    }
+    srow += pc[p].count;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// GDN recurrence (gdn.metal:176-228, T = 1) with the Q/K normalisation and
+// gates of gdn_input.metal:433-460. Grid (8 row blocks, 16 heads) x 64
+// threads; thread = (value row, quarter of the key axis), 32 f32 of state.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(64) k_gdn_recur(const __grid_constant__ RecurArgs a) {
+  __shared__ __align__(16) float st[16 * 128];
+  __shared__ float qn[128], kn[128], gb[2];
+  __shared__ __align__(8) uint64_t bar;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int rb = blockIdx.x, h = blockIdx.y;
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    mbar_expect_tx(&bar, 16 * 128 * 4);
+    bulk_g2s(st, a.state + (size_t(h) * 128 + rb * 16) * 128, 16 * 128 * 4, &bar);
+  }
+  pdl_wait();
+  pdl_launch();
+  if (a.advance_pos && rb == 0 && h == 0 && tid == 0) a.ctl->pos = a.ctl->pos_step + 1;
+  {
+    // warp 0 -> q, warp 1 -> k: gdn_input.metal:433-441
+    const int base = warp == 0 ? h * 128 : 2048 + h * 128;
+    float v[4], ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[i] = bf2f(a.conv[base + 4 * lane + i]);
+      ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+    }
+    ss = warp_sum(ss);
+    const float inv = drsqrtf(__fadd_rn(__fdiv_rn(ss, 128.0f), 1.0e-6f / 128.0f));
+    const float scale = warp == 0 ? 0.0078125f : bfr(0.08838834764831845f);
+    float* dst = warp == 0 ? qn : kn;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dst[4 * lane + i] = bfr(__fmul_rn(bfr(__fmul_rn(v[i], inv)), scale));
+  }
+  if (tid == 0) {
+    // gdn_input.metal:454-459
+    const float av = bf2f(a.a_raw[h]), bv = bf2f(a.b_raw[h]);
+    const float ax = bfr(__fadd_rn(av, bf2f(a.dt_bias[h])));
+    const float e1 = dexpf(a.a_log[h]);
+    gb[0] = dexpf(__fmul_rn(-e1, softplus_bf(ax)));
+    gb[1] = bfr(sigmoid_bf(bv));
+  }
+  __syncthreads();
+  mbar_wait(&bar, 0, a.ctl, kErrRecurWait);
+  const int row = tid >> 2, r = tid & 3;
+  const int vrow = rb * 16 + row;
+  const float gt = gb[0], beta = gb[1];
+  float s[32];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 t = *reinterpret_cast<const float4*>(&st[row * 128 + r * 32 + i * 4]);
+    s[i * 4 + 0] = t.x;
+    s[i * 4 + 1] = t.y;
+    s[i * 4 + 2] = t.z;
+    s[i * 4 + 3] = t.w;
+  }
+  const float* kk = kn + r * 32;
+  const float* qq = qn + r * 32;
+  float part[8];
+#pragma unroll
+  for (int pb = 0; pb < 8; ++pb) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int e = pb * 4 + i;
+      s[e] = __fmul_rn(s[e], gt);
+      acc = __fadd_rn(acc, __fmul_rn(s[e], kk[e]));
+    }
+    part[pb] = acc;
+  }
+  float memory = __fadd_rn(__fadd_rn(__fadd_rn(part[0], part[1]), __fadd_rn(part[2], part[3])),
+                           __fadd_rn(__fadd_rn(part[4], part[5]), __fadd_rn(part[6], part[7])));
+  memory = __fadd_rn(memory, __shfl_xor_sync(0xffffffffu, memory, 1));
+  memory = __fadd_rn(memory, __shfl_xor_sync(0xffffffffu, memory, 2));
+  const float delta = __fmul_rn(__fsub_rn(bf2f(a.conv[4096 + h * 128 + vrow]), memory), beta);
+#pragma unroll
+  for (int pb = 0; pb < 8; ++pb) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int e = pb * 4 + i;
+      s[e] = __fadd_rn(s[e], __fmul_rn(kk[e], delta));
+      acc = __fadd_rn(acc, __fmul_rn(s[e], qq[e]));
+    }
+    part[pb] = acc;
+  }
+  float out = __fadd_rn(__fadd_rn(__fadd_rn(part[0], part[1]), __fadd_rn(part[2], part[3])),
+                        __fadd_rn(__fadd_rn(part[4], part[5]), __fadd_rn(part[6], part[7])));
+  out = __fadd_rn(out, __shfl_xor_sync(0xffffffffu, out, 1));
+  out = __fadd_rn(out, __shfl_xor_sync(0xffffffffu, out, 2));
+  if (r == 0) a.y[h * 128 + vrow] = f2bf(out);
+  float4* dst = reinterpret_cast<float4*>(a.state + (size_t(h) * 128 + vrow) * 128 + r * 32);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) dst[i] = make_float4(s[4 * i], s[4 * i + 1], s[4 * i + 2], s[4 * i + 3]);
+}
+
+// Standalone conv/history step (the op-level GDN entry point; the decode
+// step fuses the same channel function into the projection epilogue).
+__global__ void k_gdn_conv(const uint16_t* raw, uint16_t* hist, const uint16_t* convw,
+                           uint16_t* conv_out) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c < kGdnConv) gdn_conv_channel(c, raw[c], hist, convw, conv_out);
+}
+
+// ---------------------------------------------------------------------------
+// GQA decode attention, bit-exact with the reference's two routes
+// (attention_decode.metal):
+//   len <  1024: sdpa_vector (:51-213): 32 chains per query head, chain g
+//                visits keys g, g+32, ...; f32 partials, then the in-group
+//                combine (:194-212) and attn_gate (attention.metal:133-151);
+//   len >= 1024: sdpa_vector_2pass_1 (:215-431): 64 chains, chain b visits
+//                keys b, b+64, ...; bf16 unnormalised partials, then
+//                attn_decode_split2_gate (:830-891).
+// Each chain is an online softmax over its keys in order:
+//   m' = max(m, s); f = exp(m - m'); e = exp(s - m'); S = S*f + e;
+//   o = o*f + e*v.
+// One CTA owns one chain for the four query heads of a kv head, so every
+// K/V row is read once. Rows stream through a ring of bulk copies. Scores use
+// the reference's per-lane order (eight products per lane, then a SIMD sum);
+// the running max is a prefix scan and f, e are independent, so only the S/o
+// recurrence runs key by key. The last CTA of each kv head combines the
+// chains and applies the BF16 output gate.
+// ---------------------------------------------------------------------------
+struct AttnSmem {
+  uint16_t kt[kAttnStages][kAttnTile][kHeadDim];
+  uint16_t vt[kAttnStages][kAttnTile][kHeadDim];
+  float q[4][kHeadDim];
+  float nrm[5][kHeadDim];
+  float kr[kHeadDim];
+  uint16_t kf[kHeadDim], vf[kHeadDim];
+  float sc[4][kAttnTile];
+  uint64_t bar[kAttnStages];
+  int last;
+};
+
+size_t attn_smem_bytes() { return sizeof(AttnSmem); }
+
+// Per-head RMSNorm (attention.metal:37-53: two 32-thread partials of 128
+// values) followed by partial RoPE (attention.metal:55-70). One warp, one
+// head; out[d] gets the bf16 value as f32.
+__device__ __forceinline__ void head_norm_rope(const uint16_t* x, const uint16_t* gain,
+                                               const float* cs, float* nrm, float* out, int lane) {
+  float pa = 0.0f, pb = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float va = bf2f(x[4 * lane + i]), vb = bf2f(x[128 + 4 * lane + i]);
+    pa = __fadd_rn(pa, __fmul_rn(va, va));
+    pb = __fadd_rn(pb, __fmul_rn(vb, vb));
+  }
+  const float s0 = warp_sum(pa), s1 = warp_sum(pb);
+  const float inv = drsqrtf(__fadd_rn(__fdiv_rn(__fadd_rn(s0, s1), 256.0f), 1e-6f));
+  for (int d = lane; d < kHeadDim; d += 32)
+    nrm[d] = bfr(__fmul_rn(bfr(__fmul_rn(bf2f(x[d]), inv)), bf2f(gain[d])));
+  __syncwarp();
+  for (int d = lane; d < kHeadDim; d += 32) {
+    float v = nrm[d];
+    if (d < 64) {
+      const int pair = d & 31;
+      const float c = cs[2 * pair], s = cs[2 * pair + 1];
+      const float lo = nrm[pair], hi = nrm[pair + 32];
+      v = d < 32 ? bfr(__fsub_rn(__fmul_rn(lo, c), __fmul_rn(hi, s)))
+                 : bfr(__fadd_rn(__fmul_rn(lo, s), __fmul_rn(hi, c)));
+    }
+    out[d] = v;
+  }
+  __syncwarp();
+}
+
+// Butterfly-order transpose reduction of 16 per-lane values: afterwards lane
+// L (and L^1) holds the sum of value (L >> 1).
+__device__ __forceinline__ float reduce16(float* v, int lane) {
+#pragma unroll
+  for (int m = 16, h = 8; m >= 2; m >>= 1, h >>= 1) {
+    const bool hi = lane & m;
+#pragma unroll
+    for (int i = 0; i < h; ++i) {
+      const float keep = hi ? v[i + h] : v[i];
+      const float send = hi ? v[i] : v[i + h];
+      v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, m));
+    }
+  }
+  return __fadd_rn(v[0], __shfl_xor_sync(0xffffffffu, v[0], 1));
+}
+
+__global__ void __launch_bounds__(kAttnThreads) k_attn(const __grid_constant__ AttnArgs a) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  AttnSmem& S = *reinterpret_cast<AttnSmem*>(smem_raw);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int chain = blockIdx.x, kh = blockIdx.y;
+  const uint32_t cap = a.capacity;
+  constexpr float kMin = -3.4028234663852886e38f;
+
+  // pos_step was written by the step's first launch (>= 2 launches back).
+  const uint32_t pos = ld_cg_u32(&a.ctl->pos_step);
+  const uint32_t len = pos + 1;
+  const bool split = len >= 1024;
+  const int stride = split ? 64 : 32;
+  const int nkeys = (chain < stride && uint32_t(chain) < len) ? int((len - 1 - chain) / stride) + 1 : 0;
+  const int ntiles = (nkeys + kAttnTile - 1) / kAttnTile;
+  const uint16_t* kbase = a.kcache + size_t(kh) * cap * kHeadDim;
+  const uint16_t* vbase = a.vcache + size_t(kh) * cap * kHeadDim;
+  // the current token is key `pos`: chain pos % stride, local index pos / stride
+  const bool owner = chain == int(pos % stride);
+  const int own_idx = int(pos / stride);
+
+  auto issue = [&](int t, int st) {  // warp 0 only
+    const int n = min(kAttnTile, nkeys - t * kAttnTile);
+    if (lane == 0) mbar_expect_tx(&S.bar[st], uint32_t(n) * 2 * kHeadDim * 2);
+    __syncwarp();
+    if (lane < n) {
+      const size_t key = size_t(chain) + size_t(stride) * size_t(t * kAttnTile + lane);
+      bulk_g2s(&S.kt[st][lane][0], kbase + key * kHeadDim, kHeadDim * 2, &S.bar[st]);
+      bulk_g2s(&S.vt[st][lane][0], vbase + key * kHeadDim, kHeadDim * 2, &S.bar[st]);
+    }
+  };
+  if (tid == 0) {
+    for (int s = 0; s < kAttnStages; ++s) mbar_init(&S.bar[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (warp == 0)
+    for (int t = 0; t < kAttnStages && t < ntiles; ++t) issue(t, t);
+  pdl_wait();
+  pdl_launch();
+
+  // Query heads 4kh..4kh+3 (warps 0-3) scaled by 1/16 (attention_decode.metal:289);
+  // warp 4 prepares the current token's key (attention.metal:295-311).
+  if (warp < 4) {
+    const int qh = 4 * kh + warp;
+    head_norm_rope(a.q_raw + qh * 512, a.q_gain, a.ctl->rope_cs, S.nrm[warp], S.q[warp], lane);
+    for (int d = lane; d < kHeadDim; d += 32) S.q[warp][d] = __fmul_rn(0.0625f, S.q[warp][d]);
+  } else if (warp == 4) {
+    head_norm_rope(a.k_raw + kh * kHeadDim, a.k_gain, a.ctl->rope_cs, S.nrm[4], S.kr, lane);
+    for (int d = lane; d < kHeadDim; d += 32) {
+      S.kf[d] = f2bf(S.kr[d]);
+      S.vf[d] = a.v_raw[kh * kHeadDim + d];
+    }
+    __syncwarp();
+    if (owner) {
+      const size_t ci = (size_t(kh) * cap + pos) * kHeadDim;
+      for (int d = lane; d < kHeadDim; d += 32) {
+        a.kcache[ci + d] = S.kf[d];
+        a.vcache[ci + d] = S.vf[d];
+      }
+    }
+  }
+  __syncthreads();
+
+  // score lanes: lane l owns dims 8l..8l+7 of every head (as the reference).
+  float qreg[4][8];
+#pragma unroll
+  for (int h = 0; h < 4; ++h)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) qreg[h][e] = S.q[h][8 * lane + e];
+  // recurrence lanes: warp w -> head w>>1, dims (w&1)*128 + 4*lane .. +3.
+  const int rh = warp >> 1, d0 = (warp & 1) * 128 + 4 * lane;
+  float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  float msum = kMin, ssum = 0.0f;
+
+  for (int t = 0; t < ntiles; ++t) {
+    const int st = t % kAttnStages;
+    mbar_wait(&S.bar[st], uint32_t(t / kAttnStages) & 1u, a.ctl, kErrAttnWait);
+    const int nk = min(kAttnTile, nkeys - t * kAttnTile);
+    if (owner && own_idx / kAttnTile == t) {
+      __syncthreads();
+      if (warp == 0)
+        for (int d = lane; d < kHeadDim; d += 32) {
+          S.kt[st][own_idx % kAttnTile][d] = S.kf[d];
+          S.vt[st][own_idx % kAttnTile][d] = S.vf[d];
+        }
+      __syncthreads();
+    }
+    // scores: warp w takes keys 4w..4w+3 of the tile for the four heads
+    {
+      float v[16];
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        const uint4 kv = *reinterpret_cast<const uint4*>(&S.kt[st][4 * warp + jj][8 * lane]);
+        const float k8[8] = {bf_lo(kv.x), bf_hi(kv.x), bf_lo(kv.y), bf_hi(kv.y),
+                             bf_lo(kv.z), bf_hi(kv.z), bf_lo(kv.w), bf_hi(kv.w)};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          float sc = 0.0f;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) sc = __fadd_rn(sc, __fmul_rn(qreg[h][e], k8[e]));
+          v[h * 4 + jj] = sc;
+        }
+      }
+      const float r = reduce16(v, lane);
+      if ((lane & 1) == 0) S.sc[lane >> 3][4 * warp + ((lane >> 1) & 3)] = r;
+    }
+    __syncthreads();
+    // running max as a prefix scan, then the independent exps
+    {
+      const float s = lane < nk ? S.sc[rh][lane] : -INFINITY;
+      float v = s;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const float u = __shfl_up_sync(0xffffffffu, v, off);
+        if (lane >= off) v = fmaxf(v, u);
+      }
+      const float mt = fmaxf(msum, v);
+      float mprev = __shfl_up_sync(0xffffffffu, mt, 1);
+      if (lane == 0) mprev = msum;
+      const float f = fexp(__fsub_rn(mprev, mt));
+      const float e = fexp(__fsub_rn(s, mt));
+      msum = __shfl_sync(0xffffffffu, mt, nk - 1);
+      for (int j = 0; j < nk; ++j) {
+        const float fj = __shfl_sync(0xffffffffu, f, j);
+        const float ej = __shfl_sync(0xffffffffu, e, j);
+        ssum = __fadd_rn(__fmul_rn(ssum, fj), ej);
+        const uint2 vv = *reinterpret_cast<const uint2*>(&S.vt[st][j][d0]);
+        const float v4[4] = {bf_lo(vv.x), bf_hi(vv.x), bf_lo(vv.y), bf_hi(vv.y)};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[i] = __fadd_rn(__fmul_rn(o[i], fj), __fmul_rn(ej, v4[i]));
+      }
+    }
+    __syncthreads();
+    if (warp == 0 && t + kAttnStages < ntiles) {
+      if (lane == 0) fence_proxy_async();
+      __syncwarp();
+      issue(t + kAttnStages, st);
+    }
+  }
+
+  // chain partials (bf16-rounded on the split route, attention_decode.metal:428-430)
+  {
+    float* po = a.part_o + ((size_t(kh) * kAttnChains + chain) * 4 + rh) * kHeadDim;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) po[d0 + i] = split ? bfr(o[i]) : o[i];
+    if ((warp & 1) == 0 && lane == 0) {
+      float* pml = a.part_ml + ((size_t(kh) * kAttnChains + chain) * 4 + rh) * 2;
+      pml[0] = msum;
+      pml[1] = ssum;
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) S.last = (atomicAdd(&a.ctl->attn_counter[kh], 1u) == kAttnChains - 1);
+  __syncthreads();
+  if (!S.last) return;
+  __threadfence();
+
+  // combine the chains of the four heads; task = (head, stripe of 8 dims)
+  for (int task = warp; task < 4 * 32; task += kAttnThreads / 32) {
+    const int h = task >> 5, stripe = task & 31;
+    const int qh = 4 * kh + h;
+    const size_t base = size_t(kh) * kAttnChains * 4 + h;  // + chain * 4
+    float res[8];
+    if (split) {
+      // attn_decode_split2_gate (attention_decode.metal:853-876): lane l owns chains l, l+32
+      const float ma = __ldcg(&a.part_ml[(base + size_t(lane) * 4) * 2]);
+      const float mb = __ldcg(&a.part_ml[(base + size_t(lane + 32) * 4) * 2]);
+      const float M = warp_max(fmaxf(fmaxf(kMin, ma), mb));
+      const float fa = fexp(__fsub_rn(ma, M)), fb = fexp(__fsub_rn(mb, M));
+      float sacc = 0.0f;
+      sacc = __fadd_rn(sacc, __fmul_rn(fa, __ldcg(&a.part_ml[(base + size_t(lane) * 4) * 2 + 1])));
+      sacc = __fadd_rn(sacc, __fmul_rn(fb, __ldcg(&a.part_ml[(base + size_t(lane + 32) * 4) * 2 + 1])));
+      const float ssum_all = warp_sum(sacc);
+      const float* pa = a.part_o + (base + size_t(lane) * 4) * kHeadDim + stripe * 8;
+      const float* pb = a.part_o + (base + size_t(lane + 32) * 4) * kHeadDim + stripe * 8;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float acc = 0.0f;
+        acc = __fadd_rn(acc, __fmul_rn(fa, __ldcg(pa + i)));
+        acc = __fadd_rn(acc, __fmul_rn(fb, __ldcg(pb + i)));
+        const float ov = warp_sum(acc);
+        res[i] = ssum_all == 0.0f ? ov : __fdiv_rn(ov, ssum_all);
+      }
+    } else {
+      // sdpa_vector's final reduction (attention_decode.metal:194-212): lane l = group l
+      const float ml = __ldcg(&a.part_ml[(base + size_t(lane) * 4) * 2]);
+      const float M = warp_max(ml);
+      const float fl = fexp(__fsub_rn(ml, M));
+      const float ssum_all =
+          warp_sum(__fmul_rn(__ldcg(&a.part_ml[(base + size_t(lane) * 4) * 2 + 1]), fl));
+      const float* pl = a.part_o + (base + size_t(lane) * 4) * kHeadDim + stripe * 8;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float ov = warp_sum(__fmul_rn(__ldcg(pl + i), fl));
+        res[i] = ssum_all == 0.0f ? ov : __fdiv_rn(ov, ssum_all);
+      }
+    }
+    if (lane < 8) {
+      // BF16 output gate, attention.metal:144-150 (same expression in :882-889)
+      float r = res[0];
+#pragma unroll
+      for (int i = 1; i < 8; ++i) r = lane == i ? res[i] : r;
+      const int d = stripe * 8 + lane;
+      const float attention = bfr(r);
+      const float x = bf2f(a.q_raw[qh * 512 + 256 + d]);
+      const float e = bfr(dexpf(fabsf(x)));
+      const float denom = bfr(__fadd_rn(1.0f, e));
+      const float inverse = bfr(__fdiv_rn(1.0f, denom));
+      const float gate = bfr(x < 0.0f ? inverse : __fsub_rn(1.0f, inverse));
+      a.gated[qh * kHeadDim + d] = f2bf(__fmul_rn(attention, gate));
+    }
+  }
+  if (tid == 0) atomicExch(&a.ctl->attn_counter[kh], 0u);
+}
+
+// Sets the control block of a standalone attention call: the position and
+// its RoPE table (the decode step's first launch does this in-line).
+__global__ void k_ctl_position(Ctl* ctl, uint32_t pos) {
+  if (threadIdx.x == 0) {
+    ctl->pos_step = pos;
+    ctl->pos = pos;
+    ctl->err = 0;
+    ctl->attn_counter[0] = 0;
+    ctl->attn_counter[1] = 0;
+    ctl->head_counter = 0;
+    ctl->out_count = 0;
+  }
+  if (threadIdx.x < 32) rope_pair(pos, threadIdx.x, ctl->rope_cs);
+}
+
+// ---------------------------------------------------------------------------
+// Vocabulary head: final RMSNorm, Q4 projection of 248,320 tied-embedding
+// rows streamed through a bulk-copy ring, per-CTA online (max, sum exp), then
+// the last-arriving CTA forms lse = bf16(log(sum) + max) and picks the lowest
+// id among the maxima of bf16(logit - lse) (head_lse.metal:66-98). Only CTAs
+// whose own maximum reaches the winning value are rescanned.
+// ---------------------------------------------------------------------------
+// Last-CTA tail shared by the head and the standalone greedy kernel:
+// lse = bf16(log(sum) + max) from the per-CTA (max, sum) partials, then the
+// lowest id among the maxima of bf16(logit - lse) (head_lse.metal:66-98).
+// Only the first CTA whose own maximum reaches the winning value is rescanned.
+__device__ void head_finish(const HeadArgs& a, float* red, uint32_t* cand, uint32_t* best) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __threadfence();
+  if (warp == 0) {
+    float M = -INFINITY;
+    for (int c = lane; c < int(gridDim.x); c += 32) M = fmaxf(M, __ldcg(&a.part[2 * c]));
+    M = warp_max(M);
+    float s = 0.0f;
+    for (int c = lane; c < int(gridDim.x); c += 32) {
+      const float sc = __ldcg(&a.part[2 * c + 1]);
+      if (sc > 0.0f) s += sc * expf(__ldcg(&a.part[2 * c]) - M);
+    }
+    s = warp_sum(s);
+    if (lane == 0) {
+      const uint16_t lse = f2bf(__fadd_rn(dlogf(s), M));
+      red[0] = bf2f(lse);
+      red[1] = bfr(__fsub_rn(M, bf2f(lse)));
+      *cand = 0xffffffffu;
+      *best = 0xffffffffu;
+      if (a.lse_out) a.lse_out[0] = lse;
+    }
+  }
+  __syncthreads();
+  const float lse = red[0], W = red[1];
+  for (int c = tid; c < int(gridDim.x); c += blockDim.x)
+    if (bfr(__fsub_rn(__ldcg(&a.part[2 * c]), lse)) == W) atomicMin(cand, uint32_t(c));
+  __syncthreads();
+  const uint32_t c = *cand;
+  if (c != 0xffffffffu) {
+    const int rb = int(c) * kHeadRowsPerCta;
+    const int re = min(kVocab, rb + kHeadRowsPerCta);
+    for (int r = rb + tid; r < re; r += blockDim.x) {
+      const float lv = bf2f(__ldcg(&a.logits[r]));
+      if (bfr(__fsub_rn(lv, lse)) == W) atomicMin(best, uint32_t(r));
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    const uint32_t token = *best == 0xffffffffu ? 0u : *best;
+    Ctl* ctl = a.ctl;
+    const uint32_t ps = ctl->pos_step;
+    if (a.seq && ps + 1 < a.seq_len) a.seq[ps + 1] = token;
+    const uint32_t oc = ctl->out_count;
+    if (a.out_tokens && oc < a.out_len) a.out_tokens[oc] = token;
+    ctl->out_count = oc + 1;
+    ctl->head_counter = 0;
+  }
+}
+
+// Per-CTA (max, sum exp) of a row range of bf16 logits, combined into the
+// CTA's partial; returns whether this CTA arrived last.
+__device__ bool head_partial(const HeadArgs& a, float run_m, float run_s, float* wm, float* ws,
+                             int* last) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float M = warp_max(run_m);
+  float s = run_s > 0.0f ? run_s * __expf(run_m - M) : 0.0f;
+  s = warp_sum(s);
+  if (lane == 0) {
+    wm[warp] = M;
+    ws[warp] = s;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    const int nw = blockDim.x / 32;
+    float MM = wm[0];
+    for (int w = 1; w < nw; ++w) MM = fmaxf(MM, wm[w]);
+    float ss = 0.0f;
+    for (int w = 0; w < nw; ++w)
+      if (ws[w] > 0.0f) ss += ws[w] * __expf(wm[w] - MM);
+    a.part[2 * blockIdx.x] = MM;
+    a.part[2 * blockIdx.x + 1] = ss;
+    __threadfence();
+    *last = (atomicAdd(&a.ctl->head_counter, 1u) == gridDim.x - 1);
+  }
+  __syncthreads();
+  return *last != 0;
+}
+
+struct HeadSmem {
+  uint32_t codes[kHeadStages][kHeadRowsPerChunk * 128];
+  uint16_t scl[kHeadStages][kHeadRowsPerChunk * 16];
+  uint16_t bia[kHeadStages][kHeadRowsPerChunk * 16];
+  float4 xq[2 * 8 * 32];
+  float xsum[2 * 32];
+  float xf[kHidden];
+  float pl[kHeadRowsPerChunk * 2 * 32];
+  float vals[kHeadRowsPerChunk];
+  float red[64];
+  float wm[8], ws[8];
+  uint64_t bar[kHeadStages];
+  int last;
+  uint32_t cand;
+  uint32_t best;
+};
+size_t head_smem_bytes() { return sizeof(HeadSmem); }
+
+__global__ void __launch_bounds__(256) k_head(const __grid_constant__ HeadArgs a) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  HeadSmem& S = *reinterpret_cast<HeadSmem*>(smem_raw);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int r0 = blockIdx.x * kHeadRowsPerCta;
+  const int nrows = min(kHeadRowsPerCta, kVocab - r0);
+  const int nchunks = (nrows + kHeadRowsPerChunk - 1) / kHeadRowsPerChunk;
+  auto issue = [&](int ch, int st) {
+    const int rows = min(kHeadRowsPerChunk, nrows - ch * kHeadRowsPerChunk);
+    const size_t row = size_t(r0) + size_t(ch) * kHeadRowsPerChunk;
+    mbar_expect_tx(&S.bar[st], uint32_t(rows) * (512 + 64));
+    bulk_g2s(S.codes[st], a.w + row * 128, uint32_t(rows) * 512, &S.bar[st]);
+    bulk_g2s(S.scl[st], a.s + row * 16, uint32_t(rows) * 32, &S.bar[st]);
+    bulk_g2s(S.bia[st], a.b + row * 16, uint32_t(rows) * 32, &S.bar[st]);
+  };
+  if (tid == 0) {
+    for (int s = 0; s < kHeadStages; ++s) mbar_init(&S.bar[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (tid == 0)
+    for (int s = 0; s < kHeadStages && s < nchunks; ++s) issue(s, s);
+  pdl_wait();
+  pdl_launch();
+  {
+    float v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = bf2f(a.x[4 * tid + j]);
+    if (a.gain) {
+      rms1024(v, a.gain, S.xf, S.red);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) S.xf[4 * tid + j] = v[j];
+    }
+  }
+  __syncthreads();
+  build_xq(S.xf, kHidden, S.xq, S.xsum);
+  __syncthreads();
+
+  float run_m = -INFINITY, run_s = 0.0f;  // per-thread online LSE over its logits
+  for (int ch = 0; ch < nchunks; ++ch) {
+    const int st = ch % kHeadStages;
+    mbar_wait(&S.bar[st], uint32_t(ch / kHeadStages) & 1u, a.ctl, kErrHeadWait);
+    const int rows = min(kHeadRowsPerChunk, nrows - ch * kHeadRowsPerChunk);
+    for (int task = warp; task < 16; task += 8) {
+      const int g = task >> 1, c = task & 1;
+      if (4 * g < rows)
+        qmv_chunk_task(S.codes[st], S.scl[st], S.bia[st], rows, 4 * g, c, kHidden, S.xq, S.xsum,
+                       S.pl, lane);
+    }
+    __syncthreads();
+    if (4 * warp < rows) qmv_finish_task(S.pl, rows, 4 * warp, 2, S.vals, lane);
+    __syncthreads();
+    if (tid < rows) {
+      const uint16_t lb = f2bf(S.vals[tid]);
+      a.logits[r0 + ch * kHeadRowsPerChunk + tid] = lb;
+      const float lv = bf2f(lb);
+      if (lv > run_m) {
+        run_s = run_s * __expf(run_m - lv) + 1.0f;
+        run_m = lv;
+      } else {
+        run_s += __expf(lv - run_m);
+      }
+    }
+    if (tid == 0 && ch + kHeadStages < nchunks) {
+      fence_proxy_async();
+      issue(ch + kHeadStages, st);
+    }
+  }
+  head_partial(a, run_m, run_s, S.wm, S.ws, &S.last);
+  if (!S.last) return;
+  head_finish(a, S.red, &S.cand, &S.best);
+}
+
+
+// Greedy selection on given logits (greedy_bf16, linear.metal:400-449), with
+// the head's partition and tail.
+__global__ void __launch_bounds__(256) k_greedy(const __grid_constant__ HeadArgs a) {
+  __shared__ float red[64], wm[8], ws[8];
+  __shared__ int last;
+  __shared__ uint32_t cand, best;
+  const int r0 = blockIdx.x * kHeadRowsPerCta;
+  const int r1 = min(kVocab, r0 + kHeadRowsPerCta);
+  float run_m = -INFINITY, run_s = 0.0f;
+  for (int r = r0 + threadIdx.x; r < r1; r += blockDim.x) {
+    const float lv = bf2f(a.logits[r]);
+    if (lv > run_m) {
+      run_s = run_s * __expf(run_m - lv) + 1.0f;
+      run_m = lv;
+    } else {
+      run_s += __expf(lv - run_m);
+    }
+  }
+  if (!head_partial(a, run_m, run_s, wm, ws, &last)) return;
+  head_finish(a, red, &cand, &best);
+}
+
+// Embedding row (linear.metal:11-24), standalone op.
+__global__ void k_embedding(const uint32_t* w, const uint16_t* s, const uint16_t* b, uint32_t token,
+                            int K, uint16_t* out) {
+  const int k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= K) return;
+  const uint32_t q = (w[size_t(token) * (K / 8) + k / 8] >> (4 * (k % 8))) & 15u;
+  const size_t g = size_t(token) * (K / 64) + k / 64;
+  out[k] = f2bf(__fadd_rn(__fmul_rn(bf2f(s[g]), float(q)), bf2f(b[g])));
+}
+
+// RMSNorm of one 1024 vector, standalone op (same device path as the fused
+// prologues).
+__global__ void __launch_bounds__(256) k_rms1024(const uint16_t* x, const uint16_t* gain,
+                                                 uint16_t* out) {
+  __shared__ float xf[kHidden];
+  __shared__ float red[64];
+  float v[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) v[j] = bf2f(x[4 * threadIdx.x + j]);
+  rms1024(v, gain, xf, red);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) out[4 * threadIdx.x + j] = f2bf(xf[4 * threadIdx.x + j]);
+}
+
+// ---------------------------------------------------------------------------
+// host-side launch helpers
+// ---------------------------------------------------------------------------
+template <typename Arg>
+static cudaError_t launch_ex(void (*kern)(Arg), dim3 grid, dim3 block, size_t smem,
+                             cudaStream_t stream, bool pdl, Arg arg) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  int n = 0;
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kern, arg);
+}
+
+cudaError_t kernels_init() {
+  cudaError_t e;
+  e = cudaFuncSetAttribute(k_qmv, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(k_attn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           int(attn_smem_bytes()));
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(k_head, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           int(head_smem_bytes()));
+  return e;
+}
+
+cudaError_t launch_qmv(const QmvArgs& a, cudaStream_t st, bool pdl) {
+  const int grid = (a.units + a.units_per_cta - 1) / a.units_per_cta;
+  return launch_ex(k_qmv, dim3(grid), dim3(256), qmv_smem_bytes(a), st, pdl, a);
+}
+cudaError_t launch_recur(const RecurArgs& a, cudaStream_t st, bool pdl) {
+  return launch_ex(k_gdn_recur, dim3(8, kGdnHeads), dim3(64), 0, st, pdl, a);
+}
+cudaError_t launch_attn(const AttnArgs& a, cudaStream_t st, bool pdl) {
+  return launch_ex(k_attn, dim3(kAttnChains, kKvHeads), dim3(kAttnThreads), attn_smem_bytes(), st,
+                   pdl, a);
+}
+cudaError_t launch_head(const HeadArgs& a, cudaStream_t st, bool pdl) {
+  return launch_ex(k_head, dim3(kHeadCtas), dim3(256), head_smem_bytes(), st, pdl, a);
+}
+cudaError_t launch_greedy(const HeadArgs& a, cudaStream_t st) {
+  return launch_ex(k_greedy, dim3(kHeadCtas), dim3(256), 0, st, false, a);
+}
+cudaError_t launch_gdn_conv(const uint16_t* raw, uint16_t* hist, const uint16_t* convw,
+                            uint16_t* conv_out, cudaStream_t st) {
+  k_gdn_conv<<<kGdnConv / 256, 256, 0, st>>>(raw, hist, convw, conv_out);
+  return cudaGetLastError();
+}
+cudaError_t launch_ctl_position(Ctl* ctl, uint32_t pos, cudaStream_t st) {
+  k_ctl_position<<<1, 32, 0, st>>>(ctl, pos);
+  return cudaGetLastError();
+}
+cudaError_t launch_embedding(const uint32_t* w, const uint16_t* s, const uint16_t* b,
+                             uint32_t token, int K, uint16_t* out, cudaStream_t st) {
+  k_embedding<<<(K + 255) / 256, 256, 0, st>>>(w, s, b, token, K, out);
+  return cudaGetLastError();
+}
+cudaError_t launch_rms1024(const uint16_t* x, const uint16_t* gain, uint16_t* out,
+                           cudaStream_t st) {
+  k_rms1024<<<1, 256, 0, st>>>(x, gain, out);
+  return cudaGetLastError();
+}
+
+}  // namespace q35

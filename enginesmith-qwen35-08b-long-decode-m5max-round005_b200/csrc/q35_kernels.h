@@ -1,0 +1,28 @@
+// Host-side launchers of the q35 decode kernels (implemented in q35_kernels.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+#include "q35_types.h"
+
+namespace q35 {
+
+cudaError_t kernels_init();
+size_t qmv_smem_bytes(const QmvArgs& a);
+size_t attn_smem_bytes();
+size_t head_smem_bytes();
+
+cudaError_t launch_qmv(const QmvArgs& a, cudaStream_t st, bool pdl);
+cudaError_t launch_recur(const RecurArgs& a, cudaStream_t st, bool pdl);
+cudaError_t launch_attn(const AttnArgs& a, cudaStream_t st, bool pdl);
+cudaError_t launch_head(const HeadArgs& a, cudaStream_t st, bool pdl);
+cudaError_t launch_greedy(const HeadArgs& a, cudaStream_t st);
+cudaError_t launch_gdn_conv(const uint16_t* raw, uint16_t* hist, const uint16_t* convw,
+                            uint16_t* conv_out, cudaStream_t st);
+cudaError_t launch_ctl_position(Ctl* ctl, uint32_t pos, cudaStream_t st);
+cudaError_t launch_embedding(const uint32_t* w, const uint16_t* s, const uint16_t* b,
+                             uint32_t token, int K, uint16_t* out, cudaStream_t st);
+cudaError_t launch_rms1024(const uint16_t* x, const uint16_t* gain, uint16_t* out,
+                           cudaStream_t st);
+
+}  // namespace q35

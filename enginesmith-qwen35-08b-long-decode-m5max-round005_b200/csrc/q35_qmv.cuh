@@ -1,0 +1,166 @@
+// Q4 affine matvec building blocks (CUDA cores, batch 1), bit-exact with the
+// reference's per-lane arithmetic.
+//
+// Layout is the MLX one the reference loads (weights.rs:50-52): codes
+// [N][K/8] u32 with nibble k at bits 4*(k%8) of word k/8, scales and biases
+// [N][K/64] bf16.
+//
+// Arithmetic (linear.metal:41-72): lane l of a SIMD group owns k = 512c +
+// 16l .. +15 of every 512-wide chunk c. Per chunk it forms
+//   xx = (x0, x1/16, x2/256, x3/4096, ...) and xs = sum of its 16 x values,
+//   dotq = sum over the four 16-bit halves of ((t0 + t1) + t2) + t3 with
+//   t_i = xx_i * float(half & (0xF << 4i)),
+//   accum += s * dotq + xs * b,
+// and the row value is the SIMD sum of the 32 accumulators (taken as an xor
+// butterfly). Every product t_i is formed exactly as the reference rounds it
+// without converting integers: the masked half-word OR'd into 0x4B000000 is
+// the float 2^23 + m, and fmaf(2^23 + m, xx, -2^23 * xx) = round(m * xx) in
+// one instruction. Products and sums are otherwise separately rounded
+// (__fadd_rn / __fmul_rn), so the result equals the CPU restatement bit for
+// bit.
+#pragma once
+#include "q35_dev.cuh"
+
+namespace q35 {
+
+constexpr float kTwo23 = 8388608.0f;
+
+// Per (chunk, lane) constants: xq[c][i][lane] float4 (i < 8: 16 xx then 16
+// -2^23*xx), xsum[c][lane].
+Q35_DEV void build_xq(const float* xf, int K, float4* xq, float* xsum) {
+  const int nch = K / 512;
+  for (int t = threadIdx.x; t < nch * 32; t += blockDim.x) {
+    const int c = t >> 5, l = t & 31;
+    const float* x = xf + 512 * c + 16 * l;
+    float xx[16];
+    float xs = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 16; j += 4) {
+      const float a = x[j], b = x[j + 1], cc = x[j + 2], d = x[j + 3];
+      xs = __fadd_rn(xs, __fadd_rn(__fadd_rn(__fadd_rn(a, b), cc), d));
+      xx[j] = a;
+      xx[j + 1] = __fdiv_rn(b, 16.0f);
+      xx[j + 2] = __fdiv_rn(cc, 256.0f);
+      xx[j + 3] = __fdiv_rn(d, 4096.0f);
+    }
+    float4* dst = xq + size_t(c) * 8 * 32 + l;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      dst[i * 32] = make_float4(xx[4 * i], xx[4 * i + 1], xx[4 * i + 2], xx[4 * i + 3]);
+      dst[(4 + i) * 32] = make_float4(-kTwo23 * xx[4 * i], -kTwo23 * xx[4 * i + 1],
+                                      -kTwo23 * xx[4 * i + 2], -kTwo23 * xx[4 * i + 3]);
+    }
+    xsum[t] = xs;
+  }
+}
+
+Q35_DEV float magic(uint32_t bits) { return __uint_as_float(bits | 0x4b000000u); }
+
+// ((t0 + t1) + t2) + t3 of one 16-bit half (low 16 bits of u).
+Q35_DEV float half_dot(uint32_t u, const float4& xx, const float4& cc) {
+  const float t0 = fmaf(magic(u & 0x000fu), xx.x, cc.x);
+  const float t1 = fmaf(magic(u & 0x00f0u), xx.y, cc.y);
+  const float t2 = fmaf(magic(u & 0x0f00u), xx.z, cc.z);
+  const float t3 = fmaf(magic(u & 0xf000u), xx.w, cc.w);
+  return __fadd_rn(__fadd_rn(__fadd_rn(t0, t1), t2), t3);
+}
+
+// One warp task: rows [r0, r0+4) (those < nrows) of the CTA's smem image,
+// chunk c (512 wide). Writes each lane's chunk term s*dotq + xs*b to
+// pl[(row * nch + c) * 32 + lane].
+Q35_DEV void qmv_chunk_task(const uint32_t* codes, const uint16_t* scl, const uint16_t* bia,
+                            int nrows, int r0, int c, int K, const float4* xq, const float* xsum,
+                            float* pl, int lane) {
+  const int KW = K / 8, KG = K / 64, nch = K / 512;
+  float4 xx[4], cc[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    xx[i] = xq[(size_t(c) * 8 + i) * 32 + lane];
+    cc[i] = xq[(size_t(c) * 8 + 4 + i) * 32 + lane];
+  }
+  const float xs = xsum[c * 32 + lane];
+  const int w0 = 64 * c + 2 * lane;
+  const int g = 8 * c + (lane >> 2);
+  uint2 q[4];
+  float sc[4], bi[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int row = r0 + r < nrows ? r0 + r : nrows - 1;
+    q[r] = *reinterpret_cast<const uint2*>(codes + size_t(row) * KW + w0);
+    sc[r] = bf2f(scl[row * KG + g]);
+    bi[r] = bf2f(bia[row * KG + g]);
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    float dotq = 0.0f;
+    dotq = __fadd_rn(dotq, half_dot(q[r].x, xx[0], cc[0]));
+    dotq = __fadd_rn(dotq, half_dot(q[r].x >> 16, xx[1], cc[1]));
+    dotq = __fadd_rn(dotq, half_dot(q[r].y, xx[2], cc[2]));
+    dotq = __fadd_rn(dotq, half_dot(q[r].y >> 16, xx[3], cc[3]));
+    const float term = __fadd_rn(__fmul_rn(sc[r], dotq), __fmul_rn(xs, bi[r]));
+    if (r0 + r < nrows) pl[(size_t(r0 + r) * nch + c) * 32 + lane] = term;
+  }
+}
+
+// Transpose-reduce four per-lane values with the pairing of an xor butterfly
+// (16, 8, 4, 2, 1): afterwards lanes 0, 8, 16, 24 hold the butterfly sums of
+// rows 0, 1, 2, 3 (bit-identical to summing each row with a butterfly).
+Q35_DEV float reduce4(float p0, float p1, float p2, float p3, int lane) {
+  const bool h16 = lane & 16;
+  float k0 = h16 ? p2 : p0, k1 = h16 ? p3 : p1;
+  const float s0 = h16 ? p0 : p2, s1 = h16 ? p1 : p3;
+  k0 = __fadd_rn(k0, __shfl_xor_sync(0xffffffffu, s0, 16));
+  k1 = __fadd_rn(k1, __shfl_xor_sync(0xffffffffu, s1, 16));
+  const bool h8 = lane & 8;
+  float q = h8 ? k1 : k0;
+  const float s = h8 ? k0 : k1;
+  q = __fadd_rn(q, __shfl_xor_sync(0xffffffffu, s, 8));
+  q = __fadd_rn(q, __shfl_xor_sync(0xffffffffu, q, 4));
+  q = __fadd_rn(q, __shfl_xor_sync(0xffffffffu, q, 2));
+  q = __fadd_rn(q, __shfl_xor_sync(0xffffffffu, q, 1));
+  return q;
+}
+
+// Finish rows [r0, r0+4): accum = sum over chunks in order (linear.metal:41
+// loop), then the SIMD sum. Writes vals[row].
+Q35_DEV void qmv_finish_task(const float* pl, int nrows, int r0, int nch, float* vals, int lane) {
+  float p[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    float acc = 0.0f;
+    if (r0 + r < nrows)
+      for (int c = 0; c < nch; ++c) acc = __fadd_rn(acc, pl[(size_t(r0 + r) * nch + c) * 32 + lane]);
+    p[r] = acc;
+  }
+  const float v = reduce4(p[0], p[1], p[2], p[3], lane);
+  if ((lane & 7) == 0) {
+    const int r = r0 + (((lane >> 4) & 1) << 1) + ((lane >> 3) & 1);
+    if (r < nrows) vals[r] = v;
+  }
+}
+
+// Block-level RMSNorm of a 1024-wide vector held as four contiguous values
+// per thread (256 threads), in the reference's reduction order
+// (linear_input_norm.metal:41-63): per-thread sequential sum of squares, SIMD
+// butterfly, then a butterfly over the eight SIMD partials. Writes the bf16
+// normalised value (as f32) to xf.
+Q35_DEV void rms1024(const float v[4], const uint16_t* gain, float* xf, float* red) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float acc = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) acc = __fadd_rn(acc, __fmul_rn(v[j], v[j]));
+  acc = warp_sum(acc);
+  if (lane == 0) red[warp] = acc;
+  __syncthreads();
+  const float t0 = __fadd_rn(red[0], red[4]), t1 = __fadd_rn(red[1], red[5]);
+  const float t2 = __fadd_rn(red[2], red[6]), t3 = __fadd_rn(red[3], red[7]);
+  const float total = __fadd_rn(__fadd_rn(t0, t2), __fadd_rn(t1, t3));
+  const float inv = drsqrtf(__fadd_rn(__fdiv_rn(total, 1024.0f), 1e-6f));
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int c = 4 * tid + j;
+    xf[c] = bfr(__fmul_rn(bfr(__fmul_rn(v[j], inv)), bf2f(gain[c])));
+  }
+}
+
+}  // namespace q35

@@ -1,0 +1,1025 @@
+// q35 runtime: model loading, decode sessions (CUDA-graph token loop) and the
+// op-level C ABI. Mirrors the reference host (source/src/model.rs,
+// source/src/weights.rs) with CUDA streams/graphs in place of Metal command
+// buffers.
+#include <dirent.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "q35.h"
+#include "q35_json.h"
+#include "q35_kernels.h"
+
+using namespace q35;
+
+namespace {
+
+// ---------------------------------------------------------------------------
+// weights (weights.rs:8-53)
+// ---------------------------------------------------------------------------
+struct Lin {
+  const uint32_t* w = nullptr;
+  const uint16_t* s = nullptr;
+  const uint16_t* b = nullptr;
+  int n = 0, k = 0;
+};
+struct LayerW {
+  bool attn = false;
+  const uint16_t* in_norm = nullptr;
+  const uint16_t* post_norm = nullptr;
+  Lin gate, up, down;
+  Lin qkv, z, a, bproj, out;  // GDN
+  const uint16_t *conv = nullptr, *gnorm = nullptr, *dt = nullptr;
+  const float* alog = nullptr;
+  Lin q, k, v, o;  // attention
+  const uint16_t *qnorm = nullptr, *knorm = nullptr;
+};
+struct ModelW {
+  uint8_t* arena = nullptr;
+  size_t bytes = 0;
+  Lin embed;
+  const uint16_t* norm = nullptr;
+  LayerW L[kLayers];
+};
+
+struct TensorRec {
+  int file = 0;
+  std::string dtype;
+  std::vector<size_t> shape;
+  size_t offset = 0, bytes = 0;
+  size_t dev_off = 0;
+  bool used = false;
+};
+
+bool read_file(const std::string& path, std::vector<char>& out, std::string& err) {
+  FILE* f = std::fopen(path.c_str(), "rb");
+  if (!f) {
+    err = "cannot open " + path;
+    return false;
+  }
+  std::fseek(f, 0, SEEK_END);
+  long n = std::ftell(f);
+  std::fseek(f, 0, SEEK_SET);
+  out.resize(size_t(n));
+  size_t got = n > 0 ? std::fread(out.data(), 1, size_t(n), f) : 0;
+  std::fclose(f);
+  if (got != size_t(n)) {
+    err = "short read " + path;
+    return false;
+  }
+  return true;
+}
+
+class Loader {
+ public:
+  std::string err;
+  bool open(const std::string& dir) {
+    std::vector<char> cfg;
+    if (!read_file(dir + "/config.json", cfg, err)) return false;
+    q35json::Value cv;
+    if (!q35json::parse(std::string(cfg.begin(), cfg.end()), cv, err)) return false;
+    const q35json::Value* tc = cv.get("text_config");
+    uint64_t hs = 0, nl = 0, vs = 0;
+    if (!tc || !tc->get("hidden_size") || !tc->get("hidden_size")->as_u64(hs) ||
+        !tc->get("num_hidden_layers") || !tc->get("num_hidden_layers")->as_u64(nl) ||
+        !tc->get("vocab_size") || !tc->get("vocab_size")->as_u64(vs) || hs != 1024 || nl != 24 ||
+        vs != 248320) {
+      err = "unsupported model configuration";  // weights.rs:14-15
+      return false;
+    }
+    DIR* d = opendir(dir.c_str());
+    if (!d) {
+      err = "cannot list " + dir;
+      return false;
+    }
+    while (dirent* e = readdir(d)) {
+      std::string n = e->d_name;
+      if (n.size() > 12 && n.compare(n.size() - 12, 12, ".safetensors") == 0) files_.push_back(dir + "/" + n);
+    }
+    closedir(d);
+    std::sort(files_.begin(), files_.end());
+    if (files_.empty()) {
+      err = "no safetensors weights";
+      return false;
+    }
+    data_.resize(files_.size());
+    for (size_t fi = 0; fi < files_.size(); ++fi) {
+      std::vector<char>& bytes = data_[fi];
+      if (!read_file(files_[fi], bytes, err)) return false;
+      if (bytes.size() < 8) {
+        err = "short safetensors file";
+        return false;
+      }
+      uint64_t hn = 0;
+      std::memcpy(&hn, bytes.data(), 8);
+      if (hn > bytes.size() - 8) {
+        err = "invalid safetensors header";
+        return false;
+      }
+      q35json::Value h;
+      if (!q35json::parse(std::string(bytes.data() + 8, size_t(hn)), h, err)) return false;
+      if (h.type != q35json::Value::Object) {
+        err = "invalid header";
+        return false;
+      }
+      const size_t data_len = bytes.size() - 8 - size_t(hn);
+      for (auto& kv : h.obj) {
+        const std::string& name = kv.first;
+        if (name == "__metadata__") continue;
+        static const std::string pre = "language_model.model.";
+        if (name.compare(0, pre.size(), pre) != 0) continue;
+        TensorRec t;
+        t.file = int(fi);
+        const q35json::Value* dt = kv.second.get("dtype");
+        const q35json::Value* sh = kv.second.get("shape");
+        const q35json::Value* of = kv.second.get("data_offsets");
+        if (!dt || dt->type != q35json::Value::String) {
+          err = "missing dtype";
+          return false;
+        }
+        t.dtype = dt->str;
+        size_t elem = 0;
+        if (t.dtype == "U32" || t.dtype == "F32") elem = 4;
+        else if (t.dtype == "BF16") elem = 2;
+        else {
+          err = "unsupported dtype " + t.dtype;
+          return false;
+        }
+        if (!sh || sh->type != q35json::Value::Array) {
+          err = "missing shape";
+          return false;
+        }
+        size_t count = 1;
+        for (auto& x : sh->arr) {
+          uint64_t v;
+          if (!x.as_u64(v)) {
+            err = "invalid shape";
+            return false;
+          }
+          t.shape.push_back(size_t(v));
+          count *= size_t(v);
+        }
+        uint64_t a = 0, b = 0;
+        if (!of || of->type != q35json::Value::Array || of->arr.size() != 2 || !of->arr[0].as_u64(a) ||
+            !of->arr[1].as_u64(b)) {
+          err = "invalid offset";
+          return false;
+        }
+        if (b < a || b > data_len || b - a != count * elem) {
+          err = "tensor bounds: " + name;
+          return false;
+        }
+        t.offset = 8 + size_t(hn) + size_t(a);
+        t.bytes = size_t(b - a);
+        std::string key = name.substr(pre.size());
+        for (auto& r : recs_)
+          if (r.first == key) {
+            err = "duplicate tensor " + key;
+            return false;
+          }
+        recs_.emplace_back(key, t);
+      }
+    }
+    if (recs_.size() != 694) {
+      err = "expected 694 text tensors, got " + std::to_string(recs_.size());
+      return false;
+    }
+    return true;
+  }
+  // Upload every tensor to one device arena, each 256-byte aligned (the bulk
+  // copies need 16-byte aligned sources; safetensors offsets are not).
+  bool upload(ModelW& M) {
+    size_t total = 0;
+    for (auto& r : recs_) {
+      r.second.dev_off = total;
+      total += (r.second.bytes + 255) & ~size_t(255);
+    }
+    if (cudaMalloc(&M.arena, total) != cudaSuccess) {
+      err = "cudaMalloc of " + std::to_string(total) + " weight bytes failed";
+      return false;
+    }
+    M.bytes = total;
+    for (auto& r : recs_) {
+      const TensorRec& t = r.second;
+      if (cudaMemcpy(M.arena + t.dev_off, data_[size_t(t.file)].data() + t.offset, t.bytes,
+                     cudaMemcpyHostToDevice) != cudaSuccess) {
+        err = "weight upload failed";
+        return false;
+      }
+    }
+    arena_ = M.arena;
+    data_.clear();
+    data_.shrink_to_fit();
+    return true;
+  }
+  // Weights::take (weights.rs:45-49)
+  const void* take(const std::string& name, std::initializer_list<size_t> shape, const char* dtype) {
+    for (auto& r : recs_)
+      if (r.first == name) {
+        TensorRec& t = r.second;
+        if (t.used || t.dtype != dtype || t.shape != std::vector<size_t>(shape)) {
+          if (err.empty()) err = "wrong shape/dtype for " + name;
+          return nullptr;
+        }
+        t.used = true;
+        return arena_ + t.dev_off;
+      }
+    if (err.empty()) err = "missing " + name;
+    return nullptr;
+  }
+  // Weights::linear (weights.rs:50-52)
+  Lin linear(const std::string& name, int n, int k) {
+    Lin l;
+    l.w = (const uint32_t*)take(name + ".weight", {size_t(n), size_t(k / 8)}, "U32");
+    l.s = (const uint16_t*)take(name + ".scales", {size_t(n), size_t(k / 64)}, "BF16");
+    l.b = (const uint16_t*)take(name + ".biases", {size_t(n), size_t(k / 64)}, "BF16");
+    l.n = n;
+    l.k = k;
+    return l;
+  }
+  // Weights::done (weights.rs:53)
+  bool done() {
+    if (!err.empty()) return false;
+    for (auto& r : recs_)
+      if (!r.second.used) {
+        err = "unused text weights: " + r.first;
+        return false;
+      }
+    return true;
+  }
+
+ private:
+  std::vector<std::string> files_;
+  std::vector<std::vector<char>> data_;
+  std::vector<std::pair<std::string, TensorRec>> recs_;
+  uint8_t* arena_ = nullptr;
+};
+
+// model.rs:41-78
+bool bind_model(Loader& ld, ModelW& M) {
+  M.embed = ld.linear("embed_tokens", kVocab, kHidden);
+  M.norm = (const uint16_t*)ld.take("norm.weight", {1024}, "BF16");
+  for (int l = 0; l < kLayers; ++l) {
+    LayerW& L = M.L[l];
+    const std::string p = "layers." + std::to_string(l);
+    L.in_norm = (const uint16_t*)ld.take(p + ".input_layernorm.weight", {1024}, "BF16");
+    L.post_norm = (const uint16_t*)ld.take(p + ".post_attention_layernorm.weight", {1024}, "BF16");
+    L.gate = ld.linear(p + ".mlp.gate_proj", kMlp, kHidden);
+    L.up = ld.linear(p + ".mlp.up_proj", kMlp, kHidden);
+    L.down = ld.linear(p + ".mlp.down_proj", kHidden, kMlp);
+    L.attn = (l % 4) == 3;
+    if (L.attn) {
+      const std::string a = p + ".self_attn";
+      L.q = ld.linear(a + ".q_proj", 4096, 1024);
+      L.k = ld.linear(a + ".k_proj", 512, 1024);
+      L.v = ld.linear(a + ".v_proj", 512, 1024);
+      L.o = ld.linear(a + ".o_proj", 1024, 2048);
+      L.qnorm = (const uint16_t*)ld.take(a + ".q_norm.weight", {256}, "BF16");
+      L.knorm = (const uint16_t*)ld.take(a + ".k_norm.weight", {256}, "BF16");
+    } else {
+      const std::string a = p + ".linear_attn";
+      L.qkv = ld.linear(a + ".in_proj_qkv", 6144, 1024);
+      L.z = ld.linear(a + ".in_proj_z", 2048, 1024);
+      L.a = ld.linear(a + ".in_proj_a", 16, 1024);
+      L.bproj = ld.linear(a + ".in_proj_b", 16, 1024);
+      L.out = ld.linear(a + ".out_proj", 1024, 2048);
+      L.conv = (const uint16_t*)ld.take(a + ".conv1d.weight", {6144, 4, 1}, "BF16");
+      L.gnorm = (const uint16_t*)ld.take(a + ".norm.weight", {128}, "BF16");
+      L.dt = (const uint16_t*)ld.take(a + ".dt_bias", {16}, "BF16");
+      L.alog = (const float*)ld.take(a + ".A_log", {16}, "F32");
+    }
+  }
+  return ld.done();
+}
+
+std::mutex g_init_mu;
+uint64_t g_init_mask = 0;
+cudaError_t ensure_kernels_init() {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lk(g_init_mu);
+  if (dev < 64 && (g_init_mask >> dev) & 1) return cudaSuccess;
+  e = kernels_init();
+  if (e == cudaSuccess && dev < 64) g_init_mask |= uint64_t(1) << dev;
+  return e;
+}
+
+void copy_err(char* dst, size_t n, const std::string& m) {
+  if (dst && n) std::snprintf(dst, n, "%s", m.c_str());
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// session
+// ---------------------------------------------------------------------------
+struct q35_session {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  uint32_t capacity = kDefaultCapacity;
+  int dbatch = 8, pbatch = 16;
+  ModelW M;
+  uint8_t* buf = nullptr;  // one allocation for all scratch/state
+  Ctl* ctl = nullptr;
+  uint16_t *h = nullptr, *conv_out = nullptr, *z = nullptr, *ab = nullptr, *y = nullptr;
+  uint16_t *q = nullptr, *k = nullptr, *v = nullptr, *gated = nullptr, *act = nullptr;
+  uint16_t *logits = nullptr, *lse = nullptr;
+  float *attn_po = nullptr, *attn_pml = nullptr, *head_part = nullptr;
+  uint32_t *seq = nullptr, *out_tokens = nullptr;
+  float* state = nullptr;
+  uint16_t* hist = nullptr;
+  uint16_t* kv = nullptr;  // [6 layers][K|V][2][capacity][256]
+  cudaGraphExec_t gdec1 = nullptr, gdecN = nullptr, gpre1 = nullptr, gpreN = nullptr;
+  uint32_t position = 0;
+  bool has_pending = false;
+  uint32_t pending = 0;
+  std::atomic<bool> cancelled{false};
+  std::string err;
+
+  uint16_t* kcache(int ai) { return kv + size_t(ai) * 2 * kKvHeads * capacity * kHeadDim; }
+  uint16_t* vcache(int ai) { return kcache(ai) + size_t(kKvHeads) * capacity * kHeadDim; }
+};
+
+namespace {
+
+int set_err(q35_session* s, int code, const std::string& m) {
+  if (s) s->err = m;
+  return code;
+}
+
+// One decode step: model.rs:228-307 for rows == 1 (+ the head when `head`).
+cudaError_t enqueue_step(q35_session* s, bool head, bool first) {
+  const ModelW& M = s->M;
+  cudaStream_t st = s->stream;
+  bool pdl = !first;
+  cudaError_t e = cudaSuccess;
+#define Q35_L(x)               \
+  do {                         \
+    e = (x);                   \
+    if (e != cudaSuccess) return e; \
+    pdl = true;                \
+  } while (0)
+  int gi = 0, ai = 0;
+  for (int l = 0; l < kLayers; ++l) {
+    const LayerW& L = M.L[l];
+    if (!L.attn) {
+      QmvArgs a = {};
+      a.seg[0] = {L.qkv.w, L.qkv.s, L.qkv.b, nullptr, 6144};
+      a.seg[1] = {L.z.w, L.z.s, L.z.b, s->z, 2048};
+      a.seg[2] = {L.a.w, L.a.s, L.a.b, s->ab, 16};
+      a.seg[3] = {L.bproj.w, L.bproj.s, L.bproj.b, s->ab + 16, 16};
+      a.nseg = 4;
+      a.K = 1024;
+      a.units = 8224;
+      a.units_per_cta = 56;
+      a.pro = l == 0 ? kProEmbedRms : kProRms;
+      a.epi = kEpiGdnConv;
+      a.x = s->h;
+      a.gain = L.in_norm;
+      a.h_out = s->h;
+      a.ew = M.embed.w;
+      a.es = M.embed.s;
+      a.eb = M.embed.b;
+      a.seq = s->seq;
+      a.hist = s->hist + size_t(gi) * 3 * kGdnConv;
+      a.convw = L.conv;
+      a.conv_out = s->conv_out;
+      a.ctl = s->ctl;
+      Q35_L(launch_qmv(a, st, pdl));
+      RecurArgs r = {};
+      r.conv = s->conv_out;
+      r.a_raw = s->ab;
+      r.b_raw = s->ab + 16;
+      r.a_log = L.alog;
+      r.dt_bias = L.dt;
+      r.state = s->state + size_t(gi) * kGdnHeads * 128 * 128;
+      r.y = s->y;
+      r.ctl = s->ctl;
+      r.advance_pos = l == 0;
+      Q35_L(launch_recur(r, st, pdl));
+      QmvArgs o = {};
+      o.seg[0] = {L.out.w, L.out.s, L.out.b, nullptr, 1024};
+      o.nseg = 1;
+      o.K = 2048;
+      o.units = 1024;
+      o.units_per_cta = 7;
+      o.pro = kProNormGate;
+      o.gy = s->y;
+      o.gz = s->z;
+      o.gw = L.gnorm;
+      o.epi = kEpiResAdd;
+      o.res = s->h;
+      o.ctl = s->ctl;
+      Q35_L(launch_qmv(o, st, pdl));
+      ++gi;
+    } else {
+      QmvArgs a = {};
+      a.seg[0] = {L.q.w, L.q.s, L.q.b, s->q, 4096};
+      a.seg[1] = {L.k.w, L.k.s, L.k.b, s->k, 512};
+      a.seg[2] = {L.v.w, L.v.s, L.v.b, s->v, 512};
+      a.nseg = 3;
+      a.K = 1024;
+      a.units = 5120;
+      a.units_per_cta = 36;
+      a.pro = kProRms;
+      a.x = s->h;
+      a.gain = L.in_norm;
+      a.epi = kEpiStore;
+      a.ctl = s->ctl;
+      Q35_L(launch_qmv(a, st, pdl));
+      AttnArgs at = {};
+      at.q_raw = s->q;
+      at.k_raw = s->k;
+      at.v_raw = s->v;
+      at.q_gain = L.qnorm;
+      at.k_gain = L.knorm;
+      at.kcache = s->kcache(ai);
+      at.vcache = s->vcache(ai);
+      at.capacity = s->capacity;
+      at.part_o = s->attn_po;
+      at.part_ml = s->attn_pml;
+      at.gated = s->gated;
+      at.ctl = s->ctl;
+      Q35_L(launch_attn(at, st, pdl));
+      QmvArgs o = {};
+      o.seg[0] = {L.o.w, L.o.s, L.o.b, nullptr, 1024};
+      o.nseg = 1;
+      o.K = 2048;
+      o.units = 1024;
+      o.units_per_cta = 7;
+      o.pro = kProPlain;
+      o.x = s->gated;
+      o.epi = kEpiResAdd;
+      o.res = s->h;
+      o.ctl = s->ctl;
+      Q35_L(launch_qmv(o, st, pdl));
+      ++ai;
+    }
+    QmvArgs m = {};
+    m.seg[0] = {L.gate.w, L.gate.s, L.gate.b, s->act, kMlp};
+    m.seg[1] = {L.up.w, L.up.s, L.up.b, nullptr, kMlp};
+    m.nseg = 2;
+    m.K = 1024;
+    m.units = kMlp;
+    m.units_per_cta = 25;
+    m.pro = kProRms;
+    m.x = s->h;
+    m.gain = L.post_norm;
+    m.epi = kEpiSwiglu;
+    m.ctl = s->ctl;
+    Q35_L(launch_qmv(m, st, pdl));
+    QmvArgs d = {};
+    d.seg[0] = {L.down.w, L.down.s, L.down.b, nullptr, 1024};
+    d.nseg = 1;
+    d.K = kMlp;
+    d.units = 1024;
+    d.units_per_cta = 7;
+    d.pro = kProPlain;
+    d.x = s->act;
+    d.epi = kEpiResAdd;
+    d.res = s->h;
+    d.ctl = s->ctl;
+    Q35_L(launch_qmv(d, st, pdl));
+  }
+  if (head) {
+    HeadArgs hd = {};
+    hd.w = M.embed.w;
+    hd.s = M.embed.s;
+    hd.b = M.embed.b;
+    hd.x = s->h;
+    hd.gain = M.norm;
+    hd.logits = s->logits;
+    hd.part = s->head_part;
+    hd.seq = s->seq;
+    hd.out_tokens = s->out_tokens;
+    hd.seq_len = s->capacity + 1;
+    hd.out_len = s->capacity;
+    hd.lse_out = s->lse;
+    hd.ctl = s->ctl;
+    Q35_L(launch_head(hd, st, pdl));
+  }
+#undef Q35_L
+  return e;
+}
+
+cudaError_t capture(q35_session* s, int steps, bool head, cudaGraphExec_t* out) {
+  cudaGraph_t g = nullptr;
+  cudaError_t e = cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal);
+  if (e != cudaSuccess) return e;
+  cudaError_t le = cudaSuccess;
+  for (int i = 0; i < steps && le == cudaSuccess; ++i) le = enqueue_step(s, head, i == 0);
+  e = cudaStreamEndCapture(s->stream, &g);
+  if (le != cudaSuccess) {
+    if (g) cudaGraphDestroy(g);
+    return le;
+  }
+  if (e != cudaSuccess) return e;
+  e = cudaGraphInstantiate(out, g, 0);
+  cudaGraphDestroy(g);
+  return e;
+}
+
+void free_session(q35_session* s) {
+  if (!s) return;
+  if (s->device >= 0) cudaSetDevice(s->device);
+  for (cudaGraphExec_t g : {s->gdec1, s->gdecN, s->gpre1, s->gpreN})
+    if (g) cudaGraphExecDestroy(g);
+  if (s->buf) cudaFree(s->buf);
+  if (s->M.arena) cudaFree(s->M.arena);
+  if (s->stream) cudaStreamDestroy(s->stream);
+  delete s;
+}
+
+// Device-state reset (Model::reset, model.rs:93-96): GDN state and history
+// zeroed, position 0, no pending token.
+cudaError_t reset_state(q35_session* s) {
+  s->position = 0;
+  s->has_pending = false;
+  cudaError_t e = cudaMemsetAsync(s->state, 0, size_t(18) * kGdnHeads * 128 * 128 * 4, s->stream);
+  if (e == cudaSuccess)
+    e = cudaMemsetAsync(s->hist, 0, size_t(18) * 3 * kGdnConv * 2, s->stream);
+  return e;
+}
+
+int device_failure(q35_session* s, cudaError_t e, const char* what) {
+  std::string m = std::string(what) + ": " + cudaGetErrorString(e);
+  cudaStreamSynchronize(s->stream);
+  reset_state(s);
+  cudaStreamSynchronize(s->stream);
+  return set_err(s, Q35_ECUDA, m);
+}
+
+// Runs `n` steps from the current device state (graphs of the batch size
+// then single steps). Returns 0, Q35_ECANCEL or a CUDA error code.
+int run_steps(q35_session* s, size_t n, bool head, cudaError_t* ce) {
+  cudaGraphExec_t g1 = head ? s->gdec1 : s->gpre1;
+  cudaGraphExec_t gN = head ? s->gdecN : s->gpreN;
+  const size_t B = size_t(head ? s->dbatch : s->pbatch);
+  size_t launched = 0;
+  while (n > 0) {
+    if (s->cancelled.load(std::memory_order_relaxed)) return Q35_ECANCEL;
+    cudaError_t e;
+    if (n >= B && gN) {
+      e = cudaGraphLaunch(gN, s->stream);
+      n -= B;
+    } else {
+      e = cudaGraphLaunch(g1, s->stream);
+      n -= 1;
+    }
+    if (e != cudaSuccess) {
+      *ce = e;
+      return Q35_ECUDA;
+    }
+    // keep the queued work bounded so a cancel is observed promptly
+    if (++launched % 16 == 0) {
+      e = cudaStreamSynchronize(s->stream);
+      if (e != cudaSuccess) {
+        *ce = e;
+        return Q35_ECUDA;
+      }
+    }
+  }
+  return Q35_OK;
+}
+
+int check_device_ctl(q35_session* s) {
+  Ctl c;
+  cudaError_t e = cudaMemcpy(&c, s->ctl, sizeof(Ctl), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return device_failure(s, e, "control read");
+  if (c.err != 0) {
+    std::string m = c.err == kErrToken ? "token outside vocabulary on device"
+                                       : "device wait expired (site " + std::to_string(c.err) + ")";
+    reset_state(s);
+    cudaStreamSynchronize(s->stream);
+    return set_err(s, Q35_ETIMEOUT, m);
+  }
+  return Q35_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* q35_version(void) { return "q35-b200 0.1 (sm_100a)"; }
+
+int q35_open(const char* model_dir, int device, const q35_opts* opts, q35_session** out,
+             char* errbuf, size_t err_len) {
+  if (!out) return Q35_EINVAL;
+  *out = nullptr;
+  if (!model_dir) {
+    copy_err(errbuf, err_len, "--model MODEL_DIR required");
+    return Q35_EINVAL;
+  }
+  q35_session* s = new q35_session();
+  s->device = device;
+  if (opts) {
+    if (opts->capacity) s->capacity = opts->capacity;
+    if (opts->decode_batch) s->dbatch = int(opts->decode_batch);
+    if (opts->prefill_batch) s->pbatch = int(opts->prefill_batch);
+  }
+  auto fail = [&](int code, const std::string& m) {
+    copy_err(errbuf, err_len, m);
+    free_session(s);
+    return code;
+  };
+  if (s->capacity % kAttnTile != 0 || s->capacity < kAttnTile || s->capacity > (1u << 30))
+    return fail(Q35_EINVAL, "capacity must be a positive multiple of 32");
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return fail(Q35_ECUDA, std::string("cudaSetDevice: ") + cudaGetErrorString(e));
+  e = ensure_kernels_init();
+  if (e != cudaSuccess) return fail(Q35_ECUDA, std::string("kernel setup: ") + cudaGetErrorString(e));
+  e = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking);
+  if (e != cudaSuccess) return fail(Q35_ECUDA, std::string("stream: ") + cudaGetErrorString(e));
+  {
+    Loader ld;
+    if (!ld.open(model_dir) || !ld.upload(s->M) || !bind_model(ld, s->M))
+      return fail(Q35_EIO, ld.err);
+  }
+  // scratch, state, caches
+  const size_t cap = s->capacity;
+  struct Part {
+    void** p;
+    size_t bytes;
+  };
+  std::vector<Part> parts = {
+      {(void**)&s->ctl, sizeof(Ctl)},
+      {(void**)&s->h, kHidden * 2},
+      {(void**)&s->conv_out, kGdnConv * 2},
+      {(void**)&s->z, 2048 * 2},
+      {(void**)&s->ab, 32 * 2},
+      {(void**)&s->y, 2048 * 2},
+      {(void**)&s->q, kQProj * 2},
+      {(void**)&s->k, 512 * 2},
+      {(void**)&s->v, 512 * 2},
+      {(void**)&s->gated, 2048 * 2},
+      {(void**)&s->act, kMlp * 2},
+      {(void**)&s->logits, size_t(kVocab) * 2},
+      {(void**)&s->lse, 16},
+      {(void**)&s->attn_po, size_t(kKvHeads) * kAttnChains * 4 * kHeadDim * 4},
+      {(void**)&s->attn_pml, size_t(kKvHeads) * kAttnChains * 4 * 2 * 4},
+      {(void**)&s->head_part, size_t(kHeadCtas) * 2 * 4},
+      {(void**)&s->seq, (cap + 1) * 4},
+      {(void**)&s->out_tokens, cap * 4},
+      {(void**)&s->state, size_t(18) * kGdnHeads * 128 * 128 * 4},
+      {(void**)&s->hist, size_t(18) * 3 * kGdnConv * 2},
+      {(void**)&s->kv, size_t(6) * 2 * kKvHeads * cap * kHeadDim * 2},
+  };
+  size_t total = 0;
+  for (auto& p : parts) total += (p.bytes + 255) & ~size_t(255);
+  e = cudaMalloc(&s->buf, total);
+  if (e != cudaSuccess) return fail(Q35_ENOMEM, "cudaMalloc of " + std::to_string(total) + " bytes failed");
+  e = cudaMemset(s->buf, 0, total);
+  if (e != cudaSuccess) return fail(Q35_ECUDA, std::string("memset: ") + cudaGetErrorString(e));
+  size_t off = 0;
+  for (auto& p : parts) {
+    *p.p = s->buf + off;
+    off += (p.bytes + 255) & ~size_t(255);
+  }
+  Ctl c = {};
+  c.capacity = s->capacity;
+  e = cudaMemcpy(s->ctl, &c, sizeof(Ctl), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = capture(s, 1, true, &s->gdec1);
+  if (e == cudaSuccess && s->dbatch > 1) e = capture(s, s->dbatch, true, &s->gdecN);
+  if (e == cudaSuccess) e = capture(s, 1, false, &s->gpre1);
+  if (e == cudaSuccess && s->pbatch > 1) e = capture(s, s->pbatch, false, &s->gpreN);
+  if (e != cudaSuccess) return fail(Q35_ECUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+  *out = s;
+  return Q35_OK;
+}
+
+void q35_close(q35_session* s) { free_session(s); }
+
+void q35_cancel(q35_session* s) {
+  if (s) s->cancelled.store(true, std::memory_order_relaxed);
+}
+
+const char* q35_last_error(const q35_session* s) { return s ? s->err.c_str() : "no session"; }
+
+uint32_t q35_position(const q35_session* s) { return s ? s->position : 0; }
+
+// Model::generate + Model::decode (model.rs:97-180)
+int q35_generate(q35_session* s, const uint32_t* prompt, size_t n_prompt, size_t max_tokens,
+                 int reset, uint32_t* out_tokens) {
+  if (!s) return Q35_EINVAL;
+  const size_t cap = s->capacity;
+  if (max_tokens == 0 || max_tokens > cap) return set_err(s, Q35_EINVAL, "invalid output length");
+  if (!out_tokens) return set_err(s, Q35_EINVAL, "output buffer required");
+  if (s->cancelled.load()) return set_err(s, Q35_ECANCEL, "input disconnected");
+  cudaSetDevice(s->device);
+  if (reset) {
+    if (n_prompt == 0 || !prompt) return set_err(s, Q35_EINVAL, "reset needs nonempty prompt");
+    if (n_prompt + max_tokens - 1 > cap) return set_err(s, Q35_EINVAL, "context capacity exceeded");
+    for (size_t i = 0; i < n_prompt; ++i)
+      if (prompt[i] >= uint32_t(kVocab)) return set_err(s, Q35_EINVAL, "token outside vocabulary");
+  } else {
+    if (n_prompt != 0) return set_err(s, Q35_EINVAL, "continuation prompt must be empty");
+    if (s->position + max_tokens > cap) return set_err(s, Q35_EINVAL, "context capacity exceeded");
+    if (!s->has_pending) return set_err(s, Q35_EINVAL, "no continuation state");
+  }
+  cudaError_t e = cudaSuccess;
+  if (reset) {
+    e = reset_state(s);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(s->seq, prompt, n_prompt * 4, cudaMemcpyHostToDevice, s->stream);
+    Ctl c = {};
+    c.capacity = s->capacity;
+    if (e == cudaSuccess) e = cudaMemcpyAsync(s->ctl, &c, sizeof(Ctl), cudaMemcpyHostToDevice, s->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+    if (e != cudaSuccess) return device_failure(s, e, "reset");
+    int rc = run_steps(s, n_prompt - 1, false, &e);
+    if (rc == Q35_ECANCEL) {
+      cudaStreamSynchronize(s->stream);
+      reset_state(s);
+      cudaStreamSynchronize(s->stream);
+      return set_err(s, Q35_ECANCEL, "input disconnected");
+    }
+    if (rc != Q35_OK) return device_failure(s, e, "prefill");
+  } else {
+    e = cudaMemsetAsync(&s->ctl->out_count, 0, 4, s->stream);
+    if (e != cudaSuccess) return device_failure(s, e, "continue");
+  }
+  int rc = run_steps(s, max_tokens, true, &e);
+  if (rc == Q35_ECANCEL) {
+    cudaStreamSynchronize(s->stream);
+    reset_state(s);
+    cudaStreamSynchronize(s->stream);
+    return set_err(s, Q35_ECANCEL, "input disconnected");
+  }
+  if (rc != Q35_OK) return device_failure(s, e, "decode");
+  e = cudaStreamSynchronize(s->stream);
+  if (e != cudaSuccess) return device_failure(s, e, "decode");
+  rc = check_device_ctl(s);
+  if (rc != Q35_OK) return rc;
+  e = cudaMemcpy(out_tokens, s->out_tokens, max_tokens * 4, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return device_failure(s, e, "token read");
+  if (s->cancelled.load()) {
+    reset_state(s);
+    cudaStreamSynchronize(s->stream);
+    return set_err(s, Q35_ECANCEL, "input disconnected");
+  }
+  s->position = uint32_t(reset ? n_prompt - 1 + max_tokens : s->position + max_tokens);
+  s->pending = out_tokens[max_tokens - 1];
+  s->has_pending = true;
+  return Q35_OK;
+}
+
+int q35_decode_timed(q35_session* s, size_t steps, float* ms) {
+  if (!s || !ms || steps == 0) return Q35_EINVAL;
+  if (!s->has_pending) return set_err(s, Q35_EINVAL, "no continuation state");
+  if (s->position + steps > s->capacity) return set_err(s, Q35_EINVAL, "context capacity exceeded");
+  cudaSetDevice(s->device);
+  cudaEvent_t a, b;
+  cudaEventCreate(&a);
+  cudaEventCreate(&b);
+  cudaError_t e = cudaMemsetAsync(&s->ctl->out_count, 0, 4, s->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+  if (e == cudaSuccess) e = cudaEventRecord(a, s->stream);
+  int rc = Q35_OK;
+  if (e == cudaSuccess) {
+    // no intermediate synchronisation inside the timed region
+    cudaGraphExec_t gN = s->gdecN, g1 = s->gdec1;
+    size_t n = steps;
+    while (n > 0 && e == cudaSuccess) {
+      if (n >= size_t(s->dbatch) && gN) {
+        e = cudaGraphLaunch(gN, s->stream);
+        n -= size_t(s->dbatch);
+      } else {
+        e = cudaGraphLaunch(g1, s->stream);
+        n -= 1;
+      }
+    }
+  }
+  if (e == cudaSuccess) e = cudaEventRecord(b, s->stream);
+  if (e == cudaSuccess) e = cudaEventSynchronize(b);
+  if (e == cudaSuccess) e = cudaEventElapsedTime(ms, a, b);
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  if (e != cudaSuccess) return device_failure(s, e, "timed decode");
+  rc = check_device_ctl(s);
+  if (rc != Q35_OK) return rc;
+  uint32_t last = 0;
+  e = cudaMemcpy(&last, s->out_tokens + (steps - 1), 4, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return device_failure(s, e, "token read");
+  s->position += uint32_t(steps);
+  s->pending = last;
+  return Q35_OK;
+}
+
+int q35_dump_state(q35_session* s, uint16_t* kv, float* state, uint16_t* hist) {
+  if (!s) return Q35_EINVAL;
+  cudaSetDevice(s->device);
+  cudaError_t e = cudaStreamSynchronize(s->stream);
+  const size_t pos = s->position;
+  for (int ai = 0; ai < 6 && e == cudaSuccess && kv; ++ai)
+    for (int which = 0; which < 2 && e == cudaSuccess; ++which)
+      for (int h = 0; h < kKvHeads && e == cudaSuccess; ++h) {
+        const uint16_t* src = (which ? s->vcache(ai) : s->kcache(ai)) + size_t(h) * s->capacity * kHeadDim;
+        uint16_t* dst = kv + ((size_t(ai) * 2 + which) * kKvHeads + h) * pos * kHeadDim;
+        e = cudaMemcpy(dst, src, pos * kHeadDim * 2, cudaMemcpyDeviceToHost);
+      }
+  if (e == cudaSuccess && state)
+    e = cudaMemcpy(state, s->state, size_t(18) * kGdnHeads * 128 * 128 * 4, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && hist)
+    e = cudaMemcpy(hist, s->hist, size_t(18) * 3 * kGdnConv * 2, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return set_err(s, Q35_ECUDA, std::string("dump: ") + cudaGetErrorString(e));
+  return Q35_OK;
+}
+
+int q35_last_logits(q35_session* s, uint16_t* logits, uint16_t* lse) {
+  if (!s) return Q35_EINVAL;
+  cudaSetDevice(s->device);
+  cudaError_t e = cudaStreamSynchronize(s->stream);
+  if (e == cudaSuccess && logits)
+    e = cudaMemcpy(logits, s->logits, size_t(kVocab) * 2, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && lse) e = cudaMemcpy(lse, s->lse, 2, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return set_err(s, Q35_ECUDA, std::string("logits: ") + cudaGetErrorString(e));
+  return Q35_OK;
+}
+
+// ---------------------------------------------------------------------------
+// op-level entry points
+// ---------------------------------------------------------------------------
+static int op_status(cudaError_t e) { return e == cudaSuccess ? Q35_OK : Q35_ECUDA; }
+
+int q35_op_qmv_q4(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
+                  const uint16_t* x, const uint16_t* residual, uint16_t* y, int n, int k,
+                  void* stream) {
+  if (!w || !scales || !biases || !x || !y || n <= 0 || k <= 0 || k % 512 != 0 || k > 4096)
+    return Q35_EINVAL;
+  if (ensure_kernels_init() != cudaSuccess) return Q35_ECUDA;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (residual && residual != y) {
+    cudaError_t e = cudaMemcpyAsync(y, residual, size_t(n) * 2, cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) return Q35_ECUDA;
+  }
+  QmvArgs a = {};
+  a.seg[0] = {w, scales, biases, y, n};
+  a.nseg = 1;
+  a.K = k;
+  a.units = n;
+  int upc = (n + 147) / 148;
+  const int max_rows = (64 * 1024) / (k / 2 + k / 16);
+  upc = std::max(1, std::min(upc, max_rows));
+  a.units_per_cta = upc;
+  a.pro = kProPlain;
+  a.x = x;
+  a.epi = residual ? kEpiResAdd : kEpiStore;
+  a.res = y;
+  return op_status(launch_qmv(a, st, false));
+}
+
+int q35_op_embedding_q4(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
+                        uint32_t token, int k, uint16_t* out, void* stream) {
+  if (!w || !scales || !biases || !out || k <= 0 || k % 64 != 0) return Q35_EINVAL;
+  return op_status(launch_embedding(w, scales, biases, token, k, out, (cudaStream_t)stream));
+}
+
+int q35_op_rms_norm(const uint16_t* x, const uint16_t* gain, uint16_t* out, void* stream) {
+  if (!x || !gain || !out) return Q35_EINVAL;
+  return op_status(launch_rms1024(x, gain, out, (cudaStream_t)stream));
+}
+
+static size_t ctl_bytes() { return (sizeof(Ctl) + 255) & ~size_t(255); }
+
+size_t q35_op_gdn_workspace_bytes(void) { return ctl_bytes() + kGdnConv * 2 + 2048 * 2; }
+
+int q35_op_gdn_step(const uint16_t* raw_qkv, const uint16_t* z, const uint16_t* a_raw,
+                    const uint16_t* b_raw, uint16_t* history, const uint16_t* conv_w,
+                    const float* a_log, const uint16_t* dt_bias, float* state,
+                    const uint16_t* norm_w, const uint32_t* ow, const uint16_t* os,
+                    const uint16_t* ob, const uint16_t* residual, uint16_t* out, void* workspace,
+                    void* stream) {
+  if (!raw_qkv || !z || !a_raw || !b_raw || !history || !conv_w || !a_log || !dt_bias || !state ||
+      !norm_w || !ow || !os || !ob || !out || !workspace)
+    return Q35_EINVAL;
+  if (ensure_kernels_init() != cudaSuccess) return Q35_ECUDA;
+  cudaStream_t st = (cudaStream_t)stream;
+  uint8_t* ws = (uint8_t*)workspace;
+  Ctl* ctl = (Ctl*)ws;
+  uint16_t* conv = (uint16_t*)(ws + ctl_bytes());
+  uint16_t* y = conv + kGdnConv;
+  cudaError_t e = cudaMemsetAsync(ctl, 0, sizeof(Ctl), st);
+  if (e == cudaSuccess) e = launch_gdn_conv(raw_qkv, history, conv_w, conv, st);
+  RecurArgs r = {};
+  r.conv = conv;
+  r.a_raw = a_raw;
+  r.b_raw = b_raw;
+  r.a_log = a_log;
+  r.dt_bias = dt_bias;
+  r.state = state;
+  r.y = y;
+  r.ctl = ctl;
+  if (e == cudaSuccess) e = launch_recur(r, st, false);
+  if (e == cudaSuccess && residual && residual != out)
+    e = cudaMemcpyAsync(out, residual, 1024 * 2, cudaMemcpyDeviceToDevice, st);
+  QmvArgs o = {};
+  o.seg[0] = {ow, os, ob, out, 1024};
+  o.nseg = 1;
+  o.K = 2048;
+  o.units = 1024;
+  o.units_per_cta = 7;
+  o.pro = kProNormGate;
+  o.gy = y;
+  o.gz = z;
+  o.gw = norm_w;
+  o.epi = residual ? kEpiResAdd : kEpiStore;
+  o.res = out;
+  o.ctl = ctl;
+  if (e == cudaSuccess) e = launch_qmv(o, st, false);
+  return op_status(e);
+}
+
+size_t q35_op_attn_workspace_bytes(void) {
+  return ctl_bytes() + size_t(kKvHeads) * kAttnChains * 4 * kHeadDim * 4 +
+         size_t(kKvHeads) * kAttnChains * 4 * 2 * 4;
+}
+
+int q35_op_attn_decode(const uint16_t* q_raw, const uint16_t* k_raw, const uint16_t* v_raw,
+                       const uint16_t* q_gain, const uint16_t* k_gain, uint16_t* kcache,
+                       uint16_t* vcache, uint32_t capacity, uint32_t pos, uint16_t* gated,
+                       void* workspace, void* stream) {
+  if (!q_raw || !k_raw || !v_raw || !q_gain || !k_gain || !kcache || !vcache || !gated ||
+      !workspace || capacity == 0 || capacity % kAttnTile != 0 || pos >= capacity)
+    return Q35_EINVAL;
+  if (ensure_kernels_init() != cudaSuccess) return Q35_ECUDA;
+  cudaStream_t st = (cudaStream_t)stream;
+  uint8_t* ws = (uint8_t*)workspace;
+  Ctl* ctl = (Ctl*)ws;
+  float* po = (float*)(ws + ctl_bytes());
+  float* pml = po + size_t(kKvHeads) * kAttnChains * 4 * kHeadDim;
+  cudaError_t e = launch_ctl_position(ctl, pos, st);
+  AttnArgs at = {};
+  at.q_raw = q_raw;
+  at.k_raw = k_raw;
+  at.v_raw = v_raw;
+  at.q_gain = q_gain;
+  at.k_gain = k_gain;
+  at.kcache = kcache;
+  at.vcache = vcache;
+  at.capacity = capacity;
+  at.part_o = po;
+  at.part_ml = pml;
+  at.gated = gated;
+  at.ctl = ctl;
+  if (e == cudaSuccess) e = launch_attn(at, st, false);
+  return op_status(e);
+}
+
+size_t q35_op_head_workspace_bytes(void) { return ctl_bytes() + size_t(kHeadCtas) * 2 * 4; }
+
+int q35_op_head_argmax(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
+                       const uint16_t* x, const uint16_t* gain, uint16_t* logits,
+                       uint32_t* token, uint16_t* lse, void* workspace, void* stream) {
+  if (!w || !scales || !biases || !x || !logits || !token || !workspace) return Q35_EINVAL;
+  if (ensure_kernels_init() != cudaSuccess) return Q35_ECUDA;
+  cudaStream_t st = (cudaStream_t)stream;
+  uint8_t* ws = (uint8_t*)workspace;
+  Ctl* ctl = (Ctl*)ws;
+  float* part = (float*)(ws + ctl_bytes());
+  cudaError_t e = launch_ctl_position(ctl, 0, st);
+  HeadArgs hd = {};
+  hd.w = w;
+  hd.s = scales;
+  hd.b = biases;
+  hd.x = x;
+  hd.gain = gain;
+  hd.logits = logits;
+  hd.part = part;
+  hd.seq = nullptr;
+  hd.out_tokens = token;
+  hd.seq_len = 0;
+  hd.out_len = 1;
+  hd.lse_out = lse;
+  hd.ctl = ctl;
+  if (e == cudaSuccess) e = launch_head(hd, st, false);
+  return op_status(e);
+}
+
+int q35_op_greedy(const uint16_t* logits, uint32_t* token, uint16_t* lse, void* workspace,
+                  void* stream) {
+  if (!logits || !token || !workspace) return Q35_EINVAL;
+  cudaStream_t st = (cudaStream_t)stream;
+  uint8_t* ws = (uint8_t*)workspace;
+  Ctl* ctl = (Ctl*)ws;
+  float* part = (float*)(ws + ctl_bytes());
+  cudaError_t e = launch_ctl_position(ctl, 0, st);
+  HeadArgs hd = {};
+  hd.logits = const_cast<uint16_t*>(logits);
+  hd.part = part;
+  hd.out_tokens = token;
+  hd.out_len = 1;
+  hd.lse_out = lse;
+  hd.ctl = ctl;
+  if (e == cudaSuccess) e = launch_greedy(hd, st);
+  return op_status(e);
+}
+
+}  // extern "C"

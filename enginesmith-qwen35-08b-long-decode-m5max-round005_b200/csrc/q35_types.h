@@ -1,0 +1,141 @@
+// Shapes, the per-session control block and kernel argument blocks shared by
+// host and device code. The model shape is the one source/src/model.rs:7-9,
+// :41-78 hard-codes (hidden 1024, 24 layers with layer l%4==3 full attention,
+// MLP 3584, vocab 248,320, GDN 16 heads x 128, attention 8 q / 2 kv heads x 256).
+#pragma once
+#include <stdint.h>
+
+namespace q35 {
+
+constexpr int kHidden = 1024;
+constexpr int kLayers = 24;
+constexpr int kMlp = 3584;
+constexpr int kVocab = 248320;
+constexpr int kGdnHeads = 16;
+constexpr int kGdnDim = 128;
+constexpr int kGdnConv = 6144;  // q 2048 | k 2048 | v 2048
+constexpr int kQHeads = 8;
+constexpr int kKvHeads = 2;
+constexpr int kHeadDim = 256;
+constexpr int kQProj = 4096;  // per q head: query 256 | gate 256
+constexpr uint32_t kDefaultCapacity = 262144;  // model.rs:8
+
+// Attention geometry: one CTA per (chain, kv head); a chain is the
+// reference's block of keys b, b + stride, ... (stride 32 below 1024 keys,
+// 64 from 1024 on).
+constexpr int kAttnChains = 64;
+constexpr int kAttnTile = 32;   // keys of one chain per ring stage
+constexpr int kAttnStages = 3;
+constexpr int kAttnThreads = 256;
+
+// Head (vocabulary projection + greedy) geometry.
+constexpr int kHeadRowsPerChunk = 32;
+constexpr int kHeadChunksPerCta = 53;
+constexpr int kHeadRowsPerCta = kHeadRowsPerChunk * kHeadChunksPerCta;  // 1696
+constexpr int kHeadCtas = (kVocab + kHeadRowsPerCta - 1) / kHeadRowsPerCta;  // 147
+constexpr int kHeadStages = 4;
+
+// Device-resident control block of one decode session (or one op call).
+struct Ctl {
+  uint32_t pos;        // next position to consume (host sets it; advanced on device)
+  uint32_t pos_step;   // position consumed by the running step
+  uint32_t out_count;  // tokens emitted by the running request
+  uint32_t err;        // nonzero: a bounded wait expired (value = site code)
+  uint32_t head_counter;
+  uint32_t attn_counter[kKvHeads];
+  uint32_t capacity;
+  float rope_cs[64];   // cos/sin of the running step's position, pairs i<32
+  uint32_t token_step; // token consumed by the running step
+  uint32_t pad[7];
+};
+
+// Error site codes written to Ctl::err.
+enum : uint32_t {
+  kErrQmvWait = 1,
+  kErrAttnWait = 2,
+  kErrHeadWait = 3,
+  kErrRecurWait = 4,
+  kErrToken = 5,
+};
+
+// ---- Q4 matvec kernel arguments ----
+enum : int { kProPlain = 0, kProRms = 1, kProEmbedRms = 2, kProNormGate = 3 };
+enum : int { kEpiStore = 0, kEpiResAdd = 1, kEpiSwiglu = 2, kEpiGdnConv = 3 };
+
+struct QmvSeg {
+  const uint32_t* w;
+  const uint16_t* s;
+  const uint16_t* b;
+  uint16_t* y;
+  int rows;
+};
+
+struct QmvArgs {
+  QmvSeg seg[4];
+  int nseg;
+  int K;
+  int units;          // rows, or activation rows for SwiGLU
+  int units_per_cta;
+  int pro, epi;
+  const uint16_t* x;     // plain / RMS input
+  const uint16_t* gain;  // RMS gain
+  uint16_t* h_out;       // embedding prologue: residual stream (written by CTA 0)
+  const uint32_t* ew;    // embedding matrix (Q4)
+  const uint16_t* es;
+  const uint16_t* eb;
+  const uint32_t* seq;   // token ring [capacity + 1]
+  const uint16_t* gy;    // norm-gate prologue: recurrence output [2048]
+  const uint16_t* gz;    // z projection [2048]
+  const uint16_t* gw;    // norm weight [128]
+  uint16_t* res;         // residual (in/out) for kEpiResAdd
+  uint16_t* hist;        // GDN conv history [3][6144]
+  const uint16_t* convw; // [6144][4]
+  uint16_t* conv_out;    // [6144]
+  Ctl* ctl;
+  int advance_pos;       // this launch moves ctl->pos to pos_step + 1
+};
+
+struct RecurArgs {
+  const uint16_t* conv;   // [6144] post-SiLU conv output (q,k not yet normalised)
+  const uint16_t* a_raw;  // [16]
+  const uint16_t* b_raw;  // [16]
+  const float* a_log;     // [16]
+  const uint16_t* dt_bias;// [16]
+  float* state;           // [16][128 v][128 k]
+  uint16_t* y;            // [2048]
+  Ctl* ctl;
+  int advance_pos;
+};
+
+struct AttnArgs {
+  const uint16_t* q_raw;  // [8][512] query | gate per head
+  const uint16_t* k_raw;  // [2][256]
+  const uint16_t* v_raw;  // [2][256]
+  const uint16_t* q_gain; // [256]
+  const uint16_t* k_gain; // [256]
+  uint16_t* kcache;       // [2][capacity][256]
+  uint16_t* vcache;
+  uint32_t capacity;
+  float* part_o;          // [2][kAttnChains][4][256]
+  float* part_ml;         // [2][kAttnChains][4][2]
+  uint16_t* gated;        // [8][256]
+  Ctl* ctl;
+};
+
+struct HeadArgs {
+  const uint32_t* w;      // [248320][128]
+  const uint16_t* s;
+  const uint16_t* b;
+  const uint16_t* x;      // hidden before the final norm (or already normed if gain == null)
+  const uint16_t* gain;   // final norm gain, or null
+  uint16_t* logits;       // [248320]
+  float* part;            // [kHeadCtas][2] (max, sum)
+  uint32_t* seq;          // token ring (writes seq[pos_step + 1])
+  uint32_t* out_tokens;   // writes out_tokens[out_count++]
+  uint32_t seq_len;       // entries in seq
+  uint32_t out_len;       // entries in out_tokens
+  uint16_t* lse_out;      // optional [1]
+  Ctl* ctl;
+};
+
+}  // namespace q35

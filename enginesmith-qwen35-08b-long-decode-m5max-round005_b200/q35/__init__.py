@@ -1,0 +1,258 @@
+"""Python host over the q35 C ABI (``lib/libq35cuda.so``).
+
+Mirrors the reference host's model interface (source/src/model.rs):
+``Model.load(path)`` (model.rs:37), ``Model.generate(prompt, count, reset)``
+(model.rs:97-122) raising on the same validation failures, and
+``Model.cancel()`` for the ``cancelled`` flag (model.rs:33). The op-level
+wrappers take torch CUDA tensors (torch is only used for device memory and
+streams) and call the CUDA kernels through the C ABI. There is no CPU
+fallback: importing this module without the built library raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import POINTER, c_char_p, c_float, c_int, c_size_t, c_uint16, c_uint32, c_uint64, c_void_p
+
+PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB_PATH = os.path.join(PKG_DIR, "lib", "libq35cuda.so")
+ENGINE_PATH = os.path.join(PKG_DIR, "lib", "engine")
+HEADER_PATH = os.path.join(os.path.dirname(PKG_DIR), "include", "q35.h")
+
+VOCAB = 248320
+HIDDEN = 1024
+DEFAULT_CAPACITY = 262144
+
+OK, EINVAL, ECUDA, ECANCEL, EIO, ENOMEM, ETIMEOUT, ENCCL = 0, -1, -2, -3, -4, -5, -6, -7
+
+
+class Q35Error(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(message)
+        self.code = code
+
+
+class _Opts(ctypes.Structure):
+    _fields_ = [("capacity", c_uint32), ("decode_batch", c_uint32),
+                ("prefill_batch", c_uint32), ("flags", c_uint32)]
+
+
+def _load() -> ctypes.CDLL:
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(f"q35 CUDA library not built: {LIB_PATH} (run `make` at the repo root)")
+    lib = ctypes.CDLL(LIB_PATH)
+    P = c_void_p
+    sig = {
+        "q35_open": (c_int, [c_char_p, c_int, POINTER(_Opts), POINTER(c_void_p), c_char_p, c_size_t]),
+        "q35_generate": (c_int, [P, POINTER(c_uint32), c_size_t, c_size_t, c_int, POINTER(c_uint32)]),
+        "q35_cancel": (None, [P]),
+        "q35_last_error": (c_char_p, [P]),
+        "q35_close": (None, [P]),
+        "q35_position": (c_uint32, [P]),
+        "q35_dump_state": (c_int, [P, P, P, P]),
+        "q35_last_logits": (c_int, [P, P, P]),
+        "q35_decode_timed": (c_int, [P, c_size_t, POINTER(c_float)]),
+        "q35_op_qmv_q4": (c_int, [P, P, P, P, P, P, c_int, c_int, P]),
+        "q35_op_embedding_q4": (c_int, [P, P, P, c_uint32, c_int, P, P]),
+        "q35_op_rms_norm": (c_int, [P, P, P, P]),
+        "q35_op_gdn_workspace_bytes": (c_size_t, []),
+        "q35_op_gdn_step": (c_int, [P] * 17),
+        "q35_op_attn_workspace_bytes": (c_size_t, []),
+        "q35_op_attn_decode": (c_int, [P, P, P, P, P, P, P, c_uint32, c_uint32, P, P, P]),
+        "q35_op_head_workspace_bytes": (c_size_t, []),
+        "q35_op_head_argmax": (c_int, [P, P, P, P, P, P, P, P, P, P]),
+        "q35_op_greedy": (c_int, [P, P, P, P, P]),
+        "q35_write_synthetic_model": (c_int, [c_char_p, c_uint64, c_char_p, c_size_t]),
+        "q35_version": (c_char_p, []),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        _lib = _load()
+    return _lib
+
+
+def write_synthetic_model(path: str, seed: int) -> None:
+    """Seeded random-init model in the MLX layout (config.json + model.safetensors)."""
+    err = ctypes.create_string_buffer(1024)
+    rc = lib().q35_write_synthetic_model(path.encode(), seed, err, len(err))
+    if rc != OK:
+        raise Q35Error(rc, err.value.decode())
+
+
+# ---------------------------------------------------------------------------
+# session API (Model)
+# ---------------------------------------------------------------------------
+class Model:
+    """One decode session on one GPU (Model in source/src/model.rs)."""
+
+    def __init__(self, handle, capacity: int):
+        self._h = handle
+        self.capacity = capacity
+
+    @classmethod
+    def load(cls, path: str, device: int = 0, capacity: int = 0, decode_batch: int = 0,
+             prefill_batch: int = 0) -> "Model":
+        opts = _Opts(capacity, decode_batch, prefill_batch, 0)
+        h = c_void_p()
+        err = ctypes.create_string_buffer(2048)
+        rc = lib().q35_open(path.encode(), device, ctypes.byref(opts), ctypes.byref(h), err, len(err))
+        if rc != OK:
+            raise Q35Error(rc, err.value.decode())
+        return cls(h, capacity or DEFAULT_CAPACITY)
+
+    def _check(self, rc: int) -> None:
+        if rc != OK:
+            raise Q35Error(rc, lib().q35_last_error(self._h).decode())
+
+    def generate(self, prompt, count: int, reset: bool) -> list[int]:
+        n = len(prompt)
+        arr = (c_uint32 * max(n, 1))(*prompt)
+        out = (c_uint32 * max(count, 1))()
+        self._check(lib().q35_generate(self._h, arr, n, count, 1 if reset else 0, out))
+        return list(out[:count])
+
+    def cancel(self) -> None:
+        lib().q35_cancel(self._h)
+
+    @property
+    def position(self) -> int:
+        return int(lib().q35_position(self._h))
+
+    def decode_timed(self, steps: int) -> float:
+        ms = c_float()
+        self._check(lib().q35_decode_timed(self._h, steps, ctypes.byref(ms)))
+        return float(ms.value)
+
+    def dump_state(self):
+        """Return (kv [6,2,2,pos,256] u16, state [18,16,128,128] f32, hist [18,3,6144] u16)."""
+        import numpy as np
+        pos = self.position
+        kv = np.zeros((6, 2, 2, pos, 256), np.uint16)
+        st = np.zeros((18, 16, 128, 128), np.float32)
+        hi = np.zeros((18, 3, 6144), np.uint16)
+        self._check(lib().q35_dump_state(self._h, kv.ctypes.data, st.ctypes.data, hi.ctypes.data))
+        return kv, st, hi
+
+    def last_logits(self):
+        import numpy as np
+        lg = np.zeros(VOCAB, np.uint16)
+        lse = np.zeros(1, np.uint16)
+        self._check(lib().q35_last_logits(self._h, lg.ctypes.data, lse.ctypes.data))
+        return lg, int(lse[0])
+
+    def close(self) -> None:
+        if self._h:
+            lib().q35_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ---------------------------------------------------------------------------
+# op API (torch CUDA tensors; nothing allocated by the library)
+# ---------------------------------------------------------------------------
+def _ptr(t):
+    return None if t is None else c_void_p(t.data_ptr())
+
+
+def _stream():
+    import torch
+    return c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _op(rc: int, what: str) -> None:
+    if rc != OK:
+        raise Q35Error(rc, f"{what} failed ({rc})")
+
+
+def qmv_q4(w, scales, biases, x, residual=None, out=None):
+    """y[N] = bf16(W x) (+ residual) — linear.metal qmv_q4 / qmv_add_q4."""
+    import torch
+    n, kw = w.shape
+    y = out if out is not None else torch.empty(n, dtype=torch.uint16, device=w.device)
+    _op(lib().q35_op_qmv_q4(_ptr(w), _ptr(scales), _ptr(biases), _ptr(x), _ptr(residual), _ptr(y),
+                            n, kw * 8, _stream()), "qmv_q4")
+    return y
+
+
+def embedding_q4(w, scales, biases, token: int):
+    import torch
+    k = w.shape[1] * 8
+    out = torch.empty(k, dtype=torch.uint16, device=w.device)
+    _op(lib().q35_op_embedding_q4(_ptr(w), _ptr(scales), _ptr(biases), token, k, _ptr(out), _stream()),
+        "embedding_q4")
+    return out
+
+
+def rms_norm(x, gain):
+    import torch
+    out = torch.empty_like(x)
+    _op(lib().q35_op_rms_norm(_ptr(x), _ptr(gain), _ptr(out), _stream()), "rms_norm")
+    return out
+
+
+def workspace(kind: str, device="cuda"):
+    import torch
+    n = {"gdn": lib().q35_op_gdn_workspace_bytes, "attn": lib().q35_op_attn_workspace_bytes,
+         "head": lib().q35_op_head_workspace_bytes}[kind]()
+    return torch.empty(n, dtype=torch.uint8, device=device)
+
+
+def gdn_step(raw_qkv, z, a_raw, b_raw, history, conv_w, a_log, dt_bias, state, norm_w, ow, os_, ob,
+             residual=None, ws=None):
+    import torch
+    out = torch.empty(1024, dtype=torch.uint16, device=raw_qkv.device)
+    ws = ws if ws is not None else workspace("gdn", raw_qkv.device)
+    _op(lib().q35_op_gdn_step(*[_ptr(t) for t in (raw_qkv, z, a_raw, b_raw, history, conv_w, a_log,
+                                                  dt_bias, state, norm_w, ow, os_, ob, residual, out,
+                                                  ws)], _stream()), "gdn_step")
+    return out
+
+
+def attn_decode(q_raw, k_raw, v_raw, q_gain, k_gain, kcache, vcache, capacity: int, pos: int, ws=None):
+    import torch
+    gated = torch.empty(2048, dtype=torch.uint16, device=q_raw.device)
+    ws = ws if ws is not None else workspace("attn", q_raw.device)
+    _op(lib().q35_op_attn_decode(_ptr(q_raw), _ptr(k_raw), _ptr(v_raw), _ptr(q_gain), _ptr(k_gain),
+                                 _ptr(kcache), _ptr(vcache), capacity, pos, _ptr(gated), _ptr(ws),
+                                 _stream()), "attn_decode")
+    return gated
+
+
+def head_argmax(w, scales, biases, x, gain=None, ws=None):
+    import torch
+    dev = w.device
+    logits = torch.empty(VOCAB, dtype=torch.uint16, device=dev)
+    token = torch.zeros(1, dtype=torch.int32, device=dev)
+    lse = torch.zeros(1, dtype=torch.uint16, device=dev)
+    ws = ws if ws is not None else workspace("head", dev)
+    _op(lib().q35_op_head_argmax(_ptr(w), _ptr(scales), _ptr(biases), _ptr(x), _ptr(gain),
+                                 _ptr(logits), _ptr(token), _ptr(lse), _ptr(ws), _stream()),
+        "head_argmax")
+    return logits, token, lse
+
+
+def greedy(logits, ws=None):
+    """Greedy selection on given bf16 logits [248320] (linear.metal greedy_bf16)."""
+    import torch
+    dev = logits.device
+    token = torch.zeros(1, dtype=torch.int32, device=dev)
+    lse = torch.zeros(1, dtype=torch.uint16, device=dev)
+    ws = ws if ws is not None else workspace("head", dev)
+    _op(lib().q35_op_greedy(_ptr(logits), _ptr(token), _ptr(lse), _ptr(ws), _stream()), "greedy")
+    return token, lse

@@ -1,0 +1,177 @@
+/*
+ * q35 — C ABI of the B200 decode engine for the Qwen3.5-0.8B-class 4-bit
+ * hybrid model (libq35cuda.so).
+ *
+ * This is the boundary the reference's Rust host would bind through FFI.
+ * Paths below are relative to the reference's source/ tree.
+ *
+ *   session API  <->  Model::load / Model::generate / Model::cancelled
+ *                     (src/model.rs:28-34, :37-92, :97-122, :123-180)
+ *   op API       <->  the Metal entry points the model dispatches through
+ *                     Gpu::dispatch (src/gpu.rs:69-79)
+ *
+ * Conventions: bf16 tensors are uint16_t bit patterns; device pointers are
+ * CUDA device addresses; `stream` is a cudaStream_t passed as void* (NULL =
+ * legacy default stream). Every function returns 0 on success or a negative
+ * Q35_E* code. Op-level calls allocate nothing: they borrow the caller's
+ * buffers (including any workspace) and enqueue work on `stream`.
+ */
+#ifndef Q35_H
+#define Q35_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define Q35_OK 0
+#define Q35_EINVAL (-1)    /* validation failed; session state untouched */
+#define Q35_ECUDA (-2)     /* device error; session state was reset */
+#define Q35_ECANCEL (-3)   /* q35_cancel() observed ("input disconnected") */
+#define Q35_EIO (-4)       /* model directory / file / format error */
+#define Q35_ENOMEM (-5)
+#define Q35_ETIMEOUT (-6)  /* a bounded device wait expired; state was reset */
+#define Q35_ENCCL (-7)
+
+#define Q35_VOCAB 248320u
+#define Q35_HIDDEN 1024u
+#define Q35_DEFAULT_CAPACITY 262144u /* model.rs:8 */
+
+typedef struct q35_session q35_session;
+
+typedef struct q35_opts {
+  uint32_t capacity;     /* context capacity in tokens (0 -> 262144); multiple of 32 */
+  uint32_t decode_batch; /* decode steps per CUDA-graph launch (0 -> 8) */
+  uint32_t prefill_batch;/* prompt steps per CUDA-graph launch (0 -> 16) */
+  uint32_t flags;        /* reserved, 0 */
+} q35_opts;
+
+/* ---------------------------------------------------------------------- */
+/* Session API                                                             */
+/* ---------------------------------------------------------------------- */
+
+/* Load MODEL_DIR (config.json + *.safetensors in the MLX layout, 694
+ * language_model.model.* tensors) onto `device`, allocate every buffer and
+ * capture the decode graphs. Replaces Model::load (model.rs:37-92) and
+ * Weights::load (weights.rs:11-44). On failure *out is NULL and, if err is
+ * non-NULL, a message is copied into err[0..err_len). */
+int q35_open(const char* model_dir, int device, const q35_opts* opts, q35_session** out,
+             char* err, size_t err_len);
+
+/* Model::generate (model.rs:97-122). reset != 0: discard state, consume
+ * prompt[0..n_prompt) (n_prompt >= 1) and emit max_tokens greedy ids.
+ * reset == 0: n_prompt must be 0; first consume the last emitted token, then
+ * emit max_tokens ids. out_tokens has room for max_tokens ids. Validation
+ * errors (empty prompt, capacity, id >= vocab, no continuation state) return
+ * Q35_EINVAL and leave the state intact; device errors and cancellation
+ * reset the session (model.rs:166-178). */
+int q35_generate(q35_session* s, const uint32_t* prompt, size_t n_prompt, size_t max_tokens,
+                 int reset, uint32_t* out_tokens);
+
+/* Model::cancelled (main.rs:23-24, model.rs:133-144): thread-safe; the
+ * running q35_generate drains its queued work and returns Q35_ECANCEL. */
+void q35_cancel(q35_session* s);
+
+/* Message of the last failure on this session (never NULL). */
+const char* q35_last_error(const q35_session* s);
+
+void q35_close(q35_session* s);
+
+/* Tokens consumed so far (Model::position, model.rs:32). */
+uint32_t q35_position(const q35_session* s);
+
+/* Copy the device state to host memory for checking: per attention layer
+ * (6) K and V caches [2][capacity][256] bf16 truncated to the first `pos`
+ * positions (layout [2][pos][256] each), per GDN layer (18) recurrent state
+ * f32 [16][128][128] and conv history bf16 [3][6144]. Buffers must hold
+ * 6*2*2*pos*256*2 bytes (kv), 18*16*128*128*4 (state), 18*3*6144*2 (hist). */
+int q35_dump_state(q35_session* s, uint16_t* kv, float* state, uint16_t* hist);
+
+/* bf16 logits [248320] and lse of the last emitted token. */
+int q35_last_logits(q35_session* s, uint16_t* logits, uint16_t* lse);
+
+/* Decode-only timing helpers for benchmarks: run `steps` greedy decode steps
+ * on the current state (as q35_generate with reset=0 would) but leave the
+ * tokens on the device; returns the device time in milliseconds. */
+int q35_decode_timed(q35_session* s, size_t steps, float* ms);
+
+/* ---------------------------------------------------------------------- */
+/* Op API (device pointers, caller-owned, nothing allocated)               */
+/* ---------------------------------------------------------------------- */
+
+/* qmv_q4 / qmv_add_q4 (kernels/linear.metal:28-123): y[N] = bf16(W x), or
+ * bf16(residual + bf16(W x)) when residual is non-NULL (residual may alias y).
+ * W: codes [N][K/8] u32, scales/biases [N][K/64] bf16; K in {1024, 2048, 3584}
+ * (any multiple of 512 up to 4096); x [K] bf16. */
+int q35_op_qmv_q4(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
+                  const uint16_t* x, const uint16_t* residual, uint16_t* y, int n, int k,
+                  void* stream);
+
+/* embedding_q4 (kernels/linear.metal:11-24): out[K] = bf16(s*q + b) of row `token`. */
+int q35_op_embedding_q4(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
+                        uint32_t token, int k, uint16_t* out, void* stream);
+
+/* rms_norm_bf16 (kernels/linear.metal:300-331) for one 1024-wide row, eps 1e-6. */
+int q35_op_rms_norm(const uint16_t* x, const uint16_t* gain, uint16_t* out, void* stream);
+
+/* Single-token gated-delta-net mixer after the input projections:
+ * gdn_input_g16's conv/prepare tail (kernels/gdn_input.metal:412-460),
+ * gdn_recur (kernels/gdn.metal:176-228), gdn_norm_gate (:230-255) and the
+ * out_proj qmv_add_q4 (model.rs:265). raw_qkv [6144], z [2048], a/b [16] bf16;
+ * history [3][6144] bf16 and state [16][128][128] f32 are updated in place;
+ * conv_w [6144][4] bf16, a_log [16] f32, dt_bias [16] bf16, norm_w [128] bf16;
+ * out_proj Q4 [1024][2048]; residual may be NULL. Workspace: at least
+ * q35_op_gdn_workspace_bytes() bytes of device memory. */
+size_t q35_op_gdn_workspace_bytes(void);
+int q35_op_gdn_step(const uint16_t* raw_qkv, const uint16_t* z, const uint16_t* a_raw,
+                    const uint16_t* b_raw, uint16_t* history, const uint16_t* conv_w,
+                    const float* a_log, const uint16_t* dt_bias, float* state,
+                    const uint16_t* norm_w, const uint32_t* ow, const uint16_t* os,
+                    const uint16_t* ob, const uint16_t* residual, uint16_t* out,
+                    void* workspace, void* stream);
+
+/* Gated GQA decode attention for one token at position `pos`:
+ * attn_prepare_qkv_decode (kernels/attention.metal:262-313) appends the
+ * token's K/V at `pos`, then split-K attention over keys 0..pos
+ * (kernels/attention_decode.metal:215-431) and the combine with the BF16
+ * output gate (:830-891). q_raw [8][512] (query | gate), k_raw/v_raw
+ * [2][256], q/k norm gains [256]; caches [2][capacity][256] bf16
+ * (capacity a multiple of 32, pos < capacity); gated [8][256] bf16. */
+size_t q35_op_attn_workspace_bytes(void);
+int q35_op_attn_decode(const uint16_t* q_raw, const uint16_t* k_raw, const uint16_t* v_raw,
+                       const uint16_t* q_gain, const uint16_t* k_gain, uint16_t* kcache,
+                       uint16_t* vcache, uint32_t capacity, uint32_t pos, uint16_t* gated,
+                       void* workspace, void* stream);
+
+/* Final RMSNorm (gain may be NULL to skip it), vocabulary projection of the
+ * tied Q4 embedding [248320][1024] and greedy selection
+ * (kernels/head_lse.metal:11-98, linear.metal:300-331): logits [248320]
+ * bf16, token [1] u32, lse [1] bf16 (may be NULL). */
+size_t q35_op_head_workspace_bytes(void);
+int q35_op_head_argmax(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
+                       const uint16_t* x, const uint16_t* gain, uint16_t* logits,
+                       uint32_t* token, uint16_t* lse, void* workspace, void* stream);
+
+/* greedy_bf16 (kernels/linear.metal:400-449) on given bf16 logits [248320]:
+ * lse = bf16(logsumexp), token = lowest id among the maxima of
+ * bf16(logit - lse). Workspace: q35_op_head_workspace_bytes(). */
+int q35_op_greedy(const uint16_t* logits, uint32_t* token, uint16_t* lse, void* workspace,
+                  void* stream);
+
+/* ---------------------------------------------------------------------- */
+/* Utility (no counterpart in the reference)                               */
+/* ---------------------------------------------------------------------- */
+
+/* Write a seeded random-init model directory in the MLX layout the loader
+ * expects: config.json + model.safetensors with the 694 tensors of the
+ * model (all linears Q4 affine group-64 quantised from N(0, 0.02)). */
+int q35_write_synthetic_model(const char* dir, uint64_t seed, char* err, size_t err_len);
+
+/* Library build string. */
+const char* q35_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* Q35_H */

@@ -1,0 +1,1105 @@
+/*
+ * q35 oracle — TEST INFRASTRUCTURE ONLY (see q35_oracle.h).
+ *
+ * Every function below restates one reference kernel; the citation names the
+ * file:line range under the reference's source/ tree. Lane/SIMD structure is
+ * kept where it fixes the f32 evaluation order; simd_sum/simd_max are taken
+ * as xor-butterflies over the 32 lanes.
+ */
+#include "q35_oracle.h"
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <condition_variable>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <functional>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+namespace {
+
+/* ------------------------------------------------------------------ */
+/* scalar helpers                                                      */
+/* ------------------------------------------------------------------ */
+inline float bf2f(uint16_t h) {
+  uint32_t u = uint32_t(h) << 16;
+  float f;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+inline uint16_t f2bf(float f) {
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return uint16_t((u >> 16) | 0x40u);
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return uint16_t(u >> 16);
+}
+inline float bfr(float f) { return bf2f(f2bf(f)); }
+inline float dexp(float x) { return (float)std::exp((double)x); }
+inline float dlog(float x) { return (float)std::log((double)x); }
+inline float drsqrt(float x) { return (float)(1.0 / std::sqrt((double)x)); }
+const float kFiniteMin = -3.4028234663852886e38f;
+
+/* The reference's fast::exp sites (attention_decode.metal softmax updates and
+ * combines, head_lse.metal) are taken as this f32 exp: Cody-Waite reduction
+ * x = n*ln2 + r, degree-7 Taylor polynomial of e^r by fmaf (Horner), 2^n from
+ * exponent bits. Built only from IEEE-exact operations, so the CUDA path can
+ * produce the same bits; relative error below 2 ulp. */
+inline float fexp(float x) {
+  if (x != x) return x;
+  if (x > 88.72283935546875f) return INFINITY;
+  if (x < -103.97208404541016f) return 0.0f;
+  const float n = std::rint(x * 1.4426950408889634f);
+  float r = std::fmaf(-n, 0.693145751953125f, x);
+  r = std::fmaf(-n, 1.428606765330187e-06f, r);
+  float p = 1.0f / 5040.0f;
+  p = std::fmaf(p, r, 1.0f / 720.0f);
+  p = std::fmaf(p, r, 1.0f / 120.0f);
+  p = std::fmaf(p, r, 1.0f / 24.0f);
+  p = std::fmaf(p, r, 1.0f / 6.0f);
+  p = std::fmaf(p, r, 0.5f);
+  p = std::fmaf(p, r, 1.0f);
+  p = std::fmaf(p, r, 1.0f);
+  const int ni = int(n);
+  auto pow2 = [](int e) {
+    uint32_t u = uint32_t(e) << 23;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+  };
+  if (ni >= -125) return (p * pow2(ni + 126)) * 2.0f;
+  return (p * pow2(ni + 127 + 64)) * pow2(127 - 64);
+}
+
+/* simd_sum as an xor butterfly over 32 lanes (all lanes end equal) */
+inline float bsum32(const float* v) {
+  float a[32], b[32];
+  std::memcpy(a, v, sizeof(a));
+  for (int m = 16; m >= 1; m >>= 1) {
+    for (int l = 0; l < 32; ++l) b[l] = a[l] + a[l ^ m];
+    std::memcpy(a, b, sizeof(a));
+  }
+  return a[0];
+}
+inline float bmax32(const float* v) {
+  float m = v[0];
+  for (int l = 1; l < 32; ++l) m = std::max(m, v[l]);
+  return m;
+}
+
+/* gdn.metal:10-15 (and gdn_input.metal:21-26): BF16-stepped sigmoid */
+inline float sigmoid_bf(float x) {
+  float e = bfr(dexp(std::fabs(x)));
+  float d = bfr(1.0f + e);
+  float y = bfr(1.0f / d);
+  return bfr(x < 0.0f ? y : 1.0f - y);
+}
+/* gdn.metal:19-23: MLX utils.h log1p specialised to [0,1] */
+inline float log1p_mlx(float x) {
+  float xp1 = 1.0f + x;
+  if (xp1 == 1.0f) return x;
+  return x * (dlog(xp1) / (xp1 - 1.0f));
+}
+/* gdn.metal:25-29 */
+inline float softplus_bf(float x) {
+  float e = bfr(dexp(-std::fabs(x)));
+  float l = bfr(log1p_mlx(e));
+  return bfr(std::max(x, 0.0f) + l);
+}
+/* attention.metal:145-149, linear.metal:389-395: BF16 gate sigmoid */
+inline float gate_sigmoid_bf(float x) {
+  float e = bfr(dexp(std::fabs(x)));
+  float denom = bfr(1.0f + e);
+  float inverse = bfr(1.0f / denom);
+  return bfr(x < 0.0f ? inverse : 1.0f - inverse);
+}
+/* linear.metal:389-395 / linear_norm.metal:95-103 */
+inline uint16_t swiglu1(float g, float up) {
+  float e = bfr(dexp(std::fabs(g)));
+  float denom = bfr(1.0f + e);
+  float prob = bfr(1.0f / denom);
+  float s = bfr(g < 0 ? prob : 1.0f - prob);
+  float silu = bfr(g * s);
+  return f2bf(silu * up);
+}
+
+/* ------------------------------------------------------------------ */
+/* thread pool: deterministic (each output owned by one task)          */
+/* ------------------------------------------------------------------ */
+class Pool {
+ public:
+  void set(int n) {
+    stop();
+    nthreads_ = std::max(1, n);
+    for (int i = 1; i < nthreads_; ++i) workers_.emplace_back([this, i] { loop(i); });
+  }
+  int size() const { return nthreads_; }
+  ~Pool() { stop(); }
+  void run(long n, const std::function<void(long, long)>& fn) {
+    if (nthreads_ <= 1 || n < 2) {
+      fn(0, n);
+      return;
+    }
+    std::unique_lock<std::mutex> lk(mu_);
+    job_ = &fn;
+    total_ = n;
+    next_.store(0);
+    pending_ = nthreads_ - 1;
+    ++gen_;
+    cv_.notify_all();
+    lk.unlock();
+    work();
+    lk.lock();
+    done_cv_.wait(lk, [this] { return pending_ == 0; });
+    job_ = nullptr;
+  }
+
+ private:
+  void work() {
+    const long chunk = std::max<long>(1, total_ / (nthreads_ * 8));
+    for (;;) {
+      long b = next_.fetch_add(chunk);
+      if (b >= total_) break;
+      (*job_)(b, std::min(total_, b + chunk));
+    }
+  }
+  void loop(int) {
+    unsigned long seen = 0;
+    for (;;) {
+      std::unique_lock<std::mutex> lk(mu_);
+      cv_.wait(lk, [&] { return quit_ || gen_ != seen; });
+      if (quit_) return;
+      seen = gen_;
+      lk.unlock();
+      work();
+      lk.lock();
+      if (--pending_ == 0) done_cv_.notify_all();
+    }
+  }
+  void stop() {
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      quit_ = true;
+      cv_.notify_all();
+    }
+    for (auto& t : workers_) t.join();
+    workers_.clear();
+    quit_ = false;
+  }
+  int nthreads_ = 1;
+  std::vector<std::thread> workers_;
+  std::mutex mu_;
+  std::condition_variable cv_, done_cv_;
+  const std::function<void(long, long)>* job_ = nullptr;
+  long total_ = 0;
+  std::atomic<long> next_{0};
+  int pending_ = 0;
+  unsigned long gen_ = 0;
+  bool quit_ = false;
+};
+Pool& pool() {
+  static Pool p;
+  static bool init = [] {
+    const char* e = std::getenv("Q35_ORACLE_THREADS");
+    p.set(e ? std::atoi(e) : 1);
+    return true;
+  }();
+  (void)init;
+  return p;
+}
+
+/* ------------------------------------------------------------------ */
+/* Q4 affine matvec: per-row value exactly as qmv_q4 (linear.metal:38-71) */
+/* ------------------------------------------------------------------ */
+float qmv_row(const uint32_t* w, const uint16_t* s, const uint16_t* b, const float* x, int n,
+              int K) {
+  float lanes[32];
+  for (int lane = 0; lane < 32; ++lane) {
+    float accum = 0.0f;
+    for (int k0 = 0; k0 < K; k0 += 512) {
+      const int k = k0 + lane * 16;
+      float xx[16];
+      float xs = 0.0f;
+      for (int j = 0; j < 16; j += 4) {
+        float a = x[k + j], bb = x[k + j + 1], c = x[k + j + 2], d = x[k + j + 3];
+        xs += ((a + bb) + c) + d;
+        xx[j] = a;
+        xx[j + 1] = bb / 16.0f;
+        xx[j + 2] = c / 256.0f;
+        xx[j + 3] = d / 4096.0f;
+      }
+      const uint16_t* ww = reinterpret_cast<const uint16_t*>(w + size_t(n) * (K / 8) + k / 8);
+      float dotq = 0.0f;
+      for (int j = 0; j < 4; ++j) {
+        uint16_t v = ww[j];
+        float t0 = xx[4 * j] * float(v & 0x000f);
+        float t1 = xx[4 * j + 1] * float(v & 0x00f0);
+        float t2 = xx[4 * j + 2] * float(v & 0x0f00);
+        float t3 = xx[4 * j + 3] * float(v & 0xf000);
+        dotq += ((t0 + t1) + t2) + t3;
+      }
+      const size_t gi = size_t(n) * (K / 64) + k / 64;
+      float p1 = bf2f(s[gi]) * dotq;
+      float p2 = xs * bf2f(b[gi]);
+      accum += p1 + p2;
+    }
+    lanes[lane] = accum;
+  }
+  return bsum32(lanes);
+}
+
+void qmv_f32(const uint32_t* w, const uint16_t* s, const uint16_t* b, const uint16_t* x, int N,
+             int K, float* y) {
+  std::vector<float> xf(K);
+  for (int i = 0; i < K; ++i) xf[i] = bf2f(x[i]);
+  pool().run(N, [&](long b0, long b1) {
+    for (long n = b0; n < b1; ++n) y[n] = qmv_row(w, s, b, xf.data(), int(n), K);
+  });
+}
+
+/* rms_norm_bf16, linear.metal:300-331: threads of 4 contiguous values,
+ * SIMD sums then a 32-entry SIMD sum of the per-SIMD partials. */
+void rms_norm(const uint16_t* x, const uint16_t* gain, int cols, float eps, uint16_t* out) {
+  const int threads = ((cols + 127) / 128) * 32;
+  std::vector<float> v(size_t(threads) * 4, 0.0f), acc(threads, 0.0f);
+  for (int t = 0; t < threads; ++t) {
+    float a = 0.0f;
+    for (int j = 0; j < 4; ++j) {
+      int c = t * 4 + j;
+      v[t * 4 + j] = c < cols ? bf2f(x[c]) : 0.0f;
+      a += v[t * 4 + j] * v[t * 4 + j];
+    }
+    acc[t] = a;
+  }
+  float sums[32] = {0};
+  for (int sg = 0; sg < threads / 32; ++sg) sums[sg] = bsum32(&acc[sg * 32]);
+  float total = bsum32(sums);
+  float inv = drsqrt(total / float(cols) + eps);
+  for (int c = 0; c < cols; ++c) out[c] = f2bf(bfr(v[c] * inv) * bf2f(gain[c]));
+}
+
+/* attention.metal:37-53 + the normalised-value line of :287: one head of 256,
+ * 64 threads x 4 values, two SIMD partials. */
+void head_rms(const uint16_t* x, const uint16_t* gain, float* normalized) {
+  float part[64];
+  for (int t = 0; t < 64; ++t) {
+    float s = 0.0f;
+    for (int i = 0; i < 4; ++i) {
+      float v = bf2f(x[4 * t + i]);
+      s += v * v;
+    }
+    part[t] = s;
+  }
+  float s0 = bsum32(part), s1 = bsum32(part + 32);
+  float inv = drsqrt((s0 + s1) / 256.0f + 1e-6f);
+  for (int d = 0; d < 256; ++d) normalized[d] = bfr(bfr(bf2f(x[d]) * inv) * bf2f(gain[d]));
+}
+
+/* attention.metal:55-70 */
+float rope(const float* normalized, int d, uint32_t position) {
+  if (d >= 64) return normalized[d];
+  int pair = d % 32;
+  float arg = (-(float(pair) / 32.0f)) * 23.253496170043945f;
+  float inv_freq = (float)std::exp2((double)arg);
+  float angle = float(position) * inv_freq;
+  float c = (float)std::cos((double)angle);
+  float s = (float)std::sin((double)angle);
+  float lo = normalized[pair], hi = normalized[pair + 32];
+  if (d < 32) {
+    float t0 = lo * c, t1 = hi * s;
+    return bfr(t0 - t1);
+  }
+  float t0 = lo * s, t1 = hi * c;
+  return bfr(t0 + t1);
+}
+
+/* One SIMD group's online-softmax walk over keys i = first, first+stride, ...
+ * (attention_decode.metal:149-193 and :300-418 share this per-key update). */
+struct Walk {
+  float o[32][8];
+  float maxs[32];
+  float sums[32];
+};
+void walk_keys(const float* qf /*[256], already scaled*/, const uint16_t* kc, const uint16_t* vc,
+               int first, int stride, int n, float o_out[256], float* max_out, float* sum_out) {
+  float o[256] = {0};
+  float max_score = kFiniteMin, sum_exp = 0.0f;
+  float lanes[32];
+  for (int i = first; i < n; i += stride) {
+    const uint16_t* kr = kc + size_t(i) * 256;
+    const uint16_t* vr = vc + size_t(i) * 256;
+    for (int l = 0; l < 32; ++l) {
+      float sc = 0.0f;
+      for (int j = 0; j < 8; ++j) sc += qf[l * 8 + j] * bf2f(kr[l * 8 + j]);
+      lanes[l] = sc;
+    }
+    float score = bsum32(lanes);
+    float new_max = std::max(max_score, score);
+    float factor = fexp(max_score - new_max);
+    float exp_score = fexp(score - new_max);
+    max_score = new_max;
+    sum_exp = sum_exp * factor + exp_score;
+    for (int d = 0; d < 256; ++d) {
+      float t0 = o[d] * factor, t1 = exp_score * bf2f(vr[d]);
+      o[d] = t0 + t1;
+    }
+  }
+  std::memcpy(o_out, o, sizeof(o));
+  *max_out = max_score;
+  *sum_out = sum_exp;
+}
+
+/* f32 attention output for all 8 query heads (before the bf16 store).
+ * len < 1024: sdpa_vector (attention_decode.metal:51-213), 32 groups.
+ * len >= 1024: sdpa_vector_2pass_1 with 64 blocks storing bf16 unnormalised
+ * partials (:215-431) and the combine of attn_decode_split2_gate (:853-876). */
+void attn_f32(const uint16_t* query, const uint16_t* kcache, const uint16_t* vcache, uint32_t len,
+              uint32_t capacity, float* out /*[8*256]*/) {
+  const bool split = len >= 1024;
+  const int parts = split ? 64 : 32;
+  std::vector<float> po(size_t(8) * parts * 256), pm(size_t(8) * parts), ps(size_t(8) * parts);
+  pool().run(8L * parts, [&](long b0, long b1) {
+    for (long t = b0; t < b1; ++t) {
+      int qh = int(t / parts), p = int(t % parts);
+      int kh = qh / 4;
+      float qf[256];
+      for (int d = 0; d < 256; ++d) qf[d] = 0.0625f * bf2f(query[qh * 256 + d]);
+      const uint16_t* kc = kcache + size_t(kh) * capacity * 256;
+      const uint16_t* vc = vcache + size_t(kh) * capacity * 256;
+      float o[256], m, s;
+      walk_keys(qf, kc, vc, p, parts, int(len), o, &m, &s);
+      float* dst = &po[(size_t(qh) * parts + p) * 256];
+      for (int d = 0; d < 256; ++d) dst[d] = split ? bfr(o[d]) : o[d];
+      pm[qh * parts + p] = m;
+      ps[qh * parts + p] = s;
+    }
+  });
+  for (int qh = 0; qh < 8; ++qh) {
+    const float* m = &pm[qh * parts];
+    const float* s = &ps[qh * parts];
+    const float* o = &po[size_t(qh) * parts * 256];
+    if (!split) {
+      /* :198-205: thread (g,l) uses group l's factor; butterfly over l. */
+      float gmax = bmax32(m);
+      float fac[32], tmp[32];
+      for (int l = 0; l < 32; ++l) {
+        fac[l] = fexp(m[l] - gmax);
+        tmp[l] = s[l] * fac[l];
+      }
+      float sum = bsum32(tmp);
+      for (int d = 0; d < 256; ++d) {
+        for (int l = 0; l < 32; ++l) tmp[l] = o[l * 256 + d] * fac[l];
+        float v = bsum32(tmp);
+        out[qh * 256 + d] = sum == 0.0f ? v : v / sum;
+      }
+    } else {
+      /* :853-876: lane l owns blocks l and l+32. */
+      float lm[32];
+      for (int l = 0; l < 32; ++l) lm[l] = std::max(std::max(kFiniteMin, m[l]), m[l + 32]);
+      float gmax = bmax32(lm);
+      float tmp[32];
+      for (int l = 0; l < 32; ++l) {
+        float acc = 0.0f;
+        for (int b = 0; b < 2; ++b) {
+          float f = fexp(m[l + 32 * b] - gmax);
+          acc += f * s[l + 32 * b];
+        }
+        tmp[l] = acc;
+      }
+      float sum = bsum32(tmp);
+      for (int d = 0; d < 256; ++d) {
+        for (int l = 0; l < 32; ++l) {
+          float acc = 0.0f;
+          for (int b = 0; b < 2; ++b) {
+            float f = fexp(m[l + 32 * b] - gmax);
+            acc += f * o[(l + 32 * b) * 256 + d];
+          }
+          tmp[l] = acc;
+        }
+        float v = bsum32(tmp);
+        out[qh * 256 + d] = sum == 0.0f ? v : v / sum;
+      }
+    }
+  }
+}
+
+/* head_lse_g8 partials + head_lse_tail LSE (head_lse.metal:11-64, :66-82) */
+uint16_t lse_of(const uint16_t* logits, int N) {
+  float pmax[1024], psum[1024];
+  const int tiles = (N + 4095) / 4096;
+  for (int owner = 0; owner < 1024; ++owner) {
+    float vmax = -3.4028234663852886e38f, normalizer = 0.0f;
+    for (int tile = 0; tile < tiles; ++tile) {
+      int row0 = tile * 4096 + owner * 4;
+      float vals[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      if (row0 < N)
+        for (int q = 0; q < 4; ++q)
+          if (row0 + q < N) vals[q] = bf2f(logits[row0 + q]);
+      float prev = vmax;
+      for (int j = 0; j < 4; ++j) vmax = std::max(vmax, vals[j]);
+      normalizer *= fexp(prev - vmax);
+      for (int j = 0; j < 4; ++j) normalizer += fexp(vals[j] - vmax);
+    }
+    pmax[owner] = vmax;
+    psum[owner] = normalizer;
+  }
+  float maxima[32], sums[32];
+  for (int sg = 0; sg < 32; ++sg) {
+    float m = bmax32(pmax + sg * 32);
+    float t[32];
+    for (int l = 0; l < 32; ++l) t[l] = psum[sg * 32 + l] * fexp(pmax[sg * 32 + l] - m);
+    maxima[sg] = m;
+    sums[sg] = bsum32(t);
+  }
+  float gm = bmax32(maxima);
+  float t[32];
+  for (int sg = 0; sg < 32; ++sg) t[sg] = sums[sg] * fexp(maxima[sg] - gm);
+  float normalizer = bsum32(t);
+  return f2bf(dlog(normalizer) + gm);
+}
+
+/* head_lse.metal:83-96: lowest id among the maxima of bf16(logit - lse) */
+uint32_t greedy_lse(const uint16_t* logits, int N, uint16_t lse) {
+  const float l = bf2f(lse);
+  float best = -INFINITY;
+  uint32_t id = 0xffffffffu;
+  for (int i = 0; i < N; ++i) {
+    float v = bfr(bf2f(logits[i]) - l);
+    if (v > best) {
+      best = v;
+      id = uint32_t(i);
+    }
+  }
+  return id;
+}
+
+/* ------------------------------------------------------------------ */
+/* safetensors reading (test-side copy; format per weights.rs:17-53)   */
+/* ------------------------------------------------------------------ */
+struct Tensor {
+  std::string dtype;
+  std::vector<size_t> shape;
+  size_t offset = 0, bytes = 0;
+};
+
+bool parse_header(const std::string& js, std::map<std::string, Tensor>& out, std::string& err) {
+  size_t i = 0;
+  auto ws = [&] {
+    while (i < js.size() && isspace((unsigned char)js[i])) ++i;
+  };
+  auto str = [&](std::string& s) -> bool {
+    ws();
+    if (i >= js.size() || js[i] != '"') return false;
+    ++i;
+    s.clear();
+    while (i < js.size() && js[i] != '"') {
+      if (js[i] == '\\' && i + 1 < js.size()) ++i;
+      s += js[i++];
+    }
+    ++i;
+    return true;
+  };
+  auto num = [&](size_t& v) -> bool {
+    ws();
+    size_t st = i;
+    while (i < js.size() && isdigit((unsigned char)js[i])) ++i;
+    if (st == i) return false;
+    v = std::stoull(js.substr(st, i - st));
+    return true;
+  };
+  auto skip_value = [&]() {
+    ws();
+    int depth = 0;
+    bool instr = false;
+    for (; i < js.size(); ++i) {
+      char c = js[i];
+      if (instr) {
+        if (c == '\\') ++i;
+        else if (c == '"') instr = false;
+        continue;
+      }
+      if (c == '"') instr = true;
+      else if (c == '{' || c == '[') ++depth;
+      else if (c == '}' || c == ']') {
+        if (depth == 0) return;
+        if (--depth == 0) {
+          ++i;
+          return;
+        }
+      } else if (c == ',' && depth == 0)
+        return;
+    }
+  };
+  ws();
+  if (js[i] != '{') {
+    err = "header not an object";
+    return false;
+  }
+  ++i;
+  for (;;) {
+    ws();
+    if (js[i] == '}') break;
+    std::string name;
+    if (!str(name)) {
+      err = "bad key";
+      return false;
+    }
+    ws();
+    ++i; /* ':' */
+    ws();
+    if (name == "__metadata__") {
+      skip_value();
+    } else {
+      Tensor t;
+      ++i; /* '{' */
+      for (;;) {
+        ws();
+        if (js[i] == '}') {
+          ++i;
+          break;
+        }
+        std::string key;
+        str(key);
+        ws();
+        ++i;
+        ws();
+        if (key == "dtype") {
+          str(t.dtype);
+        } else if (key == "shape") {
+          ++i;
+          for (;;) {
+            ws();
+            if (js[i] == ']') {
+              ++i;
+              break;
+            }
+            size_t v;
+            num(v);
+            t.shape.push_back(v);
+            ws();
+            if (js[i] == ',') ++i;
+          }
+        } else if (key == "data_offsets") {
+          ++i;
+          size_t a = 0, b = 0;
+          num(a);
+          ws();
+          ++i;
+          num(b);
+          ws();
+          ++i;
+          t.offset = a;
+          t.bytes = b - a;
+        } else {
+          skip_value();
+        }
+        ws();
+        if (js[i] == ',') ++i;
+      }
+      out[name] = t;
+    }
+    ws();
+    if (js[i] == ',') ++i;
+  }
+  return true;
+}
+
+}  // namespace
+
+/* ==================================================================== */
+/* C API: ops                                                            */
+/* ==================================================================== */
+extern "C" {
+
+void orc_set_threads(int n) { pool().set(n); }
+int orc_get_threads(void) { return pool().size(); }
+uint16_t orc_f2bf(float f) { return f2bf(f); }
+float orc_bf2f(uint16_t h) { return bf2f(h); }
+float orc_sigmoid_bf(float x) { return sigmoid_bf(x); }
+float orc_softplus_bf(float x) { return softplus_bf(x); }
+float orc_fexp(float x) { return fexp(x); }
+
+/* linear.metal:19-23 */
+void orc_embedding_q4(const uint32_t* w, const uint16_t* s, const uint16_t* b, uint32_t token,
+                      int K, uint16_t* out) {
+  for (int k = 0; k < K; ++k) {
+    uint32_t q = (w[size_t(token) * (K / 8) + k / 8] >> (4 * (k % 8))) & 15u;
+    size_t g = size_t(token) * (K / 64) + k / 64;
+    float t = bf2f(s[g]) * float(q);
+    out[k] = f2bf(t + bf2f(b[g]));
+  }
+}
+
+void orc_qmv_q4_f32(const uint32_t* w, const uint16_t* s, const uint16_t* b, const uint16_t* x,
+                    int N, int K, float* y) {
+  qmv_f32(w, s, b, x, N, K, y);
+}
+
+/* linear.metal:69-72 and :119-122 */
+void orc_qmv_q4(const uint32_t* w, const uint16_t* s, const uint16_t* b, const uint16_t* x,
+                const uint16_t* residual, int N, int K, uint16_t* y) {
+  std::vector<float> v(N);
+  qmv_f32(w, s, b, x, N, K, v.data());
+  for (int n = 0; n < N; ++n)
+    y[n] = residual ? f2bf(bf2f(residual[n]) + bfr(v[n])) : f2bf(v[n]);
+}
+
+void orc_rms_norm(const uint16_t* x, const uint16_t* gain, int cols, float eps, uint16_t* out) {
+  rms_norm(x, gain, cols, eps, out);
+}
+
+void orc_swiglu(const uint16_t* gate, const uint16_t* up, int n, uint16_t* out) {
+  for (int i = 0; i < n; ++i) out[i] = swiglu1(bf2f(gate[i]), bf2f(up[i]));
+}
+
+/* gdn_input.metal:412-460 (and gdn.metal:121-171 for the same tail) */
+void orc_gdn_conv_prepare(const uint16_t* raw, const uint16_t* a_raw, const uint16_t* b_raw,
+                          uint16_t* history, const uint16_t* conv_w, const float* a_log,
+                          const uint16_t* dt_bias, uint16_t* conv, float* g, uint16_t* beta) {
+  const float q_scale = 0.0078125f;
+  const float k_scale = bfr(0.08838834764831845f);
+  for (int group = 0; group < 48; ++group) {
+    int block = group / 16, h = group % 16;
+    float v[32][4], ss[32];
+    for (int lane = 0; lane < 32; ++lane) {
+      int off = block * 2048 + h * 128 + lane * 4;
+      float acc2 = 0.0f;
+      for (int i = 0; i < 4; ++i) {
+        int c = off + i;
+        uint16_t old[3] = {history[c], history[6144 + c], history[12288 + c]};
+        float acc = 0.0f;
+        for (int tap = 0; tap < 4; ++tap) {
+          float xin = tap < 3 ? bf2f(old[tap]) : bf2f(raw[c]);
+          acc = std::fmaf(xin, bf2f(conv_w[c * 4 + tap]), acc);
+        }
+        float xq = bfr(acc);
+        v[lane][i] = bfr(xq * sigmoid_bf(xq));
+        acc2 += v[lane][i] * v[lane][i];
+        history[c] = old[1];
+        history[6144 + c] = old[2];
+        history[12288 + c] = raw[c];
+      }
+      ss[lane] = acc2;
+    }
+    if (block < 2) {
+      float tot = bsum32(ss);
+      float inv = drsqrt(tot / 128.0f + 1.0e-6f / 128.0f);
+      float scale = block == 0 ? q_scale : k_scale;
+      for (int lane = 0; lane < 32; ++lane)
+        for (int i = 0; i < 4; ++i)
+          conv[block * 2048 + h * 128 + lane * 4 + i] = f2bf(bfr(v[lane][i] * inv) * scale);
+    } else {
+      for (int lane = 0; lane < 32; ++lane)
+        for (int i = 0; i < 4; ++i) conv[block * 2048 + h * 128 + lane * 4 + i] = f2bf(v[lane][i]);
+    }
+  }
+  for (int h = 0; h < 16; ++h) {
+    float a = bf2f(a_raw[h]), bb = bf2f(b_raw[h]);
+    float ax = bfr(a + bf2f(dt_bias[h]));
+    float e1 = dexp(a_log[h]);
+    float arg = (-e1) * softplus_bf(ax);
+    g[h] = dexp(arg);
+    beta[h] = f2bf(sigmoid_bf(bb));
+  }
+}
+
+/* gdn.metal:176-228 for one token */
+void orc_gdn_recur(const uint16_t* qkv, const float* g, const uint16_t* beta, float* state_io,
+                   uint16_t* y) {
+  pool().run(16L * 128, [&](long b0, long b1) {
+    for (long t = b0; t < b1; ++t) {
+      int h = int(t / 128), row = int(t % 128);
+      float st[4][32], mem[4], outp[4];
+      const float gt = g[h];
+      for (int r = 0; r < 4; ++r) {
+        const size_t so = (size_t(h) * 128 + row) * 128 + r * 32;
+        for (int i = 0; i < 32; ++i) st[r][i] = state_io[so + i];
+        const int k_off = 2048 + h * 128 + r * 32;
+        float part[8];
+        for (int pb = 0; pb < 8; ++pb) {
+          float acc = 0.0f;
+          for (int i = 0; i < 4; ++i) {
+            int e = pb * 4 + i;
+            st[r][e] = st[r][e] * gt;
+            acc += st[r][e] * bf2f(qkv[k_off + e]);
+          }
+          part[pb] = acc;
+        }
+        mem[r] = ((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7]));
+      }
+      float m1[4];
+      for (int r = 0; r < 4; ++r) m1[r] = mem[r] + mem[r ^ 1];
+      float memory = m1[0] + m1[2];
+      float delta = (bf2f(qkv[4096 + h * 128 + row]) - memory) * bf2f(beta[h]);
+      for (int r = 0; r < 4; ++r) {
+        const int q_off = h * 128 + r * 32, k_off = 2048 + h * 128 + r * 32;
+        float part[8];
+        for (int pb = 0; pb < 8; ++pb) {
+          float acc = 0.0f;
+          for (int i = 0; i < 4; ++i) {
+            int e = pb * 4 + i;
+            float kd = bf2f(qkv[k_off + e]) * delta;
+            st[r][e] = st[r][e] + kd;
+            acc += st[r][e] * bf2f(qkv[q_off + e]);
+          }
+          part[pb] = acc;
+        }
+        outp[r] = ((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7]));
+        const size_t so = (size_t(h) * 128 + row) * 128 + r * 32;
+        for (int i = 0; i < 32; ++i) state_io[so + i] = st[r][i];
+      }
+      float o1[4];
+      for (int r = 0; r < 4; ++r) o1[r] = outp[r] + outp[r ^ 1];
+      y[h * 128 + row] = f2bf(o1[0] + o1[2]);
+    }
+  });
+}
+
+/* gdn.metal:238-254 */
+void orc_gdn_norm_gate(const uint16_t* y, const uint16_t* z, const uint16_t* w, uint16_t* out) {
+  for (int h = 0; h < 16; ++h) {
+    float ss[32];
+    for (int lane = 0; lane < 32; ++lane) {
+      float a = 0.0f;
+      for (int i = 0; i < 4; ++i) {
+        float v = bf2f(y[h * 128 + lane * 4 + i]);
+        a += v * v;
+      }
+      ss[lane] = a;
+    }
+    float inv = drsqrt(bsum32(ss) / 128.0f + 1e-6f);
+    for (int d = 0; d < 128; ++d) {
+      float v = bf2f(y[h * 128 + d]);
+      float norm = bfr(bfr(v * inv) * bf2f(w[d]));
+      float gate = bf2f(z[h * 128 + d]);
+      float sy = 1.0f / (1.0f + dexp(std::fabs(gate)));
+      float sig = gate < 0.0f ? sy : 1.0f - sy;
+      out[h * 128 + d] = f2bf((gate * sig) * norm);
+    }
+  }
+}
+
+void orc_gdn_step(const uint16_t* raw_qkv, const uint16_t* z, const uint16_t* a_raw,
+                  const uint16_t* b_raw, uint16_t* history, const uint16_t* conv_w,
+                  const float* a_log, const uint16_t* dt_bias, float* state,
+                  const uint16_t* norm_w, const uint32_t* ow, const uint16_t* os,
+                  const uint16_t* ob, const uint16_t* residual, uint16_t* out) {
+  std::vector<uint16_t> conv(6144), beta(16), y(2048), gated(2048);
+  std::vector<float> g(16);
+  orc_gdn_conv_prepare(raw_qkv, a_raw, b_raw, history, conv_w, a_log, dt_bias, conv.data(),
+                       g.data(), beta.data());
+  orc_gdn_recur(conv.data(), g.data(), beta.data(), state, y.data());
+  orc_gdn_norm_gate(y.data(), z, norm_w, gated.data());
+  orc_qmv_q4(ow, os, ob, gated.data(), residual, 1024, 2048, out);
+}
+
+/* attention.metal:262-313 */
+void orc_attn_prepare(const uint16_t* q_raw, const uint16_t* k_raw, const uint16_t* v_raw,
+                      const uint16_t* q_gain, const uint16_t* k_gain, uint32_t pos,
+                      uint32_t capacity, uint16_t* query, uint16_t* kcache, uint16_t* vcache) {
+  float nrm[256];
+  for (int head = 0; head < 8; ++head) {
+    head_rms(q_raw + head * 512, q_gain, nrm);
+    for (int d = 0; d < 256; ++d) query[head * 256 + d] = f2bf(rope(nrm, d, pos));
+  }
+  for (int head = 0; head < 2; ++head) {
+    head_rms(k_raw + head * 256, k_gain, nrm);
+    const size_t ci = (size_t(head) * capacity + pos) * 256;
+    for (int d = 0; d < 256; ++d) {
+      vcache[ci + d] = v_raw[head * 256 + d];
+      kcache[ci + d] = f2bf(rope(nrm, d, pos));
+    }
+  }
+}
+
+void orc_attn_decode_f32(const uint16_t* query, const uint16_t* kcache, const uint16_t* vcache,
+                         uint32_t len, uint32_t capacity, float* o) {
+  attn_f32(query, kcache, vcache, len, capacity, o);
+}
+
+/* attention.metal:140-150 / attention_decode.metal:882-889 */
+void orc_attn_decode_gate(const uint16_t* query, const uint16_t* kcache, const uint16_t* vcache,
+                          uint32_t len, uint32_t capacity, const uint16_t* q_raw,
+                          uint16_t* gated) {
+  std::vector<float> o(2048);
+  attn_f32(query, kcache, vcache, len, capacity, o.data());
+  for (int head = 0; head < 8; ++head)
+    for (int d = 0; d < 256; ++d) {
+      float attention = bfr(o[head * 256 + d]);
+      float gate = gate_sigmoid_bf(bf2f(q_raw[head * 512 + 256 + d]));
+      gated[head * 256 + d] = f2bf(attention * gate);
+    }
+}
+
+uint32_t orc_greedy(const uint16_t* logits, int N, uint16_t* lse_out) {
+  uint16_t lse = lse_of(logits, N);
+  if (lse_out) *lse_out = lse;
+  return greedy_lse(logits, N, lse);
+}
+
+/* examples/greedy_audit.rs:6 and :28-40: xorshift64 (<<13, >>7, <<17) logits
+ * scaled/offset per case, bf16 by truncation, planted maxima every 7th case. */
+void orc_xorshift_logits(uint64_t* seed, int si, int N, uint16_t* out) {
+  static const float scales[8] = {0.0f, 0.001f, 0.1f, 1.0f, 8.0f, 100.0f, 1000.0f, 30000.0f};
+  static const float offsets[4] = {0.0f, -100.0f, 100.0f, -10000.0f};
+  const float scale = scales[si % 8], offset = offsets[(si / 8) % 4];
+  uint64_t x = *seed;
+  for (int i = 0; i < N; ++i) {
+    x ^= x << 13;
+    x ^= x >> 7;
+    x ^= x << 17;
+    float v = (float(x >> 40) / float(1u << 23) - 1.0f) * scale + offset;
+    uint32_t u;
+    std::memcpy(&u, &v, 4);
+    out[i] = uint16_t(u >> 16);
+  }
+  *seed = x;
+  if (si % 7 == 0) {
+    const int plant[9] = {0, 31, 32, 1023, 1024, 1025, 4095, 4096, N - 1};
+    float v = offset + scale * 1.01f;
+    uint32_t u;
+    std::memcpy(&u, &v, 4);
+    for (int i : plant)
+      if (i >= 0 && i < N) out[i] = uint16_t(u >> 16);
+  }
+}
+
+uint32_t orc_greedy_with_lse(const uint16_t* logits, int N, uint16_t lse) {
+  return greedy_lse(logits, N, lse);
+}
+
+/* head_lse.metal:275-278 stores bf16 logits; then the tail */
+uint32_t orc_head(const uint32_t* w, const uint16_t* s, const uint16_t* b, const uint16_t* x,
+                  int N, int K, uint16_t* logits, uint16_t* lse_out) {
+  orc_qmv_q4(w, s, b, x, nullptr, N, K, logits);
+  return orc_greedy(logits, N, lse_out);
+}
+
+}  // extern "C"
+
+/* ==================================================================== */
+/* full model: model.rs:37-92 (shapes/names), :228-350 (rows=1 route)    */
+/* ==================================================================== */
+struct OLin {
+  const uint32_t* w = nullptr;
+  const uint16_t* s = nullptr;
+  const uint16_t* b = nullptr;
+  int n = 0, k = 0;
+};
+struct OLayer {
+  bool attn = false;
+  const uint16_t *input_norm, *post_norm;
+  OLin gate, up, down;
+  /* gdn */
+  OLin qkv, z, a, bproj, out;
+  const uint16_t *conv, *norm, *dt;
+  const float* alog;
+  /* attention */
+  OLin q, k, v, o;
+  const uint16_t *qnorm, *knorm;
+};
+struct orc_model {
+  std::vector<char> blob;
+  OLin embed;
+  const uint16_t* norm;
+  OLayer layers[24];
+};
+struct orc_session {
+  orc_model* m;
+  uint32_t capacity, position = 0;
+  std::vector<std::vector<uint16_t>> kc, vc, hist;
+  std::vector<std::vector<float>> state;
+  std::vector<uint16_t> logits, final_h;
+  uint16_t lse = 0;
+};
+
+extern "C" {
+
+orc_model* orc_model_load(const char* dir, char* err, int err_len) {
+  auto fail = [&](const std::string& e) -> orc_model* {
+    if (err && err_len > 0) std::snprintf(err, size_t(err_len), "%s", e.c_str());
+    return nullptr;
+  };
+  std::string path = std::string(dir) + "/model.safetensors";
+  FILE* f = std::fopen(path.c_str(), "rb");
+  if (!f) return fail("cannot open " + path);
+  std::fseek(f, 0, SEEK_END);
+  long size = std::ftell(f);
+  std::fseek(f, 0, SEEK_SET);
+  auto m = std::make_unique<orc_model>();
+  m->blob.resize(size_t(size));
+  if (std::fread(m->blob.data(), 1, size_t(size), f) != size_t(size)) {
+    std::fclose(f);
+    return fail("short read");
+  }
+  std::fclose(f);
+  uint64_t hn;
+  std::memcpy(&hn, m->blob.data(), 8);
+  std::map<std::string, Tensor> ts;
+  std::string perr;
+  if (!parse_header(std::string(m->blob.data() + 8, hn), ts, perr)) return fail(perr);
+  const char* base = m->blob.data() + 8 + hn;
+  const std::string pre = "language_model.model.";
+  auto get = [&](const std::string& name, const char* dtype) -> const void* {
+    auto it = ts.find(pre + name);
+    if (it == ts.end() || it->second.dtype != dtype) return nullptr;
+    return base + it->second.offset;
+  };
+  bool ok = true;
+  auto lin = [&](const std::string& name, int n, int k) {
+    OLin l;
+    l.w = (const uint32_t*)get(name + ".weight", "U32");
+    l.s = (const uint16_t*)get(name + ".scales", "BF16");
+    l.b = (const uint16_t*)get(name + ".biases", "BF16");
+    l.n = n;
+    l.k = k;
+    if (!l.w || !l.s || !l.b) ok = false;
+    return l;
+  };
+  auto bf = [&](const std::string& name) {
+    auto p = (const uint16_t*)get(name, "BF16");
+    if (!p) ok = false;
+    return p;
+  };
+  m->embed = lin("embed_tokens", 248320, 1024);
+  m->norm = bf("norm.weight");
+  for (int l = 0; l < 24; ++l) {
+    OLayer& L = m->layers[l];
+    std::string p = "layers." + std::to_string(l);
+    L.input_norm = bf(p + ".input_layernorm.weight");
+    L.post_norm = bf(p + ".post_attention_layernorm.weight");
+    L.gate = lin(p + ".mlp.gate_proj", 3584, 1024);
+    L.up = lin(p + ".mlp.up_proj", 3584, 1024);
+    L.down = lin(p + ".mlp.down_proj", 1024, 3584);
+    L.attn = (l % 4) == 3;
+    if (L.attn) {
+      std::string a = p + ".self_attn";
+      L.q = lin(a + ".q_proj", 4096, 1024);
+      L.k = lin(a + ".k_proj", 512, 1024);
+      L.v = lin(a + ".v_proj", 512, 1024);
+      L.o = lin(a + ".o_proj", 1024, 2048);
+      L.qnorm = bf(a + ".q_norm.weight");
+      L.knorm = bf(a + ".k_norm.weight");
+    } else {
+      std::string a = p + ".linear_attn";
+      L.qkv = lin(a + ".in_proj_qkv", 6144, 1024);
+      L.z = lin(a + ".in_proj_z", 2048, 1024);
+      L.a = lin(a + ".in_proj_a", 16, 1024);
+      L.bproj = lin(a + ".in_proj_b", 16, 1024);
+      L.out = lin(a + ".out_proj", 1024, 2048);
+      L.conv = bf(a + ".conv1d.weight");
+      L.norm = bf(a + ".norm.weight");
+      L.dt = bf(a + ".dt_bias");
+      L.alog = (const float*)get(a + ".A_log", "F32");
+      if (!L.alog) ok = false;
+    }
+  }
+  if (!ok) return fail("missing or mistyped tensor");
+  return m.release();
+}
+
+void orc_model_free(orc_model* m) { delete m; }
+
+orc_session* orc_session_new(orc_model* m, uint32_t capacity) {
+  auto s = new orc_session();
+  s->m = m;
+  s->capacity = capacity;
+  for (int a = 0; a < 6; ++a) {
+    s->kc.emplace_back(size_t(2) * capacity * 256, 0);
+    s->vc.emplace_back(size_t(2) * capacity * 256, 0);
+  }
+  for (int g = 0; g < 18; ++g) {
+    s->hist.emplace_back(3 * 6144, 0);
+    s->state.emplace_back(16 * 128 * 128, 0.0f);
+  }
+  s->logits.assign(248320, 0);
+  s->final_h.assign(1024, 0);
+  return s;
+}
+void orc_session_free(orc_session* s) { delete s; }
+void orc_session_reset(orc_session* s) {
+  s->position = 0;
+  for (auto& h : s->hist) std::fill(h.begin(), h.end(), 0);
+  for (auto& st : s->state) std::fill(st.begin(), st.end(), 0.0f);
+}
+uint32_t orc_session_position(const orc_session* s) { return s->position; }
+void orc_session_logits(const orc_session* s, uint16_t* out) {
+  std::memcpy(out, s->logits.data(), s->logits.size() * 2);
+}
+uint16_t orc_session_lse(const orc_session* s) { return s->lse; }
+void orc_session_final_hidden(const orc_session* s, uint16_t* out) {
+  std::memcpy(out, s->final_h.data(), 2048);
+}
+
+void orc_session_import(orc_session* s, uint32_t pos, uint32_t cap_src,
+                        const uint16_t* const* kcaches, const uint16_t* const* vcaches,
+                        const float* const* states, const uint16_t* const* histories) {
+  s->position = pos;
+  for (int a = 0; a < 6; ++a)
+    for (int h = 0; h < 2; ++h) {
+      std::memcpy(&s->kc[a][size_t(h) * s->capacity * 256], kcaches[a] + size_t(h) * cap_src * 256,
+                  size_t(pos) * 512);
+      std::memcpy(&s->vc[a][size_t(h) * s->capacity * 256], vcaches[a] + size_t(h) * cap_src * 256,
+                  size_t(pos) * 512);
+    }
+  for (int g = 0; g < 18; ++g) {
+    std::memcpy(s->state[g].data(), states[g], s->state[g].size() * 4);
+    std::memcpy(s->hist[g].data(), histories[g], s->hist[g].size() * 2);
+  }
+}
+
+/* model.rs:228-307 with rows=1 */
+uint32_t orc_session_step(orc_session* S, uint32_t token, int want_head) {
+  orc_model* M = S->m;
+  std::vector<uint16_t> h(1024), u(1024), raw(6144), z(2048), a(16), b(16), conv(6144),
+      beta(16), y(2048), gated(2048), q(4096), k(512), v(512), query(2048), gate(3584),
+      up(3584), act(3584);
+  std::vector<float> g(16);
+  orc_embedding_q4(M->embed.w, M->embed.s, M->embed.b, token, 1024, h.data());
+  int gi = 0, ai = 0;
+  for (int l = 0; l < 24; ++l) {
+    const OLayer& L = M->layers[l];
+    orc_rms_norm(h.data(), L.input_norm, 1024, 1e-6f, u.data());
+    if (!L.attn) {
+      orc_qmv_q4(L.qkv.w, L.qkv.s, L.qkv.b, u.data(), nullptr, 6144, 1024, raw.data());
+      orc_qmv_q4(L.z.w, L.z.s, L.z.b, u.data(), nullptr, 2048, 1024, z.data());
+      orc_qmv_q4(L.a.w, L.a.s, L.a.b, u.data(), nullptr, 16, 1024, a.data());
+      orc_qmv_q4(L.bproj.w, L.bproj.s, L.bproj.b, u.data(), nullptr, 16, 1024, b.data());
+      orc_gdn_conv_prepare(raw.data(), a.data(), b.data(), S->hist[gi].data(), L.conv, L.alog,
+                           L.dt, conv.data(), g.data(), beta.data());
+      orc_gdn_recur(conv.data(), g.data(), beta.data(), S->state[gi].data(), y.data());
+      orc_gdn_norm_gate(y.data(), z.data(), L.norm, gated.data());
+      orc_qmv_q4(L.out.w, L.out.s, L.out.b, gated.data(), h.data(), 1024, 2048, h.data());
+      ++gi;
+    } else {
+      orc_qmv_q4(L.q.w, L.q.s, L.q.b, u.data(), nullptr, 4096, 1024, q.data());
+      orc_qmv_q4(L.k.w, L.k.s, L.k.b, u.data(), nullptr, 512, 1024, k.data());
+      orc_qmv_q4(L.v.w, L.v.s, L.v.b, u.data(), nullptr, 512, 1024, v.data());
+      orc_attn_prepare(q.data(), k.data(), v.data(), L.qnorm, L.knorm, S->position, S->capacity,
+                       query.data(), S->kc[ai].data(), S->vc[ai].data());
+      orc_attn_decode_gate(query.data(), S->kc[ai].data(), S->vc[ai].data(), S->position + 1,
+                           S->capacity, q.data(), gated.data());
+      orc_qmv_q4(L.o.w, L.o.s, L.o.b, gated.data(), h.data(), 1024, 2048, h.data());
+      ++ai;
+    }
+    orc_rms_norm(h.data(), L.post_norm, 1024, 1e-6f, u.data());
+    orc_qmv_q4(L.gate.w, L.gate.s, L.gate.b, u.data(), nullptr, 3584, 1024, gate.data());
+    orc_qmv_q4(L.up.w, L.up.s, L.up.b, u.data(), nullptr, 3584, 1024, up.data());
+    orc_swiglu(gate.data(), up.data(), 3584, act.data());
+    orc_qmv_q4(L.down.w, L.down.s, L.down.b, act.data(), h.data(), 1024, 3584, h.data());
+  }
+  S->position += 1;
+  if (!want_head) return 0xffffffffu;
+  orc_rms_norm(h.data(), M->norm, 1024, 1e-6f, S->final_h.data());
+  return orc_head(M->embed.w, M->embed.s, M->embed.b, S->final_h.data(), 248320, 1024,
+                  S->logits.data(), &S->lse);
+}
+
+}  // extern "C"
