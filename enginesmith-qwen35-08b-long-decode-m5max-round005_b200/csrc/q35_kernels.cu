@@ -421,6 +421,28 @@ __device__ __forceinline__ float reduce16(float* v, int lane) {
   return __fadd_rn(v[0], __shfl_xor_sync(0xffffffffu, v[0], 1));
 }
 
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Launch timing: the earliest post-dependency start over CTAs to the moment
+// the last CTA finishes, accumulated in the control block when enabled.
+__device__ __forceinline__ void attn_time_start(Ctl* ctl) {
+  if (ctl->timing_on) atomicMin(&ctl->attn_t0, globaltimer_ns());
+}
+__device__ __forceinline__ void attn_time_end(Ctl* ctl) {
+  if (!ctl->timing_on) return;
+  __threadfence();
+  if (atomicAdd(&ctl->attn_done, 1u) == gridDim.x * gridDim.y - 1) {
+    const unsigned long long t0 = atomicExch(&ctl->attn_t0, ~0ull);
+    atomicAdd(&ctl->attn_ns, globaltimer_ns() - t0);
+    atomicAdd(&ctl->attn_launches, 1u);
+    atomicExch(&ctl->attn_done, 0u);
+  }
+}
+
 __global__ void __launch_bounds__(kAttnThreads) k_attn(const __grid_constant__ AttnArgs a) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   AttnSmem& S = *reinterpret_cast<AttnSmem*>(smem_raw);
@@ -461,6 +483,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const __grid_constant__ A
     for (int t = 0; t < kAttnStages && t < ntiles; ++t) issue(t, t);
   pdl_wait();
   pdl_launch();
+  if (tid == 0) attn_time_start(a.ctl);
 
   // Query heads 4kh..4kh+3 (warps 0-3) scaled by 1/16 (attention_decode.metal:289);
   // warp 4 prepares the current token's key (attention.metal:295-311).
@@ -577,7 +600,10 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const __grid_constant__ A
   __syncthreads();
   if (tid == 0) S.last = (atomicAdd(&a.ctl->attn_counter[kh], 1u) == kAttnChains - 1);
   __syncthreads();
-  if (!S.last) return;
+  if (!S.last) {
+    if (tid == 0) attn_time_end(a.ctl);
+    return;
+  }
   __threadfence();
 
   // combine the chains of the four heads; task = (head, stripe of 8 dims)
@@ -635,7 +661,11 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const __grid_constant__ A
       a.gated[qh * kHeadDim + d] = f2bf(__fmul_rn(attention, gate));
     }
   }
-  if (tid == 0) atomicExch(&a.ctl->attn_counter[kh], 0u);
+  __syncthreads();
+  if (tid == 0) {
+    atomicExch(&a.ctl->attn_counter[kh], 0u);
+    attn_time_end(a.ctl);
+  }
 }
 
 // Sets the control block of a standalone attention call: the position and
@@ -649,6 +679,7 @@ __global__ void k_ctl_position(Ctl* ctl, uint32_t pos) {
     ctl->attn_counter[1] = 0;
     ctl->head_counter = 0;
     ctl->out_count = 0;
+    ctl->timing_on = 0;
   }
   if (threadIdx.x < 32) rope_pair(pos, threadIdx.x, ctl->rope_cs);
 }

@@ -685,6 +685,7 @@ int q35_open(const char* model_dir, int device, const q35_opts* opts, q35_sessio
   }
   Ctl c = {};
   c.capacity = s->capacity;
+  c.attn_t0 = ~0ull;
   e = cudaMemcpy(s->ctl, &c, sizeof(Ctl), cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = capture(s, 1, true, &s->gdec1);
   if (e == cudaSuccess && s->dbatch > 1) e = capture(s, s->dbatch, true, &s->gdecN);
@@ -731,6 +732,7 @@ int q35_generate(q35_session* s, const uint32_t* prompt, size_t n_prompt, size_t
       e = cudaMemcpyAsync(s->seq, prompt, n_prompt * 4, cudaMemcpyHostToDevice, s->stream);
     Ctl c = {};
     c.capacity = s->capacity;
+    c.attn_t0 = ~0ull;
     if (e == cudaSuccess) e = cudaMemcpyAsync(s->ctl, &c, sizeof(Ctl), cudaMemcpyHostToDevice, s->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
     if (e != cudaSuccess) return device_failure(s, e, "reset");
@@ -810,6 +812,27 @@ int q35_decode_timed(q35_session* s, size_t steps, float* ms) {
   if (e != cudaSuccess) return device_failure(s, e, "token read");
   s->position += uint32_t(steps);
   s->pending = last;
+  return Q35_OK;
+}
+
+int q35_attn_timing(q35_session* s, int reset, double* total_us, uint32_t* launches) {
+  if (!s) return Q35_EINVAL;
+  cudaSetDevice(s->device);
+  cudaError_t e = cudaStreamSynchronize(s->stream);
+  Ctl c;
+  if (e == cudaSuccess) e = cudaMemcpy(&c, s->ctl, sizeof(Ctl), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return set_err(s, Q35_ECUDA, std::string("timing: ") + cudaGetErrorString(e));
+  if (total_us) *total_us = double(c.attn_ns) * 1e-3;
+  if (launches) *launches = c.attn_launches;
+  if (reset >= 0) {
+    c.timing_on = reset > 0 ? 1u : 0u;
+    c.attn_done = 0;
+    c.attn_launches = 0;
+    c.attn_t0 = ~0ull;
+    c.attn_ns = 0;
+    e = cudaMemcpy(s->ctl, &c, sizeof(Ctl), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return set_err(s, Q35_ECUDA, std::string("timing: ") + cudaGetErrorString(e));
+  }
   return Q35_OK;
 }
 

@@ -46,7 +46,13 @@ struct Ctl {
   uint32_t capacity;
   float rope_cs[64];   // cos/sin of the running step's position, pairs i<32
   uint32_t token_step; // token consumed by the running step
-  uint32_t pad[7];
+  // in-kernel timing of the attention launches (device clock, ns)
+  uint32_t timing_on;
+  uint32_t attn_done;            // CTAs finished in the running launch
+  uint32_t attn_launches;        // launches accounted
+  unsigned long long attn_t0;    // earliest post-dependency start of the running launch
+  unsigned long long attn_ns;    // summed launch durations
+  uint32_t pad[4];
 };
 
 // Error site codes written to Ctl::err.

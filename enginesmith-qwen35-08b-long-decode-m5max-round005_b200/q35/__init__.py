@@ -52,6 +52,7 @@ def _load() -> ctypes.CDLL:
         "q35_dump_state": (c_int, [P, P, P, P]),
         "q35_last_logits": (c_int, [P, P, P]),
         "q35_decode_timed": (c_int, [P, c_size_t, POINTER(c_float)]),
+        "q35_attn_timing": (c_int, [P, c_int, POINTER(ctypes.c_double), POINTER(c_uint32)]),
         "q35_op_qmv_q4": (c_int, [P, P, P, P, P, P, c_int, c_int, P]),
         "q35_op_embedding_q4": (c_int, [P, P, P, c_uint32, c_int, P, P]),
         "q35_op_rms_norm": (c_int, [P, P, P, P]),
@@ -133,6 +134,14 @@ class Model:
         ms = c_float()
         self._check(lib().q35_decode_timed(self._h, steps, ctypes.byref(ms)))
         return float(ms.value)
+
+    def attn_timing(self, reset: int = -1):
+        """(total_us, launches) of the attention launches since the last reset;
+        reset=1 clears and enables the device timer, 0 clears and disables."""
+        us = ctypes.c_double()
+        n = c_uint32()
+        self._check(lib().q35_attn_timing(self._h, reset, ctypes.byref(us), ctypes.byref(n)))
+        return float(us.value), int(n.value)
 
     def dump_state(self):
         """Return (kv [6,2,2,pos,256] u16, state [18,16,128,128] f32, hist [18,3,6144] u16)."""

@@ -96,6 +96,14 @@ int q35_last_logits(q35_session* s, uint16_t* logits, uint16_t* lse);
  * tokens on the device; returns the device time in milliseconds. */
 int q35_decode_timed(q35_session* s, size_t steps, float* ms);
 
+/* Device-clock timing of the attention launches (benchmark aid, no
+ * counterpart in the reference): reads the summed launch time in
+ * microseconds and the launch count since the last reset; reset > 0 clears
+ * and enables the timer, reset == 0 clears and disables it, reset < 0 only
+ * reads. A launch lasts from its earliest post-dependency start to the end of
+ * its last CTA. */
+int q35_attn_timing(q35_session* s, int reset, double* total_us, uint32_t* launches);
+
 /* ---------------------------------------------------------------------- */
 /* Op API (device pointers, caller-owned, nothing allocated)               */
 /* ---------------------------------------------------------------------- */

@@ -43,6 +43,7 @@ def lib() -> ctypes.CDLL:
             "orc_bf2f": (c_float, [c_uint16]),
             "orc_sigmoid_bf": (c_float, [c_float]),
             "orc_softplus_bf": (c_float, [c_float]),
+            "orc_fexp": (c_float, [c_float]),
             "orc_embedding_q4": (None, [P, P, P, c_uint32, c_int, P]),
             "orc_qmv_q4": (None, [P, P, P, P, P, c_int, c_int, P]),
             "orc_qmv_q4_f32": (None, [P, P, P, P, c_int, c_int, P]),
