@@ -296,7 +296,7 @@ def main():
                        "global_batch": world, "seq_len": args.context, "parallelism": f"sessions x{world}",
                        "l2": "inputs larger than L2 (each step streams ~%.2f GB)" % (step_bytes / 1e9),
                        "prefill_s": round(prefill_s, 2)},
-            "gpu_launches": args.steps * (18 * 3 + 6 * 3 + 24 * 2 + 1),
+            "gpu_launches": args.steps * (18 * 3 + 6 * 4 + 24 * 2 + 1),
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 4},
             "roofline": {"bound": "hbm", "kernel": "k_attn (split GQA decode attention)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s",

@@ -87,16 +87,21 @@ __device__ __forceinline__ void gdn_conv_channel(int c, uint16_t raw, uint16_t* 
 // attention.metal:55-70 / the RoPE table: cos/sin of position * inv_freq for
 // the 32 rotary pairs, evaluated in double from the f32 angle.
 __device__ __forceinline__ void rope_pair(uint32_t position, int pair, float* cs) {
-  const float arg = __fmul_rn(-__fdiv_rn(float(pair), 32.0f), 23.253496170043945f);
+  const float arg = __fmul_rn(-__fmul_rn(float(pair), 0.03125f), 23.253496170043945f);
   const float inv_freq = (float)exp2((double)arg);
   const float angle = __fmul_rn(float(position), inv_freq);
   cs[2 * pair] = (float)cos((double)angle);
   cs[2 * pair + 1] = (float)sin((double)angle);
 }
 
-__global__ void __launch_bounds__(256) k_qmv(const __grid_constant__ QmvArgs a) {
+// 256 threads and <= 64 registers: up to four CTAs (of consecutive launches)
+// share an SM, so a launch's weight prefetch overlaps its predecessor.
+constexpr int kQmvThreads = 256;
+
+__global__ void __launch_bounds__(kQmvThreads, 4) k_qmv(const __grid_constant__ QmvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int kWarps = kQmvThreads / 32;
   const int K = a.K, KW = K / 8, KG = K / 64, nch = K / 512;
   Piece pc[4];
   const int np = qmv_pieces(a, blockIdx.x, pc);
@@ -109,13 +114,13 @@ __global__ void __launch_bounds__(256) k_qmv(const __grid_constant__ QmvArgs a) 
   uint16_t* bia = reinterpret_cast<uint16_t*>(smem + L.bia);
   float4* xq = reinterpret_cast<float4*>(smem + L.xq);
   float* xsum = reinterpret_cast<float*>(smem + L.xsum);
-  float* xf = reinterpret_cast<float*>(smem + L.xf);
   float* pl = reinterpret_cast<float*>(smem + L.pl);
   float* vals = reinterpret_cast<float*>(smem + L.vals);
   float* red = reinterpret_cast<float*>(smem + L.red);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.bar);
 
-  // 1. weights: bulk copies issued before the dependency wait.
+  // 1. Before the dependency wait: weights by bulk copy, and everything else
+  //    written two or more launches back (gains, the residual, conv history).
   if (tid == 0) {
     mbar_init(bar, 1);
     fence_mbar_init();
@@ -127,22 +132,70 @@ __global__ void __launch_bounds__(256) k_qmv(const __grid_constant__ QmvArgs a) 
     mbar_expect_tx(bar, bytes);
     int srow = 0;
     for (int i = 0; i < np; ++i) {
-      const QmvSeg& s = a.seg[pc[i].seg];
+      const QmvSeg& sg = a.seg[pc[i].seg];
       const int n = pc[i].count;
-      bulk_g2s(codes + size_t(srow) * KW, s.w + size_t(pc[i].row0) * KW, uint32_t(n) * KW * 4, bar);
-      bulk_g2s(scl + size_t(srow) * KG, s.s + size_t(pc[i].row0) * KG, uint32_t(n) * KG * 2, bar);
-      bulk_g2s(bia + size_t(srow) * KG, s.b + size_t(pc[i].row0) * KG, uint32_t(n) * KG * 2, bar);
+      bulk_g2s(codes + size_t(srow) * KW, sg.w + size_t(pc[i].row0) * KW, uint32_t(n) * KW * 4, bar);
+      bulk_g2s(scl + size_t(srow) * KG, sg.s + size_t(pc[i].row0) * KG, uint32_t(n) * KG * 2, bar);
+      bulk_g2s(bia + size_t(srow) * KG, sg.b + size_t(pc[i].row0) * KG, uint32_t(n) * KG * 2, bar);
       srow += n;
     }
   }
+  // epilogue operands of the rows this thread finishes (thread i -> CTA row i)
+  int e_seg = -1, e_row = 0;
+  {
+    int acc = 0;
+    for (int p = 0; p < np; ++p) {
+      if (tid >= acc && tid < acc + pc[p].count) {
+        e_seg = pc[p].seg;
+        e_row = pc[p].row0 + (tid - acc);
+      }
+      acc += pc[p].count;
+    }
+    if (a.epi == kEpiSwiglu && tid >= pc[0].count) e_seg = -1;
+  }
+  uint16_t pre_res = 0, pre_h[3] = {0, 0, 0};
+  float pre_w[4] = {0.f, 0.f, 0.f, 0.f};
+  if (e_seg >= 0) {
+    if (a.epi == kEpiResAdd) pre_res = a.res[e_row];
+    if (a.epi == kEpiGdnConv && e_seg == 0) {
+      pre_h[0] = a.hist[e_row];
+      pre_h[1] = a.hist[kGdnConv + e_row];
+      pre_h[2] = a.hist[2 * kGdnConv + e_row];
+      const uint2 w4 = *reinterpret_cast<const uint2*>(a.convw + 4 * e_row);
+      pre_w[0] = bf_lo(w4.x);
+      pre_w[1] = bf_hi(w4.x);
+      pre_w[2] = bf_lo(w4.y);
+      pre_w[3] = bf_hi(w4.y);
+    }
+  }
+  float gain4[4] = {0.f, 0.f, 0.f, 0.f};
+  if ((a.pro == kProRms || a.pro == kProEmbedRms) && tid < 256) {
+    const uint2 g = *reinterpret_cast<const uint2*>(a.gain + 4 * tid);
+    gain4[0] = bf_lo(g.x);
+    gain4[1] = bf_hi(g.x);
+    gain4[2] = bf_lo(g.y);
+    gain4[3] = bf_hi(g.y);
+  }
 
-  // 2. activations.
+  // 2. Activations: every prologue leaves thread t with the group of four
+  //    activations k = 4t .. 4t+3 and emits its matvec constants.
   pdl_wait();
   pdl_launch();
   if (a.pro == kProPlain) {
-    for (int k = tid; k < K; k += blockDim.x) xf[k] = bf2f(a.x[k]);
+    const int ngroups = K / 4;
+    uint2 raw[4];
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      const int t = it * kQmvThreads + tid;
+      raw[it] = t < ngroups ? *reinterpret_cast<const uint2*>(a.x + 4 * t) : make_uint2(0u, 0u);
+    }
+#pragma unroll
+    for (int it = 0; it < 4; ++it) {
+      const int t = it * kQmvThreads + tid;
+      if (it * kQmvThreads < ngroups) emit_xq(t, t < ngroups, bf4(raw[it]), xq, xsum);
+    }
   } else if (a.pro == kProRms || a.pro == kProEmbedRms) {
-    float v[4];
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
     if (a.pro == kProEmbedRms) {
       // linear.metal:19-23 for the token the step consumes.
       const uint32_t pos = ld_cg_u32(&a.ctl->pos);
@@ -151,87 +204,99 @@ __global__ void __launch_bounds__(256) k_qmv(const __grid_constant__ QmvArgs a) 
         if (tid == 0) atomicCAS(&a.ctl->err, 0u, kErrToken);
         token = 0;
       }
-      const uint32_t word = a.ew[size_t(token) * (kHidden / 8) + tid / 2];
-      const int g = int(token) * (kHidden / 64) + (4 * tid) / 64;
-      const float sc = bf2f(a.es[g]), bs = bf2f(a.eb[g]);
+      if (tid < 256) {
+        const uint32_t word = a.ew[size_t(token) * (kHidden / 8) + tid / 2];
+        const int g = int(token) * (kHidden / 64) + (4 * tid) / 64;
+        const float sc = bf2f(a.es[g]), bs = bf2f(a.eb[g]);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int k = 4 * tid + j;
-        const uint32_t q = (word >> (4 * (k % 8))) & 15u;
-        v[j] = bfr(__fadd_rn(__fmul_rn(sc, float(q)), bs));
+        for (int j = 0; j < 4; ++j) {
+          const int k = 4 * tid + j;
+          const uint32_t q = (word >> (4 * (k % 8))) & 15u;
+          v[j] = bfr(__fadd_rn(__fmul_rn(sc, float(q)), bs));
+        }
+        if (blockIdx.x == 0) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) a.h_out[4 * tid + j] = f2bf(v[j]);
+        }
       }
       if (blockIdx.x == 0) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) a.h_out[4 * tid + j] = f2bf(v[j]);
         if (tid == 0) {
           a.ctl->pos_step = pos;
           a.ctl->token_step = token;
         }
         if (tid < 32) rope_pair(pos, tid, a.ctl->rope_cs);
       }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) v[j] = bf2f(a.x[4 * tid + j]);
+    } else if (tid < 256) {
+      const float4 x4 = bf4(*reinterpret_cast<const uint2*>(a.x + 4 * tid));
+      v[0] = x4.x;
+      v[1] = x4.y;
+      v[2] = x4.z;
+      v[3] = x4.w;
     }
-    rms1024(v, a.gain, xf, red);
-  } else {  // kProNormGate: gdn.metal:238-254 for all 16 heads
-    for (int hh = warp; hh < kGdnHeads; hh += 8) {
-      float v[4], ss = 0.0f;
+    float o[4];
+    rms1024_reg(v, gain4, o, red);
+    emit_xq(tid, tid < 256, make_float4(o[0], o[1], o[2], o[3]), xq, xsum);
+  } else {  // kProNormGate: gdn.metal:238-254, warp w -> heads w, w + 8
+    for (int hh = warp; hh < kGdnHeads; hh += kWarps) {
+    const float4 v4 = bf4(*reinterpret_cast<const uint2*>(a.gy + hh * 128 + 4 * lane));
+    const float4 z4 = bf4(*reinterpret_cast<const uint2*>(a.gz + hh * 128 + 4 * lane));
+    const float4 w4 = bf4(*reinterpret_cast<const uint2*>(a.gw + 4 * lane));
+    const float v[4] = {v4.x, v4.y, v4.z, v4.w}, z[4] = {z4.x, z4.y, z4.z, z4.w};
+    const float w[4] = {w4.x, w4.y, w4.z, w4.w};
+    float ss = 0.0f;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        v[i] = bf2f(a.gy[hh * 128 + 4 * lane + i]);
-        ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
-      }
-      ss = warp_sum(ss);
-      const float inv = drsqrtf(__fadd_rn(__fdiv_rn(ss, 128.0f), 1e-6f));
+    for (int i = 0; i < 4; ++i) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+    ss = warp_sum(ss);
+    const float inv = drsqrtf(__fadd_rn(__fmul_rn(ss, 0.0078125f), 1e-6f));
+    float o[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int d = 4 * lane + i;
-        const float norm = bfr(__fmul_rn(bfr(__fmul_rn(v[i], inv)), bf2f(a.gw[d])));
-        const float gate = bf2f(a.gz[hh * 128 + d]);
-        const float sy = __fdiv_rn(1.0f, __fadd_rn(1.0f, dexpf(fabsf(gate))));
-        const float sig = gate < 0.0f ? sy : __fsub_rn(1.0f, sy);
-        xf[hh * 128 + d] = bfr(__fmul_rn(__fmul_rn(gate, sig), norm));
-      }
+    for (int i = 0; i < 4; ++i) {
+      const float norm = bfr(__fmul_rn(bfr(__fmul_rn(v[i], inv)), w[i]));
+      const float sy = __fdiv_rn(1.0f, __fadd_rn(1.0f, dexpf(fabsf(z[i]))));
+      const float sig = z[i] < 0.0f ? sy : __fsub_rn(1.0f, sy);
+      o[i] = bfr(__fmul_rn(__fmul_rn(z[i], sig), norm));
+    }
+    emit_xq(hh * 32 + lane, true, make_float4(o[0], o[1], o[2], o[3]), xq, xsum);
     }
   }
-  __syncthreads();
-  build_xq(xf, K, xq, xsum);
   __syncthreads();
 
   // 3. dot products from shared memory.
   mbar_wait(bar, 0, a.ctl, kErrQmvWait);
   const int ngroups = (nrows + 3) / 4;
-  for (int task = warp; task < ngroups * nch; task += 8) {
+  for (int task = warp; task < ngroups * nch; task += kWarps) {
     const int g = task / nch, c = task % nch;
     qmv_chunk_task(codes, scl, bia, nrows, 4 * g, c, K, xq, xsum, pl, lane);
   }
   __syncthreads();
-  for (int g = warp; g < ngroups; g += 8) qmv_finish_task(pl, nrows, 4 * g, nch, vals, lane);
+  for (int g = warp; g < ngroups; g += kWarps) qmv_finish_task(pl, nrows, 4 * g, nch, vals, lane);
   __syncthreads();
 
-  // 4. epilogue.
+  // 4. epilogue (thread i finishes CTA row i).
+  if (e_seg < 0) return;
   if (a.epi == kEpiSwiglu) {
     const int n = pc[0].count;
-    for (int i = tid; i < n; i += blockDim.x)
-      a.seg[0].y[pc[0].row0 + i] = swiglu_bf(bfr(vals[i]), bfr(vals[n + i]));
+    a.seg[0].y[pc[0].row0 + tid] = swiglu_bf(bfr(vals[tid]), bfr(vals[n + tid]));
     return;
   }
-  int srow = 0;
-  for (int p = 0; p < np; ++p) {
-    const QmvSeg& s = a.seg[pc[p].seg];
-    for (int i = tid; i < pc[p].count; i += blockDim.x) {
-      const float v = vals[srow + i];
-      const int row = pc[p].row0 + i;
-      if (a.epi == kEpiResAdd) {
-        a.res[row] = f2bf(__fadd_rn(bf2f(a.res[row]), bfr(v)));
-      } else if (a.epi == kEpiGdnConv && pc[p].seg == 0) {
-        gdn_conv_channel(row, f2bf(v), a.hist, a.convw, a.conv_out);
-      } else {
-        s.y[row] = f2bf(v);
-      }
-    }
-    srow += pc[p].count;
+  const float v = vals[tid];
+  if (a.epi == kEpiResAdd) {
+    a.res[e_row] = f2bf(__fadd_rn(bf2f(pre_res), bfr(v)));
+  } else if (a.epi == kEpiGdnConv && e_seg == 0) {
+    // gdn_input.metal:419-431
+    const uint16_t raw = f2bf(v);
+    float acc = 0.0f;
+    acc = fmaf(bf2f(pre_h[0]), pre_w[0], acc);
+    acc = fmaf(bf2f(pre_h[1]), pre_w[1], acc);
+    acc = fmaf(bf2f(pre_h[2]), pre_w[2], acc);
+    acc = fmaf(bf2f(raw), pre_w[3], acc);
+    const float xq1 = bfr(acc);
+    a.conv_out[e_row] = f2bf(__fmul_rn(xq1, sigmoid_bf(xq1)));
+    a.hist[e_row] = pre_h[1];
+    a.hist[kGdnConv + e_row] = pre_h[2];
+    a.hist[2 * kGdnConv + e_row] = raw;
+  } else {
+    a.seg[e_seg].y[e_row] = f2bf(v);
   }
 }
 
@@ -265,19 +330,19 @@ __global__ void __launch_bounds__(64) k_gdn_recur(const __grid_constant__ RecurA
       ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
     }
     ss = warp_sum(ss);
-    const float inv = drsqrtf(__fadd_rn(__fdiv_rn(ss, 128.0f), 1.0e-6f / 128.0f));
+    const float inv = drsqrtf(__fadd_rn(__fmul_rn(ss, 0.0078125f), 1.0e-6f / 128.0f));
     const float scale = warp == 0 ? 0.0078125f : bfr(0.08838834764831845f);
     float* dst = warp == 0 ? qn : kn;
 #pragma unroll
     for (int i = 0; i < 4; ++i) dst[4 * lane + i] = bfr(__fmul_rn(bfr(__fmul_rn(v[i], inv)), scale));
   }
+  // gdn_input.metal:454-459 (g on warp 0, beta on warp 1, in parallel)
   if (tid == 0) {
-    // gdn_input.metal:454-459
-    const float av = bf2f(a.a_raw[h]), bv = bf2f(a.b_raw[h]);
-    const float ax = bfr(__fadd_rn(av, bf2f(a.dt_bias[h])));
+    const float ax = bfr(__fadd_rn(bf2f(a.a_raw[h]), bf2f(a.dt_bias[h])));
     const float e1 = dexpf(a.a_log[h]);
     gb[0] = dexpf(__fmul_rn(-e1, softplus_bf(ax)));
-    gb[1] = bfr(sigmoid_bf(bv));
+  } else if (tid == 32) {
+    gb[1] = bfr(sigmoid_bf(bf2f(a.b_raw[h])));
   }
   __syncthreads();
   mbar_wait(&bar, 0, a.ctl, kErrRecurWait);
@@ -368,8 +433,8 @@ struct AttnSmem {
   float kr[kHeadDim];
   uint16_t kf[kHeadDim], vf[kHeadDim];
   float sc[4][kAttnTile];
+  float2 fe[kAttnThreads / 32][kAttnTile];
   uint64_t bar[kAttnStages];
-  int last;
 };
 
 size_t attn_smem_bytes() { return sizeof(AttnSmem); }
@@ -387,7 +452,7 @@ __device__ __forceinline__ void head_norm_rope(const uint16_t* x, const uint16_t
     pb = __fadd_rn(pb, __fmul_rn(vb, vb));
   }
   const float s0 = warp_sum(pa), s1 = warp_sum(pb);
-  const float inv = drsqrtf(__fadd_rn(__fdiv_rn(__fadd_rn(s0, s1), 256.0f), 1e-6f));
+  const float inv = drsqrtf(__fadd_rn(__fmul_rn(__fadd_rn(s0, s1), 0.00390625f), 1e-6f));
   for (int d = lane; d < kHeadDim; d += 32)
     nrm[d] = bfr(__fmul_rn(bfr(__fmul_rn(bf2f(x[d]), inv)), bf2f(gain[d])));
   __syncwarp();
@@ -443,7 +508,7 @@ __device__ __forceinline__ void attn_time_end(Ctl* ctl) {
   }
 }
 
-__global__ void __launch_bounds__(kAttnThreads) k_attn(const __grid_constant__ AttnArgs a) {
+__global__ void __launch_bounds__(kAttnThreads, 2) k_attn(const __grid_constant__ AttnArgs a) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   AttnSmem& S = *reinterpret_cast<AttnSmem*>(smem_raw);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -458,20 +523,33 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const __grid_constant__ A
   const int stride = split ? 64 : 32;
   const int nkeys = (chain < stride && uint32_t(chain) < len) ? int((len - 1 - chain) / stride) + 1 : 0;
   const int ntiles = (nkeys + kAttnTile - 1) / kAttnTile;
+  // Chain-major cache: position p at chain p % 64, slot p / 64. A split-route
+  // tile is one contiguous run of a chain; a short-route chain (stride 32)
+  // interleaves chains c and c + 32, loaded as two runs into rows 0-15 / 16-31.
+  const size_t cps = cap / kAttnChains;
   const uint16_t* kbase = a.kcache + size_t(kh) * cap * kHeadDim;
   const uint16_t* vbase = a.vcache + size_t(kh) * cap * kHeadDim;
+  auto row_of = [&](int j) { return split ? j : ((j & 1) << 4) + (j >> 1); };
   // the current token is key `pos`: chain pos % stride, local index pos / stride
   const bool owner = chain == int(pos % stride);
   const int own_idx = int(pos / stride);
 
-  auto issue = [&](int t, int st) {  // warp 0 only
+  auto issue = [&](int t, int st) {  // one thread
     const int n = min(kAttnTile, nkeys - t * kAttnTile);
-    if (lane == 0) mbar_expect_tx(&S.bar[st], uint32_t(n) * 2 * kHeadDim * 2);
-    __syncwarp();
-    if (lane < n) {
-      const size_t key = size_t(chain) + size_t(stride) * size_t(t * kAttnTile + lane);
-      bulk_g2s(&S.kt[st][lane][0], kbase + key * kHeadDim, kHeadDim * 2, &S.bar[st]);
-      bulk_g2s(&S.vt[st][lane][0], vbase + key * kHeadDim, kHeadDim * 2, &S.bar[st]);
+    mbar_expect_tx(&S.bar[st], uint32_t(n) * 2 * kHeadDim * 2);
+    if (split) {
+      const size_t off = (size_t(chain) * cps + size_t(t) * kAttnTile) * kHeadDim;
+      bulk_g2s(&S.kt[st][0][0], kbase + off, uint32_t(n) * kHeadDim * 2, &S.bar[st]);
+      bulk_g2s(&S.vt[st][0][0], vbase + off, uint32_t(n) * kHeadDim * 2, &S.bar[st]);
+    } else {
+      const int na = (n + 1) >> 1, nb = n >> 1;
+      const size_t oa = size_t(chain) * cps * kHeadDim, ob = size_t(chain + 32) * cps * kHeadDim;
+      bulk_g2s(&S.kt[st][0][0], kbase + oa, uint32_t(na) * kHeadDim * 2, &S.bar[st]);
+      bulk_g2s(&S.vt[st][0][0], vbase + oa, uint32_t(na) * kHeadDim * 2, &S.bar[st]);
+      if (nb > 0) {
+        bulk_g2s(&S.kt[st][16][0], kbase + ob, uint32_t(nb) * kHeadDim * 2, &S.bar[st]);
+        bulk_g2s(&S.vt[st][16][0], vbase + ob, uint32_t(nb) * kHeadDim * 2, &S.bar[st]);
+      }
     }
   };
   if (tid == 0) {
@@ -479,7 +557,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const __grid_constant__ A
     fence_mbar_init();
   }
   __syncthreads();
-  if (warp == 0)
+  if (tid == 0)
     for (int t = 0; t < kAttnStages && t < ntiles; ++t) issue(t, t);
   pdl_wait();
   pdl_launch();
@@ -499,7 +577,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const __grid_constant__ A
     }
     __syncwarp();
     if (owner) {
-      const size_t ci = (size_t(kh) * cap + pos) * kHeadDim;
+      const size_t ci = (size_t(kh) * cap + size_t(pos % kAttnChains) * cps + pos / kAttnChains) * kHeadDim;
       for (int d = lane; d < kHeadDim; d += 32) {
         a.kcache[ci + d] = S.kf[d];
         a.vcache[ci + d] = S.vf[d];
@@ -527,8 +605,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const __grid_constant__ A
       __syncthreads();
       if (warp == 0)
         for (int d = lane; d < kHeadDim; d += 32) {
-          S.kt[st][own_idx % kAttnTile][d] = S.kf[d];
-          S.vt[st][own_idx % kAttnTile][d] = S.vf[d];
+          S.kt[st][row_of(own_idx % kAttnTile)][d] = S.kf[d];
+          S.vt[st][row_of(own_idx % kAttnTile)][d] = S.vf[d];
         }
       __syncthreads();
     }
@@ -537,7 +615,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const __grid_constant__ A
       float v[16];
 #pragma unroll
       for (int jj = 0; jj < 4; ++jj) {
-        const uint4 kv = *reinterpret_cast<const uint4*>(&S.kt[st][4 * warp + jj][8 * lane]);
+        const uint4 kv = *reinterpret_cast<const uint4*>(&S.kt[st][row_of(4 * warp + jj)][8 * lane]);
         const float k8[8] = {bf_lo(kv.x), bf_hi(kv.x), bf_lo(kv.y), bf_hi(kv.y),
                              bf_lo(kv.z), bf_hi(kv.z), bf_lo(kv.w), bf_hi(kv.w)};
 #pragma unroll
@@ -554,8 +632,8 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const __grid_constant__ A
     __syncthreads();
     // running max as a prefix scan, then the independent exps
     {
-      const float s = lane < nk ? S.sc[rh][lane] : -INFINITY;
-      float v = s;
+      const float sv = lane < nk ? S.sc[rh][lane] : -INFINITY;
+      float v = sv;
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
         const float u = __shfl_up_sync(0xffffffffu, v, off);
@@ -564,23 +642,27 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const __grid_constant__ A
       const float mt = fmaxf(msum, v);
       float mprev = __shfl_up_sync(0xffffffffu, mt, 1);
       if (lane == 0) mprev = msum;
-      const float f = fexp(__fsub_rn(mprev, mt));
-      const float e = fexp(__fsub_rn(s, mt));
+      S.fe[warp][lane] = make_float2(fexp(__fsub_rn(mprev, mt)), fexp(__fsub_rn(sv, mt)));
       msum = __shfl_sync(0xffffffffu, mt, nk - 1);
+      __syncwarp();
       for (int j = 0; j < nk; ++j) {
-        const float fj = __shfl_sync(0xffffffffu, f, j);
-        const float ej = __shfl_sync(0xffffffffu, e, j);
-        ssum = __fadd_rn(__fmul_rn(ssum, fj), ej);
-        const uint2 vv = *reinterpret_cast<const uint2*>(&S.vt[st][j][d0]);
-        const float v4[4] = {bf_lo(vv.x), bf_hi(vv.x), bf_lo(vv.y), bf_hi(vv.y)};
+        const float2 fe = S.fe[warp][j];
+        const uint2 vv = *reinterpret_cast<const uint2*>(&S.vt[st][row_of(j)][d0]);
+        if (fe.x != 1.0f) {  // o * 1 == o exactly
+          ssum = __fmul_rn(ssum, fe.x);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) o[i] = __fadd_rn(__fmul_rn(o[i], fj), __fmul_rn(ej, v4[i]));
+          for (int i = 0; i < 4; ++i) o[i] = __fmul_rn(o[i], fe.x);
+        }
+        ssum = __fadd_rn(ssum, fe.y);
+        o[0] = __fadd_rn(o[0], __fmul_rn(fe.y, bf_lo(vv.x)));
+        o[1] = __fadd_rn(o[1], __fmul_rn(fe.y, bf_hi(vv.x)));
+        o[2] = __fadd_rn(o[2], __fmul_rn(fe.y, bf_lo(vv.y)));
+        o[3] = __fadd_rn(o[3], __fmul_rn(fe.y, bf_hi(vv.y)));
       }
     }
     __syncthreads();
-    if (warp == 0 && t + kAttnStages < ntiles) {
-      if (lane == 0) fence_proxy_async();
-      __syncwarp();
+    if (tid == 0 && t + kAttnStages < ntiles) {
+      fence_proxy_async();
       issue(t + kAttnStages, st);
     }
   }
@@ -596,75 +678,75 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(const __grid_constant__ A
       pml[1] = ssum;
     }
   }
-  __threadfence();
   __syncthreads();
-  if (tid == 0) S.last = (atomicAdd(&a.ctl->attn_counter[kh], 1u) == kAttnChains - 1);
-  __syncthreads();
-  if (!S.last) {
-    if (tid == 0) attn_time_end(a.ctl);
-    return;
-  }
-  __threadfence();
+  if (tid == 0) attn_time_end(a.ctl);
+}
 
-  // combine the chains of the four heads; task = (head, stripe of 8 dims)
-  for (int task = warp; task < 4 * 32; task += kAttnThreads / 32) {
-    const int h = task >> 5, stripe = task & 31;
-    const int qh = 4 * kh + h;
-    const size_t base = size_t(kh) * kAttnChains * 4 + h;  // + chain * 4
-    float res[8];
-    if (split) {
-      // attn_decode_split2_gate (attention_decode.metal:853-876): lane l owns chains l, l+32
-      const float ma = __ldcg(&a.part_ml[(base + size_t(lane) * 4) * 2]);
-      const float mb = __ldcg(&a.part_ml[(base + size_t(lane + 32) * 4) * 2]);
-      const float M = warp_max(fmaxf(fmaxf(kMin, ma), mb));
-      const float fa = fexp(__fsub_rn(ma, M)), fb = fexp(__fsub_rn(mb, M));
-      float sacc = 0.0f;
-      sacc = __fadd_rn(sacc, __fmul_rn(fa, __ldcg(&a.part_ml[(base + size_t(lane) * 4) * 2 + 1])));
-      sacc = __fadd_rn(sacc, __fmul_rn(fb, __ldcg(&a.part_ml[(base + size_t(lane + 32) * 4) * 2 + 1])));
-      const float ssum_all = warp_sum(sacc);
-      const float* pa = a.part_o + (base + size_t(lane) * 4) * kHeadDim + stripe * 8;
-      const float* pb = a.part_o + (base + size_t(lane + 32) * 4) * kHeadDim + stripe * 8;
+// Chain combine and BF16 output gate. Grid (8 query heads, 8 stripes of 32
+// dims), 4 warps of 8 dims: the reference's attn_decode_split2_gate SIMD
+// layout (lane l owns chains l and l+32, attention_decode.metal:853-889), or
+// sdpa_vector's final reduction (lane l = chain l, :194-212) below 1024 keys,
+// followed by attn_gate (attention.metal:140-150).
+__global__ void __launch_bounds__(128) k_attn_combine(const __grid_constant__ AttnArgs a) {
+  constexpr float kMin = -3.4028234663852886e38f;
+  pdl_wait();
+  pdl_launch();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int qh = blockIdx.x, kh = qh >> 2, h = qh & 3;
+  const int stripe = blockIdx.y * 4 + warp;  // 8 dims
+  const uint32_t len = ld_cg_u32(&a.ctl->pos_step) + 1;
+  const bool split = len >= 1024;
+  const size_t base = size_t(kh) * kAttnChains * 4 + h;  // + chain * 4
+  float res[8];
+  if (split) {
+    const size_t ia = base + size_t(lane) * 4, ib = base + size_t(lane + 32) * 4;
+    const float2 mla = *reinterpret_cast<const float2*>(&a.part_ml[ia * 2]);
+    const float2 mlb = *reinterpret_cast<const float2*>(&a.part_ml[ib * 2]);
+    const float4 pa0 = *reinterpret_cast<const float4*>(a.part_o + ia * kHeadDim + stripe * 8);
+    const float4 pa1 = *reinterpret_cast<const float4*>(a.part_o + ia * kHeadDim + stripe * 8 + 4);
+    const float4 pb0 = *reinterpret_cast<const float4*>(a.part_o + ib * kHeadDim + stripe * 8);
+    const float4 pb1 = *reinterpret_cast<const float4*>(a.part_o + ib * kHeadDim + stripe * 8 + 4);
+    const float pa[8] = {pa0.x, pa0.y, pa0.z, pa0.w, pa1.x, pa1.y, pa1.z, pa1.w};
+    const float pb[8] = {pb0.x, pb0.y, pb0.z, pb0.w, pb1.x, pb1.y, pb1.z, pb1.w};
+    const float M = warp_max(fmaxf(fmaxf(kMin, mla.x), mlb.x));
+    const float fa = fexp(__fsub_rn(mla.x, M)), fb = fexp(__fsub_rn(mlb.x, M));
+    float sacc = __fadd_rn(0.0f, __fmul_rn(fa, mla.y));
+    sacc = __fadd_rn(sacc, __fmul_rn(fb, mlb.y));
+    const float ssum_all = warp_sum(sacc);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        float acc = 0.0f;
-        acc = __fadd_rn(acc, __fmul_rn(fa, __ldcg(pa + i)));
-        acc = __fadd_rn(acc, __fmul_rn(fb, __ldcg(pb + i)));
-        const float ov = warp_sum(acc);
-        res[i] = ssum_all == 0.0f ? ov : __fdiv_rn(ov, ssum_all);
-      }
-    } else {
-      // sdpa_vector's final reduction (attention_decode.metal:194-212): lane l = group l
-      const float ml = __ldcg(&a.part_ml[(base + size_t(lane) * 4) * 2]);
-      const float M = warp_max(ml);
-      const float fl = fexp(__fsub_rn(ml, M));
-      const float ssum_all =
-          warp_sum(__fmul_rn(__ldcg(&a.part_ml[(base + size_t(lane) * 4) * 2 + 1]), fl));
-      const float* pl = a.part_o + (base + size_t(lane) * 4) * kHeadDim + stripe * 8;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float ov = warp_sum(__fmul_rn(__ldcg(pl + i), fl));
-        res[i] = ssum_all == 0.0f ? ov : __fdiv_rn(ov, ssum_all);
-      }
+    for (int i = 0; i < 8; ++i) {
+      float acc = __fadd_rn(0.0f, __fmul_rn(fa, pa[i]));
+      acc = __fadd_rn(acc, __fmul_rn(fb, pb[i]));
+      const float ov = warp_sum(acc);
+      res[i] = ssum_all == 0.0f ? ov : __fdiv_rn(ov, ssum_all);
     }
-    if (lane < 8) {
-      // BF16 output gate, attention.metal:144-150 (same expression in :882-889)
-      float r = res[0];
+  } else {
+    const size_t il = base + size_t(lane) * 4;
+    const float2 ml = *reinterpret_cast<const float2*>(&a.part_ml[il * 2]);
+    const float4 p0 = *reinterpret_cast<const float4*>(a.part_o + il * kHeadDim + stripe * 8);
+    const float4 p1 = *reinterpret_cast<const float4*>(a.part_o + il * kHeadDim + stripe * 8 + 4);
+    const float pl[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+    const float M = warp_max(ml.x);
+    const float fl = fexp(__fsub_rn(ml.x, M));
+    const float ssum_all = warp_sum(__fmul_rn(ml.y, fl));
 #pragma unroll
-      for (int i = 1; i < 8; ++i) r = lane == i ? res[i] : r;
-      const int d = stripe * 8 + lane;
-      const float attention = bfr(r);
-      const float x = bf2f(a.q_raw[qh * 512 + 256 + d]);
-      const float e = bfr(dexpf(fabsf(x)));
-      const float denom = bfr(__fadd_rn(1.0f, e));
-      const float inverse = bfr(__fdiv_rn(1.0f, denom));
-      const float gate = bfr(x < 0.0f ? inverse : __fsub_rn(1.0f, inverse));
-      a.gated[qh * kHeadDim + d] = f2bf(__fmul_rn(attention, gate));
+    for (int i = 0; i < 8; ++i) {
+      const float ov = warp_sum(__fmul_rn(pl[i], fl));
+      res[i] = ssum_all == 0.0f ? ov : __fdiv_rn(ov, ssum_all);
     }
   }
-  __syncthreads();
-  if (tid == 0) {
-    atomicExch(&a.ctl->attn_counter[kh], 0u);
-    attn_time_end(a.ctl);
+  if (lane < 8) {
+    float r = res[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) r = lane == i ? res[i] : r;
+    const int d = stripe * 8 + lane;
+    const float attention = bfr(r);
+    const float x = bf2f(a.q_raw[qh * 512 + 256 + d]);
+    const float e = bfr(dexpf(fabsf(x)));
+    const float denom = bfr(__fadd_rn(1.0f, e));
+    const float inverse = bfr(__fdiv_rn(1.0f, denom));
+    const float gate = bfr(x < 0.0f ? inverse : __fsub_rn(1.0f, inverse));
+    a.gated[qh * kHeadDim + d] = f2bf(__fmul_rn(attention, gate));
   }
 }
 
@@ -949,14 +1031,16 @@ cudaError_t kernels_init() {
 
 cudaError_t launch_qmv(const QmvArgs& a, cudaStream_t st, bool pdl) {
   const int grid = (a.units + a.units_per_cta - 1) / a.units_per_cta;
-  return launch_ex(k_qmv, dim3(grid), dim3(256), qmv_smem_bytes(a), st, pdl, a);
+  return launch_ex(k_qmv, dim3(grid), dim3(kQmvThreads), qmv_smem_bytes(a), st, pdl, a);
 }
 cudaError_t launch_recur(const RecurArgs& a, cudaStream_t st, bool pdl) {
   return launch_ex(k_gdn_recur, dim3(8, kGdnHeads), dim3(64), 0, st, pdl, a);
 }
 cudaError_t launch_attn(const AttnArgs& a, cudaStream_t st, bool pdl) {
-  return launch_ex(k_attn, dim3(kAttnChains, kKvHeads), dim3(kAttnThreads), attn_smem_bytes(), st,
-                   pdl, a);
+  cudaError_t e = launch_ex(k_attn, dim3(kAttnChains, kKvHeads), dim3(kAttnThreads),
+                            attn_smem_bytes(), st, pdl, a);
+  if (e != cudaSuccess) return e;
+  return launch_ex(k_attn_combine, dim3(kQHeads, kHeadDim / 32), dim3(128), 0, st, true, a);
 }
 cudaError_t launch_head(const HeadArgs& a, cudaStream_t st, bool pdl) {
   return launch_ex(k_head, dim3(kHeadCtas), dim3(256), head_smem_bytes(), st, pdl, a);

@@ -25,34 +25,54 @@ namespace q35 {
 
 constexpr float kTwo23 = 8388608.0f;
 
-// Per (chunk, lane) constants: xq[c][i][lane] float4 (i < 8: 16 xx then 16
-// -2^23*xx), xsum[c][lane].
+// Per (chunk, lane) constants: xq[c][i][lane] float4 (i < 4: the 16 xx of
+// the lane, i >= 4: -2^23 * xx), xsum[c][lane] = the lane's xs. A thread
+// builds one group of four consecutive k (one float4 of xx); the lane's xs
+// is ((g0 + g1) + g2) + g3 over its four groups g = ((a + b) + c) + d, as the
+// reference accumulates it. Dividing by 16/256/4096 is multiplying by the
+// exact reciprocal powers of two (identical results). All threads must call.
 Q35_DEV void build_xq(const float* xf, int K, float4* xq, float* xsum) {
-  const int nch = K / 512;
-  for (int t = threadIdx.x; t < nch * 32; t += blockDim.x) {
-    const int c = t >> 5, l = t & 31;
-    const float* x = xf + 512 * c + 16 * l;
-    float xx[16];
-    float xs = 0.0f;
-#pragma unroll
-    for (int j = 0; j < 16; j += 4) {
-      const float a = x[j], b = x[j + 1], cc = x[j + 2], d = x[j + 3];
-      xs = __fadd_rn(xs, __fadd_rn(__fadd_rn(__fadd_rn(a, b), cc), d));
-      xx[j] = a;
-      xx[j + 1] = __fdiv_rn(b, 16.0f);
-      xx[j + 2] = __fdiv_rn(cc, 256.0f);
-      xx[j + 3] = __fdiv_rn(d, 4096.0f);
+  const int ngroups = K / 4;
+  for (int base = 0; base < ngroups; base += blockDim.x) {
+    const int t = base + threadIdx.x;
+    const bool on = t < ngroups;
+    float4 x4 = on ? *reinterpret_cast<const float4*>(xf + 4 * t) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float g = __fadd_rn(__fadd_rn(__fadd_rn(x4.x, x4.y), x4.z), x4.w);
+    const float g1 = __shfl_down_sync(0xffffffffu, g, 1);
+    const float g2 = __shfl_down_sync(0xffffffffu, g, 2);
+    const float g3 = __shfl_down_sync(0xffffffffu, g, 3);
+    if (on) {
+      const int c = t >> 7, l = (t >> 2) & 31, j = t & 3;
+      const float4 xx = make_float4(x4.x, __fmul_rn(x4.y, 0.0625f), __fmul_rn(x4.z, 0.00390625f),
+                                    __fmul_rn(x4.w, 0.000244140625f));
+      float4* dst = xq + size_t(c) * 8 * 32 + l;
+      dst[j * 32] = xx;
+      dst[(4 + j) * 32] = make_float4(-kTwo23 * xx.x, -kTwo23 * xx.y, -kTwo23 * xx.z, -kTwo23 * xx.w);
+      if (j == 0) xsum[c * 32 + l] = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.0f, g), g1), g2), g3);
     }
-    float4* dst = xq + size_t(c) * 8 * 32 + l;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      dst[i * 32] = make_float4(xx[4 * i], xx[4 * i + 1], xx[4 * i + 2], xx[4 * i + 3]);
-      dst[(4 + i) * 32] = make_float4(-kTwo23 * xx[4 * i], -kTwo23 * xx[4 * i + 1],
-                                      -kTwo23 * xx[4 * i + 2], -kTwo23 * xx[4 * i + 3]);
-    }
-    xsum[t] = xs;
   }
 }
+
+// Emit the constants of one group of four consecutive activations
+// (k = 4t .. 4t+3). The four groups of a lane (t = 4l' .. 4l'+3 within a
+// chunk) must be held by four consecutive lanes of one warp in the same call;
+// all lanes of the warp call (inactive ones with on = false).
+Q35_DEV void emit_xq(int t, bool on, float4 x4, float4* xq, float* xsum) {
+  const float g = __fadd_rn(__fadd_rn(__fadd_rn(x4.x, x4.y), x4.z), x4.w);
+  const float g1 = __shfl_down_sync(0xffffffffu, g, 1);
+  const float g2 = __shfl_down_sync(0xffffffffu, g, 2);
+  const float g3 = __shfl_down_sync(0xffffffffu, g, 3);
+  if (!on) return;
+  const int c = t >> 7, l = (t >> 2) & 31, j = t & 3;
+  const float4 xx = make_float4(x4.x, __fmul_rn(x4.y, 0.0625f), __fmul_rn(x4.z, 0.00390625f),
+                                __fmul_rn(x4.w, 0.000244140625f));
+  float4* dst = xq + size_t(c) * 8 * 32 + l;
+  dst[j * 32] = xx;
+  dst[(4 + j) * 32] = make_float4(-kTwo23 * xx.x, -kTwo23 * xx.y, -kTwo23 * xx.z, -kTwo23 * xx.w);
+  if (j == 0) xsum[c * 32 + l] = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.0f, g), g1), g2), g3);
+}
+
+Q35_DEV float4 bf4(uint2 u) { return make_float4(bf_lo(u.x), bf_hi(u.x), bf_lo(u.y), bf_hi(u.y)); }
 
 Q35_DEV float magic(uint32_t bits) { return __uint_as_float(bits | 0x4b000000u); }
 
@@ -155,12 +175,30 @@ Q35_DEV void rms1024(const float v[4], const uint16_t* gain, float* xf, float* r
   const float t0 = __fadd_rn(red[0], red[4]), t1 = __fadd_rn(red[1], red[5]);
   const float t2 = __fadd_rn(red[2], red[6]), t3 = __fadd_rn(red[3], red[7]);
   const float total = __fadd_rn(__fadd_rn(t0, t2), __fadd_rn(t1, t3));
-  const float inv = drsqrtf(__fadd_rn(__fdiv_rn(total, 1024.0f), 1e-6f));
+  const float inv = drsqrtf(__fadd_rn(__fmul_rn(total, 0.0009765625f), 1e-6f));
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const int c = 4 * tid + j;
     xf[c] = bfr(__fmul_rn(bfr(__fmul_rn(v[j], inv)), bf2f(gain[c])));
   }
+}
+
+// rms1024 for a block whose first 256 threads hold the vector (others pass
+// zeros and ignore the result): normalised bf16 values returned in out[4].
+Q35_DEV void rms1024_reg(const float v[4], const float g[4], float out[4], float* red) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float acc = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) acc = __fadd_rn(acc, __fmul_rn(v[j], v[j]));
+  acc = warp_sum(acc);
+  if (lane == 0 && warp < 8) red[warp] = acc;
+  __syncthreads();
+  const float t0 = __fadd_rn(red[0], red[4]), t1 = __fadd_rn(red[1], red[5]);
+  const float t2 = __fadd_rn(red[2], red[6]), t3 = __fadd_rn(red[3], red[7]);
+  const float total = __fadd_rn(__fadd_rn(t0, t2), __fadd_rn(t1, t3));
+  const float inv = drsqrtf(__fadd_rn(__fmul_rn(total, 0.0009765625f), 1e-6f));
+#pragma unroll
+  for (int j = 0; j < 4; ++j) out[j] = bfr(__fmul_rn(bfr(__fmul_rn(v[j], inv)), g[j]));
 }
 
 }  // namespace q35

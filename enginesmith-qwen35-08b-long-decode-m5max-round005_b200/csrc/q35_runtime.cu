@@ -630,8 +630,8 @@ int q35_open(const char* model_dir, int device, const q35_opts* opts, q35_sessio
     free_session(s);
     return code;
   };
-  if (s->capacity % kAttnTile != 0 || s->capacity < kAttnTile || s->capacity > (1u << 30))
-    return fail(Q35_EINVAL, "capacity must be a positive multiple of 32");
+  if (s->capacity % kAttnChains != 0 || s->capacity < kAttnChains || s->capacity > (1u << 30))
+    return fail(Q35_EINVAL, "capacity must be a positive multiple of 64");
   cudaError_t e = cudaSetDevice(device);
   if (e != cudaSuccess) return fail(Q35_ECUDA, std::string("cudaSetDevice: ") + cudaGetErrorString(e));
   e = ensure_kernels_init();
@@ -841,12 +841,22 @@ int q35_dump_state(q35_session* s, uint16_t* kv, float* state, uint16_t* hist) {
   cudaSetDevice(s->device);
   cudaError_t e = cudaStreamSynchronize(s->stream);
   const size_t pos = s->position;
+  // the caches are chain-major (position p at chain p % 64, slot p / 64)
+  const size_t cps = s->capacity / kAttnChains;
+  const size_t slots = (pos + kAttnChains - 1) / kAttnChains;
+  std::vector<uint16_t> tmp(slots * kHeadDim);
   for (int ai = 0; ai < 6 && e == cudaSuccess && kv; ++ai)
     for (int which = 0; which < 2 && e == cudaSuccess; ++which)
       for (int h = 0; h < kKvHeads && e == cudaSuccess; ++h) {
         const uint16_t* src = (which ? s->vcache(ai) : s->kcache(ai)) + size_t(h) * s->capacity * kHeadDim;
         uint16_t* dst = kv + ((size_t(ai) * 2 + which) * kKvHeads + h) * pos * kHeadDim;
-        e = cudaMemcpy(dst, src, pos * kHeadDim * 2, cudaMemcpyDeviceToHost);
+        for (size_t c = 0; c < size_t(kAttnChains) && e == cudaSuccess; ++c) {
+          const size_t n = pos > c ? (pos - c + kAttnChains - 1) / kAttnChains : 0;
+          if (n == 0) continue;
+          e = cudaMemcpy(tmp.data(), src + c * cps * kHeadDim, n * kHeadDim * 2, cudaMemcpyDeviceToHost);
+          for (size_t sl = 0; sl < n; ++sl)
+            std::memcpy(dst + (sl * kAttnChains + c) * kHeadDim, tmp.data() + sl * kHeadDim, kHeadDim * 2);
+        }
       }
   if (e == cudaSuccess && state)
     e = cudaMemcpy(state, s->state, size_t(18) * kGdnHeads * 128 * 128 * 4, cudaMemcpyDeviceToHost);
@@ -970,7 +980,7 @@ int q35_op_attn_decode(const uint16_t* q_raw, const uint16_t* k_raw, const uint1
                        uint16_t* vcache, uint32_t capacity, uint32_t pos, uint16_t* gated,
                        void* workspace, void* stream) {
   if (!q_raw || !k_raw || !v_raw || !q_gain || !k_gain || !kcache || !vcache || !gated ||
-      !workspace || capacity == 0 || capacity % kAttnTile != 0 || pos >= capacity)
+      !workspace || capacity == 0 || capacity % kAttnChains != 0 || pos >= capacity)
     return Q35_EINVAL;
   if (ensure_kernels_init() != cudaSuccess) return Q35_ECUDA;
   cudaStream_t st = (cudaStream_t)stream;

@@ -119,7 +119,7 @@ struct AttnArgs {
   const uint16_t* v_raw;  // [2][256]
   const uint16_t* q_gain; // [256]
   const uint16_t* k_gain; // [256]
-  uint16_t* kcache;       // [2][capacity][256]
+  uint16_t* kcache;       // [2][64 chains][capacity/64][256], position p at chain p%64, slot p/64
   uint16_t* vcache;
   uint32_t capacity;
   float* part_o;          // [2][kAttnChains][4][256]

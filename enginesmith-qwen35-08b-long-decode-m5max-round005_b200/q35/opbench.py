@@ -1,0 +1,99 @@
+"""Op-level benchmarks of the q35 kernels on the BASELINE.json configs 1-3.
+
+  python -m q35.opbench --op qmv|gdn|attn [--len N] [--iters K] [--copies R]
+
+Each call works on a fresh copy of its big operands (weights, recurrent
+state, or K/V cache), rotating over enough copies that the working set is
+larger than the 126 MB L2, so every call streams its bytes from HBM. Times
+are CUDA events on the launching stream after warm-up; the line printed is
+JSON with the per-call time and the algorithmic bytes moved per call.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, os.path.dirname(HERE))
+sys.path.insert(0, os.path.join(ROOT, "tests"))
+
+
+def main():
+    import numpy as np
+    import torch
+    import q35
+    import inputs as I
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--op", choices=["qmv", "gdn", "attn"], required=True)
+    ap.add_argument("--len", type=int, default=32768)
+    ap.add_argument("--iters", type=int, default=200)
+    ap.add_argument("--copies", type=int, default=0)
+    args = ap.parse_args()
+    dev = torch.device("cuda:0")
+    def T(a):
+        a = np.ascontiguousarray(a)
+        if a.dtype == np.uint16:
+            a = a.view(np.int16)
+        elif a.dtype == np.uint32:
+            a = a.view(np.int32)
+        return torch.from_numpy(a).to(dev)
+
+    if args.op == "qmv":
+        w, s, b, x = I.config1(0)
+        copies = args.copies or 256
+        W = T(w).repeat(copies, 1).view(copies, *w.shape)
+        S = T(s).repeat(copies, 1).view(copies, *s.shape)
+        B = T(b).repeat(copies, 1).view(copies, *b.shape)
+        X = T(x)
+        y = torch.empty(3584, dtype=torch.uint16, device=dev)
+        nbytes = w.nbytes + s.nbytes + b.nbytes + x.nbytes + 3584 * 2
+
+        def call(i):
+            q35.qmv_q4(W[i % copies], S[i % copies], B[i % copies], X, out=y)
+    elif args.op == "gdn":
+        d = I.config2(1)
+        copies = args.copies or 64
+        st = T(d["state"]).repeat(copies).view(copies, -1)
+        hist = T(d["hist"])
+        ws = q35.workspace("gdn")
+        ins = {k: T(d[k]) for k in ("raw", "z", "a", "b", "conv_w", "a_log", "dt", "norm_w", "ow", "os", "ob", "res")}
+        nbytes = 2 * d["state"].nbytes + d["conv_w"].nbytes + 2 * d["hist"].nbytes + d["ow"].nbytes + \
+            d["os"].nbytes + d["ob"].nbytes + 2 * (6144 + 2048 + 32 + 1024 + 1024)
+
+        def call(i):
+            q35.gdn_step(ins["raw"], ins["z"], ins["a"], ins["b"], hist, ins["conv_w"], ins["a_log"], ins["dt"],
+                         st[i % copies], ins["norm_w"], ins["ow"], ins["os"], ins["ob"], residual=ins["res"], ws=ws)
+    else:
+        d = I.config3(2, args.len)
+        per = d["kc"].nbytes * 2
+        copies = args.copies or max(2, int(np.ceil(300e6 / per)))
+        KC = [T(d["kc"]) for _ in range(copies)]
+        VC = [T(d["vc"]) for _ in range(copies)]
+        ins = {k: T(d[k]) for k in ("q_raw", "k_raw", "v_raw", "q_gain", "k_gain")}
+        ws = q35.workspace("attn")
+        nbytes = 2 * 2 * args.len * 256 * 2 + 4096 * 2 + 2048 * 2
+
+        def call(i):
+            q35.attn_decode(ins["q_raw"], ins["k_raw"], ins["v_raw"], ins["q_gain"], ins["k_gain"],
+                            KC[i % copies], VC[i % copies], d["cap"], d["pos"], ws=ws)
+
+    for i in range(10):
+        call(i)
+    torch.cuda.synchronize()
+    a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(args.iters):
+        call(i)
+    e.record()
+    torch.cuda.synchronize()
+    us = a.elapsed_time(e) * 1e3 / args.iters
+    print(json.dumps({"op": args.op, "len": args.len if args.op == "attn" else None, "us_per_call": us,
+                      "bytes_per_call": nbytes, "gbs": nbytes / us / 1e3, "copies": copies}))
+
+
+if __name__ == "__main__":
+    main()

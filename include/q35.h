@@ -41,7 +41,7 @@ extern "C" {
 typedef struct q35_session q35_session;
 
 typedef struct q35_opts {
-  uint32_t capacity;     /* context capacity in tokens (0 -> 262144); multiple of 32 */
+  uint32_t capacity;     /* context capacity in tokens (0 -> 262144); multiple of 64 */
   uint32_t decode_batch; /* decode steps per CUDA-graph launch (0 -> 8) */
   uint32_t prefill_batch;/* prompt steps per CUDA-graph launch (0 -> 16) */
   uint32_t flags;        /* reserved, 0 */
@@ -82,8 +82,8 @@ void q35_close(q35_session* s);
 uint32_t q35_position(const q35_session* s);
 
 /* Copy the device state to host memory for checking: per attention layer
- * (6) K and V caches [2][capacity][256] bf16 truncated to the first `pos`
- * positions (layout [2][pos][256] each), per GDN layer (18) recurrent state
+ * (6) K and V caches, converted to position order and truncated to the first
+ * `pos` positions (layout [2][pos][256] each), per GDN layer (18) recurrent state
  * f32 [16][128][128] and conv history bf16 [3][6144]. Buffers must hold
  * 6*2*2*pos*256*2 bytes (kv), 18*16*128*128*4 (state), 18*3*6144*2 (hist). */
 int q35_dump_state(q35_session* s, uint16_t* kv, float* state, uint16_t* hist);
@@ -144,8 +144,11 @@ int q35_op_gdn_step(const uint16_t* raw_qkv, const uint16_t* z, const uint16_t* 
  * token's K/V at `pos`, then split-K attention over keys 0..pos
  * (kernels/attention_decode.metal:215-431) and the combine with the BF16
  * output gate (:830-891). q_raw [8][512] (query | gate), k_raw/v_raw
- * [2][256], q/k norm gains [256]; caches [2][capacity][256] bf16
- * (capacity a multiple of 32, pos < capacity); gated [8][256] bf16. */
+ * [2][256], q/k norm gains [256]; gated [8][256] bf16. The caches are
+ * chain-major bf16 [2 kv heads][64][capacity/64][256]: position p of a kv
+ * head lives at chain p % 64, slot p / 64 (capacity a multiple of 64,
+ * pos < capacity), so each of the reference's 64 key blocks (keys b, b+64,
+ * ...) is contiguous. */
 size_t q35_op_attn_workspace_bytes(void);
 int q35_op_attn_decode(const uint16_t* q_raw, const uint16_t* k_raw, const uint16_t* v_raw,
                        const uint16_t* q_gain, const uint16_t* k_gain, uint16_t* kcache,

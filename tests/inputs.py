@@ -45,6 +45,17 @@ class Rng:
         return (self.bits(n) % np.uint64(hi)).astype(np.uint32)
 
 
+def to_chain_major(cache: np.ndarray) -> np.ndarray:
+    """[2][cap][256] position order -> [2][64][cap/64][256] (position p at chain p%64, slot p/64)."""
+    h, cap, d = cache.shape
+    return np.ascontiguousarray(cache.reshape(h, cap // 64, 64, d).transpose(0, 2, 1, 3))
+
+
+def from_chain_major(cache: np.ndarray) -> np.ndarray:
+    h, c, s, d = cache.reshape(cache.shape[0], 64, -1, cache.shape[-1]).shape
+    return np.ascontiguousarray(cache.reshape(h, 64, s, d).transpose(0, 2, 1, 3).reshape(h, s * 64, d))
+
+
 def f2bf(x) -> np.ndarray:
     u = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
     nan = (u & 0x7FFFFFFF) > 0x7F800000
@@ -108,7 +119,7 @@ def config2(seed: int = 1):
 
 def config3(seed: int = 2, length: int = 32768, capacity: int | None = None):
     """gated GQA decode at context `length` (8 q / 2 kv heads, D 256)."""
-    cap = capacity or ((length + 31) // 32) * 32
+    cap = capacity or ((length + 63) // 64) * 64
     r = Rng(seed, 3)
     d = {}
     d["q_raw"] = f2bf(r.normal(4096))

@@ -68,6 +68,6 @@ def test_open_reports_errors_without_crashing():
     import ctypes
     h = ctypes.c_void_p()
     err = ctypes.create_string_buffer(512)
-    opts = q35._Opts(33, 0, 0, 0)  # capacity not a multiple of 32
+    opts = q35._Opts(96, 0, 0, 0)  # capacity not a multiple of 64
     rc = q35.lib().q35_open(b"/nonexistent", 0, ctypes.byref(opts), ctypes.byref(h), err, len(err))
-    assert rc == q35.EINVAL and b"multiple of 32" in err.value and not h.value
+    assert rc == q35.EINVAL and b"multiple of 64" in err.value and not h.value

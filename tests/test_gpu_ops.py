@@ -133,11 +133,11 @@ def test_attn_decode(cuda, oracle_threads, length):
     d = I.config3(2, length)
     cap, pos = d["cap"], d["pos"]
     kc, vc = d["kc"].copy(), d["vc"].copy()
-    KC, VC = dev(kc), dev(vc)
+    KC, VC = dev(I.to_chain_major(kc)), dev(I.to_chain_major(vc))
     gg = host(q35.attn_decode(dev(d["q_raw"]), dev(d["k_raw"]), dev(d["v_raw"]), dev(d["q_gain"]),
                               dev(d["k_gain"]), KC, VC, cap, pos))
     query = O.attn_prepare(d["q_raw"], d["k_raw"], d["v_raw"], d["q_gain"], d["k_gain"], pos, cap, kc, vc)
-    kcg, vcg = host(KC), host(VC)
+    kcg, vcg = I.from_chain_major(host(KC)), I.from_chain_major(host(VC))
     assert np.array_equal(kcg[:, pos], kc[:, pos]), "K append"
     assert np.array_equal(vcg[:, pos], vc[:, pos]), "V append"
     gref = O.attn_decode_gate(query, kc, vc, length, cap, d["q_raw"])
