@@ -645,6 +645,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attn(const __grid_constant_
       S.fe[warp][lane] = make_float2(fexp(__fsub_rn(mprev, mt)), fexp(__fsub_rn(sv, mt)));
       msum = __shfl_sync(0xffffffffu, mt, nk - 1);
       __syncwarp();
+      // o = o*f + e*v key by key (attention_decode.metal:360-366)
       for (int j = 0; j < nk; ++j) {
         const float2 fe = S.fe[warp][j];
         const uint2 vv = *reinterpret_cast<const uint2*>(&S.vt[st][row_of(j)][d0]);
