@@ -155,6 +155,22 @@ int q35_op_attn_decode(const uint16_t* q_raw, const uint16_t* k_raw, const uint1
                        uint16_t* vcache, uint32_t capacity, uint32_t pos, uint16_t* gated,
                        void* workspace, void* stream);
 
+/* Allocation-free form of q35_op_attn_decode, for callers that cannot call
+ * cudaMalloc or hand out a workspace (no counterpart in the reference: its
+ * Metal host allocates every buffer itself). Same arguments and results as
+ * q35_op_attn_decode, minus the workspace: the scratch is a 576 KiB array in
+ * the library's device image, held by every device that loads the library
+ * until exit (this op needs 528,640 bytes of it at any context length; a
+ * larger need is rejected). The first call on a device looks up the array's
+ * address and sets kernel attributes, so make it before any stream capture.
+ * All calls on a device share the array: calls that overlap on the GPU race.
+ * Rejected arguments return Q35_EINVAL with a message in err (may be NULL). */
+int q35_op_attn_decode_noalloc(const uint16_t* q_raw, const uint16_t* k_raw,
+                               const uint16_t* v_raw, const uint16_t* q_gain,
+                               const uint16_t* k_gain, uint16_t* kcache, uint16_t* vcache,
+                               uint32_t capacity, uint32_t pos, uint16_t* gated, char* err,
+                               size_t err_len, void* stream);
+
 /* Final RMSNorm (gain may be NULL to skip it), vocabulary projection of the
  * tied Q4 embedding [248320][1024] and greedy selection
  * (kernels/head_lse.metal:11-98, linear.metal:300-331): logits [248320]
