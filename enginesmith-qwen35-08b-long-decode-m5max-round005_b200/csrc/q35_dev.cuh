@@ -20,6 +20,8 @@ namespace q35 {
 Q35_DEV float bf2f(uint32_t h) { return __uint_as_float(h << 16); }
 Q35_DEV uint16_t f2bf(float f) { return __bfloat16_as_ushort(__float2bfloat16_rn(f)); }
 Q35_DEV float bfr(float f) { return bf2f(f2bf(f)); }
+// two floats -> two bf16 (RNE) in one word, lo first
+Q35_DEV uint32_t pack_bf2(float lo, float hi) { return uint32_t(f2bf(lo)) | (uint32_t(f2bf(hi)) << 16); }
 Q35_DEV float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
 Q35_DEV float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 

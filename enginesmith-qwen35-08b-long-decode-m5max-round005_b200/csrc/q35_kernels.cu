@@ -422,19 +422,22 @@ __global__ void k_gdn_conv(const uint16_t* raw, uint16_t* hist, const uint16_t* 
 // K/V row is read once. Rows stream through a ring of bulk copies. Scores use
 // the reference's per-lane order (eight products per lane, then a SIMD sum);
 // the running max is a prefix scan and f, e are independent, so only the S/o
-// recurrence runs key by key. The last CTA of each kv head combines the
-// chains and applies the BF16 output gate.
+// recurrence runs key by key. k_attn_combine then combines the chains and
+// applies the BF16 output gate.
 // ---------------------------------------------------------------------------
 struct AttnSmem {
-  uint16_t kt[kAttnStages][kAttnTile][kHeadDim];
-  uint16_t vt[kAttnStages][kAttnTile][kHeadDim];
+  uint16_t kt[kAttnStages][kAttnTile][kHeadDim];  // K ring
+  uint16_t vt[kAttnStages][kAttnTile][kHeadDim];  // V ring
   float q[4][kHeadDim];
   float nrm[5][kHeadDim];
   float kr[kHeadDim];
   uint16_t kf[kHeadDim], vf[kHeadDim];
-  float sc[4][kAttnTile];
-  float2 fe[kAttnThreads / 32][kAttnTile];
-  uint64_t bar[kAttnStages];
+  float sc[kAttnBufs][4][kAttnTile];  // scores [buffer][head][key]
+  float4 f[kAttnBufs][kAttnTile];     // per key: the four heads' factors
+  float4 e[kAttnBufs][kAttnTile];     // per key: the four heads' weights
+  uint32_t fm[kAttnBufs][4];          // per head: keys whose factor is not 1
+  uint64_t kfull[kAttnStages], kempty[kAttnStages], vfull[kAttnStages], vempty[kAttnStages];
+  uint64_t scfull[kAttnBufs], scempty[kAttnBufs], fefull[kAttnBufs], feempty[kAttnBufs];
 };
 
 size_t attn_smem_bytes() { return sizeof(AttnSmem); }
@@ -444,29 +447,50 @@ size_t attn_smem_bytes() { return sizeof(AttnSmem); }
 // head; out[d] gets the bf16 value as f32.
 __device__ __forceinline__ void head_norm_rope(const uint16_t* x, const uint16_t* gain,
                                                const float* cs, float* nrm, float* out, int lane) {
+  // Lane l owns dims 4l..4l+3 and 128+4l..128+4l+3 (the reference's two
+  // partial sums); every global load is issued up front. x, gain 8-byte
+  // aligned, cs 16-byte aligned.
+  const uint2 xa = *reinterpret_cast<const uint2*>(x + 4 * lane);
+  const uint2 xb = *reinterpret_cast<const uint2*>(x + 128 + 4 * lane);
+  const uint2 ga = *reinterpret_cast<const uint2*>(gain + 4 * lane);
+  const uint2 gb = *reinterpret_cast<const uint2*>(gain + 128 + 4 * lane);
+  float4 c0 = make_float4(0.f, 0.f, 0.f, 0.f), c1 = c0;  // (cos, sin) of pairs 4(l&7)..+3
+  if (lane < 16) {
+    c0 = reinterpret_cast<const float4*>(cs)[2 * (lane & 7)];
+    c1 = reinterpret_cast<const float4*>(cs)[2 * (lane & 7) + 1];
+  }
+  const float va[4] = {bf_lo(xa.x), bf_hi(xa.x), bf_lo(xa.y), bf_hi(xa.y)};
+  const float vb[4] = {bf_lo(xb.x), bf_hi(xb.x), bf_lo(xb.y), bf_hi(xb.y)};
+  const float gA[4] = {bf_lo(ga.x), bf_hi(ga.x), bf_lo(ga.y), bf_hi(ga.y)};
+  const float gB[4] = {bf_lo(gb.x), bf_hi(gb.x), bf_lo(gb.y), bf_hi(gb.y)};
   float pa = 0.0f, pb = 0.0f;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const float va = bf2f(x[4 * lane + i]), vb = bf2f(x[128 + 4 * lane + i]);
-    pa = __fadd_rn(pa, __fmul_rn(va, va));
-    pb = __fadd_rn(pb, __fmul_rn(vb, vb));
+    pa = __fadd_rn(pa, __fmul_rn(va[i], va[i]));
+    pb = __fadd_rn(pb, __fmul_rn(vb[i], vb[i]));
   }
   const float s0 = warp_sum(pa), s1 = warp_sum(pb);
   const float inv = drsqrtf(__fadd_rn(__fmul_rn(__fadd_rn(s0, s1), 0.00390625f), 1e-6f));
-  for (int d = lane; d < kHeadDim; d += 32)
-    nrm[d] = bfr(__fmul_rn(bfr(__fmul_rn(bf2f(x[d]), inv)), bf2f(gain[d])));
-  __syncwarp();
-  for (int d = lane; d < kHeadDim; d += 32) {
-    float v = nrm[d];
-    if (d < 64) {
-      const int pair = d & 31;
-      const float c = cs[2 * pair], s = cs[2 * pair + 1];
-      const float lo = nrm[pair], hi = nrm[pair + 32];
-      v = d < 32 ? bfr(__fsub_rn(__fmul_rn(lo, c), __fmul_rn(hi, s)))
-                 : bfr(__fadd_rn(__fmul_rn(lo, s), __fmul_rn(hi, c)));
-    }
-    out[d] = v;
+  float na[4], nb[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    na[i] = bfr(__fmul_rn(bfr(__fmul_rn(va[i], inv)), gA[i]));
+    nb[i] = bfr(__fmul_rn(bfr(__fmul_rn(vb[i], inv)), gB[i]));
   }
+  *reinterpret_cast<float4*>(nrm + 4 * lane) = make_float4(na[0], na[1], na[2], na[3]);
+  __syncwarp();
+  if (lane < 16) {  // partial RoPE on dims 0..63: pair p = d & 31 rotates (p, p + 32)
+    const float c[4] = {c0.x, c0.z, c1.x, c1.z}, sn[4] = {c0.y, c0.w, c1.y, c1.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int pair = 4 * (lane & 7) + i;
+      const float lo = nrm[pair], hi = nrm[pair + 32];
+      na[i] = lane < 8 ? bfr(__fsub_rn(__fmul_rn(lo, c[i]), __fmul_rn(hi, sn[i])))
+                       : bfr(__fadd_rn(__fmul_rn(lo, sn[i]), __fmul_rn(hi, c[i])));
+    }
+  }
+  *reinterpret_cast<float4*>(out + 4 * lane) = make_float4(na[0], na[1], na[2], na[3]);
+  *reinterpret_cast<float4*>(out + 128 + 4 * lane) = make_float4(nb[0], nb[1], nb[2], nb[3]);
   __syncwarp();
 }
 
@@ -508,7 +532,23 @@ __device__ __forceinline__ void attn_time_end(Ctl* ctl) {
   }
 }
 
-__global__ void __launch_bounds__(kAttnThreads, 2) k_attn(const __grid_constant__ AttnArgs a) {
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Warp roles, linked only by full/empty mbarrier pairs (every wait bounded):
+//   warps 0-7   score: keys 4w..4w+3 of each tile for the four query heads
+//   warps 8-11  scan: one query head each; running max as a prefix scan,
+//               then the factors f and weights e of the tile's keys
+//   warps 12-15 recurrence: lane l of warp r owns dims 64r + 2l, +1 of all
+//               four heads, so each V element is unpacked once for 4 heads
+//   warp 16     K producer, warp 17 V producer (one bulk copy per tile)
+// The current token's key/value (written to the cache by this kernel) are
+// read from their staging copies kf/vf, never from the ring.
+constexpr int kAttnScoreWarps = 8, kAttnScanWarp0 = 8, kAttnRecWarp0 = 12;
+constexpr int kAttnKProdWarp = 16, kAttnVProdWarp = 17;
+
+__global__ void __launch_bounds__(kAttnThreads, 1) k_attn(const __grid_constant__ AttnArgs a) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   AttnSmem& S = *reinterpret_cast<AttnSmem*>(smem_raw);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -531,34 +571,46 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attn(const __grid_constant_
   const uint16_t* vbase = a.vcache + size_t(kh) * cap * kHeadDim;
   auto row_of = [&](int j) { return split ? j : ((j & 1) << 4) + (j >> 1); };
   // the current token is key `pos`: chain pos % stride, local index pos / stride
+  // (the chain's last key)
   const bool owner = chain == int(pos % stride);
   const int own_idx = int(pos / stride);
+  const int own_t = owner ? own_idx / kAttnTile : -1, own_j = own_idx % kAttnTile;
 
-  auto issue = [&](int t, int st) {  // one thread
+  auto issue = [&](const uint16_t* base, uint16_t (*ring)[kHeadDim], uint64_t* bar, int t) {
     const int n = min(kAttnTile, nkeys - t * kAttnTile);
-    mbar_expect_tx(&S.bar[st], uint32_t(n) * 2 * kHeadDim * 2);
+    mbar_expect_tx(bar, uint32_t(n) * kHeadDim * 2);
     if (split) {
       const size_t off = (size_t(chain) * cps + size_t(t) * kAttnTile) * kHeadDim;
-      bulk_g2s(&S.kt[st][0][0], kbase + off, uint32_t(n) * kHeadDim * 2, &S.bar[st]);
-      bulk_g2s(&S.vt[st][0][0], vbase + off, uint32_t(n) * kHeadDim * 2, &S.bar[st]);
+      bulk_g2s(&ring[0][0], base + off, uint32_t(n) * kHeadDim * 2, bar);
     } else {
       const int na = (n + 1) >> 1, nb = n >> 1;
-      const size_t oa = size_t(chain) * cps * kHeadDim, ob = size_t(chain + 32) * cps * kHeadDim;
-      bulk_g2s(&S.kt[st][0][0], kbase + oa, uint32_t(na) * kHeadDim * 2, &S.bar[st]);
-      bulk_g2s(&S.vt[st][0][0], vbase + oa, uint32_t(na) * kHeadDim * 2, &S.bar[st]);
-      if (nb > 0) {
-        bulk_g2s(&S.kt[st][16][0], kbase + ob, uint32_t(nb) * kHeadDim * 2, &S.bar[st]);
-        bulk_g2s(&S.vt[st][16][0], vbase + ob, uint32_t(nb) * kHeadDim * 2, &S.bar[st]);
-      }
+      bulk_g2s(&ring[0][0], base + size_t(chain) * cps * kHeadDim, uint32_t(na) * kHeadDim * 2, bar);
+      if (nb > 0)
+        bulk_g2s(&ring[16][0], base + size_t(chain + 32) * cps * kHeadDim, uint32_t(nb) * kHeadDim * 2,
+                 bar);
     }
   };
   if (tid == 0) {
-    for (int s = 0; s < kAttnStages; ++s) mbar_init(&S.bar[s], 1);
+    for (int s = 0; s < kAttnStages; ++s) {
+      mbar_init(&S.kfull[s], 1);
+      mbar_init(&S.kempty[s], kAttnScoreWarps);
+      mbar_init(&S.vfull[s], 1);
+      mbar_init(&S.vempty[s], 4);
+    }
+    for (int b = 0; b < kAttnBufs; ++b) {
+      mbar_init(&S.scfull[b], kAttnScoreWarps);
+      mbar_init(&S.scempty[b], 4);
+      mbar_init(&S.fefull[b], 4);
+      mbar_init(&S.feempty[b], 4);
+    }
     fence_mbar_init();
   }
   __syncthreads();
-  if (tid == 0)
-    for (int t = 0; t < kAttnStages && t < ntiles; ++t) issue(t, t);
+  const bool kprod = warp == kAttnKProdWarp && lane == 0, vprod = warp == kAttnVProdWarp && lane == 0;
+  if (kprod)
+    for (int t = 0; t < kAttnStages && t < ntiles; ++t) issue(kbase, S.kt[t], &S.kfull[t], t);
+  if (vprod)
+    for (int t = 0; t < kAttnStages && t < ntiles; ++t) issue(vbase, S.vt[t], &S.vfull[t], t);
   pdl_wait();
   pdl_launch();
   if (tid == 0) attn_time_start(a.ctl);
@@ -570,52 +622,40 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attn(const __grid_constant_
     head_norm_rope(a.q_raw + qh * 512, a.q_gain, a.ctl->rope_cs, S.nrm[warp], S.q[warp], lane);
     for (int d = lane; d < kHeadDim; d += 32) S.q[warp][d] = __fmul_rn(0.0625f, S.q[warp][d]);
   } else if (warp == 4) {
+    const uint4 vr = *reinterpret_cast<const uint4*>(a.v_raw + kh * kHeadDim + 8 * lane);
     head_norm_rope(a.k_raw + kh * kHeadDim, a.k_gain, a.ctl->rope_cs, S.nrm[4], S.kr, lane);
-    for (int d = lane; d < kHeadDim; d += 32) {
-      S.kf[d] = f2bf(S.kr[d]);
-      S.vf[d] = a.v_raw[kh * kHeadDim + d];
-    }
-    __syncwarp();
+    const float* kr8 = S.kr + 8 * lane;
+    const uint4 kb = make_uint4(pack_bf2(kr8[0], kr8[1]), pack_bf2(kr8[2], kr8[3]),
+                                pack_bf2(kr8[4], kr8[5]), pack_bf2(kr8[6], kr8[7]));
+    *reinterpret_cast<uint4*>(S.kf + 8 * lane) = kb;
+    *reinterpret_cast<uint4*>(S.vf + 8 * lane) = vr;
     if (owner) {
       const size_t ci = (size_t(kh) * cap + size_t(pos % kAttnChains) * cps + pos / kAttnChains) * kHeadDim;
-      for (int d = lane; d < kHeadDim; d += 32) {
-        a.kcache[ci + d] = S.kf[d];
-        a.vcache[ci + d] = S.vf[d];
-      }
+      *reinterpret_cast<uint4*>(a.kcache + ci + 8 * lane) = kb;
+      *reinterpret_cast<uint4*>(a.vcache + ci + 8 * lane) = vr;
     }
+    __syncwarp();
   }
   __syncthreads();
 
-  // score lanes: lane l owns dims 8l..8l+7 of every head (as the reference).
-  float qreg[4][8];
+  const size_t pbase = (size_t(kh) * kAttnChains + chain) * 4;  // + head
+  if (warp < kAttnScoreWarps) {
+    // ---------------- score warps ----------------
+    // lane l owns dims 8l..8l+7 of every head (as the reference).
+    float qreg[4][8];
 #pragma unroll
-  for (int h = 0; h < 4; ++h)
+    for (int h = 0; h < 4; ++h)
 #pragma unroll
-    for (int e = 0; e < 8; ++e) qreg[h][e] = S.q[h][8 * lane + e];
-  // recurrence lanes: warp w -> head w>>1, dims (w&1)*128 + 4*lane .. +3.
-  const int rh = warp >> 1, d0 = (warp & 1) * 128 + 4 * lane;
-  float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-  float msum = kMin, ssum = 0.0f;
-
-  for (int t = 0; t < ntiles; ++t) {
-    const int st = t % kAttnStages;
-    mbar_wait(&S.bar[st], uint32_t(t / kAttnStages) & 1u, a.ctl, kErrAttnWait);
-    const int nk = min(kAttnTile, nkeys - t * kAttnTile);
-    if (owner && own_idx / kAttnTile == t) {
-      __syncthreads();
-      if (warp == 0)
-        for (int d = lane; d < kHeadDim; d += 32) {
-          S.kt[st][row_of(own_idx % kAttnTile)][d] = S.kf[d];
-          S.vt[st][row_of(own_idx % kAttnTile)][d] = S.vf[d];
-        }
-      __syncthreads();
-    }
-    // scores: warp w takes keys 4w..4w+3 of the tile for the four heads
-    {
+      for (int e = 0; e < 8; ++e) qreg[h][e] = S.q[h][8 * lane + e];
+    for (int t = 0; t < ntiles; ++t) {
+      const int st = t % kAttnStages, sb = t % kAttnBufs;
+      mbar_wait(&S.kfull[st], uint32_t(t / kAttnStages) & 1u, a.ctl, kErrAttnWait);
       float v[16];
 #pragma unroll
       for (int jj = 0; jj < 4; ++jj) {
-        const uint4 kv = *reinterpret_cast<const uint4*>(&S.kt[st][row_of(4 * warp + jj)][8 * lane]);
+        const int j = 4 * warp + jj;
+        const uint16_t* krow = (t == own_t && j == own_j) ? S.kf : S.kt[st][row_of(j)];
+        const uint4 kv = *reinterpret_cast<const uint4*>(krow + 8 * lane);
         const float k8[8] = {bf_lo(kv.x), bf_hi(kv.x), bf_lo(kv.y), bf_hi(kv.y),
                              bf_lo(kv.z), bf_hi(kv.z), bf_lo(kv.w), bf_hi(kv.w)};
 #pragma unroll
@@ -626,13 +666,26 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attn(const __grid_constant_
           v[h * 4 + jj] = sc;
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.kempty[st]);
       const float r = reduce16(v, lane);
-      if ((lane & 1) == 0) S.sc[lane >> 3][4 * warp + ((lane >> 1) & 3)] = r;
+      if (t >= kAttnBufs)
+        mbar_wait(&S.scempty[sb], uint32_t(t / kAttnBufs - 1) & 1u, a.ctl, kErrAttnWait);
+      if ((lane & 1) == 0) S.sc[sb][lane >> 3][4 * warp + ((lane >> 1) & 3)] = r;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.scfull[sb]);
     }
-    __syncthreads();
-    // running max as a prefix scan, then the independent exps
-    {
-      const float sv = lane < nk ? S.sc[rh][lane] : -INFINITY;
+  } else if (warp < kAttnRecWarp0) {
+    // ---------------- scan warps ----------------
+    const int h = warp - kAttnScanWarp0;
+    float msum = kMin;  // running max of head h
+    for (int t = 0; t < ntiles; ++t) {
+      const int sb = t % kAttnBufs;
+      const int nk = min(kAttnTile, nkeys - t * kAttnTile);
+      mbar_wait(&S.scfull[sb], uint32_t(t / kAttnBufs) & 1u, a.ctl, kErrAttnWait);
+      const float sv = lane < nk ? S.sc[sb][h][lane] : -INFINITY;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.scempty[sb]);
       float v = sv;
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
@@ -642,43 +695,114 @@ __global__ void __launch_bounds__(kAttnThreads, 2) k_attn(const __grid_constant_
       const float mt = fmaxf(msum, v);
       float mprev = __shfl_up_sync(0xffffffffu, mt, 1);
       if (lane == 0) mprev = msum;
-      S.fe[warp][lane] = make_float2(fexp(__fsub_rn(mprev, mt)), fexp(__fsub_rn(sv, mt)));
+      const float fj = fexp(__fsub_rn(mprev, mt)), ej = fexp(__fsub_rn(sv, mt));
+      const uint32_t fm = __ballot_sync(0xffffffffu, lane < nk && fj != 1.0f);
       msum = __shfl_sync(0xffffffffu, mt, nk - 1);
+      if (t >= kAttnBufs)
+        mbar_wait(&S.feempty[sb], uint32_t(t / kAttnBufs - 1) & 1u, a.ctl, kErrAttnWait);
+      reinterpret_cast<float*>(&S.f[sb][lane])[h] = fj;
+      reinterpret_cast<float*>(&S.e[sb][lane])[h] = ej;
+      if (lane == 0) S.fm[sb][h] = fm;
       __syncwarp();
-      // o = o*f + e*v key by key (attention_decode.metal:360-366)
-      for (int j = 0; j < nk; ++j) {
-        const float2 fe = S.fe[warp][j];
-        const uint2 vv = *reinterpret_cast<const uint2*>(&S.vt[st][row_of(j)][d0]);
-        if (fe.x != 1.0f) {  // o * 1 == o exactly
-          ssum = __fmul_rn(ssum, fe.x);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) o[i] = __fmul_rn(o[i], fe.x);
+      if (lane == 0) mbar_arrive(&S.fefull[sb]);
+    }
+    if (lane == 0) a.part_ml[(pbase + h) * 2] = msum;
+  } else if (warp < kAttnKProdWarp) {
+    // ---------------- recurrence warps ----------------
+    const int wr = warp - kAttnRecWarp0, d = 64 * wr + 2 * lane, hs = lane & 3;
+    float o[4][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}, {0.0f, 0.0f}, {0.0f, 0.0f}};
+    float ssum = 0.0f;  // running sum of head lane & 3
+    for (int t = 0; t < ntiles; ++t) {
+      const int st = t % kAttnStages, b = t % kAttnBufs;
+      const int nk = min(kAttnTile, nkeys - t * kAttnTile);
+      mbar_wait(&S.fefull[b], uint32_t(t / kAttnBufs) & 1u, a.ctl, kErrAttnWait);
+      mbar_wait(&S.vfull[st], uint32_t(t / kAttnStages) & 1u, a.ctl, kErrAttnWait);
+      const uint32_t fm = S.fm[b][0] | S.fm[b][1] | S.fm[b][2] | S.fm[b][3];
+      // S = S*f + e, o = o*f + e*v key by key (attention_decode.metal:357-366);
+      // keys whose four factors are all 1 skip the (exact) multiply by 1.
+#define Q35_ATTN_ACC(J, VV)                                          \
+  {                                                                  \
+    const float4 e4 = S.e[b][J];                                     \
+    const float es = reinterpret_cast<const float*>(&S.e[b][J])[hs]; \
+    const float v0 = bf_lo(VV), v1 = bf_hi(VV);                      \
+    ssum = __fadd_rn(ssum, es);                                      \
+    o[0][0] = __fadd_rn(o[0][0], __fmul_rn(e4.x, v0));               \
+    o[0][1] = __fadd_rn(o[0][1], __fmul_rn(e4.x, v1));               \
+    o[1][0] = __fadd_rn(o[1][0], __fmul_rn(e4.y, v0));               \
+    o[1][1] = __fadd_rn(o[1][1], __fmul_rn(e4.y, v1));               \
+    o[2][0] = __fadd_rn(o[2][0], __fmul_rn(e4.z, v0));               \
+    o[2][1] = __fadd_rn(o[2][1], __fmul_rn(e4.z, v1));               \
+    o[3][0] = __fadd_rn(o[3][0], __fmul_rn(e4.w, v0));               \
+    o[3][1] = __fadd_rn(o[3][1], __fmul_rn(e4.w, v1));               \
+  }
+#define Q35_ATTN_RESCALE(J)                                                     \
+  {                                                                             \
+    const float4 f4 = S.f[b][J];                                                \
+    ssum = __fmul_rn(ssum, reinterpret_cast<const float*>(&S.f[b][J])[hs]);     \
+    o[0][0] = __fmul_rn(o[0][0], f4.x);                                         \
+    o[0][1] = __fmul_rn(o[0][1], f4.x);                                         \
+    o[1][0] = __fmul_rn(o[1][0], f4.y);                                         \
+    o[1][1] = __fmul_rn(o[1][1], f4.y);                                         \
+    o[2][0] = __fmul_rn(o[2][0], f4.z);                                         \
+    o[2][1] = __fmul_rn(o[2][1], f4.z);                                         \
+    o[3][0] = __fmul_rn(o[3][0], f4.w);                                         \
+    o[3][1] = __fmul_rn(o[3][1], f4.w);                                         \
+  }
+      if (split && t != own_t) {
+        if (fm == 0) {
+#pragma unroll 8
+          for (int j = 0; j < nk; ++j) {
+            const uint32_t vv = *reinterpret_cast<const uint32_t*>(&S.vt[st][j][d]);
+            Q35_ATTN_ACC(j, vv)
+          }
+        } else {  // some factor differs from 1: multiply every key (x * 1 == x)
+#pragma unroll 8
+          for (int j = 0; j < nk; ++j) {
+            const uint32_t vv = *reinterpret_cast<const uint32_t*>(&S.vt[st][j][d]);
+            Q35_ATTN_RESCALE(j)
+            Q35_ATTN_ACC(j, vv)
+          }
         }
-        ssum = __fadd_rn(ssum, fe.y);
-        o[0] = __fadd_rn(o[0], __fmul_rn(fe.y, bf_lo(vv.x)));
-        o[1] = __fadd_rn(o[1], __fmul_rn(fe.y, bf_hi(vv.x)));
-        o[2] = __fadd_rn(o[2], __fmul_rn(fe.y, bf_lo(vv.y)));
-        o[3] = __fadd_rn(o[3], __fmul_rn(fe.y, bf_hi(vv.y)));
+      } else {
+        for (int j = 0; j < nk; ++j) {
+          if ((fm >> j) & 1u) Q35_ATTN_RESCALE(j)
+          const uint16_t* vrow = (t == own_t && j == own_j) ? S.vf : S.vt[st][row_of(j)];
+          const uint32_t vv = *reinterpret_cast<const uint32_t*>(vrow + d);
+          Q35_ATTN_ACC(j, vv)
+        }
+      }
+#undef Q35_ATTN_RESCALE
+#undef Q35_ATTN_ACC
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&S.vempty[st]);
+        mbar_arrive(&S.feempty[b]);
       }
     }
-    __syncthreads();
-    if (tid == 0 && t + kAttnStages < ntiles) {
-      fence_proxy_async();
-      issue(t + kAttnStages, st);
-    }
-  }
-
-  // chain partials (bf16-rounded on the split route, attention_decode.metal:428-430)
-  {
-    float* po = a.part_o + ((size_t(kh) * kAttnChains + chain) * 4 + rh) * kHeadDim;
+    // chain partials (bf16-rounded on the split route, attention_decode.metal:428-430)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) po[d0 + i] = split ? bfr(o[i]) : o[i];
-    if ((warp & 1) == 0 && lane == 0) {
-      float* pml = a.part_ml + ((size_t(kh) * kAttnChains + chain) * 4 + rh) * 2;
-      pml[0] = msum;
-      pml[1] = ssum;
+    for (int h = 0; h < 4; ++h) {
+      float* po = a.part_o + (pbase + h) * kHeadDim + d;
+      po[0] = split ? bfr(o[h][0]) : o[h][0];
+      po[1] = split ? bfr(o[h][1]) : o[h][1];
+    }
+    if (wr == 0 && lane < 4) a.part_ml[(pbase + lane) * 2 + 1] = ssum;
+  } else if (kprod) {
+    // ---------------- K producer ----------------
+    for (int t = kAttnStages; t < ntiles; ++t) {
+      const int st = t % kAttnStages;
+      mbar_wait(&S.kempty[st], uint32_t(t / kAttnStages - 1) & 1u, a.ctl, kErrAttnWait);
+      issue(kbase, S.kt[st], &S.kfull[st], t);
+    }
+  } else if (vprod) {
+    // ---------------- V producer ----------------
+    for (int t = kAttnStages; t < ntiles; ++t) {
+      const int st = t % kAttnStages;
+      mbar_wait(&S.vempty[st], uint32_t(t / kAttnStages - 1) & 1u, a.ctl, kErrAttnWait);
+      issue(vbase, S.vt[st], &S.vfull[st], t);
     }
   }
+  __syncwarp();  // producer warps: lane 0 rejoins its warp before the barrier
   __syncthreads();
   if (tid == 0) attn_time_end(a.ctl);
 }

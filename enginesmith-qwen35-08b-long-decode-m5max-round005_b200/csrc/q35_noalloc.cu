@@ -22,6 +22,7 @@
 // scratch's device address with cudaGetSymbolAddress and sets the kernels'
 // shared-memory limits. Make that first call before any stream capture on
 // the device.
+#include <cstdint>
 #include <cstdio>
 #include <mutex>
 
@@ -65,6 +66,12 @@ extern "C" int q35_op_attn_decode_noalloc(const uint16_t* q_raw, const uint16_t*
     put_err(err, err_len, "attn_decode_noalloc: null pointer argument");
     return Q35_EINVAL;
   }
+  for (const void* p : {(const void*)q_raw, (const void*)k_raw, (const void*)v_raw, (const void*)q_gain,
+                        (const void*)k_gain, (const void*)kcache, (const void*)vcache})
+    if (reinterpret_cast<uintptr_t>(p) % 16 != 0) {
+      put_err(err, err_len, "attn_decode_noalloc: inputs and caches must be 16-byte aligned");
+      return Q35_EINVAL;
+    }
   if (capacity == 0 || capacity % kAttnChains != 0) {
     put_err(err, err_len, "attn_decode_noalloc: capacity must be a positive multiple of 64");
     return Q35_EINVAL;

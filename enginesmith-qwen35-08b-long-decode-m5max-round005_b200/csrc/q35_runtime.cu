@@ -982,6 +982,9 @@ int q35_op_attn_decode(const uint16_t* q_raw, const uint16_t* k_raw, const uint1
   if (!q_raw || !k_raw || !v_raw || !q_gain || !k_gain || !kcache || !vcache || !gated ||
       !workspace || capacity == 0 || capacity % kAttnChains != 0 || pos >= capacity)
     return Q35_EINVAL;
+  for (const void* p : {(const void*)q_raw, (const void*)k_raw, (const void*)v_raw, (const void*)q_gain,
+                        (const void*)k_gain, (const void*)kcache, (const void*)vcache})
+    if (reinterpret_cast<uintptr_t>(p) % 16 != 0) return Q35_EINVAL;
   if (ensure_kernels_init() != cudaSuccess) return Q35_ECUDA;
   cudaStream_t st = (cudaStream_t)stream;
   uint8_t* ws = (uint8_t*)workspace;

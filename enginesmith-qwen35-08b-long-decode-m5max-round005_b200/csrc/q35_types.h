@@ -25,8 +25,9 @@ constexpr uint32_t kDefaultCapacity = 262144;  // model.rs:8
 // 64 from 1024 on).
 constexpr int kAttnChains = 64;
 constexpr int kAttnTile = 32;   // keys of one chain per ring stage
-constexpr int kAttnStages = 3;
-constexpr int kAttnThreads = 256;
+constexpr int kAttnStages = 4;   // K and V ring depth (tiles)
+constexpr int kAttnThreads = 576; // 8 score, 4 scan, 4 recurrence, 2 producer warps
+constexpr int kAttnBufs = 4;      // score and f/e hand-off buffers between warp roles
 
 // Head (vocabulary projection + greedy) geometry.
 constexpr int kHeadRowsPerChunk = 32;

@@ -148,7 +148,8 @@ int q35_op_gdn_step(const uint16_t* raw_qkv, const uint16_t* z, const uint16_t* 
  * chain-major bf16 [2 kv heads][64][capacity/64][256]: position p of a kv
  * head lives at chain p % 64, slot p / 64 (capacity a multiple of 64,
  * pos < capacity), so each of the reference's 64 key blocks (keys b, b+64,
- * ...) is contiguous. */
+ * ...) is contiguous. q_raw, k_raw, v_raw, the gains and both caches must be
+ * 16-byte aligned (Q35_EINVAL otherwise). */
 size_t q35_op_attn_workspace_bytes(void);
 int q35_op_attn_decode(const uint16_t* q_raw, const uint16_t* k_raw, const uint16_t* v_raw,
                        const uint16_t* q_gain, const uint16_t* k_gain, uint16_t* kcache,
