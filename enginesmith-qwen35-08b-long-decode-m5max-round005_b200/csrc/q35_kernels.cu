@@ -1142,33 +1142,55 @@ static cudaError_t launch_ex(void (*kern)(Arg), dim3 grid, dim3 block, size_t sm
   return cudaLaunchKernelEx(&cfg, kern, arg);
 }
 
+// Dynamic shared memory requested by every kernel of the decode step: more
+// than half an SM's 228 KB, so one CTA fits per SM and every kernel's
+// 128-148 CTAs land on distinct SMs. With room for two or more, the block
+// scheduler packed a kernel launched early (programmatic launch) three or
+// four CTAs to an SM onto the SMs its predecessor left free (measured: 144
+// CTAs on 39 SMs), multiplying that kernel's time; one CTA per SM costs only
+// the overlap of a CTA's weight prefetch with the predecessor on that SM.
+constexpr size_t kSpreadSmem = 115 * 1024;
+static size_t spread(size_t bytes) { return bytes < kSpreadSmem ? kSpreadSmem : bytes; }
+
 cudaError_t kernels_init() {
   cudaError_t e;
-  e = cudaFuncSetAttribute(k_qmv, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+  e = cudaFuncSetAttribute(k_qmv, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSpreadSmem));
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(k_attn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           int(attn_smem_bytes()));
+                           int(spread(attn_smem_bytes())));
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(k_head, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           int(head_smem_bytes()));
+                           int(spread(head_smem_bytes())));
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(k_gdn_recur, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           int(kSpreadSmem));
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(k_attn_combine, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           int(kSpreadSmem));
   return e;
+}
+
+int qmv_max_rows(int K) {
+  int r = 1;  // the epilogue gives each CTA row its own thread
+  while (r < kQmvThreads && qmv_layout(K, r + 1).total <= kSpreadSmem) ++r;
+  return r;
 }
 
 cudaError_t launch_qmv(const QmvArgs& a, cudaStream_t st, bool pdl) {
   const int grid = (a.units + a.units_per_cta - 1) / a.units_per_cta;
-  return launch_ex(k_qmv, dim3(grid), dim3(kQmvThreads), qmv_smem_bytes(a), st, pdl, a);
+  return launch_ex(k_qmv, dim3(grid), dim3(kQmvThreads), spread(qmv_smem_bytes(a)), st, pdl, a);
 }
 cudaError_t launch_recur(const RecurArgs& a, cudaStream_t st, bool pdl) {
-  return launch_ex(k_gdn_recur, dim3(8, kGdnHeads), dim3(64), 0, st, pdl, a);
+  return launch_ex(k_gdn_recur, dim3(8, kGdnHeads), dim3(64), kSpreadSmem, st, pdl, a);
 }
 cudaError_t launch_attn(const AttnArgs& a, cudaStream_t st, bool pdl) {
   cudaError_t e = launch_ex(k_attn, dim3(kAttnChains, kKvHeads), dim3(kAttnThreads),
-                            attn_smem_bytes(), st, pdl, a);
+                            spread(attn_smem_bytes()), st, pdl, a);
   if (e != cudaSuccess) return e;
-  return launch_ex(k_attn_combine, dim3(kQHeads, kHeadDim / 32), dim3(128), 0, st, true, a);
+  return launch_ex(k_attn_combine, dim3(kQHeads, kHeadDim / 32), dim3(128), kSpreadSmem, st, true, a);
 }
 cudaError_t launch_head(const HeadArgs& a, cudaStream_t st, bool pdl) {
-  return launch_ex(k_head, dim3(kHeadCtas), dim3(256), head_smem_bytes(), st, pdl, a);
+  return launch_ex(k_head, dim3(kHeadCtas), dim3(256), spread(head_smem_bytes()), st, pdl, a);
 }
 cudaError_t launch_greedy(const HeadArgs& a, cudaStream_t st) {
   return launch_ex(k_greedy, dim3(kHeadCtas), dim3(256), 0, st, false, a);

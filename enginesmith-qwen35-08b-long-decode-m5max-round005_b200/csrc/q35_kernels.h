@@ -8,6 +8,8 @@
 namespace q35 {
 
 cudaError_t kernels_init();
+// Largest rows-per-CTA whose k_qmv shared-memory layout fits one CTA per SM.
+int qmv_max_rows(int K);
 size_t qmv_smem_bytes(const QmvArgs& a);
 size_t attn_smem_bytes();
 size_t head_smem_bytes();

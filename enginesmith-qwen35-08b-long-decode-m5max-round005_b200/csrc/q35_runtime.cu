@@ -899,8 +899,7 @@ int q35_op_qmv_q4(const uint32_t* w, const uint16_t* scales, const uint16_t* bia
   a.K = k;
   a.units = n;
   int upc = (n + 147) / 148;
-  const int max_rows = (64 * 1024) / (k / 2 + k / 16);
-  upc = std::max(1, std::min(upc, max_rows));
+  upc = std::max(1, std::min(upc, qmv_max_rows(k)));
   a.units_per_cta = upc;
   a.pro = kProPlain;
   a.x = x;
