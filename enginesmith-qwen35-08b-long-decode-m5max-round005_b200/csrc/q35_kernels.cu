@@ -990,15 +990,16 @@ struct HeadSmem {
   float pl[kHeadRowsPerChunk * 2 * 32];
   float vals[kHeadRowsPerChunk];
   float red[64];
-  float wm[8], ws[8];
+  float wm[kHeadThreads / 32], ws[kHeadThreads / 32];
   uint64_t bar[kHeadStages];
+  uint32_t done[kHeadStages];  // warps finished with each ring stage
   int last;
   uint32_t cand;
   uint32_t best;
 };
 size_t head_smem_bytes() { return sizeof(HeadSmem); }
 
-__global__ void __launch_bounds__(256) k_head(const __grid_constant__ HeadArgs a) {
+__global__ void __launch_bounds__(kHeadThreads, 1) k_head(const __grid_constant__ HeadArgs a) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   HeadSmem& S = *reinterpret_cast<HeadSmem*>(smem_raw);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -1014,58 +1015,87 @@ __global__ void __launch_bounds__(256) k_head(const __grid_constant__ HeadArgs a
     bulk_g2s(S.bia[st], a.b + row * 16, uint32_t(rows) * 32, &S.bar[st]);
   };
   if (tid == 0) {
-    for (int s = 0; s < kHeadStages; ++s) mbar_init(&S.bar[s], 1);
+    for (int s = 0; s < kHeadStages; ++s) {
+      mbar_init(&S.bar[s], 1);
+      S.done[s] = 0;
+    }
     fence_mbar_init();
   }
   __syncthreads();
   if (tid == 0)
     for (int s = 0; s < kHeadStages && s < nchunks; ++s) issue(s, s);
+  const bool holder = tid < kHidden / 4;  // threads 0-255 hold four activations each
+  float g[4] = {1.f, 1.f, 1.f, 1.f};
+  if (a.gain && holder) {
+    const float4 g4 = bf4(*reinterpret_cast<const uint2*>(a.gain + 4 * tid));
+    g[0] = g4.x, g[1] = g4.y, g[2] = g4.z, g[3] = g4.w;
+  }
   pdl_wait();
   pdl_launch();
   {
-    float v[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) v[j] = bf2f(a.x[4 * tid + j]);
-    if (a.gain) {
-      rms1024(v, a.gain, S.xf, S.red);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) S.xf[4 * tid + j] = v[j];
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (holder) {
+      const float4 x4 = bf4(*reinterpret_cast<const uint2*>(a.x + 4 * tid));
+      v[0] = x4.x, v[1] = x4.y, v[2] = x4.z, v[3] = x4.w;
     }
+    if (a.gain) {
+      float o[4];
+      rms1024_reg(v, g, o, S.red);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = o[j];
+    }
+    if (holder) *reinterpret_cast<float4*>(S.xf + 4 * tid) = make_float4(v[0], v[1], v[2], v[3]);
   }
   __syncthreads();
   build_xq(S.xf, kHidden, S.xq, S.xsum);
   __syncthreads();
+  // the lane's constants of both 512-wide halves stay in registers
+  float4 xx0[4], cc0[4], xx1[4], cc1[4];
+  float xs0, xs1;
+  load_xq(S.xq, S.xsum, 0, lane, xx0, cc0, xs0);
+  load_xq(S.xq, S.xsum, 1, lane, xx1, cc1, xs1);
 
-  float run_m = -INFINITY, run_s = 0.0f;  // per-thread online LSE over its logits
+  // Warp w owns rows 4w..4w+3 of every chunk: both 512-wide halves,
+  // the cross-lane finish and the logits, with no block barrier. The last
+  // warp done with a ring stage refills it. Lanes 0-3 keep the online
+  // (max, sum exp) of their row.
+  float run_m = -INFINITY, run_s = 0.0f;
+  const int g0 = 4 * warp;
   for (int ch = 0; ch < nchunks; ++ch) {
     const int st = ch % kHeadStages;
     mbar_wait(&S.bar[st], uint32_t(ch / kHeadStages) & 1u, a.ctl, kErrHeadWait);
     const int rows = min(kHeadRowsPerChunk, nrows - ch * kHeadRowsPerChunk);
-    for (int task = warp; task < 16; task += 8) {
-      const int g = task >> 1, c = task & 1;
-      if (4 * g < rows)
-        qmv_chunk_task(S.codes[st], S.scl[st], S.bia[st], rows, 4 * g, c, kHidden, S.xq, S.xsum,
-                       S.pl, lane);
+    if (g0 < rows) {
+      qmv_chunk_core(S.codes[st], S.scl[st], S.bia[st], rows, g0, 0, kHidden, xx0, cc0, xs0, S.pl, lane);
+      qmv_chunk_core(S.codes[st], S.scl[st], S.bia[st], rows, g0, 1, kHidden, xx1, cc1, xs1, S.pl, lane);
     }
-    __syncthreads();
-    if (4 * warp < rows) qmv_finish_task(S.pl, rows, 4 * warp, 2, S.vals, lane);
-    __syncthreads();
-    if (tid < rows) {
-      const uint16_t lb = f2bf(S.vals[tid]);
-      a.logits[r0 + ch * kHeadRowsPerChunk + tid] = lb;
-      const float lv = bf2f(lb);
-      if (lv > run_m) {
-        run_s = run_s * __expf(run_m - lv) + 1.0f;
-        run_m = lv;
-      } else {
-        run_s += __expf(lv - run_m);
+    __syncwarp();
+    if (lane == 0) {
+      __threadfence_block();
+      if (atomicAdd(&S.done[st], 1u) == uint32_t(kHeadThreads / 32 - 1)) {
+        S.done[st] = 0;
+        if (ch + kHeadStages < nchunks) {
+          fence_proxy_async();
+          issue(ch + kHeadStages, st);
+        }
       }
     }
-    if (tid == 0 && ch + kHeadStages < nchunks) {
-      fence_proxy_async();
-      issue(ch + kHeadStages, st);
+    if (g0 < rows) {
+      qmv_finish_task(S.pl, rows, g0, 2, S.vals, lane);
+      __syncwarp();
+      if (lane < 4 && g0 + lane < rows) {
+        const uint16_t lb = f2bf(S.vals[g0 + lane]);
+        a.logits[r0 + ch * kHeadRowsPerChunk + g0 + lane] = lb;
+        const float lv = bf2f(lb);
+        if (lv > run_m) {
+          run_s = run_s * __expf(run_m - lv) + 1.0f;
+          run_m = lv;
+        } else {
+          run_s += __expf(lv - run_m);
+        }
+      }
     }
+    __syncwarp();
   }
   head_partial(a, run_m, run_s, S.wm, S.ws, &S.last);
   if (!S.last) return;
@@ -1190,7 +1220,7 @@ cudaError_t launch_attn(const AttnArgs& a, cudaStream_t st, bool pdl) {
   return launch_ex(k_attn_combine, dim3(kQHeads, kHeadDim / 32), dim3(128), kSpreadSmem, st, true, a);
 }
 cudaError_t launch_head(const HeadArgs& a, cudaStream_t st, bool pdl) {
-  return launch_ex(k_head, dim3(kHeadCtas), dim3(256), spread(head_smem_bytes()), st, pdl, a);
+  return launch_ex(k_head, dim3(kHeadCtas), dim3(kHeadThreads), spread(head_smem_bytes()), st, pdl, a);
 }
 cudaError_t launch_greedy(const HeadArgs& a, cudaStream_t st) {
   return launch_ex(k_greedy, dim3(kHeadCtas), dim3(256), 0, st, false, a);

@@ -85,20 +85,13 @@ Q35_DEV float half_dot(uint32_t u, const float4& xx, const float4& cc) {
   return __fadd_rn(__fadd_rn(__fadd_rn(t0, t1), t2), t3);
 }
 
-// One warp task: rows [r0, r0+4) (those < nrows) of the CTA's smem image,
-// chunk c (512 wide). Writes each lane's chunk term s*dotq + xs*b to
-// pl[(row * nch + c) * 32 + lane].
-Q35_DEV void qmv_chunk_task(const uint32_t* codes, const uint16_t* scl, const uint16_t* bia,
-                            int nrows, int r0, int c, int K, const float4* xq, const float* xsum,
-                            float* pl, int lane) {
+// One warp task with the lane's chunk constants in registers: rows
+// [r0, r0+4) (those < nrows) of the CTA's smem image, chunk c (512 wide).
+// Writes each lane's chunk term s*dotq + xs*b to pl[(row * nch + c) * 32 + lane].
+Q35_DEV void qmv_chunk_core(const uint32_t* codes, const uint16_t* scl, const uint16_t* bia,
+                            int nrows, int r0, int c, int K, const float4 (&xx)[4],
+                            const float4 (&cc)[4], float xs, float* pl, int lane) {
   const int KW = K / 8, KG = K / 64, nch = K / 512;
-  float4 xx[4], cc[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    xx[i] = xq[(size_t(c) * 8 + i) * 32 + lane];
-    cc[i] = xq[(size_t(c) * 8 + 4 + i) * 32 + lane];
-  }
-  const float xs = xsum[c * 32 + lane];
   const int w0 = 64 * c + 2 * lane;
   const int g = 8 * c + (lane >> 2);
   uint2 q[4];
@@ -120,6 +113,27 @@ Q35_DEV void qmv_chunk_task(const uint32_t* codes, const uint16_t* scl, const ui
     const float term = __fadd_rn(__fmul_rn(sc[r], dotq), __fmul_rn(xs, bi[r]));
     if (r0 + r < nrows) pl[(size_t(r0 + r) * nch + c) * 32 + lane] = term;
   }
+}
+
+// The lane's constants of chunk c from the shared image built by build_xq.
+Q35_DEV void load_xq(const float4* xq, const float* xsum, int c, int lane, float4 (&xx)[4],
+                     float4 (&cc)[4], float& xs) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    xx[i] = xq[(size_t(c) * 8 + i) * 32 + lane];
+    cc[i] = xq[(size_t(c) * 8 + 4 + i) * 32 + lane];
+  }
+  xs = xsum[c * 32 + lane];
+}
+
+// One warp task reading the chunk constants from shared memory.
+Q35_DEV void qmv_chunk_task(const uint32_t* codes, const uint16_t* scl, const uint16_t* bia,
+                            int nrows, int r0, int c, int K, const float4* xq, const float* xsum,
+                            float* pl, int lane) {
+  float4 xx[4], cc[4];
+  float xs;
+  load_xq(xq, xsum, c, lane, xx, cc, xs);
+  qmv_chunk_core(codes, scl, bia, nrows, r0, c, K, xx, cc, xs, pl, lane);
 }
 
 // Transpose-reduce four per-lane values with the pairing of an xor butterfly

@@ -30,10 +30,11 @@ constexpr int kAttnThreads = 576; // 8 score, 4 scan, 4 recurrence, 2 producer w
 constexpr int kAttnBufs = 4;      // score and f/e hand-off buffers between warp roles
 
 // Head (vocabulary projection + greedy) geometry.
-constexpr int kHeadRowsPerChunk = 32;
-constexpr int kHeadChunksPerCta = 53;
-constexpr int kHeadRowsPerCta = kHeadRowsPerChunk * kHeadChunksPerCta;  // 1696
-constexpr int kHeadCtas = (kVocab + kHeadRowsPerCta - 1) / kHeadRowsPerCta;  // 147
+constexpr int kHeadThreads = 384;                      // 12 warps, 4 rows each per chunk
+constexpr int kHeadRowsPerChunk = 4 * kHeadThreads / 32;  // 48
+constexpr int kHeadChunksPerCta = 35;
+constexpr int kHeadRowsPerCta = kHeadRowsPerChunk * kHeadChunksPerCta;  // 1680
+constexpr int kHeadCtas = (kVocab + kHeadRowsPerCta - 1) / kHeadRowsPerCta;  // 148
 constexpr int kHeadStages = 4;
 
 // Device-resident control block of one decode session (or one op call).

@@ -1,6 +1,6 @@
 """Op-level benchmarks of the q35 kernels on the BASELINE.json configs 1-3.
 
-  python -m q35.opbench --op qmv|gdn|attn [--len N] [--iters K] [--copies R]
+  python -m q35.opbench --op qmv|gdn|attn|head [--len N] [--iters K] [--copies R]
 
 Each call works on a fresh copy of its big operands (weights, recurrent
 state, or K/V cache), rotating over enough copies that the working set is
@@ -28,7 +28,7 @@ def main():
     import inputs as I
 
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", choices=["qmv", "gdn", "attn"], required=True)
+    ap.add_argument("--op", choices=["qmv", "gdn", "attn", "head"], required=True)
     ap.add_argument("--len", type=int, default=32768)
     ap.add_argument("--iters", type=int, default=200)
     ap.add_argument("--copies", type=int, default=0)
@@ -67,6 +67,21 @@ def main():
         def call(i):
             q35.gdn_step(ins["raw"], ins["z"], ins["a"], ins["b"], hist, ins["conv_w"], ins["a_log"], ins["dt"],
                          st[i % copies], ins["norm_w"], ins["ow"], ins["os"], ins["ob"], residual=ins["res"], ws=ws)
+    elif args.op == "head":
+        # tied-embedding head of the vocabulary: [248320][1024] Q4, final norm gain, x
+        copies = args.copies or 2
+        g = torch.Generator(device=dev).manual_seed(5)
+        W = torch.randint(-2**31, 2**31 - 1, (copies, q35.VOCAB, 128), dtype=torch.int32, device=dev, generator=g)
+        rs = I.Rng(5, 9)
+        sc = T(np.full((q35.VOCAB, 16), I.f2bf(np.array([0.004], np.float32))[0], np.uint16))
+        bi = T(I.f2bf(rs.normal(q35.VOCAB * 16, 0.03)).reshape(q35.VOCAB, 16))
+        x = T(I.f2bf(rs.normal(1024)))
+        gain = T(I.f2bf(1.0 + rs.normal(1024, 0.02)))
+        ws = q35.workspace("head")
+        nbytes = q35.VOCAB * (512 + 64) + q35.VOCAB * 2
+
+        def call(i):
+            q35.head_argmax(W[i % copies], sc, bi, x, gain, ws=ws)
     else:
         d = I.config3(2, args.len)
         per = d["kc"].nbytes * 2
