@@ -96,9 +96,9 @@ __device__ __forceinline__ void rope_pair(uint32_t position, int pair, float* cs
 
 // 256 threads and <= 64 registers: up to four CTAs (of consecutive launches)
 // share an SM, so a launch's weight prefetch overlaps its predecessor.
-constexpr int kQmvThreads = 256;
+constexpr int kQmvThreads = 512;
 
-__global__ void __launch_bounds__(kQmvThreads, 4) k_qmv(const __grid_constant__ QmvArgs a) {
+__global__ void __launch_bounds__(kQmvThreads, 1) k_qmv(const __grid_constant__ QmvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int kWarps = kQmvThreads / 32;
@@ -177,6 +177,24 @@ __global__ void __launch_bounds__(kQmvThreads, 4) k_qmv(const __grid_constant__ 
     gain4[3] = bf_hi(g.y);
   }
 
+  // Norm-gate prologue: z (written two launches back) and the norm weight are
+  // ready, so the gate factor z * sigmoid(z) of head `warp` is formed before
+  // the wait; only the RMS of y waits for the recurrence.
+  static_assert(kQmvThreads / 32 >= kGdnHeads, "one warp per GDN head");
+  float ng_zs[4] = {0.f, 0.f, 0.f, 0.f}, ng_w[4] = {0.f, 0.f, 0.f, 0.f};
+  if (a.pro == kProNormGate && warp < kGdnHeads) {
+    const float4 z4 = bf4(*reinterpret_cast<const uint2*>(a.gz + warp * 128 + 4 * lane));
+    const float4 w4 = bf4(*reinterpret_cast<const uint2*>(a.gw + 4 * lane));
+    const float z[4] = {z4.x, z4.y, z4.z, z4.w};
+    ng_w[0] = w4.x, ng_w[1] = w4.y, ng_w[2] = w4.z, ng_w[3] = w4.w;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float sy = __fdiv_rn(1.0f, __fadd_rn(1.0f, dexpf(fabsf(z[i]))));
+      const float sig = z[i] < 0.0f ? sy : __fsub_rn(1.0f, sy);
+      ng_zs[i] = __fmul_rn(z[i], sig);
+    }
+  }
+
   // 2. Activations: every prologue leaves thread t with the group of four
   //    activations k = 4t .. 4t+3 and emits its matvec constants.
   pdl_wait();
@@ -236,13 +254,9 @@ __global__ void __launch_bounds__(kQmvThreads, 4) k_qmv(const __grid_constant__ 
     float o[4];
     rms1024_reg(v, gain4, o, red);
     emit_xq(tid, tid < 256, make_float4(o[0], o[1], o[2], o[3]), xq, xsum);
-  } else {  // kProNormGate: gdn.metal:238-254, warp w -> heads w, w + 8
-    for (int hh = warp; hh < kGdnHeads; hh += kWarps) {
-    const float4 v4 = bf4(*reinterpret_cast<const uint2*>(a.gy + hh * 128 + 4 * lane));
-    const float4 z4 = bf4(*reinterpret_cast<const uint2*>(a.gz + hh * 128 + 4 * lane));
-    const float4 w4 = bf4(*reinterpret_cast<const uint2*>(a.gw + 4 * lane));
-    const float v[4] = {v4.x, v4.y, v4.z, v4.w}, z[4] = {z4.x, z4.y, z4.z, z4.w};
-    const float w[4] = {w4.x, w4.y, w4.z, w4.w};
+  } else if (warp < kGdnHeads) {  // kProNormGate: gdn.metal:238-254, warp w -> head w
+    const float4 v4 = bf4(*reinterpret_cast<const uint2*>(a.gy + warp * 128 + 4 * lane));
+    const float v[4] = {v4.x, v4.y, v4.z, v4.w};
     float ss = 0.0f;
 #pragma unroll
     for (int i = 0; i < 4; ++i) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
@@ -251,13 +265,10 @@ __global__ void __launch_bounds__(kQmvThreads, 4) k_qmv(const __grid_constant__ 
     float o[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const float norm = bfr(__fmul_rn(bfr(__fmul_rn(v[i], inv)), w[i]));
-      const float sy = __fdiv_rn(1.0f, __fadd_rn(1.0f, dexpf(fabsf(z[i]))));
-      const float sig = z[i] < 0.0f ? sy : __fsub_rn(1.0f, sy);
-      o[i] = bfr(__fmul_rn(__fmul_rn(z[i], sig), norm));
+      const float norm = bfr(__fmul_rn(bfr(__fmul_rn(v[i], inv)), ng_w[i]));
+      o[i] = bfr(__fmul_rn(ng_zs[i], norm));
     }
-    emit_xq(hh * 32 + lane, true, make_float4(o[0], o[1], o[2], o[3]), xq, xsum);
-    }
+    emit_xq(warp * 32 + lane, true, make_float4(o[0], o[1], o[2], o[3]), xq, xsum);
   }
   __syncthreads();
 
