@@ -108,6 +108,22 @@ def dist_setup():
     return world, rank, local
 
 
+def reduce_max(x: float, world: int, device) -> float:
+    """Max of a per-rank scalar over all ranks (every rank gets the result)."""
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def aggregate_tok_s(world: int, steps: int, seconds_max: float) -> float:
+    """Whole-job tokens per second: every rank decodes `steps` tokens of its own
+    session; the job takes as long as the slowest rank."""
+    return world * steps / seconds_max
+
+
 def ensure_model(world, rank):
     import q35
     import torch.distributed as dist
@@ -244,21 +260,15 @@ def main():
         ms = m.decode_timed(args.steps)
         barrier()
     attn_us, attn_launches = m.attn_timing(reset=0)
-    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
-    value = world * args.steps / (ms_max / 1e3)
+    ms_max = reduce_max(ms, world, "cuda")
+    value = aggregate_tok_s(world, args.steps, ms_max / 1e3)
 
     # ---- end to end: the public generate call, host buffers ----
     barrier()
     t0 = time.perf_counter()
     toks = m.generate([], args.steps, False)
     e2e_s = time.perf_counter() - t0
-    te = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e = world * args.steps / float(te.item())
+    e2e = aggregate_tok_s(world, args.steps, reduce_max(e2e_s, world, "cuda"))
     m._pending_for_bench = toks[-1]
 
     # ---- roofline of the dominant kernel (attention) ----

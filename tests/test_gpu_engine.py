@@ -1,0 +1,86 @@
+"""The `engine` executable end to end on the GPU: the JSON-lines protocol of
+the reference host (source/src/main.rs:10-54, docs/protocol.md:14-47) gives
+the same tokens as the session API, reports validation errors without losing
+state, and exits cleanly at end of input."""
+import json
+import subprocess
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+class Engine:
+    def __init__(self, model_dir):
+        import q35
+        self.p = subprocess.Popen([q35.ENGINE_PATH, "--model", model_dir, "--capacity", "4096"],
+                                  stdin=subprocess.PIPE, stdout=subprocess.PIPE, text=True, bufsize=1)
+
+    def ask(self, req):
+        self.p.stdin.write(json.dumps(req) + "\n")
+        self.p.stdin.flush()
+        return json.loads(self.p.stdout.readline())
+
+
+@pytest.fixture(scope="module")
+def engine(synth_model_dir):
+    e = Engine(synth_model_dir)
+    yield e
+    if e.p.poll() is None:
+        e.p.kill()
+
+
+def test_hello(engine):
+    assert engine.ask({"id": 1, "op": "hello"}) == {"id": 1, "ok": True, "protocol": 1}
+
+
+def test_generate_matches_session_api(cuda, engine, synth_model_dir):
+    import q35
+    prompt = [11, 2024, 77777, 248319, 5]
+    r1 = engine.ask({"id": 2, "op": "generate", "prompt": prompt, "max_tokens": 4, "reset": True})
+    r2 = engine.ask({"id": 3, "op": "generate", "prompt": [], "max_tokens": 3, "reset": False})
+    m = q35.Model.load(synth_model_dir, 0, capacity=4096)
+    try:
+        a = m.generate(prompt, 4, True)
+        b = m.generate([], 3, False)
+    finally:
+        m.close()
+    assert r1 == {"id": 2, "ok": True, "tokens": a}
+    assert r2 == {"id": 3, "ok": True, "tokens": b}
+
+
+def test_errors_keep_state(cuda, engine):
+    base = engine.ask({"id": 4, "op": "generate", "prompt": [7, 8, 9], "max_tokens": 2, "reset": True})
+    assert base["ok"]
+    bad = [
+        ({"id": 5, "op": "generate", "prompt": [], "max_tokens": 2, "reset": True}, "reset needs nonempty prompt"),
+        ({"id": 6, "op": "generate", "prompt": [248320], "max_tokens": 2, "reset": True}, "token outside vocabulary"),
+        ({"id": 7, "op": "generate", "prompt": [1], "max_tokens": 2, "reset": False},
+         "continuation prompt must be empty"),
+        ({"id": 8, "op": "generate", "prompt": [1] * 100, "max_tokens": 4000, "reset": True},
+         "context capacity exceeded"),
+        ({"id": 12, "op": "generate", "prompt": [1], "max_tokens": 5000, "reset": True}, "invalid output length"),
+        ({"id": 13, "op": "generate", "prompt": [1], "max_tokens": 0, "reset": True}, "invalid output length"),
+    ]
+    for req, msg in bad:
+        r = engine.ask(req)
+        assert r["id"] == req["id"] and r["ok"] is False and msg in r["error"], r
+    # the state from request 4 survives: continuing equals an uninterrupted run
+    cont = engine.ask({"id": 9, "op": "generate", "prompt": [], "max_tokens": 3, "reset": False})
+    ref = engine.ask({"id": 10, "op": "generate", "prompt": [7, 8, 9], "max_tokens": 5, "reset": True})
+    assert cont["ok"] and ref["ok"]
+    assert base["tokens"] + cont["tokens"] == ref["tokens"]
+
+
+def test_unknown_op_and_bad_json(engine):
+    r = engine.ask({"id": 11, "op": "nope"})
+    assert r["ok"] is False and r["id"] == 11
+    engine.p.stdin.write("{not json\n")
+    engine.p.stdin.flush()
+    r = json.loads(engine.p.stdout.readline())
+    assert r["ok"] is False
+
+
+def test_eof_exits_cleanly(engine):
+    engine.p.stdin.close()
+    assert engine.p.wait(timeout=60) == 0
