@@ -653,11 +653,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn(const __grid_constant_
   if (warp < kAttnScoreWarps) {
     // ---------------- score warps ----------------
     // lane l owns dims 8l..8l+7 of every head (as the reference).
-    float qreg[4][8];
+    // Heads (0,1) and (2,3) share packed f32x2 adds (__fadd2_rn rounds each
+    // component as __fadd_rn). Every product is a scalar __fmul_rn, which is
+    // never contracted into a fused multiply-add, so each score keeps the
+    // scalar sequence; a packed multiply feeding a packed add is not used
+    // because ptxas may fuse that pair.
+    float2 qp[2][8];
 #pragma unroll
-    for (int h = 0; h < 4; ++h)
+    for (int p = 0; p < 2; ++p)
 #pragma unroll
-      for (int e = 0; e < 8; ++e) qreg[h][e] = S.q[h][8 * lane + e];
+      for (int e = 0; e < 8; ++e) qp[p][e] = make_float2(S.q[2 * p][8 * lane + e], S.q[2 * p + 1][8 * lane + e]);
     for (int t = 0; t < ntiles; ++t) {
       const int st = t % kAttnStages, sb = t % kAttnBufs;
       mbar_wait(&S.kfull[st], uint32_t(t / kAttnStages) & 1u, a.ctl, kErrAttnWait);
@@ -670,11 +675,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn(const __grid_constant_
         const float k8[8] = {bf_lo(kv.x), bf_hi(kv.x), bf_lo(kv.y), bf_hi(kv.y),
                              bf_lo(kv.z), bf_hi(kv.z), bf_lo(kv.w), bf_hi(kv.w)};
 #pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          float sc = 0.0f;
+        for (int p = 0; p < 2; ++p) {
+          float2 sc = make_float2(0.0f, 0.0f);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) sc = __fadd_rn(sc, __fmul_rn(qreg[h][e], k8[e]));
-          v[h * 4 + jj] = sc;
+          for (int e = 0; e < 8; ++e)
+            sc = __fadd2_rn(sc, make_float2(__fmul_rn(qp[p][e].x, k8[e]), __fmul_rn(qp[p][e].y, k8[e])));
+          v[(2 * p) * 4 + jj] = sc.x;
+          v[(2 * p + 1) * 4 + jj] = sc.y;
         }
       }
       __syncwarp();
@@ -721,7 +728,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn(const __grid_constant_
   } else if (warp < kAttnKProdWarp) {
     // ---------------- recurrence warps ----------------
     const int wr = warp - kAttnRecWarp0, d = 64 * wr + 2 * lane, hs = lane & 3;
-    float o[4][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}, {0.0f, 0.0f}, {0.0f, 0.0f}};
+    // o2[i][p] = (o of head 2p, o of head 2p+1) at dim d + i. Products are
+    // scalar __fmul_rn (never contracted); the adds are packed __fadd2_rn.
+    float2 o2[2][2] = {{{0.0f, 0.0f}, {0.0f, 0.0f}}, {{0.0f, 0.0f}, {0.0f, 0.0f}}};
     float ssum = 0.0f;  // running sum of head lane & 3
     for (int t = 0; t < ntiles; ++t) {
       const int st = t % kAttnStages, b = t % kAttnBufs;
@@ -731,33 +740,26 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn(const __grid_constant_
       const uint32_t fm = S.fm[b][0] | S.fm[b][1] | S.fm[b][2] | S.fm[b][3];
       // S = S*f + e, o = o*f + e*v key by key (attention_decode.metal:357-366);
       // keys whose four factors are all 1 skip the (exact) multiply by 1.
-#define Q35_ATTN_ACC(J, VV)                                          \
-  {                                                                  \
-    const float4 e4 = S.e[b][J];                                     \
-    const float es = reinterpret_cast<const float*>(&S.e[b][J])[hs]; \
-    const float v0 = bf_lo(VV), v1 = bf_hi(VV);                      \
-    ssum = __fadd_rn(ssum, es);                                      \
-    o[0][0] = __fadd_rn(o[0][0], __fmul_rn(e4.x, v0));               \
-    o[0][1] = __fadd_rn(o[0][1], __fmul_rn(e4.x, v1));               \
-    o[1][0] = __fadd_rn(o[1][0], __fmul_rn(e4.y, v0));               \
-    o[1][1] = __fadd_rn(o[1][1], __fmul_rn(e4.y, v1));               \
-    o[2][0] = __fadd_rn(o[2][0], __fmul_rn(e4.z, v0));               \
-    o[2][1] = __fadd_rn(o[2][1], __fmul_rn(e4.z, v1));               \
-    o[3][0] = __fadd_rn(o[3][0], __fmul_rn(e4.w, v0));               \
-    o[3][1] = __fadd_rn(o[3][1], __fmul_rn(e4.w, v1));               \
+#define Q35_ATTN_ACC(J, VV)                                                    \
+  {                                                                            \
+    const float4 e4 = S.e[b][J];                                               \
+    const float es = reinterpret_cast<const float*>(&S.e[b][J])[hs];           \
+    const float v0 = bf_lo(VV), v1 = bf_hi(VV);                                \
+    const float2 e01 = make_float2(e4.x, e4.y), e23 = make_float2(e4.z, e4.w); \
+    ssum = __fadd_rn(ssum, es);                                                \
+    o2[0][0] = __fadd2_rn(o2[0][0], make_float2(__fmul_rn(e01.x, v0), __fmul_rn(e01.y, v0))); \
+    o2[0][1] = __fadd2_rn(o2[0][1], make_float2(__fmul_rn(e23.x, v0), __fmul_rn(e23.y, v0))); \
+    o2[1][0] = __fadd2_rn(o2[1][0], make_float2(__fmul_rn(e01.x, v1), __fmul_rn(e01.y, v1))); \
+    o2[1][1] = __fadd2_rn(o2[1][1], make_float2(__fmul_rn(e23.x, v1), __fmul_rn(e23.y, v1))); \
   }
-#define Q35_ATTN_RESCALE(J)                                                     \
-  {                                                                             \
-    const float4 f4 = S.f[b][J];                                                \
-    ssum = __fmul_rn(ssum, reinterpret_cast<const float*>(&S.f[b][J])[hs]);     \
-    o[0][0] = __fmul_rn(o[0][0], f4.x);                                         \
-    o[0][1] = __fmul_rn(o[0][1], f4.x);                                         \
-    o[1][0] = __fmul_rn(o[1][0], f4.y);                                         \
-    o[1][1] = __fmul_rn(o[1][1], f4.y);                                         \
-    o[2][0] = __fmul_rn(o[2][0], f4.z);                                         \
-    o[2][1] = __fmul_rn(o[2][1], f4.z);                                         \
-    o[3][0] = __fmul_rn(o[3][0], f4.w);                                         \
-    o[3][1] = __fmul_rn(o[3][1], f4.w);                                         \
+#define Q35_ATTN_RESCALE(J)                                                    \
+  {                                                                            \
+    const float4 f4 = S.f[b][J];                                               \
+    ssum = __fmul_rn(ssum, reinterpret_cast<const float*>(&S.f[b][J])[hs]);    \
+    o2[0][0] = make_float2(__fmul_rn(o2[0][0].x, f4.x), __fmul_rn(o2[0][0].y, f4.y)); \
+    o2[0][1] = make_float2(__fmul_rn(o2[0][1].x, f4.z), __fmul_rn(o2[0][1].y, f4.w)); \
+    o2[1][0] = make_float2(__fmul_rn(o2[1][0].x, f4.x), __fmul_rn(o2[1][0].y, f4.y)); \
+    o2[1][1] = make_float2(__fmul_rn(o2[1][1].x, f4.z), __fmul_rn(o2[1][1].y, f4.w)); \
   }
       if (split && t != own_t) {
         if (fm == 0) {
@@ -793,9 +795,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn(const __grid_constant_
     // chain partials (bf16-rounded on the split route, attention_decode.metal:428-430)
 #pragma unroll
     for (int h = 0; h < 4; ++h) {
+      const float oa = (h & 1) ? o2[0][h >> 1].y : o2[0][h >> 1].x;
+      const float ob = (h & 1) ? o2[1][h >> 1].y : o2[1][h >> 1].x;
       float* po = a.part_o + (pbase + h) * kHeadDim + d;
-      po[0] = split ? bfr(o[h][0]) : o[h][0];
-      po[1] = split ? bfr(o[h][1]) : o[h][1];
+      po[0] = split ? bfr(oa) : oa;
+      po[1] = split ? bfr(ob) : ob;
     }
     if (wr == 0 && lane < 4) a.part_ml[(pbase + lane) * 2 + 1] = ssum;
   } else if (kprod) {
