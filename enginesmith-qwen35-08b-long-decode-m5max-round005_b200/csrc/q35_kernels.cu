@@ -52,7 +52,7 @@ __host__ __device__ inline QmvLayout qmv_layout(int K, int rows) {
   L.scl = L.codes + size_t(rows) * KW * 4;
   L.bia = L.scl + size_t(rows) * KG * 2;
   L.xq = align16(L.bia + size_t(rows) * KG * 2);
-  L.xsum = L.xq + size_t(nch) * 8 * 32 * 16;
+  L.xsum = L.xq + size_t(nch) * 4 * 32 * 16;
   L.xf = L.xsum + size_t(nch) * 32 * 4;
   L.pl = L.xf + size_t(K) * 4;
   L.vals = L.pl + size_t(rows) * nch * 32 * 4;
@@ -275,9 +275,19 @@ __global__ void __launch_bounds__(kQmvThreads, 1) k_qmv(const __grid_constant__ 
   // 3. dot products from shared memory.
   mbar_wait(bar, 0, a.ctl, kErrQmvWait);
   const int ngroups = (nrows + 3) / 4;
-  for (int task = warp; task < ngroups * nch; task += kWarps) {
-    const int g = task / nch, c = task % nch;
-    qmv_chunk_task(codes, scl, bia, nrows, 4 * g, c, K, xq, xsum, pl, lane);
+  {
+    // a warp's tasks usually share their chunk: its constants are loaded once
+    float4 xx[4], cc[4];
+    float xs = 0.0f;
+    int cur = -1;
+    for (int task = warp; task < ngroups * nch; task += kWarps) {
+      const int g = task / nch, c = task % nch;
+      if (c != cur) {
+        load_xq(xq, xsum, c, lane, xx, cc, xs);
+        cur = c;
+      }
+      qmv_chunk_core(codes, scl, bia, nrows, 4 * g, c, K, xx, cc, xs, pl, lane);
+    }
   }
   __syncthreads();
   for (int g = warp; g < ngroups; g += kWarps) qmv_finish_task(pl, nrows, 4 * g, nch, vals, lane);
@@ -999,7 +1009,7 @@ struct HeadSmem {
   uint32_t codes[kHeadStages][kHeadRowsPerChunk * 128];
   uint16_t scl[kHeadStages][kHeadRowsPerChunk * 16];
   uint16_t bia[kHeadStages][kHeadRowsPerChunk * 16];
-  float4 xq[2 * 8 * 32];
+  float4 xq[2 * 4 * 32];
   float xsum[2 * 32];
   float xf[kHidden];
   float pl[kHeadRowsPerChunk * 2 * 32];

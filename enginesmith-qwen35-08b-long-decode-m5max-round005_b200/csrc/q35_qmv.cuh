@@ -26,7 +26,8 @@ namespace q35 {
 constexpr float kTwo23 = 8388608.0f;
 
 // Per (chunk, lane) constants: xq[c][i][lane] float4 (i < 4: the 16 xx of
-// the lane, i >= 4: -2^23 * xx), xsum[c][lane] = the lane's xs. A thread
+// the lane; the magic offsets -2^23 * xx are formed in registers, exactly,
+// when loaded), xsum[c][lane] = the lane's xs. A thread
 // builds one group of four consecutive k (one float4 of xx); the lane's xs
 // is ((g0 + g1) + g2) + g3 over its four groups g = ((a + b) + c) + d, as the
 // reference accumulates it. Dividing by 16/256/4096 is multiplying by the
@@ -45,9 +46,7 @@ Q35_DEV void build_xq(const float* xf, int K, float4* xq, float* xsum) {
       const int c = t >> 7, l = (t >> 2) & 31, j = t & 3;
       const float4 xx = make_float4(x4.x, __fmul_rn(x4.y, 0.0625f), __fmul_rn(x4.z, 0.00390625f),
                                     __fmul_rn(x4.w, 0.000244140625f));
-      float4* dst = xq + size_t(c) * 8 * 32 + l;
-      dst[j * 32] = xx;
-      dst[(4 + j) * 32] = make_float4(-kTwo23 * xx.x, -kTwo23 * xx.y, -kTwo23 * xx.z, -kTwo23 * xx.w);
+      xq[(size_t(c) * 4 + j) * 32 + l] = xx;
       if (j == 0) xsum[c * 32 + l] = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.0f, g), g1), g2), g3);
     }
   }
@@ -66,9 +65,7 @@ Q35_DEV void emit_xq(int t, bool on, float4 x4, float4* xq, float* xsum) {
   const int c = t >> 7, l = (t >> 2) & 31, j = t & 3;
   const float4 xx = make_float4(x4.x, __fmul_rn(x4.y, 0.0625f), __fmul_rn(x4.z, 0.00390625f),
                                 __fmul_rn(x4.w, 0.000244140625f));
-  float4* dst = xq + size_t(c) * 8 * 32 + l;
-  dst[j * 32] = xx;
-  dst[(4 + j) * 32] = make_float4(-kTwo23 * xx.x, -kTwo23 * xx.y, -kTwo23 * xx.z, -kTwo23 * xx.w);
+  xq[(size_t(c) * 4 + j) * 32 + l] = xx;
   if (j == 0) xsum[c * 32 + l] = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.0f, g), g1), g2), g3);
 }
 
@@ -120,8 +117,9 @@ Q35_DEV void load_xq(const float4* xq, const float* xsum, int c, int lane, float
                      float4 (&cc)[4], float& xs) {
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    xx[i] = xq[(size_t(c) * 8 + i) * 32 + lane];
-    cc[i] = xq[(size_t(c) * 8 + 4 + i) * 32 + lane];
+    xx[i] = xq[(size_t(c) * 4 + i) * 32 + lane];
+    cc[i] = make_float4(__fmul_rn(-kTwo23, xx[i].x), __fmul_rn(-kTwo23, xx[i].y),
+                        __fmul_rn(-kTwo23, xx[i].z), __fmul_rn(-kTwo23, xx[i].w));
   }
   xs = xsum[c * 32 + lane];
 }
