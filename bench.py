@@ -29,7 +29,8 @@ for p in (PKG, os.path.join(ROOT, "tests")):
     if p not in sys.path:
         sys.path.insert(0, p)
 
-METRIC = "decode tok/s at 64K ctx (batch 1 per session; aggregate over GPUs)"
+# BASELINE.json's metric; the context the line was measured at is config.context
+METRIC = "decode tok/s at 32K/64K/128K ctx per GPU & 8-GPU aggregate; % HBM roofline"
 SYNTH_DIR = os.environ.get("Q35_SYNTH_DIR", "/tmp/q35_synth_3")
 # bytes streamed per decode token (weights incl. tied head, GDN state R+W,
 # conv history + weights) plus 12,288 bytes of K/V per context token
