@@ -98,6 +98,10 @@ __device__ __forceinline__ void rope_pair(uint32_t position, int pair, float* cs
 // share an SM, so a launch's weight prefetch overlaps its predecessor.
 constexpr int kQmvThreads = 512;
 
+// Specialised per (prologue, epilogue) pair at compile time, so a launch runs
+// only its own code (smaller instruction footprint, no runtime branching on
+// the variant); PRO and EPI must equal PRO and EPI.
+template <int PRO, int EPI>
 __global__ void __launch_bounds__(kQmvThreads, 1) k_qmv(const __grid_constant__ QmvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -107,7 +111,7 @@ __global__ void __launch_bounds__(kQmvThreads, 1) k_qmv(const __grid_constant__ 
   const int np = qmv_pieces(a, blockIdx.x, pc);
   int nrows = 0;
   for (int i = 0; i < np; ++i) nrows += pc[i].count;
-  const int rows_alloc = a.epi == kEpiSwiglu ? 2 * a.units_per_cta : a.units_per_cta;
+  const int rows_alloc = EPI == kEpiSwiglu ? 2 * a.units_per_cta : a.units_per_cta;
   const QmvLayout L = qmv_layout(K, rows_alloc);
   uint32_t* codes = reinterpret_cast<uint32_t*>(smem + L.codes);
   uint16_t* scl = reinterpret_cast<uint16_t*>(smem + L.scl);
@@ -151,13 +155,13 @@ __global__ void __launch_bounds__(kQmvThreads, 1) k_qmv(const __grid_constant__ 
       }
       acc += pc[p].count;
     }
-    if (a.epi == kEpiSwiglu && tid >= pc[0].count) e_seg = -1;
+    if (EPI == kEpiSwiglu && tid >= pc[0].count) e_seg = -1;
   }
   uint16_t pre_res = 0, pre_h[3] = {0, 0, 0};
   float pre_w[4] = {0.f, 0.f, 0.f, 0.f};
   if (e_seg >= 0) {
-    if (a.epi == kEpiResAdd) pre_res = a.res[e_row];
-    if (a.epi == kEpiGdnConv && e_seg == 0) {
+    if (EPI == kEpiResAdd) pre_res = a.res[e_row];
+    if (EPI == kEpiGdnConv && e_seg == 0) {
       pre_h[0] = a.hist[e_row];
       pre_h[1] = a.hist[kGdnConv + e_row];
       pre_h[2] = a.hist[2 * kGdnConv + e_row];
@@ -169,7 +173,7 @@ __global__ void __launch_bounds__(kQmvThreads, 1) k_qmv(const __grid_constant__ 
     }
   }
   float gain4[4] = {0.f, 0.f, 0.f, 0.f};
-  if ((a.pro == kProRms || a.pro == kProEmbedRms) && tid < 256) {
+  if ((PRO == kProRms || PRO == kProEmbedRms) && tid < 256) {
     const uint2 g = *reinterpret_cast<const uint2*>(a.gain + 4 * tid);
     gain4[0] = bf_lo(g.x);
     gain4[1] = bf_hi(g.x);
@@ -182,7 +186,7 @@ __global__ void __launch_bounds__(kQmvThreads, 1) k_qmv(const __grid_constant__ 
   // the wait; only the RMS of y waits for the recurrence.
   static_assert(kQmvThreads / 32 >= kGdnHeads, "one warp per GDN head");
   float ng_zs[4] = {0.f, 0.f, 0.f, 0.f}, ng_w[4] = {0.f, 0.f, 0.f, 0.f};
-  if (a.pro == kProNormGate && warp < kGdnHeads) {
+  if (PRO == kProNormGate && warp < kGdnHeads) {
     const float4 z4 = bf4(*reinterpret_cast<const uint2*>(a.gz + warp * 128 + 4 * lane));
     const float4 w4 = bf4(*reinterpret_cast<const uint2*>(a.gw + 4 * lane));
     const float z[4] = {z4.x, z4.y, z4.z, z4.w};
@@ -199,7 +203,7 @@ __global__ void __launch_bounds__(kQmvThreads, 1) k_qmv(const __grid_constant__ 
   //    activations k = 4t .. 4t+3 and emits its matvec constants.
   pdl_wait();
   pdl_launch();
-  if (a.pro == kProPlain) {
+  if (PRO == kProPlain) {
     const int ngroups = K / 4;
     uint2 raw[4];
 #pragma unroll
@@ -212,9 +216,9 @@ __global__ void __launch_bounds__(kQmvThreads, 1) k_qmv(const __grid_constant__ 
       const int t = it * kQmvThreads + tid;
       if (it * kQmvThreads < ngroups) emit_xq(t, t < ngroups, bf4(raw[it]), xq, xsum);
     }
-  } else if (a.pro == kProRms || a.pro == kProEmbedRms) {
+  } else if (PRO == kProRms || PRO == kProEmbedRms) {
     float v[4] = {0.f, 0.f, 0.f, 0.f};
-    if (a.pro == kProEmbedRms) {
+    if (PRO == kProEmbedRms) {
       // linear.metal:19-23 for the token the step consumes.
       const uint32_t pos = ld_cg_u32(&a.ctl->pos);
       uint32_t token = ld_cg_u32(&a.seq[pos]);
@@ -295,15 +299,15 @@ __global__ void __launch_bounds__(kQmvThreads, 1) k_qmv(const __grid_constant__ 
 
   // 4. epilogue (thread i finishes CTA row i).
   if (e_seg < 0) return;
-  if (a.epi == kEpiSwiglu) {
+  if (EPI == kEpiSwiglu) {
     const int n = pc[0].count;
     a.seg[0].y[pc[0].row0 + tid] = swiglu_bf(bfr(vals[tid]), bfr(vals[n + tid]));
     return;
   }
   const float v = vals[tid];
-  if (a.epi == kEpiResAdd) {
+  if (EPI == kEpiResAdd) {
     a.res[e_row] = f2bf(__fadd_rn(bf2f(pre_res), bfr(v)));
-  } else if (a.epi == kEpiGdnConv && e_seg == 0) {
+  } else if (EPI == kEpiGdnConv && e_seg == 0) {
     // gdn_input.metal:419-431
     const uint16_t raw = f2bf(v);
     float acc = 0.0f;
@@ -1207,9 +1211,38 @@ static cudaError_t launch_ex(void (*kern)(Arg), dim3 grid, dim3 block, size_t sm
 constexpr size_t kSpreadSmem = 115 * 1024;
 static size_t spread(size_t bytes) { return bytes < kSpreadSmem ? kSpreadSmem : bytes; }
 
+// The (prologue, epilogue) pairs the decode step and the op entry points use.
+#define Q35_QMV_VARIANTS(X)         \
+  X(kProEmbedRms, kEpiGdnConv)      \
+  X(kProRms, kEpiGdnConv)           \
+  X(kProRms, kEpiStore)             \
+  X(kProRms, kEpiSwiglu)            \
+  X(kProNormGate, kEpiResAdd)       \
+  X(kProNormGate, kEpiStore)        \
+  X(kProPlain, kEpiResAdd)          \
+  X(kProPlain, kEpiStore)
+static void (*qmv_kernel(int pro, int epi))(QmvArgs) {
+#define Q35_QMV_PICK(P, E) \
+  if (pro == P && epi == E) return k_qmv<P, E>;
+  Q35_QMV_VARIANTS(Q35_QMV_PICK)
+#undef Q35_QMV_PICK
+  return nullptr;
+}
+template <class F>
+static cudaError_t for_each_qmv(F f) {
+  cudaError_t e = cudaSuccess;
+#define Q35_QMV_EACH(P, E) \
+  if (e == cudaSuccess) e = f(k_qmv<P, E>);
+  Q35_QMV_VARIANTS(Q35_QMV_EACH)
+#undef Q35_QMV_EACH
+  return e;
+}
+
 cudaError_t kernels_init() {
   cudaError_t e;
-  e = cudaFuncSetAttribute(k_qmv, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSpreadSmem));
+  e = for_each_qmv([](auto kern) {
+    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSpreadSmem));
+  });
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(k_attn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            int(spread(attn_smem_bytes())));
@@ -1233,7 +1266,9 @@ int qmv_max_rows(int K) {
 
 cudaError_t launch_qmv(const QmvArgs& a, cudaStream_t st, bool pdl) {
   const int grid = (a.units + a.units_per_cta - 1) / a.units_per_cta;
-  return launch_ex(k_qmv, dim3(grid), dim3(kQmvThreads), spread(qmv_smem_bytes(a)), st, pdl, a);
+  void (*kern)(QmvArgs) = qmv_kernel(a.pro, a.epi);
+  if (!kern) return cudaErrorInvalidValue;
+  return launch_ex(kern, dim3(grid), dim3(kQmvThreads), spread(qmv_smem_bytes(a)), st, pdl, a);
 }
 cudaError_t launch_recur(const RecurArgs& a, cudaStream_t st, bool pdl) {
   return launch_ex(k_gdn_recur, dim3(8, kGdnHeads), dim3(64), kSpreadSmem, st, pdl, a);
