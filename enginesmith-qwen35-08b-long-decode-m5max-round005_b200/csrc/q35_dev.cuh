@@ -138,11 +138,15 @@ Q35_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // suspend for a hardware-defined interval), records `site` in ctl->err and
 // returns false. Callers then skip their compute and exit normally.
 constexpr uint32_t kWaitLimit = 1u << 24;
-Q35_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, Ctl* ctl, uint32_t site) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i)
+Q35_DEV bool mbar_wait_limit(uint64_t* bar, uint32_t parity, uint32_t limit, uint32_t* err,
+                             uint32_t site) {
+  for (uint32_t i = 0; i < limit; ++i)
     if (mbar_try_wait(bar, parity)) return true;
-  if (ctl) atomicCAS(&ctl->err, 0u, site);
+  if (err) atomicCAS(err, 0u, site);
   return false;
+}
+Q35_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, Ctl* ctl, uint32_t site) {
+  return mbar_wait_limit(bar, parity, kWaitLimit, ctl ? &ctl->err : nullptr, site);
 }
 
 Q35_DEV uint32_t ld_cg_u32(const uint32_t* p) { return __ldcg(p); }

@@ -1154,6 +1154,20 @@ __global__ void __launch_bounds__(256) k_greedy(const __grid_constant__ HeadArgs
   head_finish(a, red, &cand, &best);
 }
 
+// Diagnostic: the bounded mbarrier wait every kernel uses, on a barrier that
+// nothing ever completes, with a caller-chosen poll limit. The wait gives up,
+// records kErrProbeWait in *err and the kernel returns normally (no copy is
+// in flight, so leaving the barrier pending is harmless).
+__global__ void k_wait_probe(uint32_t polls, uint32_t* err) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  mbar_wait_limit(&bar, 0, polls, err, kErrProbeWait);
+}
+
 // Embedding row (linear.metal:11-24), standalone op.
 __global__ void k_embedding(const uint32_t* w, const uint16_t* s, const uint16_t* b, uint32_t token,
                             int K, uint16_t* out) {
@@ -1288,6 +1302,10 @@ cudaError_t launch_greedy(const HeadArgs& a, cudaStream_t st) {
 cudaError_t launch_gdn_conv(const uint16_t* raw, uint16_t* hist, const uint16_t* convw,
                             uint16_t* conv_out, cudaStream_t st) {
   k_gdn_conv<<<kGdnConv / 256, 256, 0, st>>>(raw, hist, convw, conv_out);
+  return cudaGetLastError();
+}
+cudaError_t launch_wait_probe(uint32_t polls, uint32_t* err, cudaStream_t st) {
+  k_wait_probe<<<1, 32, 0, st>>>(polls, err);
   return cudaGetLastError();
 }
 cudaError_t launch_ctl_position(Ctl* ctl, uint32_t pos, cudaStream_t st) {

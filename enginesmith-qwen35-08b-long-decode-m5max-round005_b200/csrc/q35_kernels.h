@@ -22,6 +22,7 @@ cudaError_t launch_greedy(const HeadArgs& a, cudaStream_t st);
 cudaError_t launch_gdn_conv(const uint16_t* raw, uint16_t* hist, const uint16_t* convw,
                             uint16_t* conv_out, cudaStream_t st);
 cudaError_t launch_ctl_position(Ctl* ctl, uint32_t pos, cudaStream_t st);
+cudaError_t launch_wait_probe(uint32_t polls, uint32_t* err, cudaStream_t st);
 cudaError_t launch_embedding(const uint32_t* w, const uint16_t* s, const uint16_t* b,
                              uint32_t token, int K, uint16_t* out, cudaStream_t st);
 cudaError_t launch_rms1024(const uint16_t* x, const uint16_t* gain, uint16_t* out,

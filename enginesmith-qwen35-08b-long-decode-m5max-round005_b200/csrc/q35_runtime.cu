@@ -610,6 +610,26 @@ extern "C" {
 
 const char* q35_version(void) { return "q35-b200 0.1 (sm_100a)"; }
 
+int q35_diag_bounded_wait(uint32_t polls, uint32_t* err_dev, void* stream) {
+  if (!err_dev || polls == 0) return Q35_EINVAL;
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaError_t e = cudaMemsetAsync(err_dev, 0, sizeof(uint32_t), st);
+  if (e == cudaSuccess) e = launch_wait_probe(polls, err_dev, st);
+  uint32_t site = 0;
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&site, err_dev, sizeof(uint32_t), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return Q35_ECUDA;
+  return site == 0 ? Q35_OK : Q35_ETIMEOUT;
+}
+
+int q35_diag_inject_device_error(q35_session* s, uint32_t site) {
+  if (!s || site == 0) return Q35_EINVAL;
+  cudaSetDevice(s->device);
+  cudaError_t e = cudaStreamSynchronize(s->stream);
+  if (e == cudaSuccess) e = cudaMemcpy(&s->ctl->err, &site, sizeof(uint32_t), cudaMemcpyHostToDevice);
+  return e == cudaSuccess ? Q35_OK : Q35_ECUDA;
+}
+
 int q35_open(const char* model_dir, int device, const q35_opts* opts, q35_session** out,
              char* errbuf, size_t err_len) {
   if (!out) return Q35_EINVAL;

@@ -64,6 +64,7 @@ enum : uint32_t {
   kErrHeadWait = 3,
   kErrRecurWait = 4,
   kErrToken = 5,
+  kErrProbeWait = 6,  // the diagnostic bounded-wait probe
 };
 
 // ---- Q4 matvec kernel arguments ----

@@ -65,6 +65,8 @@ def _load() -> ctypes.CDLL:
         "q35_op_greedy": (c_int, [P, P, P, P, P]),
         "q35_write_synthetic_model": (c_int, [c_char_p, c_uint64, c_char_p, c_size_t]),
         "q35_version": (c_char_p, []),
+        "q35_diag_bounded_wait": (c_int, [c_uint32, P, P]),
+        "q35_diag_inject_device_error": (c_int, [P, c_uint32]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -160,6 +162,10 @@ class Model:
         self._check(lib().q35_last_logits(self._h, lg.ctypes.data, lse.ctypes.data))
         return lg, int(lse[0])
 
+    def inject_device_error(self, site: int) -> None:
+        """Host-side fault injection: record an expired device wait (site code)."""
+        self._check(lib().q35_diag_inject_device_error(self._h, site))
+
     def close(self) -> None:
         if self._h:
             lib().q35_close(self._h)
@@ -254,6 +260,13 @@ def head_argmax(w, scales, biases, x, gain=None, ws=None):
                                  _ptr(logits), _ptr(token), _ptr(lse), _ptr(ws), _stream()),
         "head_argmax")
     return logits, token, lse
+
+
+def diag_bounded_wait(polls: int, err_word) -> int:
+    """Run the kernels' bounded wait on a barrier nothing completes; returns the
+    status code (Q35_ETIMEOUT when the wait gave up) and leaves the site code
+    in err_word (a 1-element int32 CUDA tensor)."""
+    return lib().q35_diag_bounded_wait(polls, _ptr(err_word), _stream())
 
 
 def greedy(logits, ws=None):

@@ -199,6 +199,23 @@ int q35_write_synthetic_model(const char* dir, uint64_t seed, char* err, size_t 
 /* Library build string. */
 const char* q35_version(void);
 
+/* ---------------------------------------------------------------------- */
+/* Diagnostics for failure-detection tests (no counterpart in the          */
+/* reference, whose Metal waits are unbounded)                            */
+/* ---------------------------------------------------------------------- */
+
+/* Runs the bounded mbarrier wait that every kernel uses on a barrier nothing
+ * completes, giving up after `polls` polls: returns Q35_ETIMEOUT and leaves
+ * the wait's site code in *err_dev (a 4-byte device word), with the device
+ * context still usable. */
+int q35_diag_bounded_wait(uint32_t polls, uint32_t* err_dev, void* stream);
+
+/* Records an expired device wait with site code `site` in the session's
+ * control block, as a kernel whose bounded wait ran out would: the next
+ * continuation request then fails with Q35_ETIMEOUT and resets the session
+ * (model.rs:166-178). Host-side fault injection; runs no faulting code. */
+int q35_diag_inject_device_error(q35_session* s, uint32_t site);
+
 #ifdef __cplusplus
 }
 #endif
