@@ -1,0 +1,98 @@
+// Gated delta net arithmetic shared by the decode step and the chunked
+// prompt path, so both evaluate exactly the same operations in the same
+// order (the oracle's restatement of gdn_input.metal / gdn.metal).
+#pragma once
+#include "q35_qmv.cuh"
+
+namespace q35 {
+
+// gdn_input.metal:419-431: 4-tap causal conv (tap 3 = current token), BF16
+// boundary, SiLU with the BF16-stepped sigmoid. Returns the conv output; the
+// caller shifts the history (h0 <- h1, h1 <- h2, h2 <- raw).
+Q35_DEV uint16_t gdn_conv_value(uint16_t h0, uint16_t h1, uint16_t h2, uint16_t raw, const uint16_t* w4) {
+  float acc = 0.0f;
+  acc = fmaf(bf2f(h0), bf2f(w4[0]), acc);
+  acc = fmaf(bf2f(h1), bf2f(w4[1]), acc);
+  acc = fmaf(bf2f(h2), bf2f(w4[2]), acc);
+  acc = fmaf(bf2f(raw), bf2f(w4[3]), acc);
+  const float xq = bfr(acc);
+  return f2bf(__fmul_rn(xq, sigmoid_bf(xq)));
+}
+
+// gdn_input.metal:433-441 for one warp: q (is_q) or k of head h from the conv
+// outputs `conv` [6144]; lane l owns channels 4l..4l+3 of the head. Writes
+// the 128 normalised values (as f32) to dst.
+Q35_DEV void gdn_qk_norm(const uint16_t* conv, int h, bool is_q, int lane, float* dst) {
+  const int base = is_q ? h * 128 : 2048 + h * 128;
+  const float4 v4 = bf4(*reinterpret_cast<const uint2*>(conv + base + 4 * lane));
+  const float v[4] = {v4.x, v4.y, v4.z, v4.w};
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+  ss = warp_sum(ss);
+  const float inv = drsqrtf(__fadd_rn(__fmul_rn(ss, 0.0078125f), 1.0e-6f / 128.0f));
+  const float scale = is_q ? 0.0078125f : bfr(0.08838834764831845f);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) dst[4 * lane + i] = bfr(__fmul_rn(bfr(__fmul_rn(v[i], inv)), scale));
+}
+
+// gdn_input.metal:454-459: decay gate g = exp(-exp(A_log) * softplus_bf(bf16(a + dt_bias)))
+// (e1 = exp(A_log) is passed in) and write strength beta = bf16(sigmoid_bf(b)).
+Q35_DEV float gdn_gate(uint16_t a_raw, uint16_t dt_bias, float e1) {
+  const float ax = bfr(__fadd_rn(bf2f(a_raw), bf2f(dt_bias)));
+  return dexpf(__fmul_rn(-e1, softplus_bf(ax)));
+}
+Q35_DEV float gdn_beta(uint16_t b_raw) { return bfr(sigmoid_bf(bf2f(b_raw))); }
+
+// gdn.metal:192-225 for one value row, T = 1: 4 lanes per row (lane quarter
+// r owns keys 32r..32r+31, state in s[32]); S *= g; mem = S k (eight
+// four-term partials, then shuffle-xor 1, 2); delta = (v - mem) * beta;
+// S += k delta; out = S q (same reduction). Returns out on all 4 lanes.
+Q35_DEV float gdn_row_step(float (&s)[32], const float* kk, const float* qq, float gt, float beta,
+                           float vval) {
+  float part[8];
+#pragma unroll
+  for (int pb = 0; pb < 8; ++pb) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int e = pb * 4 + i;
+      s[e] = __fmul_rn(s[e], gt);
+      acc = __fadd_rn(acc, __fmul_rn(s[e], kk[e]));
+    }
+    part[pb] = acc;
+  }
+  float memory = __fadd_rn(__fadd_rn(__fadd_rn(part[0], part[1]), __fadd_rn(part[2], part[3])),
+                           __fadd_rn(__fadd_rn(part[4], part[5]), __fadd_rn(part[6], part[7])));
+  memory = __fadd_rn(memory, __shfl_xor_sync(0xffffffffu, memory, 1));
+  memory = __fadd_rn(memory, __shfl_xor_sync(0xffffffffu, memory, 2));
+  const float delta = __fmul_rn(__fsub_rn(vval, memory), beta);
+#pragma unroll
+  for (int pb = 0; pb < 8; ++pb) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int e = pb * 4 + i;
+      s[e] = __fadd_rn(s[e], __fmul_rn(kk[e], delta));
+      acc = __fadd_rn(acc, __fmul_rn(s[e], qq[e]));
+    }
+    part[pb] = acc;
+  }
+  float out = __fadd_rn(__fadd_rn(__fadd_rn(part[0], part[1]), __fadd_rn(part[2], part[3])),
+                        __fadd_rn(__fadd_rn(part[4], part[5]), __fadd_rn(part[6], part[7])));
+  out = __fadd_rn(out, __shfl_xor_sync(0xffffffffu, out, 1));
+  out = __fadd_rn(out, __shfl_xor_sync(0xffffffffu, out, 2));
+  return out;
+}
+
+// attention.metal:55-70 / the RoPE table: cos/sin of position * inv_freq for
+// the 32 rotary pairs, evaluated in double from the f32 angle.
+Q35_DEV void rope_pair(uint32_t position, int pair, float* cs) {
+  const float arg = __fmul_rn(-__fmul_rn(float(pair), 0.03125f), 23.253496170043945f);
+  const float inv_freq = (float)exp2((double)arg);
+  const float angle = __fmul_rn(float(position), inv_freq);
+  cs[2 * pair] = (float)cos((double)angle);
+  cs[2 * pair + 1] = (float)sin((double)angle);
+}
+
+}  // namespace q35

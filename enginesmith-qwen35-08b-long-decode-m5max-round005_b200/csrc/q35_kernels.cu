@@ -10,35 +10,15 @@
 // earlier steps, so the next launch's weight stream overlaps this one's
 // activation-dependent compute.
 #include "q35_kernels.h"
+#include "q35_launch.h"
 #include "q35_qmv.cuh"
+#include "q35_gdn.cuh"
 
 namespace q35 {
 
 // ---------------------------------------------------------------------------
 // Q4 matvec with fused prologue / epilogue
 // ---------------------------------------------------------------------------
-struct Piece {
-  int seg, row0, count;
-};
-
-__host__ __device__ inline int qmv_pieces(const QmvArgs& a, int cta, Piece* p) {
-  const int u0 = cta * a.units_per_cta;
-  const int u1 = (u0 + a.units_per_cta < a.units) ? u0 + a.units_per_cta : a.units;
-  if (u1 <= u0) return 0;
-  if (a.epi == kEpiSwiglu) {
-    p[0] = {0, u0, u1 - u0};
-    p[1] = {1, u0, u1 - u0};
-    return 2;
-  }
-  int n = 0, off = 0;
-  for (int s = 0; s < a.nseg; ++s) {
-    const int lo = u0 > off ? u0 : off;
-    const int hi = u1 < off + a.seg[s].rows ? u1 : off + a.seg[s].rows;
-    if (lo < hi) p[n++] = {s, lo - off, hi - lo};
-    off += a.seg[s].rows;
-  }
-  return n;
-}
 
 __host__ __device__ inline size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
 
@@ -72,27 +52,12 @@ size_t qmv_smem_bytes(const QmvArgs& a) {
 __device__ __forceinline__ void gdn_conv_channel(int c, uint16_t raw, uint16_t* hist,
                                                  const uint16_t* convw, uint16_t* conv_out) {
   const uint16_t h0 = hist[c], h1 = hist[kGdnConv + c], h2 = hist[2 * kGdnConv + c];
-  float acc = 0.0f;
-  acc = fmaf(bf2f(h0), bf2f(convw[4 * c + 0]), acc);
-  acc = fmaf(bf2f(h1), bf2f(convw[4 * c + 1]), acc);
-  acc = fmaf(bf2f(h2), bf2f(convw[4 * c + 2]), acc);
-  acc = fmaf(bf2f(raw), bf2f(convw[4 * c + 3]), acc);
-  const float xq = bfr(acc);
-  conv_out[c] = f2bf(__fmul_rn(xq, sigmoid_bf(xq)));
+  conv_out[c] = gdn_conv_value(h0, h1, h2, raw, convw + 4 * c);
   hist[c] = h1;
   hist[kGdnConv + c] = h2;
   hist[2 * kGdnConv + c] = raw;
 }
 
-// attention.metal:55-70 / the RoPE table: cos/sin of position * inv_freq for
-// the 32 rotary pairs, evaluated in double from the f32 angle.
-__device__ __forceinline__ void rope_pair(uint32_t position, int pair, float* cs) {
-  const float arg = __fmul_rn(-__fmul_rn(float(pair), 0.03125f), 23.253496170043945f);
-  const float inv_freq = (float)exp2((double)arg);
-  const float angle = __fmul_rn(float(position), inv_freq);
-  cs[2 * pair] = (float)cos((double)angle);
-  cs[2 * pair + 1] = (float)sin((double)angle);
-}
 
 // 256 threads and <= 64 registers: up to four CTAs (of consecutive launches)
 // share an SM, so a launch's weight prefetch overlaps its predecessor.
@@ -345,29 +310,13 @@ __global__ void __launch_bounds__(64) k_gdn_recur(const __grid_constant__ RecurA
   pdl_wait();
   pdl_launch();
   if (a.advance_pos && rb == 0 && h == 0 && tid == 0) a.ctl->pos = a.ctl->pos_step + 1;
-  {
-    // warp 0 -> q, warp 1 -> k: gdn_input.metal:433-441
-    const int base = warp == 0 ? h * 128 : 2048 + h * 128;
-    float v[4], ss = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      v[i] = bf2f(a.conv[base + 4 * lane + i]);
-      ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
-    }
-    ss = warp_sum(ss);
-    const float inv = drsqrtf(__fadd_rn(__fmul_rn(ss, 0.0078125f), 1.0e-6f / 128.0f));
-    const float scale = warp == 0 ? 0.0078125f : bfr(0.08838834764831845f);
-    float* dst = warp == 0 ? qn : kn;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) dst[4 * lane + i] = bfr(__fmul_rn(bfr(__fmul_rn(v[i], inv)), scale));
-  }
-  // gdn_input.metal:454-459 (g on warp 0, beta on warp 1, in parallel)
+  // warp 0 -> q, warp 1 -> k (gdn_input.metal:433-441); g on thread 0, beta on
+  // thread 32, in parallel (gdn_input.metal:454-459)
+  gdn_qk_norm(a.conv, h, warp == 0, lane, warp == 0 ? qn : kn);
   if (tid == 0) {
-    const float ax = bfr(__fadd_rn(bf2f(a.a_raw[h]), bf2f(a.dt_bias[h])));
-    const float e1 = dexpf(a.a_log[h]);
-    gb[0] = dexpf(__fmul_rn(-e1, softplus_bf(ax)));
+    gb[0] = gdn_gate(a.a_raw[h], a.dt_bias[h], dexpf(a.a_log[h]));
   } else if (tid == 32) {
-    gb[1] = bfr(sigmoid_bf(bf2f(a.b_raw[h])));
+    gb[1] = gdn_beta(a.b_raw[h]);
   }
   __syncthreads();
   mbar_wait(&bar, 0, a.ctl, kErrRecurWait);
@@ -383,40 +332,8 @@ __global__ void __launch_bounds__(64) k_gdn_recur(const __grid_constant__ RecurA
     s[i * 4 + 2] = t.z;
     s[i * 4 + 3] = t.w;
   }
-  const float* kk = kn + r * 32;
-  const float* qq = qn + r * 32;
-  float part[8];
-#pragma unroll
-  for (int pb = 0; pb < 8; ++pb) {
-    float acc = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int e = pb * 4 + i;
-      s[e] = __fmul_rn(s[e], gt);
-      acc = __fadd_rn(acc, __fmul_rn(s[e], kk[e]));
-    }
-    part[pb] = acc;
-  }
-  float memory = __fadd_rn(__fadd_rn(__fadd_rn(part[0], part[1]), __fadd_rn(part[2], part[3])),
-                           __fadd_rn(__fadd_rn(part[4], part[5]), __fadd_rn(part[6], part[7])));
-  memory = __fadd_rn(memory, __shfl_xor_sync(0xffffffffu, memory, 1));
-  memory = __fadd_rn(memory, __shfl_xor_sync(0xffffffffu, memory, 2));
-  const float delta = __fmul_rn(__fsub_rn(bf2f(a.conv[4096 + h * 128 + vrow]), memory), beta);
-#pragma unroll
-  for (int pb = 0; pb < 8; ++pb) {
-    float acc = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int e = pb * 4 + i;
-      s[e] = __fadd_rn(s[e], __fmul_rn(kk[e], delta));
-      acc = __fadd_rn(acc, __fmul_rn(s[e], qq[e]));
-    }
-    part[pb] = acc;
-  }
-  float out = __fadd_rn(__fadd_rn(__fadd_rn(part[0], part[1]), __fadd_rn(part[2], part[3])),
-                        __fadd_rn(__fadd_rn(part[4], part[5]), __fadd_rn(part[6], part[7])));
-  out = __fadd_rn(out, __shfl_xor_sync(0xffffffffu, out, 1));
-  out = __fadd_rn(out, __shfl_xor_sync(0xffffffffu, out, 2));
+  const float out =
+      gdn_row_step(s, kn + r * 32, qn + r * 32, gt, beta, bf2f(a.conv[4096 + h * 128 + vrow]));
   if (r == 0) a.y[h * 128 + vrow] = f2bf(out);
   float4* dst = reinterpret_cast<float4*>(a.state + (size_t(h) * 128 + vrow) * 128 + r * 32);
 #pragma unroll
@@ -581,9 +498,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn(const __grid_constant_
   const uint32_t cap = a.capacity;
   constexpr float kMin = -3.4028234663852886e38f;
 
-  // pos_step was written by the step's first launch (>= 2 launches back).
-  const uint32_t pos = ld_cg_u32(&a.ctl->pos_step);
+  // pos_step was written by the step's first launch (>= 2 launches back);
+  // a prompt chunk's token t sits pos_add = t places after it.
+  const uint32_t pos = ld_cg_u32(&a.ctl->pos_step) + uint32_t(a.pos_add);
   const uint32_t len = pos + 1;
+  const float* rope = a.rope ? a.rope : a.ctl->rope_cs;
   const bool split = len >= 1024;
   const int stride = split ? 64 : 32;
   const int nkeys = (chain < stride && uint32_t(chain) < len) ? int((len - 1 - chain) / stride) + 1 : 0;
@@ -644,11 +563,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn(const __grid_constant_
   // warp 4 prepares the current token's key (attention.metal:295-311).
   if (warp < 4) {
     const int qh = 4 * kh + warp;
-    head_norm_rope(a.q_raw + qh * 512, a.q_gain, a.ctl->rope_cs, S.nrm[warp], S.q[warp], lane);
+    head_norm_rope(a.q_raw + qh * 512, a.q_gain, rope, S.nrm[warp], S.q[warp], lane);
     for (int d = lane; d < kHeadDim; d += 32) S.q[warp][d] = __fmul_rn(0.0625f, S.q[warp][d]);
   } else if (warp == 4) {
     const uint4 vr = *reinterpret_cast<const uint4*>(a.v_raw + kh * kHeadDim + 8 * lane);
-    head_norm_rope(a.k_raw + kh * kHeadDim, a.k_gain, a.ctl->rope_cs, S.nrm[4], S.kr, lane);
+    head_norm_rope(a.k_raw + kh * kHeadDim, a.k_gain, rope, S.nrm[4], S.kr, lane);
     const float* kr8 = S.kr + 8 * lane;
     const uint4 kb = make_uint4(pack_bf2(kr8[0], kr8[1]), pack_bf2(kr8[2], kr8[3]),
                                 pack_bf2(kr8[4], kr8[5]), pack_bf2(kr8[6], kr8[7]));
@@ -848,7 +767,7 @@ __global__ void __launch_bounds__(128) k_attn_combine(const __grid_constant__ At
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int qh = blockIdx.x, kh = qh >> 2, h = qh & 3;
   const int stripe = blockIdx.y * 4 + warp;  // 8 dims
-  const uint32_t len = ld_cg_u32(&a.ctl->pos_step) + 1;
+  const uint32_t len = ld_cg_u32(&a.ctl->pos_step) + uint32_t(a.pos_add) + 1;
   const bool split = len >= 1024;
   const size_t base = size_t(kh) * kAttnChains * 4 + h;  // + chain * 4
   float res[8];
@@ -1195,25 +1114,6 @@ __global__ void __launch_bounds__(256) k_rms1024(const uint16_t* x, const uint16
 // ---------------------------------------------------------------------------
 // host-side launch helpers
 // ---------------------------------------------------------------------------
-template <typename Arg>
-static cudaError_t launch_ex(void (*kern)(Arg), dim3 grid, dim3 block, size_t smem,
-                             cudaStream_t stream, bool pdl, Arg arg) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  int n = 0;
-  if (pdl) {
-    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[n].val.programmaticStreamSerializationAllowed = 1;
-    ++n;
-  }
-  cfg.attrs = attr;
-  cfg.numAttrs = n;
-  return cudaLaunchKernelEx(&cfg, kern, arg);
-}
 
 // Dynamic shared memory requested by every kernel of the decode step: more
 // than half an SM's 228 KB, so one CTA fits per SM and every kernel's

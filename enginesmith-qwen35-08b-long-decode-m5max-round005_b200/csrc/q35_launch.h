@@ -1,0 +1,29 @@
+// Host-side kernel launch with optional programmatic dependent launch (the
+// launch may start before its predecessor finishes; the kernel orders its
+// dependent reads with griddepcontrol.wait).
+#pragma once
+#include <cuda_runtime.h>
+
+namespace q35 {
+
+template <typename Arg>
+inline cudaError_t launch_ex(void (*kern)(Arg), dim3 grid, dim3 block, size_t smem,
+                             cudaStream_t stream, bool pdl, Arg arg) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  int n = 0;
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kern, arg);
+}
+
+}  // namespace q35

@@ -25,6 +25,33 @@ namespace q35 {
 
 constexpr float kTwo23 = 8388608.0f;
 
+// Rows of a CTA of a fused matvec launch: CTA `cta` covers units
+// [cta * upc, (cta + 1) * upc) of the concatenated segments (both the gate and
+// the up row of each unit for SwiGLU), split into per-segment pieces.
+struct Piece {
+  int seg, row0, count;
+};
+
+__host__ __device__ inline int qmv_pieces(const QmvArgs& a, int cta, Piece* p) {
+  const int u0 = cta * a.units_per_cta;
+  const int u1 = (u0 + a.units_per_cta < a.units) ? u0 + a.units_per_cta : a.units;
+  if (u1 <= u0) return 0;
+  if (a.epi == kEpiSwiglu) {
+    p[0] = {0, u0, u1 - u0};
+    p[1] = {1, u0, u1 - u0};
+    return 2;
+  }
+  int n = 0, off = 0;
+  for (int s = 0; s < a.nseg; ++s) {
+    const int lo = u0 > off ? u0 : off;
+    const int hi = u1 < off + a.seg[s].rows ? u1 : off + a.seg[s].rows;
+    if (lo < hi) p[n++] = {s, lo - off, hi - lo};
+    off += a.seg[s].rows;
+  }
+  return n;
+}
+
+
 // Per (chunk, lane) constants: xq[c][i][lane] float4 (i < 4: the 16 xx of
 // the lane; the magic offsets -2^23 * xx are formed in registers, exactly,
 // when loaded), xsum[c][lane] = the lane's xs. A thread
@@ -82,13 +109,13 @@ Q35_DEV float half_dot(uint32_t u, const float4& xx, const float4& cc) {
   return __fadd_rn(__fadd_rn(__fadd_rn(t0, t1), t2), t3);
 }
 
-// One warp task with the lane's chunk constants in registers: rows
-// [r0, r0+4) (those < nrows) of the CTA's smem image, chunk c (512 wide).
-// Writes each lane's chunk term s*dotq + xs*b to pl[(row * nch + c) * 32 + lane].
-Q35_DEV void qmv_chunk_core(const uint32_t* codes, const uint16_t* scl, const uint16_t* bia,
+// The lane's chunk terms s*dotq + xs*b of rows [r0, r0+4) for chunk c (512
+// wide), with the lane's chunk constants in registers; rows at or beyond
+// nrows give 0.
+Q35_DEV void qmv_rows_terms(const uint32_t* codes, const uint16_t* scl, const uint16_t* bia,
                             int nrows, int r0, int c, int K, const float4 (&xx)[4],
-                            const float4 (&cc)[4], float xs, float* pl, int lane) {
-  const int KW = K / 8, KG = K / 64, nch = K / 512;
+                            const float4 (&cc)[4], float xs, int lane, float (&term)[4]) {
+  const int KW = K / 8, KG = K / 64;
   const int w0 = 64 * c + 2 * lane;
   const int g = 8 * c + (lane >> 2);
   uint2 q[4];
@@ -107,9 +134,23 @@ Q35_DEV void qmv_chunk_core(const uint32_t* codes, const uint16_t* scl, const ui
     dotq = __fadd_rn(dotq, half_dot(q[r].x >> 16, xx[1], cc[1]));
     dotq = __fadd_rn(dotq, half_dot(q[r].y, xx[2], cc[2]));
     dotq = __fadd_rn(dotq, half_dot(q[r].y >> 16, xx[3], cc[3]));
-    const float term = __fadd_rn(__fmul_rn(sc[r], dotq), __fmul_rn(xs, bi[r]));
-    if (r0 + r < nrows) pl[(size_t(r0 + r) * nch + c) * 32 + lane] = term;
+    const float t = __fadd_rn(__fmul_rn(sc[r], dotq), __fmul_rn(xs, bi[r]));
+    term[r] = r0 + r < nrows ? t : 0.0f;
   }
+}
+
+// One warp task with the lane's chunk constants in registers: rows
+// [r0, r0+4) (those < nrows) of the CTA's smem image, chunk c (512 wide).
+// Writes each lane's chunk term s*dotq + xs*b to pl[(row * nch + c) * 32 + lane].
+Q35_DEV void qmv_chunk_core(const uint32_t* codes, const uint16_t* scl, const uint16_t* bia,
+                            int nrows, int r0, int c, int K, const float4 (&xx)[4],
+                            const float4 (&cc)[4], float xs, float* pl, int lane) {
+  const int nch = K / 512;
+  float term[4];
+  qmv_rows_terms(codes, scl, bia, nrows, r0, c, K, xx, cc, xs, lane, term);
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+    if (r0 + r < nrows) pl[(size_t(r0 + r) * nch + c) * 32 + lane] = term[r];
 }
 
 // The lane's constants of chunk c from the shared image built by build_xq.

@@ -308,6 +308,7 @@ cudaError_t ensure_kernels_init() {
   std::lock_guard<std::mutex> lk(g_init_mu);
   if (dev < 64 && (g_init_mask >> dev) & 1) return cudaSuccess;
   e = kernels_init();
+  if (e == cudaSuccess) e = chunk_kernels_init();
   if (e == cudaSuccess && dev < 64) g_init_mask |= uint64_t(1) << dev;
   return e;
 }
@@ -338,6 +339,12 @@ struct q35_session {
   uint16_t* hist = nullptr;
   uint16_t* kv = nullptr;  // [6 layers][K|V][2][capacity][256]
   cudaGraphExec_t gdec1 = nullptr, gdecN = nullptr, gpre1 = nullptr, gpreN = nullptr;
+  // prompt chunks of kPrefillTokens tokens (per-token rows of each buffer)
+  bool chunked = true;
+  cudaGraphExec_t gchunk = nullptr;
+  uint16_t *c_h = nullptr, *c_conv = nullptr, *c_z = nullptr, *c_ab = nullptr, *c_y = nullptr;
+  uint16_t *c_q = nullptr, *c_k = nullptr, *c_v = nullptr, *c_gated = nullptr, *c_act = nullptr;
+  float* c_rope = nullptr;
   uint32_t position = 0;
   bool has_pending = false;
   uint32_t pending = 0;
@@ -510,6 +517,182 @@ cudaError_t enqueue_step(q35_session* s, bool head, bool first) {
   return e;
 }
 
+// One prompt chunk: kPrefillTokens consecutive prompt tokens through all 24
+// layers (no head), with the decode step's arithmetic per token. Matvecs and
+// the GDN recurrence take the whole chunk per launch; attention runs once per
+// token (token t attends to keys 0..pos+t, its own key appended first).
+cudaError_t enqueue_chunk(q35_session* s) {
+  const ModelW& M = s->M;
+  cudaStream_t st = s->stream;
+  constexpr int T = kPrefillTokens;
+  bool pdl = false;
+  cudaError_t e = cudaSuccess;
+#define Q35_C(x)                    \
+  do {                              \
+    e = (x);                        \
+    if (e != cudaSuccess) return e; \
+    pdl = true;                     \
+  } while (0)
+  auto chunk_args = [&](QmvArgs& a) {
+    a.ntok = T;
+    a.sub = chunk_sub_tokens(a);
+    a.ctl = s->ctl;
+  };
+  int gi = 0, ai = 0;
+  for (int l = 0; l < kLayers; ++l) {
+    const LayerW& L = M.L[l];
+    if (!L.attn) {
+      QmvArgs a = {};
+      a.seg[0] = {L.qkv.w, L.qkv.s, L.qkv.b, nullptr, 6144};
+      a.seg[1] = {L.z.w, L.z.s, L.z.b, s->c_z, 2048};
+      a.seg[2] = {L.a.w, L.a.s, L.a.b, s->c_ab, 16};
+      a.seg[3] = {L.bproj.w, L.bproj.s, L.bproj.b, s->c_ab + 16, 16};
+      a.ystride[1] = 2048;
+      a.ystride[2] = 32;
+      a.ystride[3] = 32;
+      a.nseg = 4;
+      a.K = 1024;
+      a.units = 8224;
+      a.units_per_cta = 56;
+      a.pro = l == 0 ? kProEmbedRms : kProRms;
+      a.epi = kEpiGdnConv;
+      a.x = s->c_h;
+      a.gain = L.in_norm;
+      a.h_out = s->c_h;
+      a.ew = M.embed.w;
+      a.es = M.embed.s;
+      a.eb = M.embed.b;
+      a.seq = s->seq;
+      a.rope_out = s->c_rope;
+      a.hist = s->hist + size_t(gi) * 3 * kGdnConv;
+      a.convw = L.conv;
+      a.conv_out = s->c_conv;
+      chunk_args(a);
+      Q35_C(launch_qmv_chunk(a, st, pdl));
+      RecurArgs r = {};
+      r.conv = s->c_conv;
+      r.a_raw = s->c_ab;
+      r.b_raw = s->c_ab + 16;
+      r.a_log = L.alog;
+      r.dt_bias = L.dt;
+      r.state = s->state + size_t(gi) * kGdnHeads * 128 * 128;
+      r.y = s->c_y;
+      r.ctl = s->ctl;
+      r.advance_pos = l == 0;
+      r.ntok = T;
+      Q35_C(launch_recur_chunk(r, st, pdl));
+      QmvArgs o = {};
+      o.seg[0] = {L.out.w, L.out.s, L.out.b, nullptr, 1024};
+      o.nseg = 1;
+      o.K = 2048;
+      o.units = 1024;
+      o.units_per_cta = 7;
+      o.pro = kProNormGate;
+      o.gy = s->c_y;
+      o.gz = s->c_z;
+      o.gw = L.gnorm;
+      o.epi = kEpiResAdd;
+      o.res = s->c_h;
+      chunk_args(o);
+      Q35_C(launch_qmv_chunk(o, st, pdl));
+      ++gi;
+    } else {
+      QmvArgs a = {};
+      a.seg[0] = {L.q.w, L.q.s, L.q.b, s->c_q, 4096};
+      a.seg[1] = {L.k.w, L.k.s, L.k.b, s->c_k, 512};
+      a.seg[2] = {L.v.w, L.v.s, L.v.b, s->c_v, 512};
+      a.ystride[0] = kQProj;
+      a.ystride[1] = 512;
+      a.ystride[2] = 512;
+      a.nseg = 3;
+      a.K = 1024;
+      a.units = 5120;
+      a.units_per_cta = 36;
+      a.pro = kProRms;
+      a.x = s->c_h;
+      a.gain = L.in_norm;
+      a.epi = kEpiStore;
+      chunk_args(a);
+      Q35_C(launch_qmv_chunk(a, st, pdl));
+      for (int t = 0; t < T; ++t) {
+        AttnArgs at = {};
+        at.q_raw = s->c_q + size_t(t) * kQProj;
+        at.k_raw = s->c_k + size_t(t) * 512;
+        at.v_raw = s->c_v + size_t(t) * 512;
+        at.q_gain = L.qnorm;
+        at.k_gain = L.knorm;
+        at.kcache = s->kcache(ai);
+        at.vcache = s->vcache(ai);
+        at.capacity = s->capacity;
+        at.part_o = s->attn_po;
+        at.part_ml = s->attn_pml;
+        at.gated = s->c_gated + size_t(t) * 2048;
+        at.ctl = s->ctl;
+        at.pos_add = t;
+        at.rope = s->c_rope + 64 * t;
+        Q35_C(launch_attn(at, st, pdl));
+      }
+      QmvArgs o = {};
+      o.seg[0] = {L.o.w, L.o.s, L.o.b, nullptr, 1024};
+      o.nseg = 1;
+      o.K = 2048;
+      o.units = 1024;
+      o.units_per_cta = 7;
+      o.pro = kProPlain;
+      o.x = s->c_gated;
+      o.epi = kEpiResAdd;
+      o.res = s->c_h;
+      chunk_args(o);
+      Q35_C(launch_qmv_chunk(o, st, pdl));
+      ++ai;
+    }
+    QmvArgs m = {};
+    m.seg[0] = {L.gate.w, L.gate.s, L.gate.b, s->c_act, kMlp};
+    m.seg[1] = {L.up.w, L.up.s, L.up.b, nullptr, kMlp};
+    m.ystride[0] = kMlp;
+    m.nseg = 2;
+    m.K = 1024;
+    m.units = kMlp;
+    m.units_per_cta = 25;
+    m.pro = kProRms;
+    m.x = s->c_h;
+    m.gain = L.post_norm;
+    m.epi = kEpiSwiglu;
+    chunk_args(m);
+    Q35_C(launch_qmv_chunk(m, st, pdl));
+    QmvArgs d = {};
+    d.seg[0] = {L.down.w, L.down.s, L.down.b, nullptr, 1024};
+    d.nseg = 1;
+    d.K = kMlp;
+    d.units = 1024;
+    d.units_per_cta = 7;
+    d.pro = kProPlain;
+    d.x = s->c_act;
+    d.epi = kEpiResAdd;
+    d.res = s->c_h;
+    chunk_args(d);
+    Q35_C(launch_qmv_chunk(d, st, pdl));
+  }
+#undef Q35_C
+  return e;
+}
+
+cudaError_t capture_chunk(q35_session* s, cudaGraphExec_t* out) {
+  cudaGraph_t g = nullptr;
+  cudaError_t e = cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal);
+  if (e != cudaSuccess) return e;
+  const cudaError_t le = enqueue_chunk(s);
+  e = cudaStreamEndCapture(s->stream, &g);
+  if (le != cudaSuccess) {
+    if (g) cudaGraphDestroy(g);
+    return le;
+  }
+  if (e != cudaSuccess) return e;
+  e = cudaGraphInstantiate(out, g, 0);
+  cudaGraphDestroy(g);
+  return e;
+}
+
 cudaError_t capture(q35_session* s, int steps, bool head, cudaGraphExec_t* out) {
   cudaGraph_t g = nullptr;
   cudaError_t e = cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal);
@@ -530,7 +713,7 @@ cudaError_t capture(q35_session* s, int steps, bool head, cudaGraphExec_t* out) 
 void free_session(q35_session* s) {
   if (!s) return;
   if (s->device >= 0) cudaSetDevice(s->device);
-  for (cudaGraphExec_t g : {s->gdec1, s->gdecN, s->gpre1, s->gpreN})
+  for (cudaGraphExec_t g : {s->gdec1, s->gdecN, s->gpre1, s->gpreN, s->gchunk})
     if (g) cudaGraphExecDestroy(g);
   if (s->buf) cudaFree(s->buf);
   if (s->M.arena) cudaFree(s->M.arena);
@@ -567,7 +750,10 @@ int run_steps(q35_session* s, size_t n, bool head, cudaError_t* ce) {
   while (n > 0) {
     if (s->cancelled.load(std::memory_order_relaxed)) return Q35_ECANCEL;
     cudaError_t e;
-    if (n >= B && gN) {
+    if (!head && s->gchunk && n >= size_t(kPrefillTokens)) {
+      e = cudaGraphLaunch(s->gchunk, s->stream);
+      n -= kPrefillTokens;
+    } else if (n >= B && gN) {
       e = cudaGraphLaunch(gN, s->stream);
       n -= B;
     } else {
@@ -644,6 +830,7 @@ int q35_open(const char* model_dir, int device, const q35_opts* opts, q35_sessio
     if (opts->capacity) s->capacity = opts->capacity;
     if (opts->decode_batch) s->dbatch = int(opts->decode_batch);
     if (opts->prefill_batch) s->pbatch = int(opts->prefill_batch);
+    if (opts->flags & Q35_FLAG_TOKEN_BY_TOKEN_PROMPT) s->chunked = false;
   }
   auto fail = [&](int code, const std::string& m) {
     copy_err(errbuf, err_len, m);
@@ -691,6 +878,17 @@ int q35_open(const char* model_dir, int device, const q35_opts* opts, q35_sessio
       {(void**)&s->state, size_t(18) * kGdnHeads * 128 * 128 * 4},
       {(void**)&s->hist, size_t(18) * 3 * kGdnConv * 2},
       {(void**)&s->kv, size_t(6) * 2 * kKvHeads * cap * kHeadDim * 2},
+      {(void**)&s->c_h, size_t(kPrefillTokens) * kHidden * 2},
+      {(void**)&s->c_conv, size_t(kPrefillTokens) * kGdnConv * 2},
+      {(void**)&s->c_z, size_t(kPrefillTokens) * 2048 * 2},
+      {(void**)&s->c_ab, size_t(kPrefillTokens) * 32 * 2},
+      {(void**)&s->c_y, size_t(kPrefillTokens) * 2048 * 2},
+      {(void**)&s->c_q, size_t(kPrefillTokens) * kQProj * 2},
+      {(void**)&s->c_k, size_t(kPrefillTokens) * 512 * 2},
+      {(void**)&s->c_v, size_t(kPrefillTokens) * 512 * 2},
+      {(void**)&s->c_gated, size_t(kPrefillTokens) * 2048 * 2},
+      {(void**)&s->c_act, size_t(kPrefillTokens) * kMlp * 2},
+      {(void**)&s->c_rope, size_t(kPrefillTokens) * 64 * 4},
   };
   size_t total = 0;
   for (auto& p : parts) total += (p.bytes + 255) & ~size_t(255);
@@ -711,6 +909,7 @@ int q35_open(const char* model_dir, int device, const q35_opts* opts, q35_sessio
   if (e == cudaSuccess && s->dbatch > 1) e = capture(s, s->dbatch, true, &s->gdecN);
   if (e == cudaSuccess) e = capture(s, 1, false, &s->gpre1);
   if (e == cudaSuccess && s->pbatch > 1) e = capture(s, s->pbatch, false, &s->gpreN);
+  if (e == cudaSuccess && s->chunked) e = capture_chunk(s, &s->gchunk);
   if (e != cudaSuccess) return fail(Q35_ECUDA, std::string("graph capture: ") + cudaGetErrorString(e));
   *out = s;
   return Q35_OK;

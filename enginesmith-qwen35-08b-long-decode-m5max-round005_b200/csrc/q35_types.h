@@ -36,6 +36,7 @@ constexpr int kHeadChunksPerCta = 35;
 constexpr int kHeadRowsPerCta = kHeadRowsPerChunk * kHeadChunksPerCta;  // 1680
 constexpr int kHeadCtas = (kVocab + kHeadRowsPerCta - 1) / kHeadRowsPerCta;  // 148
 constexpr int kHeadStages = 4;
+constexpr int kPrefillTokens = 16;  // prompt tokens per chunk launch
 
 // Device-resident control block of one decode session (or one op call).
 struct Ctl {
@@ -102,6 +103,12 @@ struct QmvArgs {
   uint16_t* conv_out;    // [6144]
   Ctl* ctl;
   int advance_pos;       // this launch moves ctl->pos to pos_step + 1
+  // prompt chunks (k_qmv_chunk only): ntok consecutive tokens, `sub` of them
+  // in shared memory at a time; token t's rows of x / gy / gz / res /
+  // conv_out and of seg[s].y sit at t * (row width) (ystride[s] for seg[s].y)
+  int ntok, sub;
+  int ystride[4];
+  float* rope_out;       // embedding prologue: [ntok][64] RoPE table of the chunk
 };
 
 struct RecurArgs {
@@ -114,6 +121,7 @@ struct RecurArgs {
   uint16_t* y;            // [2048]
   Ctl* ctl;
   int advance_pos;
+  int ntok;               // prompt chunks: conv [ntok][6144], a/b [ntok][32], y [ntok][2048]
 };
 
 struct AttnArgs {
@@ -129,6 +137,8 @@ struct AttnArgs {
   float* part_ml;         // [2][kAttnChains][4][2]
   uint16_t* gated;        // [8][256]
   Ctl* ctl;
+  int pos_add;            // prompt chunks: this token sits at ctl->pos_step + pos_add
+  const float* rope;      // prompt chunks: its RoPE table [64] (else ctl->rope_cs)
 };
 
 struct HeadArgs {

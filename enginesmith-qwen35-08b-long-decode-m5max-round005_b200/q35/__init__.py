@@ -24,6 +24,7 @@ HIDDEN = 1024
 DEFAULT_CAPACITY = 262144
 
 OK, EINVAL, ECUDA, ECANCEL, EIO, ENOMEM, ETIMEOUT, ENCCL = 0, -1, -2, -3, -4, -5, -6, -7
+FLAG_TOKEN_BY_TOKEN_PROMPT = 1
 
 
 class Q35Error(RuntimeError):
@@ -105,8 +106,8 @@ class Model:
 
     @classmethod
     def load(cls, path: str, device: int = 0, capacity: int = 0, decode_batch: int = 0,
-             prefill_batch: int = 0) -> "Model":
-        opts = _Opts(capacity, decode_batch, prefill_batch, 0)
+             prefill_batch: int = 0, token_by_token_prompt: bool = False) -> "Model":
+        opts = _Opts(capacity, decode_batch, prefill_batch, FLAG_TOKEN_BY_TOKEN_PROMPT if token_by_token_prompt else 0)
         h = c_void_p()
         err = ctypes.create_string_buffer(2048)
         rc = lib().q35_open(path.encode(), device, ctypes.byref(opts), ctypes.byref(h), err, len(err))

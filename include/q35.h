@@ -44,8 +44,13 @@ typedef struct q35_opts {
   uint32_t capacity;     /* context capacity in tokens (0 -> 262144); multiple of 64 */
   uint32_t decode_batch; /* decode steps per CUDA-graph launch (0 -> 8) */
   uint32_t prefill_batch;/* prompt steps per CUDA-graph launch (0 -> 16) */
-  uint32_t flags;        /* reserved, 0 */
+  uint32_t flags;        /* Q35_FLAG_* bits, 0 by default */
 } q35_opts;
+
+/* Consume prompts one token per step (the decode step without the head)
+ * instead of in chunks of 16 tokens. Both give bit-identical state; the
+ * chunked route reads each weight once per chunk. */
+#define Q35_FLAG_TOKEN_BY_TOKEN_PROMPT 1u
 
 /* ---------------------------------------------------------------------- */
 /* Session API                                                             */
