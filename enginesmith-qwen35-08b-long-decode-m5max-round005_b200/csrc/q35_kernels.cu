@@ -860,7 +860,7 @@ __device__ void head_finish(const HeadArgs& a, float* red, uint32_t* cand, uint3
     float s = 0.0f;
     for (int c = lane; c < int(gridDim.x); c += 32) {
       const float sc = __ldcg(&a.part[2 * c + 1]);
-      if (sc > 0.0f) s += sc * expf(__ldcg(&a.part[2 * c]) - M);
+      if (sc > 0.0f) s = __fmaf_rn(sc, expf(__ldcg(&a.part[2 * c]) - M), s);
     }
     s = warp_sum(s);
     if (lane == 0) {
@@ -899,31 +899,51 @@ __device__ void head_finish(const HeadArgs& a, float* red, uint32_t* cand, uint3
   }
 }
 
+// Online (max, sum exp) of one thread's logits, one logit at a time.
+__device__ __forceinline__ void lse_push(float& run_m, float& run_s, float lv) {
+  if (lv > run_m) {
+    run_s = __fmaf_rn(run_s, __expf(run_m - lv), 1.0f);
+    run_m = lv;
+  } else {
+    run_s += __expf(lv - run_m);
+  }
+}
+
+// Warp-level (max, sum exp) of the lanes' online states (warp butterfly).
+__device__ __forceinline__ void lse_warp(float run_m, float run_s, float& M, float& S) {
+  M = warp_max(run_m);
+  const float s = run_s > 0.0f ? run_s * __expf(run_m - M) : 0.0f;
+  S = warp_sum(s);
+}
+
+// One thread: the CTA's (max, sum exp) from its warps' partials, stored as
+// the CTA's grid partial; returns whether this CTA arrived last.
+__device__ __forceinline__ bool lse_cta(const float* wm, const float* ws, int nw, float* part,
+                                        uint32_t* counter) {
+  float MM = wm[0];
+  for (int w = 1; w < nw; ++w) MM = fmaxf(MM, wm[w]);
+  float ss = 0.0f;
+  for (int w = 0; w < nw; ++w)
+    if (ws[w] > 0.0f) ss = __fmaf_rn(ws[w], __expf(wm[w] - MM), ss);
+  part[2 * blockIdx.x] = MM;
+  part[2 * blockIdx.x + 1] = ss;
+  __threadfence();
+  return atomicAdd(counter, 1u) == gridDim.x - 1;
+}
+
 // Per-CTA (max, sum exp) of a row range of bf16 logits, combined into the
 // CTA's partial; returns whether this CTA arrived last.
 __device__ bool head_partial(const HeadArgs& a, float run_m, float run_s, float* wm, float* ws,
                              int* last) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  float M = warp_max(run_m);
-  float s = run_s > 0.0f ? run_s * __expf(run_m - M) : 0.0f;
-  s = warp_sum(s);
+  float M, S;
+  lse_warp(run_m, run_s, M, S);
   if (lane == 0) {
     wm[warp] = M;
-    ws[warp] = s;
+    ws[warp] = S;
   }
   __syncthreads();
-  if (tid == 0) {
-    const int nw = blockDim.x / 32;
-    float MM = wm[0];
-    for (int w = 1; w < nw; ++w) MM = fmaxf(MM, wm[w]);
-    float ss = 0.0f;
-    for (int w = 0; w < nw; ++w)
-      if (ws[w] > 0.0f) ss += ws[w] * __expf(wm[w] - MM);
-    a.part[2 * blockIdx.x] = MM;
-    a.part[2 * blockIdx.x + 1] = ss;
-    __threadfence();
-    *last = (atomicAdd(&a.ctl->head_counter, 1u) == gridDim.x - 1);
-  }
+  if (tid == 0) *last = lse_cta(wm, ws, blockDim.x / 32, a.part, &a.ctl->head_counter);
   __syncthreads();
   return *last != 0;
 }
@@ -1034,13 +1054,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1) k_head(const __grid_constant_
       if (lane < 4 && g0 + lane < rows) {
         const uint16_t lb = f2bf(S.vals[g0 + lane]);
         a.logits[r0 + ch * kHeadRowsPerChunk + g0 + lane] = lb;
-        const float lv = bf2f(lb);
-        if (lv > run_m) {
-          run_s = run_s * __expf(run_m - lv) + 1.0f;
-          run_m = lv;
-        } else {
-          run_s += __expf(lv - run_m);
-        }
+        lse_push(run_m, run_s, bf2f(lb));
       }
     }
     __syncwarp();
@@ -1050,6 +1064,160 @@ __global__ void __launch_bounds__(kHeadThreads, 1) k_head(const __grid_constant_
   head_finish(a, S.red, &S.cand, &S.best);
 }
 
+
+// Vocabulary head for up to kMaxSessions sessions at once: the head's chunk
+// ring streams each weight row once and applies it to every session; per
+// session the logits, the online (max, sum exp) of lanes 4t..4t+3 (rows
+// 0..3 of a warp's four, as lanes 0..3 in k_head), the CTA and grid
+// combines and the greedy tail are those of k_head, so each session's
+// result equals a single-session head's bit for bit.
+constexpr int kHeadBStages = 3;
+struct HeadBatchSmem {
+  uint32_t codes[kHeadBStages][kHeadRowsPerChunk * 128];
+  uint16_t scl[kHeadBStages][kHeadRowsPerChunk * 16];
+  uint16_t bia[kHeadBStages][kHeadRowsPerChunk * 16];
+  float xf[kMaxSessions][kHidden];
+  float4 xq[kMaxSessions][2 * 4 * 32];
+  float xsum[kMaxSessions][2 * 32];
+  float red[64];
+  float wm[kMaxSessions][kHeadThreads / 32], ws[kMaxSessions][kHeadThreads / 32];
+  uint64_t bar[kHeadBStages];
+  uint32_t done[kHeadBStages];
+  int last[kMaxSessions];
+  uint32_t cand;
+  uint32_t best;
+};
+size_t head_batch_smem_bytes() { return sizeof(HeadBatchSmem); }
+
+__global__ void __launch_bounds__(kHeadThreads, 1) k_head_batch(const __grid_constant__ HeadBatchArgs a) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  HeadBatchSmem& S = *reinterpret_cast<HeadBatchSmem*>(smem_raw);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n = a.n;
+  const int r0 = blockIdx.x * kHeadRowsPerCta;
+  const int nrows = min(kHeadRowsPerCta, kVocab - r0);
+  const int nchunks = (nrows + kHeadRowsPerChunk - 1) / kHeadRowsPerChunk;
+  auto issue = [&](int ch, int st) {
+    const int rows = min(kHeadRowsPerChunk, nrows - ch * kHeadRowsPerChunk);
+    const size_t row = size_t(r0) + size_t(ch) * kHeadRowsPerChunk;
+    mbar_expect_tx(&S.bar[st], uint32_t(rows) * (512 + 64));
+    bulk_g2s(S.codes[st], a.w + row * 128, uint32_t(rows) * 512, &S.bar[st]);
+    bulk_g2s(S.scl[st], a.s + row * 16, uint32_t(rows) * 32, &S.bar[st]);
+    bulk_g2s(S.bia[st], a.b + row * 16, uint32_t(rows) * 32, &S.bar[st]);
+  };
+  if (tid == 0) {
+    for (int s = 0; s < kHeadBStages; ++s) {
+      mbar_init(&S.bar[s], 1);
+      S.done[s] = 0;
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (tid == 0)
+    for (int s = 0; s < kHeadBStages && s < nchunks; ++s) issue(s, s);
+  pdl_wait();
+  pdl_launch();
+  // final RMSNorm of session `warp` (the warp-level form of rms1024_reg)
+  if (warp < n) {
+    float gain[8][4];
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+      const float4 g4 = a.gain ? bf4(*reinterpret_cast<const uint2*>(a.gain + 128 * s + 4 * lane))
+                               : make_float4(1.f, 1.f, 1.f, 1.f);
+      gain[s][0] = g4.x, gain[s][1] = g4.y, gain[s][2] = g4.z, gain[s][3] = g4.w;
+    }
+    float v[8][4];
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+      const float4 x4 = bf4(*reinterpret_cast<const uint2*>(a.x + size_t(warp) * kHidden + 128 * s + 4 * lane));
+      v[s][0] = x4.x, v[s][1] = x4.y, v[s][2] = x4.z, v[s][3] = x4.w;
+    }
+    const float inv = a.gain ? rms1024_warp_inv(v) : 1.0f;
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+      float o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        o[j] = a.gain ? bfr(__fmul_rn(bfr(__fmul_rn(v[s][j], inv)), gain[s][j])) : v[s][j];
+      *reinterpret_cast<float4*>(&S.xf[warp][128 * s + 4 * lane]) = make_float4(o[0], o[1], o[2], o[3]);
+    }
+  }
+  __syncthreads();
+  for (int t = 0; t < n; ++t) build_xq(S.xf[t], kHidden, S.xq[t], S.xsum[t]);
+  __syncthreads();
+
+  float run_m = -INFINITY, run_s = 0.0f;  // lane 4t + r: session t, row r of the warp's four
+  const int g0 = 4 * warp, my_t = lane >> 2, my_r = lane & 3;
+  for (int ch = 0; ch < nchunks; ++ch) {
+    const int st = ch % kHeadBStages;
+    mbar_wait(&S.bar[st], uint32_t(ch / kHeadBStages) & 1u, a.out[0].ctl, kErrHeadWait);
+    const int rows = min(kHeadRowsPerChunk, nrows - ch * kHeadRowsPerChunk);
+    float mine = 0.0f;
+    if (g0 < rows) {
+#pragma unroll 1
+      for (int t = 0; t < n; ++t) {
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          float4 xx[4], cc[4];
+          float xs;
+          load_xq(S.xq[t], S.xsum[t], c, lane, xx, cc, xs);
+          float term[4];
+          qmv_rows_terms(S.codes[st], S.scl[st], S.bia[st], rows, g0, c, kHidden, xx, cc, xs, lane,
+                         term);
+#pragma unroll
+          for (int r = 0; r < 4; ++r) acc[r] = __fadd_rn(acc[r], term[r]);
+        }
+        const float v = reduce4(acc[0], acc[1], acc[2], acc[3], lane);  // row r in lane 8r
+        const float vr = __shfl_sync(0xffffffffu, v, 8 * my_r);
+        if (my_t == t) mine = vr;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) {
+      __threadfence_block();
+      if (atomicAdd(&S.done[st], 1u) == uint32_t(kHeadThreads / 32 - 1)) {
+        S.done[st] = 0;
+        if (ch + kHeadBStages < nchunks) {
+          fence_proxy_async();
+          issue(ch + kHeadBStages, st);
+        }
+      }
+    }
+    if (my_t < n && g0 + my_r < rows) {
+      const uint16_t lb = f2bf(mine);
+      a.out[my_t].logits[r0 + ch * kHeadRowsPerChunk + g0 + my_r] = lb;
+      lse_push(run_m, run_s, bf2f(lb));
+    }
+    __syncwarp();
+  }
+  // per session: warp and CTA combines, then the grid tail on its last CTA
+  for (int t = 0; t < n; ++t) {
+    float M, Ssum;
+    lse_warp(my_t == t ? run_m : -INFINITY, my_t == t ? run_s : 0.0f, M, Ssum);
+    if (lane == 0) {
+      S.wm[t][warp] = M;
+      S.ws[t][warp] = Ssum;
+    }
+  }
+  __syncthreads();
+  if (tid < n) S.last[tid] = lse_cta(S.wm[tid], S.ws[tid], kHeadThreads / 32, a.out[tid].part,
+                                     &a.out[tid].ctl->head_counter);
+  __syncthreads();
+  for (int t = 0; t < n; ++t) {
+    if (!S.last[t]) continue;
+    HeadArgs v = {};
+    v.logits = a.out[t].logits;
+    v.part = a.out[t].part;
+    v.seq = a.out[t].seq;
+    v.out_tokens = a.out[t].out_tokens;
+    v.seq_len = a.out[t].seq_len;
+    v.out_len = a.out[t].out_len;
+    v.lse_out = a.out[t].lse;
+    v.ctl = a.out[t].ctl;
+    head_finish(v, S.red, &S.cand, &S.best);
+  }
+}
 
 // Greedy selection on given logits (greedy_bf16, linear.metal:400-449), with
 // the head's partition and tail.
@@ -1061,13 +1229,7 @@ __global__ void __launch_bounds__(256) k_greedy(const __grid_constant__ HeadArgs
   const int r1 = min(kVocab, r0 + kHeadRowsPerCta);
   float run_m = -INFINITY, run_s = 0.0f;
   for (int r = r0 + threadIdx.x; r < r1; r += blockDim.x) {
-    const float lv = bf2f(a.logits[r]);
-    if (lv > run_m) {
-      run_s = run_s * __expf(run_m - lv) + 1.0f;
-      run_m = lv;
-    } else {
-      run_s += __expf(lv - run_m);
-    }
+    lse_push(run_m, run_s, bf2f(a.logits[r]));
   }
   if (!head_partial(a, run_m, run_s, wm, ws, &last)) return;
   head_finish(a, red, &cand, &best);
@@ -1164,6 +1326,9 @@ cudaError_t kernels_init() {
   e = cudaFuncSetAttribute(k_head, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            int(spread(head_smem_bytes())));
   if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(k_head_batch, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           int(spread(head_batch_smem_bytes())));
+  if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(k_gdn_recur, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            int(kSpreadSmem));
   if (e != cudaSuccess) return e;
@@ -1195,6 +1360,11 @@ cudaError_t launch_attn(const AttnArgs& a, cudaStream_t st, bool pdl) {
 }
 cudaError_t launch_head(const HeadArgs& a, cudaStream_t st, bool pdl) {
   return launch_ex(k_head, dim3(kHeadCtas), dim3(kHeadThreads), spread(head_smem_bytes()), st, pdl, a);
+}
+cudaError_t launch_head_batch(const HeadBatchArgs& a, cudaStream_t st, bool pdl) {
+  if (a.n < 1 || a.n > kMaxSessions) return cudaErrorInvalidValue;
+  return launch_ex(k_head_batch, dim3(kHeadCtas), dim3(kHeadThreads), spread(head_batch_smem_bytes()), st,
+                   pdl, a);
 }
 cudaError_t launch_greedy(const HeadArgs& a, cudaStream_t st) {
   return launch_ex(k_greedy, dim3(kHeadCtas), dim3(256), 0, st, false, a);

@@ -18,6 +18,7 @@ cudaError_t launch_qmv(const QmvArgs& a, cudaStream_t st, bool pdl);
 cudaError_t launch_recur(const RecurArgs& a, cudaStream_t st, bool pdl);
 cudaError_t launch_attn(const AttnArgs& a, cudaStream_t st, bool pdl);
 cudaError_t launch_head(const HeadArgs& a, cudaStream_t st, bool pdl);
+cudaError_t launch_head_batch(const HeadBatchArgs& a, cudaStream_t st, bool pdl);
 cudaError_t launch_greedy(const HeadArgs& a, cudaStream_t st);
 cudaError_t launch_gdn_conv(const uint16_t* raw, uint16_t* hist, const uint16_t* convw,
                             uint16_t* conv_out, cudaStream_t st);
@@ -29,6 +30,7 @@ cudaError_t chunk_kernels_init();
 int chunk_sub_tokens(const QmvArgs& a);  // tokens per shared-memory sub-chunk
 cudaError_t launch_qmv_chunk(const QmvArgs& a, cudaStream_t st, bool pdl);
 cudaError_t launch_recur_chunk(const RecurArgs& a, cudaStream_t st, bool pdl);
+cudaError_t launch_recur_sessions(const RecurArgs& a, int n, cudaStream_t st, bool pdl);
 cudaError_t launch_embedding(const uint32_t* w, const uint16_t* s, const uint16_t* b,
                              uint32_t token, int K, uint16_t* out, cudaStream_t st);
 cudaError_t launch_rms1024(const uint16_t* x, const uint16_t* gain, uint16_t* out,

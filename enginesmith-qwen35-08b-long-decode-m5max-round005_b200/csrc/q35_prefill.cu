@@ -81,25 +81,6 @@ __device__ __forceinline__ void chunk_consts(const float4* xrow, int c, int lane
   xs = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.0f, g[0]), g[1]), g[2]), g[3]);
 }
 
-// RMSNorm of one 1024-vector by one warp in the reference's block order
-// (linear_input_norm.metal:41-63): lane l holds x[128 s + 4 l + j] in v[s][j],
-// i.e. the four values of thread 32 s + l of a 256-thread block; each SIMD
-// group's partial is that lane set's butterfly sum. Returns 1/rms.
-__device__ __forceinline__ float rms1024_warp_inv(const float (&v)[8][4]) {
-  float red[8];
-#pragma unroll
-  for (int s = 0; s < 8; ++s) {
-    float acc = 0.0f;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) acc = __fadd_rn(acc, __fmul_rn(v[s][j], v[s][j]));
-    red[s] = warp_sum(acc);
-  }
-  const float t0 = __fadd_rn(red[0], red[4]), t1 = __fadd_rn(red[1], red[5]);
-  const float t2 = __fadd_rn(red[2], red[6]), t3 = __fadd_rn(red[3], red[7]);
-  const float total = __fadd_rn(__fadd_rn(t0, t2), __fadd_rn(t1, t3));
-  return drsqrtf(__fadd_rn(__fmul_rn(total, 0.0009765625f), 1e-6f));
-}
-
 template <int PRO, int EPI>
 __global__ void __launch_bounds__(kChunkThreads, 1) k_qmv_chunk(const __grid_constant__ QmvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -155,11 +136,13 @@ __global__ void __launch_bounds__(kChunkThreads, 1) k_qmv_chunk(const __grid_con
   uint16_t hh[3] = {0, 0, 0};
   uint16_t cw[4] = {0, 0, 0, 0};
   if (EPI == kEpiGdnConv && e_seg == 0) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) cw[j] = a.convw[4 * e_row + j];
+  }
+  if (EPI == kEpiGdnConv && e_seg == 0 && !a.sess) {
     hh[0] = a.hist[e_row];
     hh[1] = a.hist[kGdnConv + e_row];
     hh[2] = a.hist[2 * kGdnConv + e_row];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) cw[j] = a.convw[4 * e_row + j];
   }
   // RMS gain of this lane's activations (k = 128 s + 4 lane + j)
   float gain[8][4];
@@ -174,7 +157,16 @@ __global__ void __launch_bounds__(kChunkThreads, 1) k_qmv_chunk(const __grid_con
   pdl_wait();
   pdl_launch();
   uint32_t pos0 = 0;
-  if (PRO == kProEmbedRms) {
+  if (PRO == kProEmbedRms && a.sess) {
+    // batched sessions: each session's step position and RoPE row
+    if (blockIdx.x == 0)
+      for (int i = tid; i < a.ntok * 32; i += kChunkThreads) {
+        Ctl* c = a.ctls[i >> 5];
+        const uint32_t p = ld_cg_u32(&c->pos);
+        if ((i & 31) == 0) c->pos_step = p;
+        rope_pair(p, i & 31, a.rope_out + 64 * (i >> 5));
+      }
+  } else if (PRO == kProEmbedRms) {
     pos0 = ld_cg_u32(&a.ctl->pos);
     if (blockIdx.x == 0) {
       if (tid == 0) a.ctl->pos_step = pos0;
@@ -198,9 +190,11 @@ __global__ void __launch_bounds__(kChunkThreads, 1) k_qmv_chunk(const __grid_con
         float v[8][4];
         if (PRO == kProEmbedRms) {
           // linear.metal:19-23 for the token at position pos0 + t0 + t
-          uint32_t token = ld_cg_u32(&a.seq[pos0 + uint32_t(t0 + t)]);
+          uint32_t token =
+              a.sess ? ld_cg_u32(&a.seqs[t0 + t][ld_cg_u32(&a.ctls[t0 + t]->pos)])
+                     : ld_cg_u32(&a.seq[pos0 + uint32_t(t0 + t)]);
           if (token >= uint32_t(kVocab)) {
-            if (lane == 0) atomicCAS(&a.ctl->err, 0u, kErrToken);
+            if (lane == 0) atomicCAS(&(a.sess ? a.ctls[t0 + t] : a.ctl)->err, 0u, kErrToken);
             token = 0;
           }
 #pragma unroll
@@ -302,10 +296,19 @@ __global__ void __launch_bounds__(kChunkThreads, 1) k_qmv_chunk(const __grid_con
           *r = f2bf(__fadd_rn(bf2f(*r), bfr(v)));
         } else if (EPI == kEpiGdnConv && e_seg == 0) {
           const uint16_t raw = f2bf(v);
-          a.conv_out[tt * kGdnConv + e_row] = gdn_conv_value(hh[0], hh[1], hh[2], raw, cw);
-          hh[0] = hh[1];
-          hh[1] = hh[2];
-          hh[2] = raw;
+          if (a.sess) {  // each session's own history
+            uint16_t* hs = a.hists[tt] + a.hist_off;
+            const uint16_t h0 = hs[e_row], h1 = hs[kGdnConv + e_row], h2 = hs[2 * kGdnConv + e_row];
+            a.conv_out[tt * kGdnConv + e_row] = gdn_conv_value(h0, h1, h2, raw, cw);
+            hs[e_row] = h1;
+            hs[kGdnConv + e_row] = h2;
+            hs[2 * kGdnConv + e_row] = raw;
+          } else {
+            a.conv_out[tt * kGdnConv + e_row] = gdn_conv_value(hh[0], hh[1], hh[2], raw, cw);
+            hh[0] = hh[1];
+            hh[1] = hh[2];
+            hh[2] = raw;
+          }
         } else {
           a.seg[e_seg].y[tt * a.ystride[e_seg] + e_row] = f2bf(v);
         }
@@ -313,7 +316,7 @@ __global__ void __launch_bounds__(kChunkThreads, 1) k_qmv_chunk(const __grid_con
     }
     __syncthreads();
   }
-  if (EPI == kEpiGdnConv && e_seg == 0) {
+  if (EPI == kEpiGdnConv && e_seg == 0 && !a.sess) {
     a.hist[e_row] = hh[0];
     a.hist[kGdnConv + e_row] = hh[1];
     a.hist[2 * kGdnConv + e_row] = hh[2];
@@ -371,6 +374,52 @@ __global__ void __launch_bounds__(64) k_gdn_recur_chunk(const __grid_constant__ 
   for (int i = 0; i < 8; ++i) dst[i] = make_float4(s[4 * i], s[4 * i + 1], s[4 * i + 2], s[4 * i + 3]);
 }
 
+// GDN recurrence for batched sessions: the decode step's k_gdn_recur for
+// session blockIdx.z (its own state, conv row, gates and output row).
+__global__ void __launch_bounds__(64) k_gdn_recur_sessions(const __grid_constant__ RecurArgs a) {
+  __shared__ __align__(16) float st[16 * 128];
+  __shared__ float qn[128], kn[128], gb[2];
+  __shared__ __align__(8) uint64_t bar;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int rb = blockIdx.x, h = blockIdx.y, z = blockIdx.z;
+  float* state = a.states[z] + a.state_off;
+  const uint16_t* conv = a.conv + size_t(z) * kGdnConv;
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    mbar_expect_tx(&bar, 16 * 128 * 4);
+    bulk_g2s(st, state + (size_t(h) * 128 + rb * 16) * 128, 16 * 128 * 4, &bar);
+  }
+  pdl_wait();
+  pdl_launch();
+  Ctl* ctl = a.ctls[z];
+  if (a.advance_pos && rb == 0 && h == 0 && tid == 0) ctl->pos = ctl->pos_step + 1;
+  gdn_qk_norm(conv, h, warp == 0, lane, warp == 0 ? qn : kn);
+  if (tid == 0) {
+    gb[0] = gdn_gate(a.a_raw[z * 32 + h], a.dt_bias[h], dexpf(a.a_log[h]));
+  } else if (tid == 32) {
+    gb[1] = gdn_beta(a.b_raw[z * 32 + h]);
+  }
+  __syncthreads();
+  mbar_wait(&bar, 0, ctl, kErrRecurWait);
+  const int row = tid >> 2, r = tid & 3;
+  const int vrow = rb * 16 + row;
+  float s[32];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 t = *reinterpret_cast<const float4*>(&st[row * 128 + r * 32 + i * 4]);
+    s[i * 4 + 0] = t.x;
+    s[i * 4 + 1] = t.y;
+    s[i * 4 + 2] = t.z;
+    s[i * 4 + 3] = t.w;
+  }
+  const float out = gdn_row_step(s, kn + r * 32, qn + r * 32, gb[0], gb[1], bf2f(conv[4096 + h * 128 + vrow]));
+  if (r == 0) a.y[size_t(z) * 2048 + h * 128 + vrow] = f2bf(out);
+  float4* dst = reinterpret_cast<float4*>(state + (size_t(h) * 128 + vrow) * 128 + r * 32);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) dst[i] = make_float4(s[4 * i], s[4 * i + 1], s[4 * i + 2], s[4 * i + 3]);
+}
+
 // ---------------------------------------------------------------------------
 // launchers
 // ---------------------------------------------------------------------------
@@ -406,6 +455,11 @@ cudaError_t launch_qmv_chunk(const QmvArgs& a, cudaStream_t st, bool pdl) {
   if (!kern || a.ntok < 1 || a.ntok > kPrefillTokens || a.sub < 1) return cudaErrorInvalidValue;
   const int grid = (a.units + a.units_per_cta - 1) / a.units_per_cta;
   return launch_ex(kern, dim3(grid), dim3(kChunkThreads), chunk_smem_bytes(a), st, pdl, a);
+}
+
+cudaError_t launch_recur_sessions(const RecurArgs& a, int n, cudaStream_t st, bool pdl) {
+  if (n < 1 || n > kMaxSessions) return cudaErrorInvalidValue;
+  return launch_ex(k_gdn_recur_sessions, dim3(8, kGdnHeads, n), dim3(64), 0, st, pdl, a);
 }
 
 cudaError_t launch_recur_chunk(const RecurArgs& a, cudaStream_t st, bool pdl) {

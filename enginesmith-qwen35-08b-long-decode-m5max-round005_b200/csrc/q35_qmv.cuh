@@ -254,4 +254,23 @@ Q35_DEV void rms1024_reg(const float v[4], const float g[4], float out[4], float
   for (int j = 0; j < 4; ++j) out[j] = bfr(__fmul_rn(bfr(__fmul_rn(v[j], inv)), g[j]));
 }
 
+// RMSNorm of one 1024-vector by one warp in the reference's block order
+// (linear_input_norm.metal:41-63): lane l holds x[128 s + 4 l + j] in v[s][j],
+// i.e. the four values of thread 32 s + l of a 256-thread block; each SIMD
+// group's partial is that lane set's butterfly sum. Returns 1/rms.
+Q35_DEV float rms1024_warp_inv(const float (&v)[8][4]) {
+  float red[8];
+#pragma unroll
+  for (int s = 0; s < 8; ++s) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc = __fadd_rn(acc, __fmul_rn(v[s][j], v[s][j]));
+    red[s] = warp_sum(acc);
+  }
+  const float t0 = __fadd_rn(red[0], red[4]), t1 = __fadd_rn(red[1], red[5]);
+  const float t2 = __fadd_rn(red[2], red[6]), t3 = __fadd_rn(red[3], red[7]);
+  const float total = __fadd_rn(__fadd_rn(t0, t2), __fadd_rn(t1, t3));
+  return drsqrtf(__fadd_rn(__fmul_rn(total, 0.0009765625f), 1e-6f));
+}
+
 }  // namespace q35

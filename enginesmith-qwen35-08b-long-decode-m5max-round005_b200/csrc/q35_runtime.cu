@@ -3,6 +3,8 @@
 // source/src/weights.rs) with CUDA streams/graphs in place of Metal command
 // buffers.
 #include <dirent.h>
+#include <limits.h>
+#include <stdlib.h>
 
 #include <algorithm>
 #include <atomic>
@@ -350,6 +352,7 @@ struct q35_session {
   uint32_t pending = 0;
   std::atomic<bool> cancelled{false};
   std::string err;
+  std::string model_id;  // canonical model directory (batched sessions must share it)
 
   uint16_t* kcache(int ai) { return kv + size_t(ai) * 2 * kKvHeads * capacity * kHeadDim; }
   uint16_t* vcache(int ai) { return kcache(ai) + size_t(kKvHeads) * capacity * kHeadDim; }
@@ -792,9 +795,404 @@ int check_device_ctl(q35_session* s) {
 
 }  // namespace
 
+// ---------------------------------------------------------------------------
+// Batched sessions: up to kMaxSessions sessions of one device decoded together.
+// Each step streams the weights once for all of them (chunk matvecs over the
+// sessions' pending tokens, the batched head), while each session keeps its
+// own control block, token ring, GDN state, conv history and KV cache; its
+// tokens are those it would produce decoding alone.
+// ---------------------------------------------------------------------------
+struct q35_batch {
+  int n = 0;
+  int device = 0;
+  q35_session* s[kMaxSessions] = {};
+  cudaStream_t stream = nullptr;
+  uint8_t* buf = nullptr;
+  Ctl** ctls = nullptr;
+  uint32_t** seqs = nullptr;
+  uint16_t** hists = nullptr;
+  float** states = nullptr;
+  uint16_t *h = nullptr, *conv = nullptr, *z = nullptr, *ab = nullptr, *y = nullptr;
+  uint16_t *q = nullptr, *k = nullptr, *v = nullptr, *gated = nullptr, *act = nullptr;
+  float *rope = nullptr, *po = nullptr, *pml = nullptr;
+  cudaGraphExec_t g1 = nullptr, gN = nullptr;
+  int nbatch = 8;
+  std::string err;
+};
+
+namespace {
+
+cudaError_t enqueue_batch_step(q35_batch* b, bool first) {
+  const ModelW& M = b->s[0]->M;
+  cudaStream_t st = b->stream;
+  const int n = b->n;
+  bool pdl = !first;
+  cudaError_t e = cudaSuccess;
+#define Q35_B(x)                    \
+  do {                              \
+    e = (x);                        \
+    if (e != cudaSuccess) return e; \
+    pdl = true;                     \
+  } while (0)
+  auto rows = [&](QmvArgs& a) {
+    a.ntok = n;
+    a.sub = chunk_sub_tokens(a);
+    a.ctl = b->s[0]->ctl;
+  };
+  int gi = 0, ai = 0;
+  for (int l = 0; l < kLayers; ++l) {
+    const LayerW& L = M.L[l];
+    if (!L.attn) {
+      QmvArgs a = {};
+      a.seg[0] = {L.qkv.w, L.qkv.s, L.qkv.b, nullptr, 6144};
+      a.seg[1] = {L.z.w, L.z.s, L.z.b, b->z, 2048};
+      a.seg[2] = {L.a.w, L.a.s, L.a.b, b->ab, 16};
+      a.seg[3] = {L.bproj.w, L.bproj.s, L.bproj.b, b->ab + 16, 16};
+      a.ystride[1] = 2048;
+      a.ystride[2] = 32;
+      a.ystride[3] = 32;
+      a.nseg = 4;
+      a.K = 1024;
+      a.units = 8224;
+      a.units_per_cta = 56;
+      a.pro = l == 0 ? kProEmbedRms : kProRms;
+      a.epi = kEpiGdnConv;
+      a.x = b->h;
+      a.gain = L.in_norm;
+      a.h_out = b->h;
+      a.ew = M.embed.w;
+      a.es = M.embed.s;
+      a.eb = M.embed.b;
+      a.rope_out = b->rope;
+      a.convw = L.conv;
+      a.conv_out = b->conv;
+      a.sess = 1;
+      a.ctls = b->ctls;
+      a.seqs = b->seqs;
+      a.hists = b->hists;
+      a.hist_off = size_t(gi) * 3 * kGdnConv;
+      rows(a);
+      Q35_B(launch_qmv_chunk(a, st, pdl));
+      RecurArgs r = {};
+      r.conv = b->conv;
+      r.a_raw = b->ab;
+      r.b_raw = b->ab + 16;
+      r.a_log = L.alog;
+      r.dt_bias = L.dt;
+      r.y = b->y;
+      r.advance_pos = l == 0;
+      r.states = b->states;
+      r.state_off = size_t(gi) * kGdnHeads * 128 * 128;
+      r.ctls = b->ctls;
+      Q35_B(launch_recur_sessions(r, n, st, pdl));
+      QmvArgs o = {};
+      o.seg[0] = {L.out.w, L.out.s, L.out.b, nullptr, 1024};
+      o.nseg = 1;
+      o.K = 2048;
+      o.units = 1024;
+      o.units_per_cta = 7;
+      o.pro = kProNormGate;
+      o.gy = b->y;
+      o.gz = b->z;
+      o.gw = L.gnorm;
+      o.epi = kEpiResAdd;
+      o.res = b->h;
+      rows(o);
+      Q35_B(launch_qmv_chunk(o, st, pdl));
+      ++gi;
+    } else {
+      QmvArgs a = {};
+      a.seg[0] = {L.q.w, L.q.s, L.q.b, b->q, 4096};
+      a.seg[1] = {L.k.w, L.k.s, L.k.b, b->k, 512};
+      a.seg[2] = {L.v.w, L.v.s, L.v.b, b->v, 512};
+      a.ystride[0] = kQProj;
+      a.ystride[1] = 512;
+      a.ystride[2] = 512;
+      a.nseg = 3;
+      a.K = 1024;
+      a.units = 5120;
+      a.units_per_cta = 36;
+      a.pro = kProRms;
+      a.x = b->h;
+      a.gain = L.in_norm;
+      a.epi = kEpiStore;
+      rows(a);
+      Q35_B(launch_qmv_chunk(a, st, pdl));
+      for (int t = 0; t < n; ++t) {
+        q35_session* ss = b->s[t];
+        AttnArgs at = {};
+        at.q_raw = b->q + size_t(t) * kQProj;
+        at.k_raw = b->k + size_t(t) * 512;
+        at.v_raw = b->v + size_t(t) * 512;
+        at.q_gain = L.qnorm;
+        at.k_gain = L.knorm;
+        at.kcache = ss->kcache(ai);
+        at.vcache = ss->vcache(ai);
+        at.capacity = ss->capacity;
+        at.part_o = b->po;
+        at.part_ml = b->pml;
+        at.gated = b->gated + size_t(t) * 2048;
+        at.ctl = ss->ctl;
+        at.rope = b->rope + 64 * t;
+        Q35_B(launch_attn(at, st, pdl));
+      }
+      QmvArgs o = {};
+      o.seg[0] = {L.o.w, L.o.s, L.o.b, nullptr, 1024};
+      o.nseg = 1;
+      o.K = 2048;
+      o.units = 1024;
+      o.units_per_cta = 7;
+      o.pro = kProPlain;
+      o.x = b->gated;
+      o.epi = kEpiResAdd;
+      o.res = b->h;
+      rows(o);
+      Q35_B(launch_qmv_chunk(o, st, pdl));
+      ++ai;
+    }
+    QmvArgs m = {};
+    m.seg[0] = {L.gate.w, L.gate.s, L.gate.b, b->act, kMlp};
+    m.seg[1] = {L.up.w, L.up.s, L.up.b, nullptr, kMlp};
+    m.ystride[0] = kMlp;
+    m.nseg = 2;
+    m.K = 1024;
+    m.units = kMlp;
+    m.units_per_cta = 25;
+    m.pro = kProRms;
+    m.x = b->h;
+    m.gain = L.post_norm;
+    m.epi = kEpiSwiglu;
+    rows(m);
+    Q35_B(launch_qmv_chunk(m, st, pdl));
+    QmvArgs d = {};
+    d.seg[0] = {L.down.w, L.down.s, L.down.b, nullptr, 1024};
+    d.nseg = 1;
+    d.K = kMlp;
+    d.units = 1024;
+    d.units_per_cta = 7;
+    d.pro = kProPlain;
+    d.x = b->act;
+    d.epi = kEpiResAdd;
+    d.res = b->h;
+    rows(d);
+    Q35_B(launch_qmv_chunk(d, st, pdl));
+  }
+  HeadBatchArgs hb = {};
+  hb.w = M.embed.w;
+  hb.s = M.embed.s;
+  hb.b = M.embed.b;
+  hb.x = b->h;
+  hb.gain = M.norm;
+  hb.n = n;
+  for (int t = 0; t < n; ++t) {
+    q35_session* ss = b->s[t];
+    hb.out[t] = {ss->logits, ss->head_part, ss->seq, ss->out_tokens, ss->capacity + 1, ss->capacity,
+                 ss->lse, ss->ctl};
+  }
+  Q35_B(launch_head_batch(hb, st, pdl));
+#undef Q35_B
+  return e;
+}
+
+cudaError_t capture_batch(q35_batch* b, int steps, cudaGraphExec_t* out) {
+  cudaGraph_t g = nullptr;
+  cudaError_t e = cudaStreamBeginCapture(b->stream, cudaStreamCaptureModeThreadLocal);
+  if (e != cudaSuccess) return e;
+  cudaError_t le = cudaSuccess;
+  for (int i = 0; i < steps && le == cudaSuccess; ++i) le = enqueue_batch_step(b, i == 0);
+  e = cudaStreamEndCapture(b->stream, &g);
+  if (le != cudaSuccess) {
+    if (g) cudaGraphDestroy(g);
+    return le;
+  }
+  if (e != cudaSuccess) return e;
+  e = cudaGraphInstantiate(out, g, 0);
+  cudaGraphDestroy(g);
+  return e;
+}
+
+void free_batch(q35_batch* b) {
+  if (!b) return;
+  cudaSetDevice(b->device);
+  for (cudaGraphExec_t g : {b->g1, b->gN})
+    if (g) cudaGraphExecDestroy(g);
+  if (b->buf) cudaFree(b->buf);
+  if (b->stream) cudaStreamDestroy(b->stream);
+  delete b;
+}
+
+int batch_err(q35_batch* b, int code, const std::string& m) {
+  b->err = m;
+  return code;
+}
+
+// Runs `steps` batched steps; returns Q35_OK or an error (sessions reset on
+// device errors, as single sessions are).
+int batch_run(q35_batch* b, size_t steps, float* ms) {
+  for (int t = 0; t < b->n; ++t) {
+    q35_session* ss = b->s[t];
+    if (!ss->has_pending) return batch_err(b, Q35_EINVAL, "session " + std::to_string(t) + ": no continuation state");
+    if (ss->position + steps > ss->capacity)
+      return batch_err(b, Q35_EINVAL, "session " + std::to_string(t) + ": context capacity exceeded");
+  }
+  cudaSetDevice(b->device);
+  cudaError_t e = cudaSuccess;
+  for (int t = 0; t < b->n && e == cudaSuccess; ++t) {
+    e = cudaStreamSynchronize(b->s[t]->stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(&b->s[t]->ctl->out_count, 0, 4, b->stream);
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+  cudaEvent_t ea = nullptr, eb = nullptr;
+  if (ms) {
+    cudaEventCreate(&ea);
+    cudaEventCreate(&eb);
+    if (e == cudaSuccess) e = cudaEventRecord(ea, b->stream);
+  }
+  size_t left = steps, launched = 0;
+  while (left > 0 && e == cudaSuccess) {
+    if (left >= size_t(b->nbatch) && b->gN) {
+      e = cudaGraphLaunch(b->gN, b->stream);
+      left -= size_t(b->nbatch);
+    } else {
+      e = cudaGraphLaunch(b->g1, b->stream);
+      left -= 1;
+    }
+    if (!ms && e == cudaSuccess && ++launched % 16 == 0) e = cudaStreamSynchronize(b->stream);
+  }
+  if (ms) {
+    if (e == cudaSuccess) e = cudaEventRecord(eb, b->stream);
+    if (e == cudaSuccess) e = cudaEventSynchronize(eb);
+    if (e == cudaSuccess) e = cudaEventElapsedTime(ms, ea, eb);
+    cudaEventDestroy(ea);
+    cudaEventDestroy(eb);
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+  if (e != cudaSuccess) {
+    const std::string m = std::string("batched decode: ") + cudaGetErrorString(e);
+    for (int t = 0; t < b->n; ++t) device_failure(b->s[t], e, "batched decode");
+    return batch_err(b, Q35_ECUDA, m);
+  }
+  int rc = Q35_OK;
+  for (int t = 0; t < b->n; ++t) {
+    const int r = check_device_ctl(b->s[t]);
+    if (r != Q35_OK && rc == Q35_OK) {
+      rc = r;
+      b->err = "session " + std::to_string(t) + ": " + b->s[t]->err;
+    }
+  }
+  return rc;
+}
+
+}  // namespace
+
 extern "C" {
 
 const char* q35_version(void) { return "q35-b200 0.1 (sm_100a)"; }
+
+int q35_batch_create(q35_session** sessions, int n, q35_batch** out, char* errbuf, size_t err_len) {
+  if (!out) return Q35_EINVAL;
+  *out = nullptr;
+  auto fail = [&](int code, const std::string& m) {
+    copy_err(errbuf, err_len, m);
+    return code;
+  };
+  if (!sessions || n < 1 || n > kMaxSessions) return fail(Q35_EINVAL, "batch needs 1..8 sessions");
+  for (int t = 0; t < n; ++t) {
+    if (!sessions[t]) return fail(Q35_EINVAL, "null session");
+    if (sessions[t]->device != sessions[0]->device) return fail(Q35_EINVAL, "sessions on different devices");
+    if (sessions[t]->model_id != sessions[0]->model_id) return fail(Q35_EINVAL, "sessions of different models");
+    for (int u = 0; u < t; ++u)
+      if (sessions[u] == sessions[t]) return fail(Q35_EINVAL, "session listed twice");
+  }
+  q35_batch* b = new q35_batch();
+  b->n = n;
+  b->device = sessions[0]->device;
+  for (int t = 0; t < n; ++t) b->s[t] = sessions[t];
+  cudaSetDevice(b->device);
+  cudaError_t e = cudaStreamCreateWithFlags(&b->stream, cudaStreamNonBlocking);
+  struct Part {
+    void** p;
+    size_t bytes;
+  };
+  const size_t N = size_t(n);
+  std::vector<Part> parts = {
+      {(void**)&b->ctls, 8 * N}, {(void**)&b->seqs, 8 * N}, {(void**)&b->hists, 8 * N},
+      {(void**)&b->states, 8 * N}, {(void**)&b->h, N * kHidden * 2}, {(void**)&b->conv, N * kGdnConv * 2},
+      {(void**)&b->z, N * 2048 * 2}, {(void**)&b->ab, N * 32 * 2}, {(void**)&b->y, N * 2048 * 2},
+      {(void**)&b->q, N * kQProj * 2}, {(void**)&b->k, N * 512 * 2}, {(void**)&b->v, N * 512 * 2},
+      {(void**)&b->gated, N * 2048 * 2}, {(void**)&b->act, N * kMlp * 2}, {(void**)&b->rope, N * 64 * 4},
+      {(void**)&b->po, size_t(kKvHeads) * kAttnChains * 4 * kHeadDim * 4},
+      {(void**)&b->pml, size_t(kKvHeads) * kAttnChains * 4 * 2 * 4},
+  };
+  size_t total = 0;
+  for (auto& pt : parts) total += (pt.bytes + 255) & ~size_t(255);
+  if (e == cudaSuccess) e = cudaMalloc(&b->buf, total);
+  if (e == cudaSuccess) e = cudaMemset(b->buf, 0, total);
+  if (e != cudaSuccess) {
+    free_batch(b);
+    return fail(Q35_ENOMEM, std::string("batch buffers: ") + cudaGetErrorString(e));
+  }
+  size_t off = 0;
+  for (auto& pt : parts) {
+    *pt.p = b->buf + off;
+    off += (pt.bytes + 255) & ~size_t(255);
+  }
+  Ctl* hc[kMaxSessions];
+  uint32_t* hs[kMaxSessions];
+  uint16_t* hh[kMaxSessions];
+  float* hst[kMaxSessions];
+  for (int t = 0; t < n; ++t) {
+    hc[t] = sessions[t]->ctl;
+    hs[t] = sessions[t]->seq;
+    hh[t] = sessions[t]->hist;
+    hst[t] = sessions[t]->state;
+  }
+  e = cudaMemcpy(b->ctls, hc, 8 * N, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(b->seqs, hs, 8 * N, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(b->hists, hh, 8 * N, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(b->states, hst, 8 * N, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = capture_batch(b, 1, &b->g1);
+  if (e == cudaSuccess) e = capture_batch(b, b->nbatch, &b->gN);
+  if (e != cudaSuccess) {
+    free_batch(b);
+    return fail(Q35_ECUDA, std::string("batch graph capture: ") + cudaGetErrorString(e));
+  }
+  *out = b;
+  return Q35_OK;
+}
+
+int q35_batch_decode(q35_batch* b, size_t steps, uint32_t* out_tokens) {
+  if (!b || !out_tokens || steps == 0) return Q35_EINVAL;
+  int rc = batch_run(b, steps, nullptr);
+  if (rc != Q35_OK) return rc;
+  for (int t = 0; t < b->n; ++t) {
+    q35_session* ss = b->s[t];
+    cudaError_t e = cudaMemcpy(out_tokens + size_t(t) * steps, ss->out_tokens, steps * 4, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return batch_err(b, device_failure(ss, e, "token read"), "token read");
+    ss->position += uint32_t(steps);
+    ss->pending = out_tokens[size_t(t) * steps + steps - 1];
+  }
+  return Q35_OK;
+}
+
+int q35_batch_decode_timed(q35_batch* b, size_t steps, float* ms) {
+  if (!b || !ms || steps == 0) return Q35_EINVAL;
+  int rc = batch_run(b, steps, ms);
+  if (rc != Q35_OK) return rc;
+  for (int t = 0; t < b->n; ++t) {
+    q35_session* ss = b->s[t];
+    uint32_t last = 0;
+    cudaError_t e = cudaMemcpy(&last, ss->out_tokens + (steps - 1), 4, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return batch_err(b, device_failure(ss, e, "token read"), "token read");
+    ss->position += uint32_t(steps);
+    ss->pending = last;
+  }
+  return Q35_OK;
+}
+
+const char* q35_batch_last_error(const q35_batch* b) { return b ? b->err.c_str() : "no batch"; }
+
+void q35_batch_destroy(q35_batch* b) { free_batch(b); }
 
 int q35_diag_bounded_wait(uint32_t polls, uint32_t* err_dev, void* stream) {
   if (!err_dev || polls == 0) return Q35_EINVAL;
@@ -826,6 +1224,11 @@ int q35_open(const char* model_dir, int device, const q35_opts* opts, q35_sessio
   }
   q35_session* s = new q35_session();
   s->device = device;
+  {
+    char* rp = realpath(model_dir, nullptr);
+    s->model_id = rp ? rp : model_dir;
+    free(rp);
+  }
   if (opts) {
     if (opts->capacity) s->capacity = opts->capacity;
     if (opts->decode_batch) s->dbatch = int(opts->decode_batch);
@@ -1082,6 +1485,39 @@ int q35_dump_state(q35_session* s, uint16_t* kv, float* state, uint16_t* hist) {
   if (e == cudaSuccess && hist)
     e = cudaMemcpy(hist, s->hist, size_t(18) * 3 * kGdnConv * 2, cudaMemcpyDeviceToHost);
   if (e != cudaSuccess) return set_err(s, Q35_ECUDA, std::string("dump: ") + cudaGetErrorString(e));
+  return Q35_OK;
+}
+
+int q35_session_copy(q35_session* dst, q35_session* src) {
+  if (!dst || !src || dst == src) return Q35_EINVAL;
+  if (dst->device != src->device) return set_err(dst, Q35_EINVAL, "copy: sessions on different devices");
+  if (dst->model_id != src->model_id) return set_err(dst, Q35_EINVAL, "copy: sessions of different models");
+  if (dst->capacity != src->capacity) return set_err(dst, Q35_EINVAL, "copy: capacities differ");
+  cudaSetDevice(dst->device);
+  cudaError_t e = cudaStreamSynchronize(src->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(dst->stream);
+  const size_t cap = dst->capacity;
+  struct Part {
+    void* d;
+    const void* s;
+    size_t bytes;
+  };
+  const Part parts[] = {
+      {dst->ctl, src->ctl, sizeof(Ctl)},
+      {dst->seq, src->seq, (cap + 1) * 4},
+      {dst->state, src->state, size_t(18) * kGdnHeads * 128 * 128 * 4},
+      {dst->hist, src->hist, size_t(18) * 3 * kGdnConv * 2},
+      {dst->kv, src->kv, size_t(6) * 2 * kKvHeads * cap * kHeadDim * 2},
+      {dst->logits, src->logits, size_t(kVocab) * 2},
+      {dst->lse, src->lse, 2},
+  };
+  for (const Part& pt : parts)
+    if (e == cudaSuccess) e = cudaMemcpyAsync(pt.d, pt.s, pt.bytes, cudaMemcpyDeviceToDevice, dst->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(dst->stream);
+  if (e != cudaSuccess) return device_failure(dst, e, "copy");
+  dst->position = src->position;
+  dst->pending = src->pending;
+  dst->has_pending = src->has_pending;
   return Q35_OK;
 }
 

@@ -109,6 +109,14 @@ struct QmvArgs {
   int ntok, sub;
   int ystride[4];
   float* rope_out;       // embedding prologue: [ntok][64] RoPE table of the chunk
+  // batched sessions (sess != 0): token t is the pending token of session t,
+  // whose control block, token ring and conv history come from these device
+  // tables (history of this layer at hists[t] + hist_off)
+  int sess;
+  Ctl* const* ctls;
+  uint32_t* const* seqs;
+  uint16_t* const* hists;
+  size_t hist_off;
 };
 
 struct RecurArgs {
@@ -122,6 +130,10 @@ struct RecurArgs {
   Ctl* ctl;
   int advance_pos;
   int ntok;               // prompt chunks: conv [ntok][6144], a/b [ntok][32], y [ntok][2048]
+  // batched sessions: session z's state at states[z] + state_off, control block ctls[z]
+  float* const* states;
+  size_t state_off;
+  Ctl* const* ctls;
 };
 
 struct AttnArgs {
@@ -155,6 +167,27 @@ struct HeadArgs {
   uint32_t out_len;       // entries in out_tokens
   uint16_t* lse_out;      // optional [1]
   Ctl* ctl;
+};
+
+// Batched sessions: per-session outputs of the vocabulary head.
+constexpr int kMaxSessions = 8;
+struct HeadOut {
+  uint16_t* logits;     // [248320]
+  float* part;          // [kHeadCtas][2]
+  uint32_t* seq;        // the session's token ring
+  uint32_t* out_tokens; // the session's output ring
+  uint32_t seq_len, out_len;
+  uint16_t* lse;        // [1]
+  Ctl* ctl;             // the session's control block
+};
+struct HeadBatchArgs {
+  const uint32_t* w;
+  const uint16_t* s;
+  const uint16_t* b;
+  const uint16_t* x;      // [n][1024] hidden states before the final norm
+  const uint16_t* gain;
+  int n;                  // sessions, <= kMaxSessions
+  HeadOut out[kMaxSessions];
 };
 
 }  // namespace q35

@@ -68,6 +68,12 @@ def _load() -> ctypes.CDLL:
         "q35_version": (c_char_p, []),
         "q35_diag_bounded_wait": (c_int, [c_uint32, P, P]),
         "q35_diag_inject_device_error": (c_int, [P, c_uint32]),
+        "q35_session_copy": (c_int, [P, P]),
+        "q35_batch_create": (c_int, [POINTER(c_void_p), c_int, POINTER(c_void_p), c_char_p, c_size_t]),
+        "q35_batch_decode": (c_int, [P, c_size_t, POINTER(c_uint32)]),
+        "q35_batch_decode_timed": (c_int, [P, c_size_t, POINTER(c_float)]),
+        "q35_batch_last_error": (c_char_p, [P]),
+        "q35_batch_destroy": (None, [P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -163,6 +169,10 @@ class Model:
         self._check(lib().q35_last_logits(self._h, lg.ctypes.data, lse.ctypes.data))
         return lg, int(lse[0])
 
+    def copy_from(self, other: "Model") -> None:
+        """Take `other`'s whole decode state (same device, model and capacity)."""
+        self._check(lib().q35_session_copy(self._h, other._h))
+
     def inject_device_error(self, site: int) -> None:
         """Host-side fault injection: record an expired device wait (site code)."""
         self._check(lib().q35_diag_inject_device_error(self._h, site))
@@ -170,6 +180,51 @@ class Model:
     def close(self) -> None:
         if self._h:
             lib().q35_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Batch:
+    """Sessions of one device and one model decoded together: each step reads
+    the weights once for all members, and each member emits the tokens it
+    would emit alone. Members must hold a continuation state (a generate call
+    succeeded on them). Keep the member Models alive while the batch is."""
+
+    def __init__(self, models: list["Model"]):
+        n = len(models)
+        arr = (c_void_p * max(n, 1))(*[m._h.value if isinstance(m._h, c_void_p) else m._h for m in models])
+        h = c_void_p()
+        err = ctypes.create_string_buffer(1024)
+        rc = lib().q35_batch_create(arr, n, ctypes.byref(h), err, len(err))
+        if rc != OK:
+            raise Q35Error(rc, err.value.decode())
+        self._h = h
+        self._models = list(models)
+        self.n = n
+
+    def _check(self, rc: int) -> None:
+        if rc != OK:
+            raise Q35Error(rc, lib().q35_batch_last_error(self._h).decode())
+
+    def decode(self, steps: int) -> list[list[int]]:
+        """`steps` greedy tokens per member; row t belongs to models[t]."""
+        out = (c_uint32 * (self.n * steps))()
+        self._check(lib().q35_batch_decode(self._h, steps, out))
+        return [list(out[t * steps:(t + 1) * steps]) for t in range(self.n)]
+
+    def decode_timed(self, steps: int) -> float:
+        ms = c_float()
+        self._check(lib().q35_batch_decode_timed(self._h, steps, ctypes.byref(ms)))
+        return float(ms.value)
+
+    def close(self) -> None:
+        if self._h:
+            lib().q35_batch_destroy(self._h)
             self._h = None
 
     def __del__(self):

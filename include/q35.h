@@ -101,6 +101,33 @@ int q35_last_logits(q35_session* s, uint16_t* logits, uint16_t* lse);
  * tokens on the device; returns the device time in milliseconds. */
 int q35_decode_timed(q35_session* s, size_t steps, float* ms);
 
+/* Session copy (no counterpart in the reference): dst takes src's whole
+ * decode state (position, continuation token, token history, KV cache,
+ * recurrent state, conv history, last logits), so both continue identically;
+ * e.g. one prompt consumed once and decoded by several sessions. Same device,
+ * model directory and capacity; device-to-device copies on dst's stream. */
+int q35_session_copy(q35_session* dst, q35_session* src);
+
+/* Batched sessions (no counterpart in the reference, whose engine serves one
+ * stream): 1..8 sessions of one device, each already holding a continuation
+ * state (a q35_generate call returned Q35_OK on it), decoded together. Each
+ * batched step streams the weights once for all sessions; every session
+ * keeps its own KV cache, recurrent state, position and token ring, and emits
+ * exactly the tokens and logits it would emit decoding alone. The batch keeps
+ * pointers to the sessions: destroy the batch before any of them, and do not
+ * call q35_generate on a member while a batch call runs. q35_generate with
+ * reset=0 continues a member after a batch call, as after its own. */
+typedef struct q35_batch q35_batch;
+int q35_batch_create(q35_session** sessions, int n, q35_batch** out, char* err, size_t err_len);
+/* `steps` greedy steps for every member; out_tokens is [n][steps] (row t =
+ * session t). Fails (Q35_EINVAL, nothing run) when a member lacks a
+ * continuation state or would pass its capacity. */
+int q35_batch_decode(q35_batch* b, size_t steps, uint32_t* out_tokens);
+/* As q35_batch_decode, tokens left on the device; device time in ms. */
+int q35_batch_decode_timed(q35_batch* b, size_t steps, float* ms);
+const char* q35_batch_last_error(const q35_batch* b);
+void q35_batch_destroy(q35_batch* b);
+
 /* Device-clock timing of the attention launches (benchmark aid, no
  * counterpart in the reference): reads the summed launch time in
  * microseconds and the launch count since the last reset; reset > 0 clears
