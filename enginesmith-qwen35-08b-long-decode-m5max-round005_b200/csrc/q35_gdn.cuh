@@ -44,6 +44,14 @@ Q35_DEV float gdn_gate(uint16_t a_raw, uint16_t dt_bias, float e1) {
 }
 Q35_DEV float gdn_beta(uint16_t b_raw) { return bfr(sigmoid_bf(bf2f(b_raw))); }
 
+// gdn.metal:246-253: the output gate z * sigmoid(z) with sigmoid in plain f32
+// (1 / (1 + e^|z|) mirrored by sign), as the norm-gate prologue forms it.
+Q35_DEV float gdn_zgate(float z) {
+  const float sy = __fdiv_rn(1.0f, __fadd_rn(1.0f, dexpf(fabsf(z))));
+  const float sig = z < 0.0f ? sy : __fsub_rn(1.0f, sy);
+  return __fmul_rn(z, sig);
+}
+
 // gdn.metal:192-225 for one value row, T = 1: 4 lanes per row (lane quarter
 // r owns keys 32r..32r+31, state in s[32]); S *= g; mem = S k (eight
 // four-term partials, then shuffle-xor 1, 2); delta = (v - mem) * beta;

@@ -1154,23 +1154,33 @@ __global__ void __launch_bounds__(kHeadThreads, 1) k_head_batch(const __grid_con
     const int rows = min(kHeadRowsPerChunk, nrows - ch * kHeadRowsPerChunk);
     float mine = 0.0f;
     if (g0 < rows) {
+      // sessions in blocks of kBlockTokens: each block decodes the rows once
 #pragma unroll 1
-      for (int t = 0; t < n; ++t) {
-        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      for (int j0 = 0; j0 < n; j0 += kBlockTokens) {
+        const int nj = min(kBlockTokens, n - j0);
+        float acc[kBlockTokens][4];
+#pragma unroll
+        for (int j = 0; j < kBlockTokens; ++j)
+#pragma unroll
+          for (int r = 0; r < 4; ++r) acc[j][r] = 0.0f;
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
-          float4 xx[4], cc[4];
-          float xs;
-          load_xq(S.xq[t], S.xsum[t], c, lane, xx, cc, xs);
-          float term[4];
-          qmv_rows_terms(S.codes[st], S.scl[st], S.bia[st], rows, g0, c, kHidden, xx, cc, xs, lane,
-                         term);
+          float term[kBlockTokens][4];
+          qmv_block_terms(S.codes[st], S.scl[st], S.bia[st], rows, g0, c, kHidden / 8, kHidden / 64, 2,
+                          &S.xq[0][0], &S.xsum[0][0], j0, nj, lane, term);
 #pragma unroll
-          for (int r = 0; r < 4; ++r) acc[r] = __fadd_rn(acc[r], term[r]);
+          for (int j = 0; j < kBlockTokens; ++j)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) acc[j][r] = __fadd_rn(acc[j][r], term[j][r]);
         }
-        const float v = reduce4(acc[0], acc[1], acc[2], acc[3], lane);  // row r in lane 8r
-        const float vr = __shfl_sync(0xffffffffu, v, 8 * my_r);
-        if (my_t == t) mine = vr;
+#pragma unroll
+        for (int j = 0; j < kBlockTokens; ++j) {
+          if (j < nj) {
+            const float v = reduce4(acc[j][0], acc[j][1], acc[j][2], acc[j][3], lane);  // row r in lane 8r
+            const float vr = __shfl_sync(0xffffffffu, v, 8 * my_r);
+            if (my_t == j0 + j) mine = vr;
+          }
+        }
       }
     }
     __syncwarp();

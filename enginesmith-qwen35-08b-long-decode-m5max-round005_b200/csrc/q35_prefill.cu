@@ -19,7 +19,7 @@
 
 namespace q35 {
 
-constexpr int kChunkThreads = 256;
+constexpr int kChunkThreads = 512;
 constexpr int kChunkWarps = kChunkThreads / 32;
 constexpr size_t kChunkSmemMax = 200 * 1024;
 
@@ -27,11 +27,17 @@ __host__ __device__ inline size_t chunk_align16(size_t v) { return (v + 15) & ~s
 
 // Shared image of a chunk matvec CTA: its weight rows, the f32 activations of
 // `sub` tokens in the lane-major layout the tasks read (token t, chunk c,
-// group i, lane l -> float4 index (t * nch * 4 + c * 4 + i) * 32 + l), the
-// row values of those tokens, a reduction scratch and the weight barrier.
+// group i, lane l -> float4 index (t * nch * 4 + c * 4 + i) * 32 + l; first
+// the raw values, then the scaled x/16^j form), each lane's group-sum xs per
+// (token, chunk), the row values of those tokens and the weight barrier.
 struct ChunkLayout {
-  size_t codes, scl, bia, xf, vals, bar, total;
+  size_t codes, scl, bia, xf, xs, vals, pl, bar, total;
 };
+
+// Rows of K >= 2048 (four or more 512-wide chunks) spread their chunks over
+// warps and stage the per-lane chunk terms in shared memory (pl), summed in
+// chunk order afterwards; shorter rows accumulate their chunks in registers.
+__host__ __device__ inline bool chunk_split(int K) { return K >= 2048; }
 __host__ __device__ inline ChunkLayout chunk_layout(int K, int rows, int sub) {
   ChunkLayout L;
   const int KW = K / 8, KG = K / 64;
@@ -39,8 +45,11 @@ __host__ __device__ inline ChunkLayout chunk_layout(int K, int rows, int sub) {
   L.scl = L.codes + size_t(rows) * KW * 4;
   L.bia = L.scl + size_t(rows) * KG * 2;
   L.xf = chunk_align16(L.bia + size_t(rows) * KG * 2);
-  L.vals = L.xf + size_t(sub) * K * 4;
-  L.bar = chunk_align16(L.vals + size_t(sub) * rows * 4);
+  L.xs = L.xf + size_t(sub) * K * 4;
+  L.vals = L.xs + size_t(sub) * (K / 512) * 32 * 4;
+  L.pl = chunk_align16(L.vals + size_t(sub) * rows * 4);
+  const size_t pl_bytes = chunk_split(K) ? size_t(sub) * rows * (K / 512) * 32 * 4 : 0;
+  L.bar = chunk_align16(L.pl + pl_bytes);
   L.total = L.bar + 16;
   return L;
 }
@@ -63,24 +72,6 @@ __device__ __forceinline__ int xf_slot(int t, int nch, int k) {
   return ((t * nch + c) * 4 + i) * 32 + l;
 }
 
-// The lane's constants of chunk c of one token (exactly as build_xq/emit_xq
-// and load_xq form them): xx = (x0, x1/16, x2/256, x3/4096) per group of
-// four, the magic offsets -2^23 * xx, and xs = (((g0 + g1) + g2) + g3).
-__device__ __forceinline__ void chunk_consts(const float4* xrow, int c, int lane, float4 (&xx)[4],
-                                             float4 (&cc)[4], float& xs) {
-  float g[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float4 v = xrow[(c * 4 + i) * 32 + lane];
-    xx[i] = make_float4(v.x, __fmul_rn(v.y, 0.0625f), __fmul_rn(v.z, 0.00390625f),
-                        __fmul_rn(v.w, 0.000244140625f));
-    cc[i] = make_float4(__fmul_rn(-kTwo23, xx[i].x), __fmul_rn(-kTwo23, xx[i].y),
-                        __fmul_rn(-kTwo23, xx[i].z), __fmul_rn(-kTwo23, xx[i].w));
-    g[i] = __fadd_rn(__fadd_rn(__fadd_rn(v.x, v.y), v.z), v.w);
-  }
-  xs = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.0f, g[0]), g[1]), g[2]), g[3]);
-}
-
 template <int PRO, int EPI>
 __global__ void __launch_bounds__(kChunkThreads, 1) k_qmv_chunk(const __grid_constant__ QmvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -96,7 +87,9 @@ __global__ void __launch_bounds__(kChunkThreads, 1) k_qmv_chunk(const __grid_con
   uint16_t* scl = reinterpret_cast<uint16_t*>(smem + L.scl);
   uint16_t* bia = reinterpret_cast<uint16_t*>(smem + L.bia);
   float4* xf = reinterpret_cast<float4*>(smem + L.xf);
+  float* xsum = reinterpret_cast<float*>(smem + L.xs);
   float* vals = reinterpret_cast<float*>(smem + L.vals);
+  float* pl = reinterpret_cast<float*>(smem + L.pl);
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.bar);
 
   // 1. Weights by bulk copy before the dependency wait (once for all tokens).
@@ -143,15 +136,6 @@ __global__ void __launch_bounds__(kChunkThreads, 1) k_qmv_chunk(const __grid_con
     hh[0] = a.hist[e_row];
     hh[1] = a.hist[kGdnConv + e_row];
     hh[2] = a.hist[2 * kGdnConv + e_row];
-  }
-  // RMS gain of this lane's activations (k = 128 s + 4 lane + j)
-  float gain[8][4];
-  if (PRO == kProRms || PRO == kProEmbedRms) {
-#pragma unroll
-    for (int s = 0; s < 8; ++s) {
-      const float4 g4 = bf4(*reinterpret_cast<const uint2*>(a.gain + 128 * s + 4 * lane));
-      gain[s][0] = g4.x, gain[s][1] = g4.y, gain[s][2] = g4.z, gain[s][3] = g4.w;
-    }
   }
 
   pdl_wait();
@@ -224,9 +208,11 @@ __global__ void __launch_bounds__(kChunkThreads, 1) k_qmv_chunk(const __grid_con
         const float inv = rms1024_warp_inv(v);
 #pragma unroll
         for (int s = 0; s < 8; ++s) {
+          const float4 g4 = bf4(*reinterpret_cast<const uint2*>(a.gain + 128 * s + 4 * lane));
+          const float gn[4] = {g4.x, g4.y, g4.z, g4.w};
           float o[4];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) o[j] = bfr(__fmul_rn(bfr(__fmul_rn(v[s][j], inv)), gain[s][j]));
+          for (int j = 0; j < 4; ++j) o[j] = bfr(__fmul_rn(bfr(__fmul_rn(v[s][j], inv)), gn[j]));
           xf[xf_slot(t, nch, 128 * s + 4 * lane)] = make_float4(o[0], o[1], o[2], o[3]);
         }
       }
@@ -244,40 +230,109 @@ __global__ void __launch_bounds__(kChunkThreads, 1) k_qmv_chunk(const __grid_con
         for (int i = 0; i < 4; ++i) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
         ss = warp_sum(ss);
         const float inv = drsqrtf(__fadd_rn(__fmul_rn(ss, 0.0078125f), 1e-6f));
+        float zg[4];
+        if (a.gzs) {
+          const float4 g4 = *reinterpret_cast<const float4*>(a.gzs + off);
+          zg[0] = g4.x, zg[1] = g4.y, zg[2] = g4.z, zg[3] = g4.w;
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) zg[i] = gdn_zgate(z[i]);
+        }
         float o[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const float norm = bfr(__fmul_rn(bfr(__fmul_rn(v[i], inv)), w[i]));
-          const float sy = __fdiv_rn(1.0f, __fadd_rn(1.0f, dexpf(fabsf(z[i]))));
-          const float sig = z[i] < 0.0f ? sy : __fsub_rn(1.0f, sy);
-          o[i] = bfr(__fmul_rn(__fmul_rn(z[i], sig), norm));
+          o[i] = bfr(__fmul_rn(zg[i], norm));
         }
         xf[xf_slot(t, nch, hd * 128 + 4 * lane)] = make_float4(o[0], o[1], o[2], o[3]);
       }
     }
     __syncthreads();
+    // The decode step's per-lane constants of every (token, chunk): the
+    // group sum xs = (((g0 + g1) + g2) + g3), g = ((x0 + x1) + x2) + x3 of the
+    // lane's four groups, and the activations scaled to (x0, x1/16, x2/256,
+    // x3/4096) in place.
+    for (int idx = tid; idx < nt * nch * 32; idx += kChunkThreads) {
+      const int t = idx / (nch * 32), rem = idx - t * nch * 32, c = rem >> 5, l = rem & 31;
+      float g[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float4& v = xf[((t * nch + c) * 4 + i) * 32 + l];
+        const float4 x = v;
+        g[i] = __fadd_rn(__fadd_rn(__fadd_rn(x.x, x.y), x.z), x.w);
+        v = make_float4(x.x, __fmul_rn(x.y, 0.0625f), __fmul_rn(x.z, 0.00390625f),
+                        __fmul_rn(x.w, 0.000244140625f));
+      }
+      xsum[idx] = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.0f, g[0]), g[1]), g[2]), g[3]);
+    }
+    __syncthreads();
     if (t0 == 0) mbar_wait(bar, 0, a.ctl, kErrQmvWait);
 
-    // 3. One warp per (row group, token): all chunks of four rows accumulated
-    //    in chunk order per lane, then the cross-lane butterfly (reduce4),
-    //    exactly the decode step's chunk terms and finish.
-    for (int task = warp; task < ngroups * nt; task += kChunkWarps) {
-      const int g = task / nt, t = task - g * nt;
-      const float4* xrow = xf + size_t(t) * nch * 4 * 32;
-      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      for (int c = 0; c < nch; ++c) {
-        float4 xx[4], cc[4];
-        float xs;
-        chunk_consts(xrow, c, lane, xx, cc, xs);
-        float term[4];
-        qmv_rows_terms(codes, scl, bia, nrows, 4 * g, c, K, xx, cc, xs, lane, term);
+    // 3. Row terms per (group of four rows, block of kBlockTokens tokens),
+    //    summed over the chunks in chunk order per lane, then the butterfly
+    //    across lanes (reduce4): the decode step's finish.
+    const int ntb = (nt + kBlockTokens - 1) / kBlockTokens;
+    if (!chunk_split(K)) {
+      for (int task = warp; task < ngroups * ntb; task += kChunkWarps) {
+        const int g = task / ntb, j0 = (task - g * ntb) * kBlockTokens;
+        const int nj = min(kBlockTokens, nt - j0);
+        float acc[kBlockTokens][4];
 #pragma unroll
-        for (int r = 0; r < 4; ++r) acc[r] = __fadd_rn(acc[r], term[r]);
+        for (int j = 0; j < kBlockTokens; ++j)
+#pragma unroll
+          for (int r = 0; r < 4; ++r) acc[j][r] = 0.0f;
+#pragma unroll 1
+        for (int c = 0; c < nch; ++c) {
+          float term[kBlockTokens][4];
+          qmv_block_terms(codes, scl, bia, nrows, 4 * g, c, KW, KG, nch, xf, xsum, j0, nj, lane, term);
+#pragma unroll
+          for (int j = 0; j < kBlockTokens; ++j)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) acc[j][r] = __fadd_rn(acc[j][r], term[j][r]);
+        }
+#pragma unroll
+        for (int j = 0; j < kBlockTokens; ++j) {
+          if (j < nj) {
+            const float v = reduce4(acc[j][0], acc[j][1], acc[j][2], acc[j][3], lane);
+            if ((lane & 7) == 0) {
+              const int r = 4 * g + (((lane >> 4) & 1) << 1) + ((lane >> 3) & 1);
+              if (r < nrows) vals[(j0 + j) * rows_alloc + r] = v;
+            }
+          }
+        }
       }
-      const float v = reduce4(acc[0], acc[1], acc[2], acc[3], lane);
-      if ((lane & 7) == 0) {
-        const int r = 4 * g + (((lane >> 4) & 1) << 1) + ((lane >> 3) & 1);
-        if (r < nrows) vals[t * rows_alloc + r] = v;
+    } else {
+      // chunks over warps: per-lane terms to pl[((t * rows + row) * nch + c) * 32 + lane]
+      for (int task = warp; task < ngroups * nch * ntb; task += kChunkWarps) {
+        const int g = task / (nch * ntb), rem = task - g * nch * ntb;
+        const int c = rem / ntb, j0 = (rem - c * ntb) * kBlockTokens;
+        const int nj = min(kBlockTokens, nt - j0);
+        float term[kBlockTokens][4];
+        qmv_block_terms(codes, scl, bia, nrows, 4 * g, c, KW, KG, nch, xf, xsum, j0, nj, lane, term);
+#pragma unroll
+        for (int j = 0; j < kBlockTokens; ++j)
+#pragma unroll
+          for (int r = 0; r < 4; ++r)
+            if (j < nj && 4 * g + r < nrows)
+              pl[((size_t(j0 + j) * rows_alloc + 4 * g + r) * nch + c) * 32 + lane] = term[j][r];
+      }
+      __syncthreads();
+      for (int task = warp; task < ngroups * nt; task += kChunkWarps) {
+        const int g = task / nt, t = task - g * nt;
+        float p[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          float acc = 0.0f;
+          if (4 * g + r < nrows)
+            for (int c = 0; c < nch; ++c)
+              acc = __fadd_rn(acc, pl[((size_t(t) * rows_alloc + 4 * g + r) * nch + c) * 32 + lane]);
+          p[r] = acc;
+        }
+        const float v = reduce4(p[0], p[1], p[2], p[3], lane);
+        if ((lane & 7) == 0) {
+          const int r = 4 * g + (((lane >> 4) & 1) << 1) + ((lane >> 3) & 1);
+          if (r < nrows) vals[t * rows_alloc + r] = v;
+        }
       }
     }
     __syncthreads();
@@ -351,6 +406,11 @@ __global__ void __launch_bounds__(64) k_gdn_recur_chunk(const __grid_constant__ 
     gdn_qk_norm(a.conv + size_t(t) * kGdnConv, h, warp == 0, lane, warp == 0 ? qn[t] : kn[t]);
   if (warp == 0 && lane < nt) gts[lane] = gdn_gate(a.a_raw[lane * 32 + h], dt, e1);
   if (warp == 1 && lane < nt) bts[lane] = gdn_beta(a.b_raw[lane * 32 + h]);
+  if (a.zs)  // this CTA's 16 channels of every token
+    for (int i = tid; i < nt * 16; i += 64) {
+      const size_t off = size_t(i >> 4) * 2048 + h * 128 + rb * 16 + (i & 15);
+      a.zs[off] = gdn_zgate(bf2f(a.z[off]));
+    }
   __syncthreads();
   mbar_wait(&bar, 0, a.ctl, kErrRecurWait);
   const int row = tid >> 2, r = tid & 3;
@@ -399,6 +459,10 @@ __global__ void __launch_bounds__(64) k_gdn_recur_sessions(const __grid_constant
     gb[0] = gdn_gate(a.a_raw[z * 32 + h], a.dt_bias[h], dexpf(a.a_log[h]));
   } else if (tid == 32) {
     gb[1] = gdn_beta(a.b_raw[z * 32 + h]);
+  }
+  if (a.zs && tid >= 48) {  // this CTA's 16 channels of session z
+    const size_t off = size_t(z) * 2048 + h * 128 + rb * 16 + (tid - 48);
+    a.zs[off] = gdn_zgate(bf2f(a.z[off]));
   }
   __syncthreads();
   mbar_wait(&bar, 0, ctl, kErrRecurWait);

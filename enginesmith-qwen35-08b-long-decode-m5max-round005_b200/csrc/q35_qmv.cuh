@@ -175,6 +175,79 @@ Q35_DEV void qmv_chunk_task(const uint32_t* codes, const uint16_t* scl, const ui
   qmv_chunk_core(codes, scl, bia, nrows, r0, c, K, xx, cc, xs, pl, lane);
 }
 
+// Tokens per warp task of the multi-token matvecs (prompt chunks, batched
+// sessions, batched head): a task decodes its weight slice once and applies
+// it to this many tokens.
+constexpr int kBlockTokens = 4;
+
+// Terms s*dot + xs*b of rows [r0, r0+4) (zero for rows >= nrows) for 512-wide
+// chunk c and tokens j0 .. j0+nj-1 of a shared image holding, per token t,
+// the scaled activations (x0, x1/16, x2/256, x3/4096) at float4
+// ((t * nch + c) * 4 + i) * 32 + lane and the group sums at
+// (t * nch + c) * 32 + lane (the layout build_xq writes per token). The lane's 16 nibbles
+// of each row are decoded once into exact floats (the masked value n * 16^j,
+// as the reference's pre-divided activations expect) and applied to every
+// token. Each product n * x/16^j is exact, so fma(n, x, s) rounds exactly
+// like the reference's s + n * x: the four-term sums, the lane's dot sum and
+// s*dot + xs*b are the decode step's operations in the decode step's order.
+Q35_DEV void qmv_block_terms(const uint32_t* codes, const uint16_t* scl,
+                                                  const uint16_t* bia, int nrows, int r0, int c,
+                                                  int KW, int KG, int nch, const float4* xf,
+                                                  const float* xsum, int j0, int nj, int lane,
+                                                  float (&term)[kBlockTokens][4]) {
+  const int w0 = 64 * c + 2 * lane, gi = 8 * c + (lane >> 2);
+  uint2 q[4];
+  float sc[4], bi[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int row = r0 + r < nrows ? r0 + r : nrows - 1;
+    q[r] = *reinterpret_cast<const uint2*>(codes + size_t(row) * KW + w0);
+    sc[r] = bf2f(scl[row * KG + gi]);
+    bi[r] = bf2f(bia[row * KG + gi]);
+  }
+#pragma unroll
+  for (int j = 0; j < kBlockTokens; ++j)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) term[j][r] = 0.0f;
+#pragma unroll
+  for (int hq = 0; hq < 4; ++hq) {
+    float nv[4][4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const uint32_t u = ((hq < 2) ? q[r].x : q[r].y) >> (16 * (hq & 1));
+      nv[r][0] = __fadd_rn(magic(u & 0x000fu), -kTwo23);
+      nv[r][1] = __fadd_rn(magic(u & 0x00f0u), -kTwo23);
+      nv[r][2] = __fadd_rn(magic(u & 0x0f00u), -kTwo23);
+      nv[r][3] = __fadd_rn(magic(u & 0xf000u), -kTwo23);
+    }
+#pragma unroll
+    for (int j = 0; j < kBlockTokens; ++j) {
+      if (j < nj) {
+        const float4 x = xf[(((j0 + j) * nch + c) * 4 + hq) * 32 + lane];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          float h4 = __fmul_rn(nv[r][0], x.x);
+          h4 = __fmaf_rn(nv[r][1], x.y, h4);
+          h4 = __fmaf_rn(nv[r][2], x.z, h4);
+          h4 = __fmaf_rn(nv[r][3], x.w, h4);
+          term[j][r] = __fadd_rn(term[j][r], h4);  // the lane's dot sum
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kBlockTokens; ++j) {
+    if (j < nj) {
+      const float xs = xsum[((j0 + j) * nch + c) * 32 + lane];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const float t = __fadd_rn(__fmul_rn(sc[r], term[j][r]), __fmul_rn(xs, bi[r]));
+        term[j][r] = r0 + r < nrows ? t : 0.0f;
+      }
+    }
+  }
+}
+
 // Transpose-reduce four per-lane values with the pairing of an xor butterfly
 // (16, 8, 4, 2, 1): afterwards lanes 0, 8, 16, 24 hold the butterfly sums of
 // rows 0, 1, 2, 3 (bit-identical to summing each row with a butterfly).

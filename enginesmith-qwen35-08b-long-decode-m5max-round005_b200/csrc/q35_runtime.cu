@@ -347,6 +347,7 @@ struct q35_session {
   uint16_t *c_h = nullptr, *c_conv = nullptr, *c_z = nullptr, *c_ab = nullptr, *c_y = nullptr;
   uint16_t *c_q = nullptr, *c_k = nullptr, *c_v = nullptr, *c_gated = nullptr, *c_act = nullptr;
   float* c_rope = nullptr;
+  float* c_zs = nullptr;  // z * sigmoid(z) of the chunk's tokens [16][2048]
   uint32_t position = 0;
   bool has_pending = false;
   uint32_t pending = 0;
@@ -580,6 +581,8 @@ cudaError_t enqueue_chunk(q35_session* s) {
       r.dt_bias = L.dt;
       r.state = s->state + size_t(gi) * kGdnHeads * 128 * 128;
       r.y = s->c_y;
+      r.z = s->c_z;
+      r.zs = s->c_zs;
       r.ctl = s->ctl;
       r.advance_pos = l == 0;
       r.ntok = T;
@@ -593,6 +596,7 @@ cudaError_t enqueue_chunk(q35_session* s) {
       o.pro = kProNormGate;
       o.gy = s->c_y;
       o.gz = s->c_z;
+      o.gzs = s->c_zs;
       o.gw = L.gnorm;
       o.epi = kEpiResAdd;
       o.res = s->c_h;
@@ -814,7 +818,7 @@ struct q35_batch {
   float** states = nullptr;
   uint16_t *h = nullptr, *conv = nullptr, *z = nullptr, *ab = nullptr, *y = nullptr;
   uint16_t *q = nullptr, *k = nullptr, *v = nullptr, *gated = nullptr, *act = nullptr;
-  float *rope = nullptr, *po = nullptr, *pml = nullptr;
+  float *rope = nullptr, *po = nullptr, *pml = nullptr, *zs = nullptr;
   cudaGraphExec_t g1 = nullptr, gN = nullptr;
   int nbatch = 8;
   std::string err;
@@ -884,6 +888,8 @@ cudaError_t enqueue_batch_step(q35_batch* b, bool first) {
       r.states = b->states;
       r.state_off = size_t(gi) * kGdnHeads * 128 * 128;
       r.ctls = b->ctls;
+      r.z = b->z;
+      r.zs = b->zs;
       Q35_B(launch_recur_sessions(r, n, st, pdl));
       QmvArgs o = {};
       o.seg[0] = {L.out.w, L.out.s, L.out.b, nullptr, 1024};
@@ -894,6 +900,7 @@ cudaError_t enqueue_batch_step(q35_batch* b, bool first) {
       o.pro = kProNormGate;
       o.gy = b->y;
       o.gz = b->z;
+      o.gzs = b->zs;
       o.gw = L.gnorm;
       o.epi = kEpiResAdd;
       o.res = b->h;
@@ -1121,6 +1128,7 @@ int q35_batch_create(q35_session** sessions, int n, q35_batch** out, char* errbu
       {(void**)&b->z, N * 2048 * 2}, {(void**)&b->ab, N * 32 * 2}, {(void**)&b->y, N * 2048 * 2},
       {(void**)&b->q, N * kQProj * 2}, {(void**)&b->k, N * 512 * 2}, {(void**)&b->v, N * 512 * 2},
       {(void**)&b->gated, N * 2048 * 2}, {(void**)&b->act, N * kMlp * 2}, {(void**)&b->rope, N * 64 * 4},
+      {(void**)&b->zs, N * 2048 * 4},
       {(void**)&b->po, size_t(kKvHeads) * kAttnChains * 4 * kHeadDim * 4},
       {(void**)&b->pml, size_t(kKvHeads) * kAttnChains * 4 * 2 * 4},
   };
@@ -1292,6 +1300,7 @@ int q35_open(const char* model_dir, int device, const q35_opts* opts, q35_sessio
       {(void**)&s->c_gated, size_t(kPrefillTokens) * 2048 * 2},
       {(void**)&s->c_act, size_t(kPrefillTokens) * kMlp * 2},
       {(void**)&s->c_rope, size_t(kPrefillTokens) * 64 * 4},
+      {(void**)&s->c_zs, size_t(kPrefillTokens) * 2048 * 4},
   };
   size_t total = 0;
   for (auto& p : parts) total += (p.bytes + 255) & ~size_t(255);

@@ -97,6 +97,7 @@ struct QmvArgs {
   const uint16_t* gy;    // norm-gate prologue: recurrence output [2048]
   const uint16_t* gz;    // z projection [2048]
   const uint16_t* gw;    // norm weight [128]
+  const float* gzs;      // chunk norm-gate prologue: precomputed z * sigmoid(z) [rows][2048] (optional)
   uint16_t* res;         // residual (in/out) for kEpiResAdd
   uint16_t* hist;        // GDN conv history [3][6144]
   const uint16_t* convw; // [6144][4]
@@ -134,6 +135,10 @@ struct RecurArgs {
   float* const* states;
   size_t state_off;
   Ctl* const* ctls;
+  // optional: the output gate z * sigmoid(z) in f32 (gdn.metal:246-253), formed
+  // once per channel from z [rows][2048] for the norm-gate prologue
+  const uint16_t* z;
+  float* zs;
 };
 
 struct AttnArgs {
