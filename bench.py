@@ -7,7 +7,12 @@ uniform random ids consumed by the engine, then greedy decode at batch 1. A
 step is one decode token of one session; every GPU runs its own session
 (independent sessions, weak scaling). Inputs are synthetic and seeded.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--context C] [--impl q35|reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--context C] [--impl q35|reference] [--split]
+
+--split (N > 1, config 5's second part): ONE session whose attention K/V is
+sequence-split over the N GPUs (rank r keeps positions p % N == r, the ranks
+exchange partial (m, l, o) over NVLink every attention layer); `value` is
+that single stream's tok/s (strong scaling).
 
 Rank 0 prints one JSON line. `value` is device-timed (CUDA events on the
 session stream, max over ranks); `e2e` times the public q35_generate call
@@ -221,6 +226,7 @@ def main():
     ap.add_argument("--impl", default="q35", choices=["q35", "reference"])
     ap.add_argument("--cpu-tokens", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--split", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -242,7 +248,11 @@ def main():
     model_dir = ensure_model(world, rank)
     cap = ((args.context + args.warmup + 2 * args.steps + args.cpu_tokens + 64) // 32) * 32
     m = q35.Model.load(model_dir, local, capacity=cap)
-    prompt = [int(v) for v in I.Rng(3 + rank, 50).ints(args.context, 248320)]
+    split = args.split and world > 1
+    if split:
+        q35.split_connect_dist(m)  # one stream over all ranks: the same prompt everywhere
+    streams = 1 if split else world
+    prompt = [int(v) for v in I.Rng(3 + (0 if split else rank), 50).ints(args.context, 248320)]
     t0 = time.perf_counter()
     first = m.generate(prompt, 1, True)
     prefill_s = time.perf_counter() - t0
@@ -262,30 +272,32 @@ def main():
         barrier()
     attn_us, attn_launches = m.attn_timing(reset=0)
     ms_max = reduce_max(ms, world, "cuda")
-    value = aggregate_tok_s(world, args.steps, ms_max / 1e3)
+    value = aggregate_tok_s(streams, args.steps, ms_max / 1e3)
 
     # ---- end to end: the public generate call, host buffers ----
     barrier()
     t0 = time.perf_counter()
     toks = m.generate([], args.steps, False)
     e2e_s = time.perf_counter() - t0
-    e2e = aggregate_tok_s(world, args.steps, reduce_max(e2e_s, world, "cuda"))
+    e2e = aggregate_tok_s(streams, args.steps, reduce_max(e2e_s, world, "cuda"))
     m._pending_for_bench = toks[-1]
 
     # ---- roofline of the dominant kernel (attention) ----
     peak, peak_kind = peaks()
     avg_len = start_pos + (args.steps + 1) / 2.0
-    attn_bytes = 2 * 2 * 256 * 2 * avg_len + 4096 * 2 + 2 * 512 * 2 + 2048 * 2
+    # K/V rows this rank's attention launches read (its share under a split)
+    local_len = avg_len / world if split else avg_len
+    attn_bytes = 2 * 2 * 256 * 2 * local_len + 4096 * 2 + 2 * 512 * 2 + 2048 * 2
     attn_avg_s = attn_us / max(attn_launches, 1) * 1e-6
     achieved = attn_bytes / attn_avg_s / 1e9 if attn_launches else None
     traffic = None
     try:
         with open(os.path.join(ROOT, "profiles", "attn_traffic.json")) as f:
             tr = json.load(f)
-        traffic = tr["dram_bytes_per_ctx_token"] * avg_len
+        traffic = tr["dram_bytes_per_ctx_token"] * local_len
     except Exception:
         pass
-    step_bytes = BYTES_FIXED + BYTES_PER_CTX * (start_pos + args.steps / 2.0)
+    step_bytes = BYTES_FIXED + BYTES_PER_CTX * (start_pos + args.steps / 2.0) / (world if split else 1)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -299,12 +311,16 @@ def main():
         out = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (Q4 weights, f32 state/accumulation)",
+            "scaling": "strong" if split else "weak", "vs_baseline": None,
+            "dtype": "bf16 (Q4 weights, f32 state/accumulation)",
             "data": "synthetic (seeded random-init weights and prompt ids)",
-            "config": {"workload": f"config4: Qwen3.5-0.8B-class hybrid Q4 model, {args.context}-token "
-                                   f"prompt then greedy decode, batch 1 per GPU",
+            "config": {"workload": (f"config5 (sequence split): one session, {args.context}-token prompt, "
+                                    f"attention K/V split over {world} GPUs" if split else
+                                    f"config4: Qwen3.5-0.8B-class hybrid Q4 model, {args.context}-token "
+                                    f"prompt then greedy decode, batch 1 per GPU"),
                        "model": "q35-0.8B-hybrid-q4 (random init, seed 3)", "context": args.context,
-                       "global_batch": world, "seq_len": args.context, "parallelism": f"sessions x{world}",
+                       "global_batch": streams, "seq_len": args.context,
+                       "parallelism": f"sequence split x{world}" if split else f"sessions x{world}",
                        "l2": "inputs larger than L2 (each step streams ~%.2f GB)" % (step_bytes / 1e9),
                        "prefill_s": round(prefill_s, 2)},
             "gpu_launches": args.steps * (18 * 3 + 6 * 4 + 24 * 2 + 1),
@@ -316,12 +332,14 @@ def main():
                          "algorithmic_bytes_per_launch": attn_bytes,
                          "avg_launch_us": attn_avg_s * 1e6, "launches": attn_launches},
             "step_roofline": {"bytes_per_token": step_bytes,
-                              "achieved_gbs": step_bytes * (value / world) / 1e9,
-                              "frac": step_bytes * (value / world) / 1e9 / peak},
+                              "achieved_gbs": step_bytes * (value / streams) / 1e9,
+                              "frac": step_bytes * (value / streams) / 1e9 / peak},
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
         }
         print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.barrier()  # no rank unmaps its exchange buffer while a peer still decodes
     m.close()
     if world > 1:
         dist.destroy_process_group()

@@ -102,6 +102,16 @@ Q35_DEV float warp_max(float v) {
 // more launches earlier before pdl_wait(); it triggers its dependents right
 // after pdl_wait(), so when a kernel starts, the launch two places before it
 // has completed.
+// System-scope flag accesses for flags that other GPUs write or read over
+// NVLink (sequence-split exchange).
+Q35_DEV unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+Q35_DEV void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
 Q35_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 Q35_DEV void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 

@@ -501,9 +501,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn(const __grid_constant_
   // pos_step was written by the step's first launch (>= 2 launches back);
   // a prompt chunk's token t sits pos_add = t places after it.
   const uint32_t pos = ld_cg_u32(&a.ctl->pos_step) + uint32_t(a.pos_add);
-  const uint32_t len = pos + 1;
+  // sequence split: the local keys are positions r, r + G, ... <= pos; the
+  // current token is local (at local index len - 1) on rank pos % G only
+  const bool xs = a.xworld > 1;
+  const uint32_t xg = xs ? uint32_t(a.xworld) : 1u, xr = xs ? uint32_t(a.xrank) : 0u;
+  const uint32_t len = xs ? (pos >= xr ? (pos - xr) / xg + 1 : 0u) : pos + 1;
+  const bool mine = !xs || pos % xg == xr;
+  const uint32_t lpos = mine ? len - 1 : 0u;
   const float* rope = a.rope ? a.rope : a.ctl->rope_cs;
-  const bool split = len >= 1024;
+  const bool split = xs || len >= 1024;
   const int stride = split ? 64 : 32;
   const int nkeys = (chain < stride && uint32_t(chain) < len) ? int((len - 1 - chain) / stride) + 1 : 0;
   const int ntiles = (nkeys + kAttnTile - 1) / kAttnTile;
@@ -516,8 +522,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn(const __grid_constant_
   auto row_of = [&](int j) { return split ? j : ((j & 1) << 4) + (j >> 1); };
   // the current token is key `pos`: chain pos % stride, local index pos / stride
   // (the chain's last key)
-  const bool owner = chain == int(pos % stride);
-  const int own_idx = int(pos / stride);
+  const bool owner = mine && chain == int(lpos % stride);
+  const int own_idx = int(lpos / stride);
   const int own_t = owner ? own_idx / kAttnTile : -1, own_j = own_idx % kAttnTile;
 
   auto issue = [&](const uint16_t* base, uint16_t (*ring)[kHeadDim], uint64_t* bar, int t) {
@@ -574,7 +580,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn(const __grid_constant_
     *reinterpret_cast<uint4*>(S.kf + 8 * lane) = kb;
     *reinterpret_cast<uint4*>(S.vf + 8 * lane) = vr;
     if (owner) {
-      const size_t ci = (size_t(kh) * cap + size_t(pos % kAttnChains) * cps + pos / kAttnChains) * kHeadDim;
+      const size_t ci = (size_t(kh) * cap + size_t(lpos % kAttnChains) * cps + lpos / kAttnChains) * kHeadDim;
       *reinterpret_cast<uint4*>(a.kcache + ci + 8 * lane) = kb;
       *reinterpret_cast<uint4*>(a.vcache + ci + 8 * lane) = vr;
     }
@@ -725,14 +731,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn(const __grid_constant_
         mbar_arrive(&S.feempty[b]);
       }
     }
-    // chain partials (bf16-rounded on the split route, attention_decode.metal:428-430)
+    // chain partials (bf16-rounded on the split route, attention_decode.metal:428-430;
+    // kept in f32 under a sequence split, whose rank merge has no reference form)
+    const bool round_part = split && !xs;
 #pragma unroll
     for (int h = 0; h < 4; ++h) {
       const float oa = (h & 1) ? o2[0][h >> 1].y : o2[0][h >> 1].x;
       const float ob = (h & 1) ? o2[1][h >> 1].y : o2[1][h >> 1].x;
       float* po = a.part_o + (pbase + h) * kHeadDim + d;
-      po[0] = split ? bfr(oa) : oa;
-      po[1] = split ? bfr(ob) : ob;
+      po[0] = round_part ? bfr(oa) : oa;
+      po[1] = round_part ? bfr(ob) : ob;
     }
     if (wr == 0 && lane < 4) a.part_ml[(pbase + lane) * 2 + 1] = ssum;
   } else if (kprod) {
@@ -755,6 +763,68 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn(const __grid_constant_
   if (tid == 0) attn_time_end(a.ctl);
 }
 
+// Sequence split, inside the combine: this rank's record (lanes 0-7 of warp
+// w hold dims 8w..8w+7 of the CTA's 32 unnormalised o values; m, l) goes to
+// every rank's receive buffer, then a flag tagged (epoch, pos + 1) per rank;
+// the CTA waits (bounded) for every rank's flag and merges the records in
+// rank order: M = max m_q, f_q = e^(m_q - M), o = sum f_q o_q / sum f_q l_q.
+// Every rank merges the same records in the same order, so all ranks get
+// the same bits. Returns the lane's normalised value.
+constexpr unsigned long long kXWaitNs = 10ull * 1000 * 1000 * 1000;  // 10 s
+__device__ __noinline__ float x_exchange(const AttnArgs& a, float r, float m, float l, uint32_t pos) {
+  constexpr float kMin = -3.4028234663852886e38f;
+  __shared__ int xfail;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int G = a.xworld, R = a.xrank;
+  const int slot = a.xlayer * 2 + int(pos & 1u);
+  const int cta = blockIdx.x * gridDim.y + blockIdx.y;
+  const unsigned long long tag = (static_cast<unsigned long long>(ld_cg_u32(&a.ctl->epoch)) << 32) | (pos + 1u);
+  for (int p = 0; p < G; ++p) {
+    float* dst = a.xrecv[p] + x_rec_off(slot, R, cta, G);
+    if (lane < 8) dst[warp * 8 + lane] = r;
+    if (tid == 0) {
+      dst[32] = m;
+      dst[33] = l;
+    }
+  }
+  if (tid == 0) xfail = 0;
+  __syncthreads();
+  if (tid < G) {
+    __threadfence_system();
+    st_release_sys_u64(a.xflag[tid] + x_flag_off(slot, R, cta, G), tag);
+    const unsigned long long* f = a.xflag[R] + x_flag_off(slot, tid, cta, G);
+    // after any expired wait of this session (err set) the rest of the
+    // queued work falls through instead of waiting again
+    const unsigned long long t0 = globaltimer_ns();
+    while (ld_acquire_sys_u64(f) != tag) {
+      if (ld_cg_u32(&a.ctl->err) != 0u) {
+        xfail = 1;
+        break;
+      }
+      if (globaltimer_ns() - t0 > kXWaitNs) {
+        atomicCAS(&a.ctl->err, 0u, kErrXWait);
+        xfail = 1;
+        break;
+      }
+      __nanosleep(32);
+    }
+  }
+  __syncthreads();
+  if (xfail || lane >= 8) return 0.0f;
+  const float* rec = a.xrecv[R] + x_rec_off(slot, 0, cta, G);
+  const size_t src_stride = size_t(kXCtas) * kXRec;
+  float M = kMin;
+  for (int q = 0; q < G; ++q) M = fmaxf(M, __ldcv(rec + q * src_stride + 32));
+  float L = 0.0f, O = 0.0f;
+  for (int q = 0; q < G; ++q) {
+    const float* rq = rec + q * src_stride;
+    const float f = fexp(__fsub_rn(__ldcv(rq + 32), M));
+    L = __fadd_rn(L, __fmul_rn(f, __ldcv(rq + 33)));
+    O = __fadd_rn(O, __fmul_rn(f, __ldcv(rq + warp * 8 + lane)));
+  }
+  return L == 0.0f ? O : __fdiv_rn(O, L);
+}
+
 // Chain combine and BF16 output gate. Grid (8 query heads, 8 stripes of 32
 // dims), 4 warps of 8 dims: the reference's attn_decode_split2_gate SIMD
 // layout (lane l owns chains l and l+32, attention_decode.metal:853-889), or
@@ -768,9 +838,11 @@ __global__ void __launch_bounds__(128) k_attn_combine(const __grid_constant__ At
   const int qh = blockIdx.x, kh = qh >> 2, h = qh & 3;
   const int stripe = blockIdx.y * 4 + warp;  // 8 dims
   const uint32_t len = ld_cg_u32(&a.ctl->pos_step) + uint32_t(a.pos_add) + 1;
-  const bool split = len >= 1024;
+  const bool xs = a.xworld > 1;
+  const bool split = xs || len >= 1024;
   const size_t base = size_t(kh) * kAttnChains * 4 + h;  // + chain * 4
   float res[8];
+  float xm = 0.0f, xl = 0.0f;  // sequence split: this rank's max and sum
   if (split) {
     const size_t ia = base + size_t(lane) * 4, ib = base + size_t(lane + 32) * 4;
     const float2 mla = *reinterpret_cast<const float2*>(&a.part_ml[ia * 2]);
@@ -791,8 +863,10 @@ __global__ void __launch_bounds__(128) k_attn_combine(const __grid_constant__ At
       float acc = __fadd_rn(0.0f, __fmul_rn(fa, pa[i]));
       acc = __fadd_rn(acc, __fmul_rn(fb, pb[i]));
       const float ov = warp_sum(acc);
-      res[i] = ssum_all == 0.0f ? ov : __fdiv_rn(ov, ssum_all);
+      res[i] = (xs || ssum_all == 0.0f) ? ov : __fdiv_rn(ov, ssum_all);
     }
+    xm = M;
+    xl = ssum_all;
   } else {
     const size_t il = base + size_t(lane) * 4;
     const float2 ml = *reinterpret_cast<const float2*>(&a.part_ml[il * 2]);
@@ -808,10 +882,11 @@ __global__ void __launch_bounds__(128) k_attn_combine(const __grid_constant__ At
       res[i] = ssum_all == 0.0f ? ov : __fdiv_rn(ov, ssum_all);
     }
   }
-  if (lane < 8) {
-    float r = res[0];
+  float r = res[0];
 #pragma unroll
-    for (int i = 1; i < 8; ++i) r = lane == i ? res[i] : r;
+  for (int i = 1; i < 8; ++i) r = lane == i ? res[i] : r;
+  if (xs) r = x_exchange(a, r, xm, xl, len - 1);
+  if (lane < 8) {
     const int d = stripe * 8 + lane;
     const float attention = bfr(r);
     const float x = bf2f(a.q_raw[qh * 512 + 256 + d]);

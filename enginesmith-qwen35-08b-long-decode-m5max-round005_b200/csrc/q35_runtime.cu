@@ -354,7 +354,20 @@ struct q35_session {
   std::atomic<bool> cancelled{false};
   std::string err;
   std::string model_id;  // canonical model directory (batched sessions must share it)
+  uint32_t epoch = 0;    // reset generation, tags the sequence-split exchange
+  // sequence split (xworld > 1 once connected): this rank's exchange buffers
+  // (records, then flags), the peers' mapped buffers and the device tables
+  int xrank = 0, xworld = 1, xpend_world = 0;
+  uint8_t* xbuf = nullptr;
+  std::vector<void*> xpeer;
+  void** xtab = nullptr;  // [xworld] record pointers, then [xworld] flag pointers
 
+  // K/V capacity of this rank's caches (the local share under a sequence split)
+  uint32_t kv_capacity() const {
+    if (xworld <= 1) return capacity;
+    const uint32_t per = (capacity + uint32_t(xworld) - 1) / uint32_t(xworld);
+    return (per + kAttnChains - 1) / kAttnChains * kAttnChains;
+  }
   uint16_t* kcache(int ai) { return kv + size_t(ai) * 2 * kKvHeads * capacity * kHeadDim; }
   uint16_t* vcache(int ai) { return kcache(ai) + size_t(kKvHeads) * capacity * kHeadDim; }
 };
@@ -364,6 +377,17 @@ namespace {
 int set_err(q35_session* s, int code, const std::string& m) {
   if (s) s->err = m;
   return code;
+}
+
+// Attention-launch fields of the session's sequence split (none when off).
+void split_attn_args(const q35_session* s, AttnArgs& at, int ai) {
+  at.capacity = s->kv_capacity();
+  if (s->xworld <= 1) return;
+  at.xrank = s->xrank;
+  at.xworld = s->xworld;
+  at.xlayer = ai;
+  at.xrecv = reinterpret_cast<float* const*>(s->xtab);
+  at.xflag = reinterpret_cast<unsigned long long* const*>(s->xtab + s->xworld);
 }
 
 // One decode step: model.rs:228-307 for rows == 1 (+ the head when `head`).
@@ -459,6 +483,7 @@ cudaError_t enqueue_step(q35_session* s, bool head, bool first) {
       at.part_ml = s->attn_pml;
       at.gated = s->gated;
       at.ctl = s->ctl;
+      split_attn_args(s, at, ai);
       Q35_L(launch_attn(at, st, pdl));
       QmvArgs o = {};
       o.seg[0] = {L.o.w, L.o.s, L.o.b, nullptr, 1024};
@@ -637,6 +662,7 @@ cudaError_t enqueue_chunk(q35_session* s) {
         at.ctl = s->ctl;
         at.pos_add = t;
         at.rope = s->c_rope + 64 * t;
+        split_attn_args(s, at, ai);
         Q35_C(launch_attn(at, st, pdl));
       }
       QmvArgs o = {};
@@ -722,6 +748,10 @@ void free_session(q35_session* s) {
   if (s->device >= 0) cudaSetDevice(s->device);
   for (cudaGraphExec_t g : {s->gdec1, s->gdecN, s->gpre1, s->gpreN, s->gchunk})
     if (g) cudaGraphExecDestroy(g);
+  for (void* p : s->xpeer)
+    if (p) cudaIpcCloseMemHandle(p);
+  if (s->xtab) cudaFree(s->xtab);
+  if (s->xbuf) cudaFree(s->xbuf);
   if (s->buf) cudaFree(s->buf);
   if (s->M.arena) cudaFree(s->M.arena);
   if (s->stream) cudaStreamDestroy(s->stream);
@@ -788,8 +818,9 @@ int check_device_ctl(q35_session* s) {
   cudaError_t e = cudaMemcpy(&c, s->ctl, sizeof(Ctl), cudaMemcpyDeviceToHost);
   if (e != cudaSuccess) return device_failure(s, e, "control read");
   if (c.err != 0) {
-    std::string m = c.err == kErrToken ? "token outside vocabulary on device"
-                                       : "device wait expired (site " + std::to_string(c.err) + ")";
+    std::string m = c.err == kErrToken   ? std::string("token outside vocabulary on device")
+                    : c.err == kErrXWait ? std::string("sequence split: a peer's attention record did not arrive")
+                                         : "device wait expired (site " + std::to_string(c.err) + ")";
     reset_state(s);
     cudaStreamSynchronize(s->stream);
     return set_err(s, Q35_ETIMEOUT, m);
@@ -1108,6 +1139,7 @@ int q35_batch_create(q35_session** sessions, int n, q35_batch** out, char* errbu
     if (!sessions[t]) return fail(Q35_EINVAL, "null session");
     if (sessions[t]->device != sessions[0]->device) return fail(Q35_EINVAL, "sessions on different devices");
     if (sessions[t]->model_id != sessions[0]->model_id) return fail(Q35_EINVAL, "sessions of different models");
+    if (sessions[t]->xworld > 1) return fail(Q35_EINVAL, "sequence-split sessions cannot be batched");
     for (int u = 0; u < t; ++u)
       if (sessions[u] == sessions[t]) return fail(Q35_EINVAL, "session listed twice");
   }
@@ -1201,6 +1233,87 @@ int q35_batch_decode_timed(q35_batch* b, size_t steps, float* ms) {
 const char* q35_batch_last_error(const q35_batch* b) { return b ? b->err.c_str() : "no batch"; }
 
 void q35_batch_destroy(q35_batch* b) { free_batch(b); }
+
+int q35_force_pending(q35_session* s, uint32_t token) {
+  if (!s) return Q35_EINVAL;
+  if (!s->has_pending) return set_err(s, Q35_EINVAL, "no continuation state");
+  if (token >= uint32_t(kVocab)) return set_err(s, Q35_EINVAL, "token outside vocabulary");
+  cudaSetDevice(s->device);
+  // the next continuation's first step embeds seq[position]
+  cudaError_t e = cudaMemcpyAsync(s->seq + s->position, &token, 4, cudaMemcpyHostToDevice, s->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+  if (e != cudaSuccess) return device_failure(s, e, "force pending");
+  s->pending = token;
+  return Q35_OK;
+}
+
+int q35_split_prepare(q35_session* s, int rank, int world, void* handle) {
+  if (!s || !handle) return Q35_EINVAL;
+  if (world < 2 || world > kMaxSplit || rank < 0 || rank >= world)
+    return set_err(s, Q35_EINVAL, "split: world must be 2..8 and rank in [0, world)");
+  if (s->xworld > 1 || s->xbuf) return set_err(s, Q35_EINVAL, "split: already prepared");
+  cudaSetDevice(s->device);
+  const size_t bytes = x_recv_bytes(world) + x_flag_bytes(world);
+  cudaError_t e = cudaMalloc(&s->xbuf, bytes);
+  if (e == cudaSuccess) e = cudaMemset(s->xbuf, 0, bytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, s->xbuf);
+  if (e != cudaSuccess) {
+    if (s->xbuf) cudaFree(s->xbuf);
+    s->xbuf = nullptr;
+    return set_err(s, Q35_ECUDA, std::string("split: exchange buffer: ") + cudaGetErrorString(e));
+  }
+  static_assert(sizeof(cudaIpcMemHandle_t) == Q35_SPLIT_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle, &h, sizeof(h));
+  s->xrank = rank;
+  s->xpend_world = world;
+  return Q35_OK;
+}
+
+int q35_split_connect(q35_session* s, const void* handles) {
+  if (!s || !handles) return Q35_EINVAL;
+  if (!s->xbuf || s->xpend_world < 2 || s->xworld > 1) return set_err(s, Q35_EINVAL, "split: prepare first");
+  const int G = s->xpend_world;
+  cudaSetDevice(s->device);
+  cudaError_t e = cudaStreamSynchronize(s->stream);
+  std::vector<void*> base(G, nullptr);
+  for (int p = 0; p < G && e == cudaSuccess; ++p) {
+    if (p == s->xrank) {
+      base[p] = s->xbuf;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, static_cast<const uint8_t*>(handles) + size_t(p) * Q35_SPLIT_HANDLE_BYTES, sizeof(h));
+    e = cudaIpcOpenMemHandle(&base[p], h, cudaIpcMemLazyEnablePeerAccess);
+    if (e == cudaSuccess) s->xpeer.push_back(base[p]);
+  }
+  std::vector<void*> tab(2 * G);
+  for (int p = 0; p < G; ++p) {
+    tab[p] = base[p];
+    tab[G + p] = static_cast<uint8_t*>(base[p]) + x_recv_bytes(G);
+  }
+  if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&s->xtab), 2 * G * sizeof(void*));
+  if (e == cudaSuccess) e = cudaMemcpy(s->xtab, tab.data(), 2 * G * sizeof(void*), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return set_err(s, Q35_ECUDA, std::string("split: peer mapping: ") + cudaGetErrorString(e));
+  // the graphs bake the attention arguments: capture them again with the split
+  s->xworld = G;
+  for (cudaGraphExec_t* g : {&s->gdec1, &s->gdecN, &s->gpre1, &s->gpreN, &s->gchunk})
+    if (*g) {
+      cudaGraphExecDestroy(*g);
+      *g = nullptr;
+    }
+  e = capture(s, 1, true, &s->gdec1);
+  if (e == cudaSuccess && s->dbatch > 1) e = capture(s, s->dbatch, true, &s->gdecN);
+  if (e == cudaSuccess) e = capture(s, 1, false, &s->gpre1);
+  if (e == cudaSuccess && s->pbatch > 1) e = capture(s, s->pbatch, false, &s->gpreN);
+  if (e == cudaSuccess && s->chunked) e = capture_chunk(s, &s->gchunk);
+  if (e == cudaSuccess) e = reset_state(s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+  if (e != cudaSuccess) return set_err(s, Q35_ECUDA, std::string("split: graph capture: ") + cudaGetErrorString(e));
+  return Q35_OK;
+}
+
+int q35_split_world(const q35_session* s) { return s ? s->xworld : 0; }
 
 int q35_diag_bounded_wait(uint32_t polls, uint32_t* err_dev, void* stream) {
   if (!err_dev || polls == 0) return Q35_EINVAL;
@@ -1364,6 +1477,7 @@ int q35_generate(q35_session* s, const uint32_t* prompt, size_t n_prompt, size_t
     Ctl c = {};
     c.capacity = s->capacity;
     c.attn_t0 = ~0ull;
+    c.epoch = ++s->epoch;  // ranks of a sequence split reset in step, so epochs agree
     if (e == cudaSuccess) e = cudaMemcpyAsync(s->ctl, &c, sizeof(Ctl), cudaMemcpyHostToDevice, s->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
     if (e != cudaSuccess) return device_failure(s, e, "reset");
@@ -1472,21 +1586,28 @@ int q35_dump_state(q35_session* s, uint16_t* kv, float* state, uint16_t* hist) {
   cudaSetDevice(s->device);
   cudaError_t e = cudaStreamSynchronize(s->stream);
   const size_t pos = s->position;
-  // the caches are chain-major (position p at chain p % 64, slot p / 64)
-  const size_t cps = s->capacity / kAttnChains;
-  const size_t slots = (pos + kAttnChains - 1) / kAttnChains;
+  // the caches are chain-major (local index i at chain i % 64, slot i / 64);
+  // under a sequence split local index i holds position i * G + rank and the
+  // other positions are left zero
+  const size_t G = size_t(s->xworld), R = size_t(s->xrank);
+  const size_t cap = s->kv_capacity();
+  const size_t cps = cap / kAttnChains;
+  const size_t nloc = pos > R ? (pos - R + G - 1) / G : 0;
+  const size_t slots = (nloc + kAttnChains - 1) / kAttnChains;
   std::vector<uint16_t> tmp(slots * kHeadDim);
+  if (kv && G > 1) std::memset(kv, 0, size_t(6) * 2 * kKvHeads * pos * kHeadDim * 2);
   for (int ai = 0; ai < 6 && e == cudaSuccess && kv; ++ai)
     for (int which = 0; which < 2 && e == cudaSuccess; ++which)
       for (int h = 0; h < kKvHeads && e == cudaSuccess; ++h) {
-        const uint16_t* src = (which ? s->vcache(ai) : s->kcache(ai)) + size_t(h) * s->capacity * kHeadDim;
+        const uint16_t* src = (which ? s->vcache(ai) : s->kcache(ai)) + size_t(h) * cap * kHeadDim;
         uint16_t* dst = kv + ((size_t(ai) * 2 + which) * kKvHeads + h) * pos * kHeadDim;
         for (size_t c = 0; c < size_t(kAttnChains) && e == cudaSuccess; ++c) {
-          const size_t n = pos > c ? (pos - c + kAttnChains - 1) / kAttnChains : 0;
+          const size_t n = nloc > c ? (nloc - c + kAttnChains - 1) / kAttnChains : 0;
           if (n == 0) continue;
           e = cudaMemcpy(tmp.data(), src + c * cps * kHeadDim, n * kHeadDim * 2, cudaMemcpyDeviceToHost);
           for (size_t sl = 0; sl < n; ++sl)
-            std::memcpy(dst + (sl * kAttnChains + c) * kHeadDim, tmp.data() + sl * kHeadDim, kHeadDim * 2);
+            std::memcpy(dst + ((sl * kAttnChains + c) * G + R) * kHeadDim, tmp.data() + sl * kHeadDim,
+                        kHeadDim * 2);
         }
       }
   if (e == cudaSuccess && state)
@@ -1502,6 +1623,7 @@ int q35_session_copy(q35_session* dst, q35_session* src) {
   if (dst->device != src->device) return set_err(dst, Q35_EINVAL, "copy: sessions on different devices");
   if (dst->model_id != src->model_id) return set_err(dst, Q35_EINVAL, "copy: sessions of different models");
   if (dst->capacity != src->capacity) return set_err(dst, Q35_EINVAL, "copy: capacities differ");
+  if (dst->xworld > 1 || src->xworld > 1) return set_err(dst, Q35_EINVAL, "copy: sequence-split sessions");
   cudaSetDevice(dst->device);
   cudaError_t e = cudaStreamSynchronize(src->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(dst->stream);

@@ -55,7 +55,8 @@ struct Ctl {
   uint32_t attn_launches;        // launches accounted
   unsigned long long attn_t0;    // earliest post-dependency start of the running launch
   unsigned long long attn_ns;    // summed launch durations
-  uint32_t pad[4];
+  uint32_t epoch;      // reset generation (sequence-split exchange tags)
+  uint32_t pad[3];
 };
 
 // Error site codes written to Ctl::err.
@@ -66,6 +67,7 @@ enum : uint32_t {
   kErrRecurWait = 4,
   kErrToken = 5,
   kErrProbeWait = 6,  // the diagnostic bounded-wait probe
+  kErrXWait = 7,      // sequence split: a peer's attention record did not arrive
 };
 
 // ---- Q4 matvec kernel arguments ----
@@ -156,7 +158,31 @@ struct AttnArgs {
   Ctl* ctl;
   int pos_add;            // prompt chunks: this token sits at ctl->pos_step + pos_add
   const float* rope;      // prompt chunks: its RoPE table [64] (else ctl->rope_cs)
+  // Sequence split over xworld ranks (xworld <= 1: off). This rank keeps the
+  // K/V of positions p with p % xworld == xrank at local index p / xworld
+  // (capacity is then the local capacity); the combine exchanges per-rank
+  // (m, l, o) records through every rank's receive buffer (xrecv, xflag:
+  // device addresses of each rank's buffers, this rank's included).
+  int xrank, xworld, xlayer;
+  float* const* xrecv;
+  unsigned long long* const* xflag;
 };
+
+// Sequence-split exchange buffers of one rank: records [slot][source][cta]
+// of kXRec floats (32 dims of o, then m and l) and flags [slot][source][cta].
+// Slot = attention layer * 2 + position parity.
+constexpr int kMaxSplit = 8;
+constexpr int kXSlots = 12;
+constexpr int kXCtas = 64;  // combine CTAs: 8 query heads x 8 stripes of 32 dims
+constexpr int kXRec = 40;
+__host__ __device__ inline size_t x_rec_off(int slot, int src, int cta, int world) {
+  return ((size_t(slot) * world + src) * kXCtas + cta) * kXRec;
+}
+__host__ __device__ inline size_t x_flag_off(int slot, int src, int cta, int world) {
+  return (size_t(slot) * world + src) * kXCtas + cta;
+}
+inline size_t x_recv_bytes(int world) { return size_t(kXSlots) * world * kXCtas * kXRec * 4; }
+inline size_t x_flag_bytes(int world) { return size_t(kXSlots) * world * kXCtas * 8; }
 
 struct HeadArgs {
   const uint32_t* w;      // [248320][128]

@@ -22,6 +22,7 @@ HEADER_PATH = os.path.join(os.path.dirname(PKG_DIR), "include", "q35.h")
 VOCAB = 248320
 HIDDEN = 1024
 DEFAULT_CAPACITY = 262144
+SPLIT_HANDLE_BYTES = 64
 
 OK, EINVAL, ECUDA, ECANCEL, EIO, ENOMEM, ETIMEOUT, ENCCL = 0, -1, -2, -3, -4, -5, -6, -7
 FLAG_TOKEN_BY_TOKEN_PROMPT = 1
@@ -69,6 +70,10 @@ def _load() -> ctypes.CDLL:
         "q35_diag_bounded_wait": (c_int, [c_uint32, P, P]),
         "q35_diag_inject_device_error": (c_int, [P, c_uint32]),
         "q35_session_copy": (c_int, [P, P]),
+        "q35_force_pending": (c_int, [P, c_uint32]),
+        "q35_split_prepare": (c_int, [P, c_int, c_int, P]),
+        "q35_split_connect": (c_int, [P, P]),
+        "q35_split_world": (c_int, [P]),
         "q35_batch_create": (c_int, [POINTER(c_void_p), c_int, POINTER(c_void_p), c_char_p, c_size_t]),
         "q35_batch_decode": (c_int, [P, c_size_t, POINTER(c_uint32)]),
         "q35_batch_decode_timed": (c_int, [P, c_size_t, POINTER(c_float)]),
@@ -169,6 +174,28 @@ class Model:
         self._check(lib().q35_last_logits(self._h, lg.ctypes.data, lse.ctypes.data))
         return lg, int(lse[0])
 
+    def split_prepare(self, rank: int, world: int) -> bytes:
+        """First half of the sequence-split set-up: this rank's exchange-buffer
+        handle (SPLIT_HANDLE_BYTES bytes) for the other ranks."""
+        h = ctypes.create_string_buffer(SPLIT_HANDLE_BYTES)
+        self._check(lib().q35_split_prepare(self._h, rank, world, h))
+        return h.raw
+
+    def split_connect(self, handles: list) -> None:
+        """Second half: every rank's handle in rank order."""
+        blob = b"".join(handles)
+        buf = ctypes.create_string_buffer(blob, len(blob))
+        self._check(lib().q35_split_connect(self._h, buf))
+
+    @property
+    def split_world(self) -> int:
+        return int(lib().q35_split_world(self._h))
+
+    def force_pending(self, token: int) -> None:
+        """Teacher forcing: the next continuation consumes `token` instead of
+        the last emitted id."""
+        self._check(lib().q35_force_pending(self._h, token))
+
     def copy_from(self, other: "Model") -> None:
         """Take `other`'s whole decode state (same device, model and capacity)."""
         self._check(lib().q35_session_copy(self._h, other._h))
@@ -187,6 +214,21 @@ class Model:
             self.close()
         except Exception:
             pass
+
+
+def split_connect_dist(model, group=None) -> None:
+    """Sequence-split set-up over torch.distributed, one process per GPU: each
+    rank prepares its exchange buffer, the handles are all-gathered in rank
+    order (any backend; the handles are plain bytes) and each rank connects.
+    Every rank of `group` must call this with its own session."""
+    import torch.distributed as dist
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    mine = model.split_prepare(rank, world)
+    handles = [None] * world
+    dist.all_gather_object(handles, mine, group=group)
+    if any(not isinstance(h, (bytes, bytearray)) or len(h) != SPLIT_HANDLE_BYTES for h in handles):
+        raise Q35Error(EINVAL, "split: malformed exchange handle")
+    model.split_connect([bytes(h) for h in handles])
 
 
 class Batch:

@@ -108,6 +108,33 @@ int q35_decode_timed(q35_session* s, size_t steps, float* ms);
  * model directory and capacity; device-to-device copies on dst's stream. */
 int q35_session_copy(q35_session* dst, q35_session* src);
 
+/* Teacher forcing (test and evaluation aid, no reference counterpart):
+ * replace the pending token, i.e. the last emitted id that the next
+ * q35_generate(reset=0) consumes first. Needs a continuation state. */
+int q35_force_pending(q35_session* s, uint32_t token);
+
+/* Sequence-split attention (the reference runs one GPU):
+ * one decode stream over `world` GPUs, one session and one process per GPU,
+ * all opened on the same model with the same capacity. Every rank runs the
+ * replicated non-attention layers; rank r keeps the K/V of positions p with
+ * p % world == r, and each attention combine exchanges the ranks' partial
+ * (max, sum, unnormalised o) over NVLink: every rank writes its record into
+ * every rank's receive buffer (CUDA IPC mappings) and merges all records in
+ * rank order, so all ranks emit the same tokens. Attention always takes the
+ * 64-chain route here, so tokens agree with a single-GPU session within the
+ * floating-point tolerance rather than bit for bit.
+ * Set-up: q35_split_prepare on every rank (allocates the exchange buffer and
+ * returns its IPC handle), exchange the handles between the processes (any
+ * channel), then q35_split_connect with all `world` handles in rank order
+ * (maps the peers' buffers, recaptures the graphs, resets the state). After
+ * that every rank must make the same q35_generate calls in the same order;
+ * a rank whose peers stop answering gets Q35_ETIMEOUT after about 10 s.
+ * q35_split_world returns the connected world size (1 when not split). */
+#define Q35_SPLIT_HANDLE_BYTES 64
+int q35_split_prepare(q35_session* s, int rank, int world, void* handle);
+int q35_split_connect(q35_session* s, const void* handles);
+int q35_split_world(const q35_session* s);
+
 /* Batched sessions (no counterpart in the reference, whose engine serves one
  * stream): 1..8 sessions of one device, each already holding a continuation
  * state (a q35_generate call returned Q35_OK on it), decoded together. Each

@@ -430,6 +430,74 @@ void attn_f32(const uint16_t* query, const uint16_t* kcache, const uint16_t* vca
   }
 }
 
+/* Sequence split over `world` ranks (the engine's config-5 path; the
+ * reference runs on one device, so this has no reference counterpart). Rank
+ * r holds positions r, r + world, ...; on each rank 64 chains walk its keys
+ * (chain c: local indices c, c + 64, ..., i.e. positions (c + 64 k) world + r)
+ * with the per-key update above and f32 partials; the rank's record is the
+ * split-route combine (:853-876) without the division (max M_r, sum L_r,
+ * unnormalised O_r), and the records are merged in rank order:
+ * M = max M_q, f_q = e^(M_q - M), out = sum f_q O_q / sum f_q L_q. */
+void attn_f32_split(const uint16_t* query, const uint16_t* kcache, const uint16_t* vcache, uint32_t len,
+                    uint32_t capacity, int world, float* out /*[8*256]*/) {
+  const int parts = 64;
+  std::vector<float> rm(size_t(world) * 8), rl(size_t(world) * 8), ro(size_t(world) * 8 * 256);
+  for (int r = 0; r < world; ++r) {
+    std::vector<float> po(size_t(8) * parts * 256), pm(size_t(8) * parts), ps(size_t(8) * parts);
+    pool().run(8L * parts, [&](long b0, long b1) {
+      for (long t = b0; t < b1; ++t) {
+        int qh = int(t / parts), c = int(t % parts);
+        int kh = qh / 4;
+        float qf[256];
+        for (int d = 0; d < 256; ++d) qf[d] = 0.0625f * bf2f(query[qh * 256 + d]);
+        const uint16_t* kc = kcache + size_t(kh) * capacity * 256;
+        const uint16_t* vc = vcache + size_t(kh) * capacity * 256;
+        float o[256], m, sm;
+        walk_keys(qf, kc, vc, c * world + r, parts * world, int(len), o, &m, &sm);
+        std::memcpy(&po[(size_t(qh) * parts + c) * 256], o, sizeof(o));
+        pm[qh * parts + c] = m;
+        ps[qh * parts + c] = sm;
+      }
+    });
+    for (int qh = 0; qh < 8; ++qh) {
+      const float* m = &pm[qh * parts];
+      const float* sm = &ps[qh * parts];
+      const float* o = &po[size_t(qh) * parts * 256];
+      float lm[32];
+      for (int l = 0; l < 32; ++l) lm[l] = std::max(std::max(kFiniteMin, m[l]), m[l + 32]);
+      const float gmax = bmax32(lm);
+      float tmp[32];
+      for (int l = 0; l < 32; ++l) {
+        float acc = 0.0f;
+        for (int b = 0; b < 2; ++b) acc += fexp(m[l + 32 * b] - gmax) * sm[l + 32 * b];
+        tmp[l] = acc;
+      }
+      rm[r * 8 + qh] = gmax;
+      rl[r * 8 + qh] = bsum32(tmp);
+      for (int d = 0; d < 256; ++d) {
+        for (int l = 0; l < 32; ++l) {
+          float acc = 0.0f;
+          for (int b = 0; b < 2; ++b) acc += fexp(m[l + 32 * b] - gmax) * o[(l + 32 * b) * 256 + d];
+          tmp[l] = acc;
+        }
+        ro[(size_t(r) * 8 + qh) * 256 + d] = bsum32(tmp);
+      }
+    }
+  }
+  for (int qh = 0; qh < 8; ++qh)
+    for (int d = 0; d < 256; ++d) {
+      float M = kFiniteMin;
+      for (int q = 0; q < world; ++q) M = std::max(M, rm[q * 8 + qh]);
+      float L = 0.0f, O = 0.0f;
+      for (int q = 0; q < world; ++q) {
+        const float f = fexp(rm[q * 8 + qh] - M);
+        L = L + f * rl[q * 8 + qh];
+        O = O + f * ro[(size_t(q) * 8 + qh) * 256 + d];
+      }
+      out[qh * 256 + d] = L == 0.0f ? O : O / L;
+    }
+}
+
 /* head_lse_g8 partials + head_lse_tail LSE (head_lse.metal:11-64, :66-82) */
 uint16_t lse_of(const uint16_t* logits, int N) {
   float pmax[1024], psum[1024];
@@ -828,8 +896,17 @@ void orc_attn_decode_f32(const uint16_t* query, const uint16_t* kcache, const ui
 void orc_attn_decode_gate(const uint16_t* query, const uint16_t* kcache, const uint16_t* vcache,
                           uint32_t len, uint32_t capacity, const uint16_t* q_raw,
                           uint16_t* gated) {
+  orc_attn_decode_gate_split(query, kcache, vcache, len, capacity, 1, q_raw, gated);
+}
+
+void orc_attn_decode_gate_split(const uint16_t* query, const uint16_t* kcache, const uint16_t* vcache,
+                                uint32_t len, uint32_t capacity, int world, const uint16_t* q_raw,
+                                uint16_t* gated) {
   std::vector<float> o(2048);
-  attn_f32(query, kcache, vcache, len, capacity, o.data());
+  if (world > 1)
+    attn_f32_split(query, kcache, vcache, len, capacity, world, o.data());
+  else
+    attn_f32(query, kcache, vcache, len, capacity, o.data());
   for (int head = 0; head < 8; ++head)
     for (int d = 0; d < 256; ++d) {
       float attention = bfr(o[head * 256 + d]);
@@ -918,6 +995,7 @@ struct orc_session {
   std::vector<std::vector<float>> state;
   std::vector<uint16_t> logits, final_h;
   uint16_t lse = 0;
+  int split_world = 1;  // attention as a sequence split over this many ranks
 };
 
 extern "C" {
@@ -1055,6 +1133,8 @@ void orc_session_import(orc_session* s, uint32_t pos, uint32_t cap_src,
   }
 }
 
+void orc_session_set_split(orc_session* s, int world) { s->split_world = world > 1 ? world : 1; }
+
 /* model.rs:228-307 with rows=1 */
 uint32_t orc_session_step(orc_session* S, uint32_t token, int want_head) {
   orc_model* M = S->m;
@@ -1084,8 +1164,8 @@ uint32_t orc_session_step(orc_session* S, uint32_t token, int want_head) {
       orc_qmv_q4(L.v.w, L.v.s, L.v.b, u.data(), nullptr, 512, 1024, v.data());
       orc_attn_prepare(q.data(), k.data(), v.data(), L.qnorm, L.knorm, S->position, S->capacity,
                        query.data(), S->kc[ai].data(), S->vc[ai].data());
-      orc_attn_decode_gate(query.data(), S->kc[ai].data(), S->vc[ai].data(), S->position + 1,
-                           S->capacity, q.data(), gated.data());
+      orc_attn_decode_gate_split(query.data(), S->kc[ai].data(), S->vc[ai].data(), S->position + 1,
+                                 S->capacity, S->split_world, q.data(), gated.data());
       orc_qmv_q4(L.o.w, L.o.s, L.o.b, gated.data(), h.data(), 1024, 2048, h.data());
       ++ai;
     }

@@ -83,6 +83,12 @@ void orc_attn_prepare(const uint16_t* q_raw, const uint16_t* k_raw, const uint16
  * (attention_decode.metal:215-431 + :830-891). Writes gated[2048]. */
 void orc_attn_decode_gate(const uint16_t* query, const uint16_t* kcache, const uint16_t* vcache,
                           uint32_t len, uint32_t capacity, const uint16_t* q_raw, uint16_t* gated);
+/* The same output under the engine's sequence split over `world` ranks
+ * (positions p % world == r on rank r, f32 chain partials, per-rank records
+ * merged in rank order; world 1 = orc_attn_decode_gate). */
+void orc_attn_decode_gate_split(const uint16_t* query, const uint16_t* kcache, const uint16_t* vcache,
+                                uint32_t len, uint32_t capacity, int world, const uint16_t* q_raw,
+                                uint16_t* gated);
 /* f32 attention output before rounding (for tolerance tests), o[8*256] */
 void orc_attn_decode_f32(const uint16_t* query, const uint16_t* kcache, const uint16_t* vcache,
                          uint32_t len, uint32_t capacity, float* o);
@@ -110,6 +116,8 @@ void orc_session_reset(orc_session* s);
 uint32_t orc_session_position(const orc_session* s);
 /* consume `token` at the current position; if want_head, returns the greedy
  * next token (and keeps logits), else returns 0xffffffff. */
+/* attention of later steps as the engine's sequence split over `world` ranks */
+void orc_session_set_split(orc_session* s, int world);
 uint32_t orc_session_step(orc_session* s, uint32_t token, int want_head);
 void orc_session_logits(const orc_session* s, uint16_t* out); /* [248320] */
 uint16_t orc_session_lse(const orc_session* s);

@@ -67,6 +67,7 @@ def lib() -> ctypes.CDLL:
             "orc_session_reset": (None, [P]),
             "orc_session_position": (c_uint32, [P]),
             "orc_session_step": (c_uint32, [P, c_uint32, c_int]),
+            "orc_session_set_split": (None, [P, c_int]),
             "orc_session_logits": (None, [P, P]),
             "orc_session_lse": (c_uint16, [P]),
             "orc_session_final_hidden": (None, [P, P]),
@@ -242,6 +243,11 @@ class OracleSession:
     @property
     def position(self) -> int:
         return int(lib().orc_session_position(self.s))
+
+    def set_split(self, world: int) -> None:
+        """Attention of later steps as the engine's sequence split over
+        `world` ranks (1 = the reference's single-device attention)."""
+        lib().orc_session_set_split(self.s, world)
 
     def step(self, token: int, head: bool = True) -> int:
         return int(lib().orc_session_step(self.s, token, 1 if head else 0))
