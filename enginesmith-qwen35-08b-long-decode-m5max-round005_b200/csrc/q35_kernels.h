@@ -25,6 +25,12 @@ cudaError_t launch_gdn_conv(const uint16_t* raw, uint16_t* hist, const uint16_t*
 cudaError_t launch_ctl_position(Ctl* ctl, uint32_t pos, cudaStream_t st);
 cudaError_t launch_wait_probe(uint32_t polls, uint32_t* err, cudaStream_t st);
 
+// Q4 GEMM on the tensor cores (q35_gemm.cu)
+cudaError_t qgemm_init();
+size_t qgemm_workspace_bytes(int N, int K, int T);
+cudaError_t launch_qgemm(QGemmArgs a, void* ws, size_t ws_bytes, bool zero_counters, cudaStream_t st,
+                         bool pdl);
+
 // prompt chunks (q35_prefill.cu)
 cudaError_t chunk_kernels_init();
 int chunk_sub_tokens(const QmvArgs& a);  // tokens per shared-memory sub-chunk

@@ -6,9 +6,9 @@
 
 namespace q35 {
 
-template <typename Arg>
-inline cudaError_t launch_ex(void (*kern)(Arg), dim3 grid, dim3 block, size_t smem,
-                             cudaStream_t stream, bool pdl, Arg arg) {
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                             cudaStream_t stream, bool pdl, Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -23,7 +23,7 @@ inline cudaError_t launch_ex(void (*kern)(Arg), dim3 grid, dim3 block, size_t sm
   }
   cfg.attrs = attr;
   cfg.numAttrs = n;
-  return cudaLaunchKernelEx(&cfg, kern, arg);
+  return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
 }  // namespace q35

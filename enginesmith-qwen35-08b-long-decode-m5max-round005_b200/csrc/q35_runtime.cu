@@ -311,6 +311,7 @@ cudaError_t ensure_kernels_init() {
   if (dev < 64 && (g_init_mask >> dev) & 1) return cudaSuccess;
   e = kernels_init();
   if (e == cudaSuccess) e = chunk_kernels_init();
+  if (e == cudaSuccess) e = qgemm_init();
   if (e == cudaSuccess && dev < 64) g_init_mask |= uint64_t(1) << dev;
   return e;
 }
@@ -1692,6 +1693,38 @@ int q35_op_qmv_q4(const uint32_t* w, const uint16_t* scales, const uint16_t* bia
   a.epi = residual ? kEpiResAdd : kEpiStore;
   a.res = y;
   return op_status(launch_qmv(a, st, false));
+}
+
+size_t q35_op_qgemm_workspace_bytes(uint32_t tokens, uint32_t n, uint32_t k) {
+  if (tokens == 0 || tokens > 256 || n == 0 || k < 512 || k % 512 != 0 || k > 4096) return 0;
+  return qgemm_workspace_bytes(int(n), int(k), int(tokens));
+}
+
+int q35_op_qgemm_q4(const uint32_t* w, const uint16_t* scales, const uint16_t* biases, const uint16_t* x,
+                    uint32_t tokens, uint32_t n, uint32_t k, const uint16_t* residual, uint16_t* y,
+                    void* workspace, size_t workspace_bytes, void* stream) {
+  if (!w || !scales || !biases || !x || !y || !workspace || tokens < 1 || tokens > 256 || n < 1 ||
+      k < 512 || k % 512 != 0 || k > 4096)
+    return Q35_EINVAL;
+  for (const void* p : {static_cast<const void*>(scales), static_cast<const void*>(biases)})
+    if (reinterpret_cast<uintptr_t>(p) % 16 != 0) return Q35_EINVAL;
+  for (const void* p : {static_cast<const void*>(w), static_cast<const void*>(x),
+                        static_cast<const void*>(workspace)})
+    if (reinterpret_cast<uintptr_t>(p) % 16 != 0) return Q35_EINVAL;
+  if (workspace_bytes < qgemm_workspace_bytes(int(n), int(k), int(tokens))) return Q35_EINVAL;
+  if (ensure_kernels_init() != cudaSuccess) return Q35_ECUDA;
+  QGemmArgs a = {};
+  a.w = w;
+  a.s = scales;
+  a.b = biases;
+  a.x = x;
+  a.N = int(n);
+  a.K = int(k);
+  a.T = int(tokens);
+  a.y = y;
+  a.ystride = int(n);
+  a.res = residual;
+  return op_status(launch_qgemm(a, workspace, workspace_bytes, true, (cudaStream_t)stream, false));
 }
 
 int q35_op_embedding_q4(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,

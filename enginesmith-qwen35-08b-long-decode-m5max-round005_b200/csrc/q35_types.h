@@ -168,6 +168,23 @@ struct AttnArgs {
   unsigned long long* const* xflag;
 };
 
+// Q4 affine GEMM on the tensor cores (several tokens per launch):
+// y[t][n] = bf16(sum_k W[n][k] x[t][k]) (+ residual), W = bf16(s q + b).
+struct QGemmArgs {
+  const uint32_t* w;     // [N][K/8] codes
+  const uint16_t* s;     // [N][K/64] bf16 scales
+  const uint16_t* b;     // [N][K/64] bf16 biases
+  const uint16_t* x;     // [T][K] bf16 activations
+  int N, K, T, Np;       // Np: T rounded up to a multiple of 16 (the MMA N)
+  int kblocks;           // 64-wide K blocks per split (gridDim.y splits)
+  float* part;           // split partials [splits][T][N] f32 (gridDim.y > 1)
+  uint32_t* counters;    // [row tiles], zero between launches
+  uint16_t* y;           // [T][ystride]
+  int ystride;
+  const uint16_t* res;   // optional residual [T][ystride] (may alias y)
+  uint32_t* err;         // bounded-wait failure flag (optional)
+};
+
 // Sequence-split exchange buffers of one rank: records [slot][source][cta]
 // of kXRec floats (32 dims of o, then m and l) and flags [slot][source][cta].
 // Slot = attention layer * 2 + position parity.

@@ -57,6 +57,8 @@ def _load() -> ctypes.CDLL:
         "q35_attn_timing": (c_int, [P, c_int, POINTER(ctypes.c_double), POINTER(c_uint32)]),
         "q35_op_qmv_q4": (c_int, [P, P, P, P, P, P, c_int, c_int, P]),
         "q35_op_embedding_q4": (c_int, [P, P, P, c_uint32, c_int, P, P]),
+        "q35_op_qgemm_workspace_bytes": (c_size_t, [c_uint32, c_uint32, c_uint32]),
+        "q35_op_qgemm_q4": (c_int, [P, P, P, P, c_uint32, c_uint32, c_uint32, P, P, P, c_size_t, P]),
         "q35_op_rms_norm": (c_int, [P, P, P, P]),
         "q35_op_gdn_workspace_bytes": (c_size_t, []),
         "q35_op_gdn_step": (c_int, [P] * 17),
@@ -300,6 +302,21 @@ def qmv_q4(w, scales, biases, x, residual=None, out=None):
     y = out if out is not None else torch.empty(n, dtype=torch.uint16, device=w.device)
     _op(lib().q35_op_qmv_q4(_ptr(w), _ptr(scales), _ptr(biases), _ptr(x), _ptr(residual), _ptr(y),
                             n, kw * 8, _stream()), "qmv_q4")
+    return y
+
+
+def qgemm_q4(w, scales, biases, x, residual=None, out=None, ws=None):
+    """y[T][N] = bf16(x W^T) (+ residual) on the tensor cores (tcgen05), W the
+    Q4 matrix dequantised as bf16(s q + b); x [T][K] bf16 with T <= 256."""
+    import torch
+    n, kw = w.shape
+    t = x.shape[0]
+    y = out if out is not None else torch.empty((t, n), dtype=torch.uint16, device=w.device)
+    need = int(lib().q35_op_qgemm_workspace_bytes(t, n, kw * 8))
+    if ws is None or ws.numel() < need:
+        ws = torch.empty(need, dtype=torch.uint8, device=w.device)
+    _op(lib().q35_op_qgemm_q4(_ptr(w), _ptr(scales), _ptr(biases), _ptr(x), t, n, kw * 8, _ptr(residual),
+                              _ptr(y), _ptr(ws), ws.numel(), _stream()), "qgemm_q4")
     return y
 
 

@@ -1,6 +1,7 @@
 """Op-level benchmarks of the q35 kernels on the BASELINE.json configs 1-3.
 
-  python -m q35.opbench --op qmv|gdn|attn|head [--len N] [--iters K] [--copies R]
+  python -m q35.opbench --op qmv|gdn|attn|head|qgemm [--len N] [--iters K] [--copies R]
+                        [--tokens T --rows N --k K]   (qgemm: the tensor-core Q4 GEMM)
 
 Each call works on a fresh copy of its big operands (weights, recurrent
 state, or K/V cache), rotating over enough copies that the working set is
@@ -29,7 +30,10 @@ def main():
     import inputs as I
 
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", choices=["qmv", "gdn", "attn", "head"], required=True)
+    ap.add_argument("--op", choices=["qmv", "gdn", "attn", "head", "qgemm"], required=True)
+    ap.add_argument("--tokens", type=int, default=64)
+    ap.add_argument("--rows", type=int, default=7168)
+    ap.add_argument("--k", type=int, default=1024)
     ap.add_argument("--len", type=int, default=32768)
     ap.add_argument("--iters", type=int, default=200)
     ap.add_argument("--copies", type=int, default=0)
@@ -83,6 +87,24 @@ def main():
 
         def call(i):
             q35.head_argmax(W[i % copies], sc, bi, x, gain, ws=ws)
+    elif args.op == "qgemm":
+        n, k, t = args.rows, args.k, args.tokens
+        g = torch.Generator(device="cpu").manual_seed(5)
+        w = torch.randint(-2**31, 2**31 - 1, (n, k // 8), generator=g, dtype=torch.int64).to(torch.int32)
+        sc = (torch.rand((n, k // 64), generator=g) * 0.015 + 0.005).to(torch.bfloat16)
+        per = n * k // 2 + 2 * n * (k // 64) * 2
+        copies = args.copies or max(2, int(np.ceil(300e6 / per)))
+        W = [w.to(dev) for _ in range(copies)]
+        S = sc.to(dev).view(torch.int16)
+        B = (-8.0 * sc.float()).to(torch.bfloat16).to(dev).view(torch.int16)
+        X = torch.randn((t, k), generator=g).to(torch.bfloat16).to(dev).view(torch.int16)
+        Y = torch.empty((t, n), dtype=torch.int16, device=dev)
+        wsb = torch.empty(int(q35.lib().q35_op_qgemm_workspace_bytes(t, n, k)), dtype=torch.uint8, device=dev)
+        nbytes = per + t * k * 2 + t * n * 2
+        flops = 2.0 * n * k * t
+
+        def call(i):
+            q35.qgemm_q4(W[i % copies], S, B, X, out=Y, ws=wsb)
     else:
         d = I.config3(2, args.len)
         per = d["kc"].nbytes * 2
@@ -114,8 +136,11 @@ def main():
     e.record()
     torch.cuda.synchronize()
     us = a.elapsed_time(e) * 1e3 / args.iters
-    print(json.dumps({"op": args.op, "len": args.len if args.op == "attn" else None, "us_per_call": us,
-                      "bytes_per_call": nbytes, "gbs": nbytes / us / 1e3, "copies": copies}))
+    out = {"op": args.op, "len": args.len if args.op == "attn" else None, "us_per_call": us,
+           "bytes_per_call": nbytes, "gbs": nbytes / us / 1e3, "copies": copies}
+    if args.op == "qgemm":
+        out.update({"tokens": args.tokens, "rows": args.rows, "k": args.k, "tflops": flops / us / 1e6})
+    print(json.dumps(out))
 
 
 if __name__ == "__main__":

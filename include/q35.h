@@ -175,6 +175,21 @@ int q35_op_qmv_q4(const uint32_t* w, const uint16_t* scales, const uint16_t* bia
                   const uint16_t* x, const uint16_t* residual, uint16_t* y, int n, int k,
                   void* stream);
 
+/* Batched Q4 matmul on the tensor cores (tcgen05; the batched-session route,
+ * in the place of the reference's quantised matmul qmm_q4_nax,
+ * kernels/linear_nax.metal:1096-1139): y[t][n] = bf16(sum_k W[n][k] x[t][k]),
+ * or bf16(residual[t][n] + bf16(.)) when residual is non-NULL (may alias y),
+ * for t < tokens (1..256), with W dequantised as bf16(s*q + b). x [tokens][k]
+ * bf16, y [tokens][n]; k a multiple of 512 up to 4096; w, x, scales, biases and
+ * workspace 16-byte aligned. The float32 accumulation runs in
+ * the tensor core's order, so results match a float32 reference within
+ * tolerance rather than the matvec bit for bit. workspace: at least
+ * q35_op_qgemm_workspace_bytes(tokens, n, k) bytes (0 = invalid shape). */
+size_t q35_op_qgemm_workspace_bytes(uint32_t tokens, uint32_t n, uint32_t k);
+int q35_op_qgemm_q4(const uint32_t* w, const uint16_t* scales, const uint16_t* biases, const uint16_t* x,
+                    uint32_t tokens, uint32_t n, uint32_t k, const uint16_t* residual, uint16_t* y,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
 /* embedding_q4 (kernels/linear.metal:11-24): out[K] = bf16(s*q + b) of row `token`. */
 int q35_op_embedding_q4(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
                         uint32_t token, int k, uint16_t* out, void* stream);
