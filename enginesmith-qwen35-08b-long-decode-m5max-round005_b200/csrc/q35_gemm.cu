@@ -128,16 +128,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_qgemm(const __grid_constant
   constexpr int kBRegs = kGemmMaxTokens * 8 / kGemmThreads;
   uint4 breg[kBRegs];
   // activations of block kb: element i = j * T + t (token fastest, so the
-  // shared-memory stores of 8 consecutive threads are one 128-byte row)
+  // shared-memory stores of 8 consecutive threads are one 128-byte row);
+  // each slot's source offset and tile offset are fixed for the kernel
+  size_t bsrc[kBRegs];
+  uint32_t bdst[kBRegs];
+#pragma unroll
+  for (int q = 0; q < kBRegs; ++q) {
+    const int i = tid + q * kGemmThreads, j = i / T, t = i - j * T;
+    bsrc[q] = size_t(t) * K + size_t(j) * 8;
+    bdst[q] = sw128_off(t, j);
+  }
   auto load_b = [&](int kb) {
 #pragma unroll
-    for (int q = 0; q < kBRegs; ++q) {
-      const int i = tid + q * kGemmThreads;
-      if (i < T * 8) {
-        const int j = i / T, t = i - j * T;
-        breg[q] = __ldg(reinterpret_cast<const uint4*>(a.x + size_t(t) * K + size_t(kb) * kGemmKb + j * 8));
-      }
-    }
+    for (int q = 0; q < kBRegs; ++q)
+      if (tid + q * kGemmThreads < T * 8)
+        breg[q] = __ldg(reinterpret_cast<const uint4*>(a.x + bsrc[q] + size_t(kb) * kGemmKb));
   };
   const uint32_t idesc = tc_idesc_bf16(kGemmRows, Np);
   const uint32_t tbase = tmem + (uint32_t(32 * (warp & 3)) << 16);
@@ -165,13 +170,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_qgemm(const __grid_constant
       uint8_t* A = As + s * gemm_a_bytes();
       uint8_t* B = Bs + s * gemm_b_bytes(Np);
 #pragma unroll
-      for (int q = 0; q < kBRegs; ++q) {
-        const int i = tid + q * kGemmThreads;
-        if (i < T * 8) {
-          const int j = i / T, t = i - j * T;
-          *reinterpret_cast<uint4*>(B + sw128_off(t, j)) = breg[q];
-        }
-      }
+      for (int q = 0; q < kBRegs; ++q)
+        if (tid + q * kGemmThreads < T * 8) *reinterpret_cast<uint4*>(B + bdst[q]) = breg[q];
       if (it + 1 < nit) load_b(kb0 + (ib + 1 < nit ? ib + 1 : 0));
       // this thread's 32 of its row's 64 values -> bf16(s q + b), 4 core matrices
       uint2 c = make_uint2(0u, 0u);
