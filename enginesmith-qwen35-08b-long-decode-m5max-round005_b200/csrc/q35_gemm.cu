@@ -35,6 +35,12 @@ constexpr int kGemmQuarters = kGemmThreads / 128;
 constexpr int kGemmMaxTokens = 256;
 constexpr int kGemmMaxKb = 16;  // K blocks per work item (its codes are staged whole)
 constexpr uint32_t kErrGemmWait = 8;
+// The workspace starts with the split counters (kGemmMaxTiles words, then the
+// error word) at a fixed offset, so GEMMs of different shapes can share one
+// workspace: every counter is zero between launches (the last CTA of a split
+// tile resets its own), whatever the other GEMMs left in the partials.
+constexpr int kGemmMaxTiles = 4096;
+constexpr size_t kGemmCounterBytes = size_t(kGemmMaxTiles) * 4 + 256;
 
 __host__ __device__ inline int gemm_np(int T) { return ((T + 15) / 16) * 16; }
 __host__ __device__ inline size_t gemm_a_bytes() { return size_t(kGemmRows) * kGemmKb * 2; }
@@ -64,8 +70,26 @@ __host__ __device__ inline uint32_t gemm_tmem_cols(int Np) {
 
 // Persistent: CTA c takes work items c, c + gridDim.x, ... of the
 // (row tile, K split) grid `tiles x splits` (item = tile * splits + split).
-__global__ void __launch_bounds__(kGemmThreads, 1) k_qgemm(const __grid_constant__ QGemmArgs a, int tiles,
-                                                           int splits) {
+// The segment of global row tile `tile`, its first tile and its first row in
+// the concatenated row space.
+__device__ __forceinline__ int gemm_seg_of(const QGemmArgs& a, int tile, int* tile0, int* grow0) {
+  int t0 = 0, r0 = 0;
+#pragma unroll
+  for (int i = 0; i < kGemmSegs; ++i) {
+    const int nt = (a.seg[i].rows + kGemmRows - 1) / kGemmRows;
+    if (i == a.nseg - 1 || tile < t0 + nt) {
+      *tile0 = t0;
+      *grow0 = r0;
+      return i;
+    }
+    t0 += nt;
+    r0 += a.seg[i].rows;
+  }
+  return 0;
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1) k_qgemm(const __grid_constant__ QGemmArgs a) {
+  const int tiles = a.tiles, splits = a.splits;
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ int last;
   const int tid = threadIdx.x, warp = tid >> 5;
@@ -107,18 +131,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_qgemm(const __grid_constant
   // row) and its tile's scales and biases (one copy each)
   auto stage = [&](int item) {
     const int tile = item / splits, sp = item - tile * splits;
-    const int row0 = tile * kGemmRows, nrows = min(kGemmRows, a.N - row0);
+    int stile0, sgrow0;
+    const QGemmSeg& sg = a.seg[gemm_seg_of(a, tile, &stile0, &sgrow0)];
+    const int row0 = (tile - stile0) * kGemmRows, nrows = min(kGemmRows, sg.rows - row0);
     const int kb0 = sp * a.kblocks, nit = min(nkb, kb0 + a.kblocks) - kb0;
     fence_proxy_async();  // earlier generic reads of these buffers before the copies
     if (tid == 0) {
       const uint32_t sb = uint32_t(nrows) * KG * 2;
       mbar_expect_tx(&bar[2], uint32_t(nrows) * nit * 32 + 2 * sb);
-      bulk_g2s(smem + L.scl, a.s + size_t(row0) * KG, sb, &bar[2]);
-      bulk_g2s(smem + L.bia, a.b + size_t(row0) * KG, sb, &bar[2]);
+      bulk_g2s(smem + L.scl, sg.s + size_t(row0) * KG, sb, &bar[2]);
+      bulk_g2s(smem + L.bia, sg.b + size_t(row0) * KG, sb, &bar[2]);
     }
     __syncthreads();  // expect_tx is registered before any code copy lands
     if (tid < nrows)
-      bulk_g2s(codes + tid * gemm_code_stride(a.kblocks), a.w + size_t(row0 + tid) * KW + size_t(kb0) * 8,
+      bulk_g2s(codes + tid * gemm_code_stride(a.kblocks), sg.w + size_t(row0 + tid) * KW + size_t(kb0) * 8,
                uint32_t(nit) * 32, &bar[2]);
   };
   if (int(blockIdx.x) < nitems) stage(blockIdx.x);
@@ -150,10 +176,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_qgemm(const __grid_constant
 
   for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
     const int tile = item / splits, sp = item - tile * splits;
-    const int row0 = tile * kGemmRows, nrows = min(kGemmRows, a.N - row0);
+    int stile0, sgrow0;
+    const QGemmSeg& sg = a.seg[gemm_seg_of(a, tile, &stile0, &sgrow0)];
+    const int row0 = (tile - stile0) * kGemmRows, nrows = min(kGemmRows, sg.rows - row0);
     const int kb0 = sp * a.kblocks, nit = min(nkb, kb0 + a.kblocks) - kb0;
     const bool rok = r < nrows;
-    const int row = row0 + r;
+    const int row = row0 + r;              // row within the segment
+    const int grow = sgrow0 + row;         // row in the concatenated space (partials)
     // CTAs walk their K blocks from different starting blocks, so they do
     // not all read the same activation lines at the same moment
     const int rot = nit > 0 ? int(blockIdx.x) % nit : 0;
@@ -240,11 +269,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_qgemm(const __grid_constant
           const int t = cc + e;
           if (t >= c1) break;
           if (splitk) {
-            a.part[(size_t(sp) * T + t) * a.N + row] = v[e];
+            a.part[(size_t(sp) * T + t) * a.rows_total + grow] = v[e];
           } else {
-            uint16_t* y = a.y + size_t(t) * a.ystride + row;
-            if (a.res)
-              *y = f2bf(__fadd_rn(bf2f(a.res[size_t(t) * a.ystride + row]), bfr(v[e])));
+            uint16_t* y = sg.y + size_t(t) * sg.ystride + row;
+            if (sg.res)
+              *y = f2bf(__fadd_rn(bf2f(sg.res[size_t(t) * sg.ystride + row]), bfr(v[e])));
             else
               *y = f2bf(v[e]);
           }
@@ -271,15 +300,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_qgemm(const __grid_constant
         for (int q = 0; q < splits; ++q) {
 #pragma unroll
           for (int e = 0; e < 8; ++e)
-            if (t0 + e < T) acc[e] = __fadd_rn(acc[e], __ldcg(&a.part[(size_t(q) * T + t0 + e) * a.N + row]));
+            if (t0 + e < T) acc[e] = __fadd_rn(acc[e], __ldcg(&a.part[(size_t(q) * T + t0 + e) * a.rows_total + grow]));
         }
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const int t = t0 + e;
           if (t >= T) break;
-          uint16_t* y = a.y + size_t(t) * a.ystride + row;
-          if (a.res)
-            *y = f2bf(__fadd_rn(bf2f(a.res[size_t(t) * a.ystride + row]), bfr(acc[e])));
+          uint16_t* y = sg.y + size_t(t) * sg.ystride + row;
+          if (sg.res)
+            *y = f2bf(__fadd_rn(bf2f(sg.res[size_t(t) * sg.ystride + row]), bfr(acc[e])));
           else
             *y = f2bf(acc[e]);
         }
@@ -293,23 +322,43 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_qgemm(const __grid_constant
 }
 
 // Host side ------------------------------------------------------------------
-void qgemm_plan(int N, int K, int T, int* tiles, int* splits, int* kblocks) {
+static int gemm_tiles(const QGemmArgs& a) {
+  int t = 0;
+  for (int i = 0; i < a.nseg; ++i) t += (a.seg[i].rows + kGemmRows - 1) / kGemmRows;
+  return t;
+}
+static int gemm_rows(const QGemmArgs& a) {
+  int r = 0;
+  for (int i = 0; i < a.nseg; ++i) r += a.seg[i].rows;
+  return r;
+}
+
+void qgemm_plan(int tiles, int K, int* splits, int* kblocks) {
   const int nkb = K / kGemmKb > 0 ? K / kGemmKb : 1;
-  *tiles = (N + kGemmRows - 1) / kGemmRows;
-  int sp = (148 + *tiles - 1) / *tiles;
+  int sp = (148 + tiles - 1) / tiles;
   if (sp > nkb) sp = nkb;
   if (sp < (nkb + kGemmMaxKb - 1) / kGemmMaxKb) sp = (nkb + kGemmMaxKb - 1) / kGemmMaxKb;
   if (sp < 1) sp = 1;
-  int kb = (nkb + sp - 1) / sp;
+  const int kb = (nkb + sp - 1) / sp;
   *kblocks = kb;
   *splits = (nkb + kb - 1) / kb;
 }
 
+size_t qgemm_workspace_bytes(const QGemmArgs& a) {
+  const int tiles = gemm_tiles(a);
+  int splits, kb;
+  qgemm_plan(tiles, a.K, &splits, &kb);
+  const size_t part = splits > 1 ? size_t(splits) * a.T * gemm_rows(a) * 4 : 0;
+  return kGemmCounterBytes + part;
+}
+
 size_t qgemm_workspace_bytes(int N, int K, int T) {
-  int tiles, splits, kb;
-  qgemm_plan(N, K, T, &tiles, &splits, &kb);
-  const size_t part = splits > 1 ? size_t(splits) * T * N * 4 : 0;
-  return ((part + 255) & ~size_t(255)) + size_t(tiles) * 4 + 256;
+  QGemmArgs a = {};
+  a.nseg = 1;
+  a.seg[0].rows = N;
+  a.K = K;
+  a.T = T;
+  return qgemm_workspace_bytes(a);
 }
 
 cudaError_t qgemm_init() {
@@ -320,27 +369,34 @@ cudaError_t qgemm_init() {
 // Validates, lays out the workspace (partials, counters, error word) and
 // launches. The counters must be zero; `zero_counters` clears them first.
 cudaError_t launch_qgemm(QGemmArgs a, void* ws, size_t ws_bytes, bool zero_counters, cudaStream_t st, bool pdl) {
-  if (a.T < 1 || a.T > kGemmMaxTokens || a.K % 512 != 0 || a.K < 512 || a.K > 4096 || a.N < 1)
+  if (a.T < 1 || a.T > kGemmMaxTokens || a.K % 512 != 0 || a.K < 512 || a.K > 4096 || a.nseg < 1 ||
+      a.nseg > kGemmSegs || !a.x)
     return cudaErrorInvalidValue;
-  int tiles, splits, kb;
-  qgemm_plan(a.N, a.K, a.T, &tiles, &splits, &kb);
-  if (ws_bytes < qgemm_workspace_bytes(a.N, a.K, a.T)) return cudaErrorInvalidValue;
-  const size_t part = splits > 1 ? size_t(splits) * a.T * a.N * 4 : 0;
-  uint8_t* w = static_cast<uint8_t*>(ws);
-  a.part = reinterpret_cast<float*>(w);
-  a.counters = reinterpret_cast<uint32_t*>(w + ((part + 255) & ~size_t(255)));
-  if (!a.err) a.err = a.counters + tiles;
-  a.Np = gemm_np(a.T);
+  for (int i = 0; i < a.nseg; ++i)
+    if (a.seg[i].rows < 1 || !a.seg[i].w || !a.seg[i].s || !a.seg[i].b || !a.seg[i].y ||
+        a.seg[i].ystride < a.seg[i].rows)
+      return cudaErrorInvalidValue;
+  if (ws_bytes < qgemm_workspace_bytes(a)) return cudaErrorInvalidValue;
+  const int tiles = gemm_tiles(a);
+  if (tiles > kGemmMaxTiles) return cudaErrorInvalidValue;
+  int splits, kb;
+  qgemm_plan(tiles, a.K, &splits, &kb);
+  a.tiles = tiles;
+  a.splits = splits;
   a.kblocks = kb;
+  a.rows_total = gemm_rows(a);
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  a.counters = reinterpret_cast<uint32_t*>(w);
+  a.part = reinterpret_cast<float*>(w + kGemmCounterBytes);
+  if (!a.err) a.err = a.counters + kGemmMaxTiles;
+  a.Np = gemm_np(a.T);
   if (zero_counters) {
-    cudaError_t e = cudaMemsetAsync(a.counters, 0, size_t(tiles) * 4 + 4, st);
+    cudaError_t e = cudaMemsetAsync(a.counters, 0, kGemmCounterBytes, st);
     if (e != cudaSuccess) return e;
   }
-  if (a.K > 4096) return cudaErrorInvalidValue;
   const int items = tiles * splits;
   const int grid = items < 148 ? items : 148;
-  return launch_ex(k_qgemm, dim3(grid), dim3(kGemmThreads), gemm_layout(a.Np, kb, a.K).total, st, pdl, a,
-                   tiles, splits);
+  return launch_ex(k_qgemm, dim3(grid), dim3(kGemmThreads), gemm_layout(a.Np, kb, a.K).total, st, pdl, a);
 }
 
 }  // namespace q35

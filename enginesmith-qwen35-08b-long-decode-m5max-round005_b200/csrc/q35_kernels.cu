@@ -490,7 +490,29 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 constexpr int kAttnScoreWarps = 8, kAttnScanWarp0 = 8, kAttnRecWarp0 = 12;
 constexpr int kAttnKProdWarp = 16, kAttnVProdWarp = 17;
 
-__global__ void __launch_bounds__(kAttnThreads, 1) k_attn(const __grid_constant__ AttnArgs a) {
+// Session z's view of a batched launch's arguments.
+__device__ __forceinline__ AttnArgs attn_session_view(const AttnArgs& a, int z) {
+  AttnArgs v = a;
+  const AttnSess& ss = a.sess[z];
+  v.kcache = ss.kcache;
+  v.vcache = ss.vcache;
+  v.capacity = ss.capacity;
+  v.ctl = ss.ctl;
+  v.q_raw = a.q_raw + size_t(z) * kQProj;
+  v.k_raw = a.k_raw + size_t(z) * kKvHeads * kHeadDim;
+  v.v_raw = a.v_raw + size_t(z) * kKvHeads * kHeadDim;
+  v.gated = a.gated + size_t(z) * kQHeads * kHeadDim;
+  v.rope = a.rope + 64 * z;
+  v.part_o = a.part_o + size_t(z) * kKvHeads * kAttnChains * 4 * kHeadDim;
+  v.part_ml = a.part_ml + size_t(z) * kKvHeads * kAttnChains * 4 * 2;
+  return v;
+}
+
+template <bool SESS>
+__global__ void __launch_bounds__(kAttnThreads, 1) k_attn(const __grid_constant__ AttnArgs a_in) {
+  AttnArgs sv;
+  if constexpr (SESS) sv = attn_session_view(a_in, blockIdx.z);
+  const AttnArgs& a = SESS ? sv : a_in;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   AttnSmem& S = *reinterpret_cast<AttnSmem*>(smem_raw);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -830,7 +852,11 @@ __device__ __noinline__ float x_exchange(const AttnArgs& a, float r, float m, fl
 // layout (lane l owns chains l and l+32, attention_decode.metal:853-889), or
 // sdpa_vector's final reduction (lane l = chain l, :194-212) below 1024 keys,
 // followed by attn_gate (attention.metal:140-150).
-__global__ void __launch_bounds__(128) k_attn_combine(const __grid_constant__ AttnArgs a) {
+template <bool SESS>
+__global__ void __launch_bounds__(128) k_attn_combine(const __grid_constant__ AttnArgs a_in) {
+  AttnArgs sv;
+  if constexpr (SESS) sv = attn_session_view(a_in, blockIdx.z);
+  const AttnArgs& a = SESS ? sv : a_in;
   constexpr float kMin = -3.4028234663852886e38f;
   pdl_wait();
   pdl_launch();
@@ -1320,6 +1346,36 @@ __global__ void __launch_bounds__(256) k_greedy(const __grid_constant__ HeadArgs
   head_finish(a, red, &cand, &best);
 }
 
+// Greedy selection for batched sessions: grid (148, n), session blockIdx.y
+// runs k_greedy's partition and tail on its own logits row and outputs.
+__global__ void __launch_bounds__(256) k_greedy_sessions(const HeadOut* __restrict__ outs) {
+  __shared__ float red[64], wm[8], ws[8];
+  __shared__ int last;
+  __shared__ uint32_t cand, best;
+  const HeadOut& o = outs[blockIdx.y];
+  HeadArgs a = {};
+  a.logits = o.logits;
+  a.part = o.part;
+  a.seq = o.seq;
+  a.out_tokens = o.out_tokens;
+  a.seq_len = o.seq_len;
+  a.out_len = o.out_len;
+  a.lse_out = o.lse;
+  a.ctl = o.ctl;
+  pdl_wait();
+  pdl_launch();
+  const int r0 = blockIdx.x * kHeadRowsPerCta;
+  const int r1 = min(kVocab, r0 + kHeadRowsPerCta);
+  float run_m = -INFINITY, run_s = 0.0f;
+  for (int r = r0 + threadIdx.x; r < r1; r += blockDim.x) lse_push(run_m, run_s, bf2f(a.logits[r]));
+  if (!head_partial(a, run_m, run_s, wm, ws, &last)) return;
+  head_finish(a, red, &cand, &best);
+}
+
+cudaError_t launch_greedy_sessions(const HeadOut* outs, int n, cudaStream_t st, bool pdl) {
+  return launch_ex(k_greedy_sessions, dim3(kHeadCtas, n), dim3(256), 0, st, pdl, outs);
+}
+
 // Diagnostic: the bounded mbarrier wait every kernel uses, on a barrier that
 // nothing ever completes, with a caller-chosen poll limit. The wait gives up,
 // records kErrProbeWait in *err and the kernel returns normally (no copy is
@@ -1405,9 +1461,10 @@ cudaError_t kernels_init() {
     return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSpreadSmem));
   });
   if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(k_attn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           int(spread(attn_smem_bytes())));
-  if (e != cudaSuccess) return e;
+  for (auto kern : {k_attn<false>, k_attn<true>}) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(spread(attn_smem_bytes())));
+    if (e != cudaSuccess) return e;
+  }
   e = cudaFuncSetAttribute(k_head, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            int(spread(head_smem_bytes())));
   if (e != cudaSuccess) return e;
@@ -1417,8 +1474,10 @@ cudaError_t kernels_init() {
   e = cudaFuncSetAttribute(k_gdn_recur, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            int(kSpreadSmem));
   if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(k_attn_combine, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           int(kSpreadSmem));
+  for (auto kern : {k_attn_combine<false>, k_attn_combine<true>}) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSpreadSmem));
+    if (e != cudaSuccess) return e;
+  }
   return e;
 }
 
@@ -1438,10 +1497,17 @@ cudaError_t launch_recur(const RecurArgs& a, cudaStream_t st, bool pdl) {
   return launch_ex(k_gdn_recur, dim3(8, kGdnHeads), dim3(64), kSpreadSmem, st, pdl, a);
 }
 cudaError_t launch_attn(const AttnArgs& a, cudaStream_t st, bool pdl) {
-  cudaError_t e = launch_ex(k_attn, dim3(kAttnChains, kKvHeads), dim3(kAttnThreads),
+  cudaError_t e = launch_ex(k_attn<false>, dim3(kAttnChains, kKvHeads), dim3(kAttnThreads),
                             spread(attn_smem_bytes()), st, pdl, a);
   if (e != cudaSuccess) return e;
-  return launch_ex(k_attn_combine, dim3(kQHeads, kHeadDim / 32), dim3(128), kSpreadSmem, st, true, a);
+  return launch_ex(k_attn_combine<false>, dim3(kQHeads, kHeadDim / 32), dim3(128), kSpreadSmem, st, true, a);
+}
+cudaError_t launch_attn_sessions(const AttnArgs& a, int n, cudaStream_t st, bool pdl) {
+  if (n < 1 || !a.sess || a.xworld > 1 || !a.rope) return cudaErrorInvalidValue;
+  cudaError_t e = launch_ex(k_attn<true>, dim3(kAttnChains, kKvHeads, n), dim3(kAttnThreads),
+                            spread(attn_smem_bytes()), st, pdl, a);
+  if (e != cudaSuccess) return e;
+  return launch_ex(k_attn_combine<true>, dim3(kQHeads, kHeadDim / 32, n), dim3(128), kSpreadSmem, st, true, a);
 }
 cudaError_t launch_head(const HeadArgs& a, cudaStream_t st, bool pdl) {
   return launch_ex(k_head, dim3(kHeadCtas), dim3(kHeadThreads), spread(head_smem_bytes()), st, pdl, a);

@@ -23,11 +23,20 @@ cudaError_t launch_greedy(const HeadArgs& a, cudaStream_t st);
 cudaError_t launch_gdn_conv(const uint16_t* raw, uint16_t* hist, const uint16_t* convw,
                             uint16_t* conv_out, cudaStream_t st);
 cudaError_t launch_ctl_position(Ctl* ctl, uint32_t pos, cudaStream_t st);
+cudaError_t launch_greedy_sessions(const HeadOut* outs, int n, cudaStream_t st, bool pdl);
+cudaError_t launch_attn_sessions(const AttnArgs& a, int n, cudaStream_t st, bool pdl);
 cudaError_t launch_wait_probe(uint32_t polls, uint32_t* err, cudaStream_t st);
+
+// Per-token steps of the tensor-core batched route (q35_tokens.cu)
+cudaError_t launch_tok_rms(const TokArgs& a, cudaStream_t st, bool pdl);
+cudaError_t launch_tok_conv(const TokArgs& a, cudaStream_t st, bool pdl);
+cudaError_t launch_tok_normgate(const TokArgs& a, cudaStream_t st, bool pdl);
+cudaError_t launch_tok_swiglu(const TokArgs& a, cudaStream_t st, bool pdl);
 
 // Q4 GEMM on the tensor cores (q35_gemm.cu)
 cudaError_t qgemm_init();
 size_t qgemm_workspace_bytes(int N, int K, int T);
+size_t qgemm_workspace_bytes(const QGemmArgs& a);
 cudaError_t launch_qgemm(QGemmArgs a, void* ws, size_t ws_bytes, bool zero_counters, cudaStream_t st,
                          bool pdl);
 

@@ -522,7 +522,7 @@ cudaError_t launch_qmv_chunk(const QmvArgs& a, cudaStream_t st, bool pdl) {
 }
 
 cudaError_t launch_recur_sessions(const RecurArgs& a, int n, cudaStream_t st, bool pdl) {
-  if (n < 1 || n > kMaxSessions) return cudaErrorInvalidValue;
+  if (n < 1 || n > kMaxTensorSessions) return cudaErrorInvalidValue;
   return launch_ex(k_gdn_recur_sessions, dim3(8, kGdnHeads, n), dim3(64), 0, st, pdl, a);
 }
 

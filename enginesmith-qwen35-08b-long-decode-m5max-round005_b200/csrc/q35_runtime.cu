@@ -841,7 +841,8 @@ int check_device_ctl(q35_session* s) {
 struct q35_batch {
   int n = 0;
   int device = 0;
-  q35_session* s[kMaxSessions] = {};
+  bool tensor = false;  // tensor-core route (GEMMs on tcgen05) instead of the exact matvecs
+  q35_session* s[kMaxTensorSessions] = {};
   cudaStream_t stream = nullptr;
   uint8_t* buf = nullptr;
   Ctl** ctls = nullptr;
@@ -851,6 +852,13 @@ struct q35_batch {
   uint16_t *h = nullptr, *conv = nullptr, *z = nullptr, *ab = nullptr, *y = nullptr;
   uint16_t *q = nullptr, *k = nullptr, *v = nullptr, *gated = nullptr, *act = nullptr;
   float *rope = nullptr, *po = nullptr, *pml = nullptr, *zs = nullptr;
+  // tensor route: normalised inputs, projection outputs, logits, GEMM
+  // workspace, per-session attention and head tables
+  uint16_t *xn = nullptr, *raw = nullptr, *gu = nullptr, *logits = nullptr;
+  uint8_t* gws = nullptr;
+  size_t gws_bytes = 0;
+  AttnSess* asess = nullptr;
+  HeadOut* hout = nullptr;
   cudaGraphExec_t g1 = nullptr, gN = nullptr;
   int nbatch = 8;
   std::string err;
@@ -1033,12 +1041,143 @@ cudaError_t enqueue_batch_step(q35_batch* b, bool first) {
   return e;
 }
 
+// One batched step on the tensor cores: the per-token steps of q35_tokens.cu
+// around one multi-segment GEMM per fused projection (q35_gemm.cu), the
+// sessions' recurrences and attention in one launch each, the head as a GEMM
+// over the vocabulary and a per-session greedy selection.
+cudaError_t enqueue_batch_step_tensor(q35_batch* b, bool first) {
+  const ModelW& M = b->s[0]->M;
+  cudaStream_t st = b->stream;
+  const int n = b->n;
+  bool pdl = !first;
+  cudaError_t e = cudaSuccess;
+#define Q35_T(x)                    \
+  do {                              \
+    e = (x);                        \
+    if (e != cudaSuccess) return e; \
+    pdl = true;                     \
+  } while (0)
+  auto gemm = [&](const uint16_t* x, int K, std::initializer_list<QGemmSeg> segs) {
+    QGemmArgs g = {};
+    int i = 0;
+    for (const QGemmSeg& sg : segs) g.seg[i++] = sg;
+    g.nseg = i;
+    g.x = x;
+    g.K = K;
+    g.T = n;
+    g.err = &b->s[0]->ctl->err;
+    return launch_qgemm(g, b->gws, b->gws_bytes, false, st, pdl);
+  };
+  auto rms = [&](const uint16_t* gain, bool embed) {
+    TokArgs t = {};
+    t.n = n;
+    t.h_in = b->h;
+    t.gain = gain;
+    t.xn = b->xn;
+    if (embed) {
+      t.ew = M.embed.w;
+      t.es = M.embed.s;
+      t.eb = M.embed.b;
+      t.h_out = b->h;
+      t.ctls = b->ctls;
+      t.seqs = b->seqs;
+      t.rope = b->rope;
+    }
+    return launch_tok_rms(t, st, pdl);
+  };
+  auto mlp = [&](const LayerW& L) -> cudaError_t {
+    cudaError_t r = rms(L.post_norm, false);
+    if (r != cudaSuccess) return r;
+    pdl = true;
+    r = gemm(b->xn, kHidden, {{L.gate.w, L.gate.s, L.gate.b, b->gu, nullptr, kMlp, kMlp},
+                              {L.up.w, L.up.s, L.up.b, b->gu + size_t(n) * kMlp, nullptr, kMlp, kMlp}});
+    if (r != cudaSuccess) return r;
+    TokArgs t = {};
+    t.n = n;
+    t.g = b->gu;
+    t.u = b->gu + size_t(n) * kMlp;
+    t.act = b->act;
+    r = launch_tok_swiglu(t, st, true);
+    if (r != cudaSuccess) return r;
+    return gemm(b->act, kMlp, {{L.down.w, L.down.s, L.down.b, b->h, b->h, kHidden, kHidden}});
+  };
+  int gi = 0, ai = 0;
+  for (int l = 0; l < kLayers; ++l) {
+    const LayerW& L = M.L[l];
+    Q35_T(rms(L.in_norm, l == 0));
+    if (!L.attn) {
+      Q35_T(gemm(b->xn, kHidden, {{L.qkv.w, L.qkv.s, L.qkv.b, b->raw, nullptr, kGdnConv, kGdnConv},
+                                  {L.z.w, L.z.s, L.z.b, b->z, nullptr, 2048, 2048},
+                                  {L.a.w, L.a.s, L.a.b, b->ab, nullptr, 16, 32},
+                                  {L.bproj.w, L.bproj.s, L.bproj.b, b->ab + 16, nullptr, 16, 32}}));
+      TokArgs c = {};
+      c.n = n;
+      c.raw = b->raw;
+      c.raw_stride = kGdnConv;
+      c.conv = b->conv;
+      c.hists = b->hists;
+      c.hist_off = size_t(gi) * 3 * kGdnConv;
+      c.convw = L.conv;
+      Q35_T(launch_tok_conv(c, st, pdl));
+      RecurArgs r = {};
+      r.conv = b->conv;
+      r.a_raw = b->ab;
+      r.b_raw = b->ab + 16;
+      r.a_log = L.alog;
+      r.dt_bias = L.dt;
+      r.y = b->y;
+      r.advance_pos = l == 0;
+      r.states = b->states;
+      r.state_off = size_t(gi) * kGdnHeads * 128 * 128;
+      r.ctls = b->ctls;
+      r.z = b->z;
+      r.zs = b->zs;
+      Q35_T(launch_recur_sessions(r, n, st, pdl));
+      TokArgs g = {};
+      g.n = n;
+      g.y = b->y;
+      g.zs = b->zs;
+      g.gw = L.gnorm;
+      g.gated = b->gated;
+      Q35_T(launch_tok_normgate(g, st, pdl));
+      Q35_T(gemm(b->gated, 2048, {{L.out.w, L.out.s, L.out.b, b->h, b->h, kHidden, kHidden}}));
+      ++gi;
+    } else {
+      Q35_T(gemm(b->xn, kHidden, {{L.q.w, L.q.s, L.q.b, b->q, nullptr, kQProj, kQProj},
+                                  {L.k.w, L.k.s, L.k.b, b->k, nullptr, 512, 512},
+                                  {L.v.w, L.v.s, L.v.b, b->v, nullptr, 512, 512}}));
+      AttnArgs at = {};
+      at.q_raw = b->q;
+      at.k_raw = b->k;
+      at.v_raw = b->v;
+      at.q_gain = L.qnorm;
+      at.k_gain = L.knorm;
+      at.part_o = b->po;
+      at.part_ml = b->pml;
+      at.gated = b->gated;
+      at.rope = b->rope;
+      at.sess = b->asess + size_t(ai) * n;
+      at.ctl = b->s[0]->ctl;
+      Q35_T(launch_attn_sessions(at, n, st, pdl));
+      Q35_T(gemm(b->gated, 2048, {{L.o.w, L.o.s, L.o.b, b->h, b->h, kHidden, kHidden}}));
+      ++ai;
+    }
+    Q35_T(mlp(L));
+  }
+  Q35_T(rms(M.norm, false));
+  Q35_T(gemm(b->xn, kHidden, {{M.embed.w, M.embed.s, M.embed.b, b->logits, nullptr, kVocab, kVocab}}));
+  Q35_T(launch_greedy_sessions(b->hout, n, st, pdl));
+#undef Q35_T
+  return e;
+}
+
 cudaError_t capture_batch(q35_batch* b, int steps, cudaGraphExec_t* out) {
   cudaGraph_t g = nullptr;
   cudaError_t e = cudaStreamBeginCapture(b->stream, cudaStreamCaptureModeThreadLocal);
   if (e != cudaSuccess) return e;
   cudaError_t le = cudaSuccess;
-  for (int i = 0; i < steps && le == cudaSuccess; ++i) le = enqueue_batch_step(b, i == 0);
+  for (int i = 0; i < steps && le == cudaSuccess; ++i)
+    le = b->tensor ? enqueue_batch_step_tensor(b, i == 0) : enqueue_batch_step(b, i == 0);
   e = cudaStreamEndCapture(b->stream, &g);
   if (le != cudaSuccess) {
     if (g) cudaGraphDestroy(g);
@@ -1111,6 +1250,16 @@ int batch_run(q35_batch* b, size_t steps, float* ms) {
     for (int t = 0; t < b->n; ++t) device_failure(b->s[t], e, "batched decode");
     return batch_err(b, Q35_ECUDA, m);
   }
+  if (b->tensor) {  // each member's last logits into its own buffer (q35_last_logits)
+    for (int t = 0; t < b->n && e == cudaSuccess; ++t)
+      e = cudaMemcpyAsync(b->s[t]->logits, b->logits + size_t(t) * kVocab, size_t(kVocab) * 2,
+                          cudaMemcpyDeviceToDevice, b->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(b->stream);
+    if (e != cudaSuccess) {
+      for (int t = 0; t < b->n; ++t) device_failure(b->s[t], e, "batched decode");
+      return batch_err(b, Q35_ECUDA, std::string("batched decode: ") + cudaGetErrorString(e));
+    }
+  }
   int rc = Q35_OK;
   for (int t = 0; t < b->n; ++t) {
     const int r = check_device_ctl(b->s[t]);
@@ -1129,13 +1278,21 @@ extern "C" {
 const char* q35_version(void) { return "q35-b200 0.1 (sm_100a)"; }
 
 int q35_batch_create(q35_session** sessions, int n, q35_batch** out, char* errbuf, size_t err_len) {
+  return q35_batch_create_ex(sessions, n, 0u, out, errbuf, err_len);
+}
+
+int q35_batch_create_ex(q35_session** sessions, int n, uint32_t flags, q35_batch** out, char* errbuf,
+                        size_t err_len) {
   if (!out) return Q35_EINVAL;
   *out = nullptr;
   auto fail = [&](int code, const std::string& m) {
     copy_err(errbuf, err_len, m);
     return code;
   };
-  if (!sessions || n < 1 || n > kMaxSessions) return fail(Q35_EINVAL, "batch needs 1..8 sessions");
+  const bool tensor = (flags & Q35_BATCH_TENSOR_CORES) != 0;
+  if (flags & ~uint32_t(Q35_BATCH_TENSOR_CORES)) return fail(Q35_EINVAL, "unknown batch flags");
+  if (!sessions || n < 1 || n > (tensor ? kMaxTensorSessions : kMaxSessions))
+    return fail(Q35_EINVAL, tensor ? "tensor-core batch needs 1..64 sessions" : "batch needs 1..8 sessions");
   for (int t = 0; t < n; ++t) {
     if (!sessions[t]) return fail(Q35_EINVAL, "null session");
     if (sessions[t]->device != sessions[0]->device) return fail(Q35_EINVAL, "sessions on different devices");
@@ -1146,6 +1303,7 @@ int q35_batch_create(q35_session** sessions, int n, q35_batch** out, char* errbu
   }
   q35_batch* b = new q35_batch();
   b->n = n;
+  b->tensor = tensor;
   b->device = sessions[0]->device;
   for (int t = 0; t < n; ++t) b->s[t] = sessions[t];
   cudaSetDevice(b->device);
@@ -1162,9 +1320,31 @@ int q35_batch_create(q35_session** sessions, int n, q35_batch** out, char* errbu
       {(void**)&b->q, N * kQProj * 2}, {(void**)&b->k, N * 512 * 2}, {(void**)&b->v, N * 512 * 2},
       {(void**)&b->gated, N * 2048 * 2}, {(void**)&b->act, N * kMlp * 2}, {(void**)&b->rope, N * 64 * 4},
       {(void**)&b->zs, N * 2048 * 4},
-      {(void**)&b->po, size_t(kKvHeads) * kAttnChains * 4 * kHeadDim * 4},
-      {(void**)&b->pml, size_t(kKvHeads) * kAttnChains * 4 * 2 * 4},
+      {(void**)&b->po, (tensor ? N : 1) * kKvHeads * kAttnChains * 4 * kHeadDim * 4},
+      {(void**)&b->pml, (tensor ? N : 1) * kKvHeads * kAttnChains * 4 * 2 * 4},
   };
+  if (tensor) {
+    // the largest GEMM workspace of the step (split partials + counters)
+    const ModelW& M = sessions[0]->M;
+    (void)M;
+    auto ws = [&](std::initializer_list<int> rows, int K) {
+      QGemmArgs g = {};
+      for (int r : rows) g.seg[g.nseg++].rows = r;
+      g.K = K;
+      g.T = n;
+      return qgemm_workspace_bytes(g);
+    };
+    for (size_t w : {ws({kGdnConv, 2048, 16, 16}, kHidden), ws({kHidden}, 2048), ws({kMlp, kMlp}, kHidden),
+                     ws({kHidden}, kMlp), ws({kQProj, 512, 512}, kHidden), ws({kVocab}, kHidden)})
+      b->gws_bytes = std::max(b->gws_bytes, w);
+    parts.push_back({(void**)&b->xn, N * kHidden * 2});
+    parts.push_back({(void**)&b->raw, N * kGdnConv * 2});
+    parts.push_back({(void**)&b->gu, 2 * N * kMlp * 2});
+    parts.push_back({(void**)&b->logits, N * kVocab * 2});
+    parts.push_back({(void**)&b->gws, b->gws_bytes});
+    parts.push_back({(void**)&b->asess, 6 * N * sizeof(AttnSess)});
+    parts.push_back({(void**)&b->hout, N * sizeof(HeadOut)});
+  }
   size_t total = 0;
   for (auto& pt : parts) total += (pt.bytes + 255) & ~size_t(255);
   if (e == cudaSuccess) e = cudaMalloc(&b->buf, total);
@@ -1178,10 +1358,10 @@ int q35_batch_create(q35_session** sessions, int n, q35_batch** out, char* errbu
     *pt.p = b->buf + off;
     off += (pt.bytes + 255) & ~size_t(255);
   }
-  Ctl* hc[kMaxSessions];
-  uint32_t* hs[kMaxSessions];
-  uint16_t* hh[kMaxSessions];
-  float* hst[kMaxSessions];
+  Ctl* hc[kMaxTensorSessions];
+  uint32_t* hs[kMaxTensorSessions];
+  uint16_t* hh[kMaxTensorSessions];
+  float* hst[kMaxTensorSessions];
   for (int t = 0; t < n; ++t) {
     hc[t] = sessions[t]->ctl;
     hs[t] = sessions[t]->seq;
@@ -1192,6 +1372,18 @@ int q35_batch_create(q35_session** sessions, int n, q35_batch** out, char* errbu
   if (e == cudaSuccess) e = cudaMemcpy(b->seqs, hs, 8 * N, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMemcpy(b->hists, hh, 8 * N, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMemcpy(b->states, hst, 8 * N, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess && tensor) {
+    std::vector<AttnSess> as(6 * N);
+    std::vector<HeadOut> ho(N);
+    for (int t = 0; t < n; ++t) {
+      q35_session* ss = sessions[t];
+      for (int ai = 0; ai < 6; ++ai) as[size_t(ai) * N + t] = {ss->kcache(ai), ss->vcache(ai), ss->ctl, ss->kv_capacity()};
+      ho[t] = {b->logits + size_t(t) * kVocab, ss->head_part, ss->seq, ss->out_tokens, ss->capacity + 1, ss->capacity,
+               ss->lse, ss->ctl};
+    }
+    e = cudaMemcpy(b->asess, as.data(), as.size() * sizeof(AttnSess), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(b->hout, ho.data(), ho.size() * sizeof(HeadOut), cudaMemcpyHostToDevice);
+  }
   if (e == cudaSuccess) e = capture_batch(b, 1, &b->g1);
   if (e == cudaSuccess) e = capture_batch(b, b->nbatch, &b->gN);
   if (e != cudaSuccess) {
@@ -1696,7 +1888,7 @@ int q35_op_qmv_q4(const uint32_t* w, const uint16_t* scales, const uint16_t* bia
 }
 
 size_t q35_op_qgemm_workspace_bytes(uint32_t tokens, uint32_t n, uint32_t k) {
-  if (tokens == 0 || tokens > 256 || n == 0 || k < 512 || k % 512 != 0 || k > 4096) return 0;
+  if (tokens == 0 || tokens > 256 || n == 0 || n > 524288 || k < 512 || k % 512 != 0 || k > 4096) return 0;
   return qgemm_workspace_bytes(int(n), int(k), int(tokens));
 }
 
@@ -1704,7 +1896,7 @@ int q35_op_qgemm_q4(const uint32_t* w, const uint16_t* scales, const uint16_t* b
                     uint32_t tokens, uint32_t n, uint32_t k, const uint16_t* residual, uint16_t* y,
                     void* workspace, size_t workspace_bytes, void* stream) {
   if (!w || !scales || !biases || !x || !y || !workspace || tokens < 1 || tokens > 256 || n < 1 ||
-      k < 512 || k % 512 != 0 || k > 4096)
+      n > 524288 || k < 512 || k % 512 != 0 || k > 4096)
     return Q35_EINVAL;
   for (const void* p : {static_cast<const void*>(scales), static_cast<const void*>(biases)})
     if (reinterpret_cast<uintptr_t>(p) % 16 != 0) return Q35_EINVAL;
@@ -1714,16 +1906,11 @@ int q35_op_qgemm_q4(const uint32_t* w, const uint16_t* scales, const uint16_t* b
   if (workspace_bytes < qgemm_workspace_bytes(int(n), int(k), int(tokens))) return Q35_EINVAL;
   if (ensure_kernels_init() != cudaSuccess) return Q35_ECUDA;
   QGemmArgs a = {};
-  a.w = w;
-  a.s = scales;
-  a.b = biases;
+  a.nseg = 1;
+  a.seg[0] = {w, scales, biases, y, residual, int(n), int(n)};
   a.x = x;
-  a.N = int(n);
   a.K = int(k);
   a.T = int(tokens);
-  a.y = y;
-  a.ystride = int(n);
-  a.res = residual;
   return op_status(launch_qgemm(a, workspace, workspace_bytes, true, (cudaStream_t)stream, false));
 }
 

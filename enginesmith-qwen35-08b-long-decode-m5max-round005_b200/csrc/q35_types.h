@@ -166,23 +166,70 @@ struct AttnArgs {
   int xrank, xworld, xlayer;
   float* const* xrecv;
   unsigned long long* const* xflag;
+  // batched sessions (launch grid z = session): each session's cache and
+  // control block; its q/k/v, gated, RoPE and partial rows sit at z times the
+  // row size from the pointers above
+  const struct AttnSess* sess;
+};
+
+struct AttnSess {
+  uint16_t* kcache;
+  uint16_t* vcache;
+  Ctl* ctl;
+  uint32_t capacity;
 };
 
 // Q4 affine GEMM on the tensor cores (several tokens per launch):
-// y[t][n] = bf16(sum_k W[n][k] x[t][k]) (+ residual), W = bf16(s q + b).
+// y[t][n] = bf16(sum_k W[n][k] x[t][k]) (+ residual), W = bf16(s q + b), for
+// up to kGemmSegs weight matrices sharing the input x (a fused row space).
+constexpr int kGemmSegs = 4;
+struct QGemmSeg {
+  const uint32_t* w;     // [rows][K/8] codes
+  const uint16_t* s;     // [rows][K/64] bf16 scales
+  const uint16_t* b;     // [rows][K/64] bf16 biases
+  uint16_t* y;           // [T][ystride] output (row n at column n)
+  const uint16_t* res;   // optional residual, same layout as y (may alias it)
+  int rows, ystride;
+};
 struct QGemmArgs {
-  const uint32_t* w;     // [N][K/8] codes
-  const uint16_t* s;     // [N][K/64] bf16 scales
-  const uint16_t* b;     // [N][K/64] bf16 biases
+  QGemmSeg seg[kGemmSegs];
+  int nseg;
   const uint16_t* x;     // [T][K] bf16 activations
-  int N, K, T, Np;       // Np: T rounded up to a multiple of 16 (the MMA N)
-  int kblocks;           // 64-wide K blocks per split (gridDim.y splits)
-  float* part;           // split partials [splits][T][N] f32 (gridDim.y > 1)
-  uint32_t* counters;    // [row tiles], zero between launches
-  uint16_t* y;           // [T][ystride]
-  int ystride;
-  const uint16_t* res;   // optional residual [T][ystride] (may alias y)
+  int K, T, Np;          // Np: T rounded up to a multiple of 16 (the MMA N)
+  int kblocks;           // 64-wide K blocks per split
+  int tiles, splits;     // 128-row tiles over all segments, K splits
+  int rows_total;        // sum of the segments' rows (partials row index)
+  float* part;           // split partials [splits][T][rows_total] f32 (splits > 1)
+  uint32_t* counters;    // [tiles], zero between launches
   uint32_t* err;         // bounded-wait failure flag (optional)
+};
+
+// Per-token steps of the tensor-core batched-session route (q35_tokens.cu).
+struct TokArgs {
+  int n;                       // tokens = sessions
+  const uint16_t* h_in;        // rms: [n][1024]
+  uint16_t* h_out;             // embedding: [n][1024]
+  const uint16_t* gain;        // rms gain [1024]
+  uint16_t* xn;                // rms output [n][1024]
+  const uint32_t* ew;          // embedding codes (non-null: embed the sessions' tokens first)
+  const uint16_t* es;
+  const uint16_t* eb;
+  Ctl* const* ctls;            // [n] sessions' control blocks
+  uint32_t* const* seqs;       // [n] sessions' token rings
+  float* rope;                 // [n][64] RoPE rows of the step positions
+  const uint16_t* raw;         // conv: [n][raw_stride] qkv projections
+  int raw_stride;
+  uint16_t* conv;              // [n][6144]
+  uint16_t* const* hists;      // [n] sessions' conv histories (+ hist_off)
+  size_t hist_off;
+  const uint16_t* convw;       // [6144][4]
+  const uint16_t* y;           // normgate: [n][2048] recurrence output
+  const float* zs;             // [n][2048] z * sigmoid(z)
+  const uint16_t* gw;          // [128] norm weight
+  uint16_t* gated;             // [n][2048]
+  const uint16_t* g;           // swiglu: [n][3584] gate
+  const uint16_t* u;           // [n][3584] up
+  uint16_t* act;               // [n][3584]
 };
 
 // Sequence-split exchange buffers of one rank: records [slot][source][cta]
@@ -218,7 +265,8 @@ struct HeadArgs {
 };
 
 // Batched sessions: per-session outputs of the vocabulary head.
-constexpr int kMaxSessions = 8;
+constexpr int kMaxSessions = 8;         // exact batched route (CUDA cores)
+constexpr int kMaxTensorSessions = 64;  // tensor-core batched route
 struct HeadOut {
   uint16_t* logits;     // [248320]
   float* part;          // [kHeadCtas][2]

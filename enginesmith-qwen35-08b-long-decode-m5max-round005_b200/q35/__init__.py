@@ -23,6 +23,7 @@ VOCAB = 248320
 HIDDEN = 1024
 DEFAULT_CAPACITY = 262144
 SPLIT_HANDLE_BYTES = 64
+BATCH_TENSOR_CORES = 1
 
 OK, EINVAL, ECUDA, ECANCEL, EIO, ENOMEM, ETIMEOUT, ENCCL = 0, -1, -2, -3, -4, -5, -6, -7
 FLAG_TOKEN_BY_TOKEN_PROMPT = 1
@@ -77,6 +78,7 @@ def _load() -> ctypes.CDLL:
         "q35_split_connect": (c_int, [P, P]),
         "q35_split_world": (c_int, [P]),
         "q35_batch_create": (c_int, [POINTER(c_void_p), c_int, POINTER(c_void_p), c_char_p, c_size_t]),
+        "q35_batch_create_ex": (c_int, [POINTER(c_void_p), c_int, c_uint32, POINTER(c_void_p), c_char_p, c_size_t]),
         "q35_batch_decode": (c_int, [P, c_size_t, POINTER(c_uint32)]),
         "q35_batch_decode_timed": (c_int, [P, c_size_t, POINTER(c_float)]),
         "q35_batch_last_error": (c_char_p, [P]),
@@ -235,16 +237,19 @@ def split_connect_dist(model, group=None) -> None:
 
 class Batch:
     """Sessions of one device and one model decoded together: each step reads
-    the weights once for all members, and each member emits the tokens it
-    would emit alone. Members must hold a continuation state (a generate call
-    succeeded on them). Keep the member Models alive while the batch is."""
+    the weights once for all members. Exact route (default, up to 8 members):
+    each member emits the tokens it would emit alone. tensor_cores=True (up to
+    64 members): projections and head as tcgen05 GEMMs, equal to the exact
+    route within tolerance. Members must hold a continuation state (a generate
+    call succeeded on them). Keep the member Models alive while the batch is."""
 
-    def __init__(self, models: list["Model"]):
+    def __init__(self, models: list["Model"], tensor_cores: bool = False):
         n = len(models)
         arr = (c_void_p * max(n, 1))(*[m._h.value if isinstance(m._h, c_void_p) else m._h for m in models])
         h = c_void_p()
         err = ctypes.create_string_buffer(1024)
-        rc = lib().q35_batch_create(arr, n, ctypes.byref(h), err, len(err))
+        rc = lib().q35_batch_create_ex(arr, n, BATCH_TENSOR_CORES if tensor_cores else 0, ctypes.byref(h), err,
+                                       len(err))
         if rc != OK:
             raise Q35Error(rc, err.value.decode())
         self._h = h

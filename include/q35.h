@@ -146,6 +146,16 @@ int q35_split_world(const q35_session* s);
  * reset=0 continues a member after a batch call, as after its own. */
 typedef struct q35_batch q35_batch;
 int q35_batch_create(q35_session** sessions, int n, q35_batch** out, char* err, size_t err_len);
+/* Q35_BATCH_TENSOR_CORES: 1..64 sessions, every projection and the head as a
+ * Q4 GEMM on the tensor cores (q35_op_qgemm_q4's arithmetic: weights
+ * dequantised to bf16, float32 accumulation in the tensor core's order), the
+ * other steps as in decode; the sessions' attention and recurrences run in
+ * one launch each. Results agree with the exact route within floating-point
+ * tolerance, not bit for bit. Without the flag: the exact route, 1..8
+ * sessions. */
+#define Q35_BATCH_TENSOR_CORES 1u
+int q35_batch_create_ex(q35_session** sessions, int n, uint32_t flags, q35_batch** out, char* err,
+                        size_t err_len);
 /* `steps` greedy steps for every member; out_tokens is [n][steps] (row t =
  * session t). Fails (Q35_EINVAL, nothing run) when a member lacks a
  * continuation state or would pass its capacity. */
@@ -180,7 +190,7 @@ int q35_op_qmv_q4(const uint32_t* w, const uint16_t* scales, const uint16_t* bia
  * kernels/linear_nax.metal:1096-1139): y[t][n] = bf16(sum_k W[n][k] x[t][k]),
  * or bf16(residual[t][n] + bf16(.)) when residual is non-NULL (may alias y),
  * for t < tokens (1..256), with W dequantised as bf16(s*q + b). x [tokens][k]
- * bf16, y [tokens][n]; k a multiple of 512 up to 4096; w, x, scales, biases and
+ * bf16, y [tokens][n]; n up to 524,288; k a multiple of 512 up to 4096; w, x, scales, biases and
  * workspace 16-byte aligned. The float32 accumulation runs in
  * the tensor core's order, so results match a float32 reference within
  * tolerance rather than the matvec bit for bit. workspace: at least

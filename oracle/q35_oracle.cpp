@@ -711,10 +711,34 @@ void orc_qmv_q4_f32(const uint32_t* w, const uint16_t* s, const uint16_t* b, con
 }
 
 /* linear.metal:69-72 and :119-122 */
+/* The engine's tensor-core route (batched sessions): every weight
+ * dequantised to bf16(s q + b) (fma in f32, one rounding to bf16), the dot
+ * product accumulated in double and rounded to f32 once. The tensor core's
+ * own float32 order is not restated; this is the exact value it
+ * approximates. */
+static bool g_gemm_numerics = false;
+void qmv_gemm_f32(const uint32_t* w, const uint16_t* s, const uint16_t* b, const uint16_t* x, int N, int K,
+                  float* y) {
+  pool().run(N, [&](long n0, long n1) {
+    for (long n = n0; n < n1; ++n) {
+      double acc = 0.0;
+      for (int k = 0; k < K; ++k) {
+        const uint32_t q = (w[size_t(n) * (K / 8) + k / 8] >> (4 * (k % 8))) & 15u;
+        const float wv = bfr(std::fma(bf2f(s[size_t(n) * (K / 64) + k / 64]), float(q),
+                                      bf2f(b[size_t(n) * (K / 64) + k / 64])));
+        acc += double(wv) * double(bf2f(x[k]));
+      }
+      y[n] = float(acc);
+    }
+  });
+}
 void orc_qmv_q4(const uint32_t* w, const uint16_t* s, const uint16_t* b, const uint16_t* x,
                 const uint16_t* residual, int N, int K, uint16_t* y) {
   std::vector<float> v(N);
-  qmv_f32(w, s, b, x, N, K, v.data());
+  if (g_gemm_numerics)
+    qmv_gemm_f32(w, s, b, x, N, K, v.data());
+  else
+    qmv_f32(w, s, b, x, N, K, v.data());
   for (int n = 0; n < N; ++n)
     y[n] = residual ? f2bf(bf2f(residual[n]) + bfr(v[n])) : f2bf(v[n]);
 }
@@ -996,6 +1020,7 @@ struct orc_session {
   std::vector<uint16_t> logits, final_h;
   uint16_t lse = 0;
   int split_world = 1;  // attention as a sequence split over this many ranks
+  bool gemm = false;     // projections and head with the tensor-core route's numerics
 };
 
 extern "C" {
@@ -1134,10 +1159,15 @@ void orc_session_import(orc_session* s, uint32_t pos, uint32_t cap_src,
 }
 
 void orc_session_set_split(orc_session* s, int world) { s->split_world = world > 1 ? world : 1; }
+void orc_session_set_gemm(orc_session* s, int on) { s->gemm = on != 0; }
 
 /* model.rs:228-307 with rows=1 */
 uint32_t orc_session_step(orc_session* S, uint32_t token, int want_head) {
   orc_model* M = S->m;
+  g_gemm_numerics = S->gemm;
+  struct Restore {
+    ~Restore() { g_gemm_numerics = false; }
+  } restore;
   std::vector<uint16_t> h(1024), u(1024), raw(6144), z(2048), a(16), b(16), conv(6144),
       beta(16), y(2048), gated(2048), q(4096), k(512), v(512), query(2048), gate(3584),
       up(3584), act(3584);

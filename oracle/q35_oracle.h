@@ -116,6 +116,9 @@ void orc_session_reset(orc_session* s);
 uint32_t orc_session_position(const orc_session* s);
 /* consume `token` at the current position; if want_head, returns the greedy
  * next token (and keeps logits), else returns 0xffffffff. */
+/* projections and head of later steps with the engine's tensor-core route's
+ * numerics (weights dequantised to bf16, dot products exact then rounded) */
+void orc_session_set_gemm(orc_session* s, int on);
 /* attention of later steps as the engine's sequence split over `world` ranks */
 void orc_session_set_split(orc_session* s, int world);
 uint32_t orc_session_step(orc_session* s, uint32_t token, int want_head);

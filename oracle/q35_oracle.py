@@ -68,6 +68,7 @@ def lib() -> ctypes.CDLL:
             "orc_session_position": (c_uint32, [P]),
             "orc_session_step": (c_uint32, [P, c_uint32, c_int]),
             "orc_session_set_split": (None, [P, c_int]),
+            "orc_session_set_gemm": (None, [P, c_int]),
             "orc_session_logits": (None, [P, P]),
             "orc_session_lse": (c_uint16, [P]),
             "orc_session_final_hidden": (None, [P, P]),
@@ -248,6 +249,11 @@ class OracleSession:
         """Attention of later steps as the engine's sequence split over
         `world` ranks (1 = the reference's single-device attention)."""
         lib().orc_session_set_split(self.s, world)
+
+    def set_gemm(self, on: bool) -> None:
+        """Projections and head of later steps with the engine's tensor-core
+        route's numerics (bf16-dequantised weights, exact dot products)."""
+        lib().orc_session_set_gemm(self.s, 1 if on else 0)
 
     def step(self, token: int, head: bool = True) -> int:
         return int(lib().orc_session_step(self.s, token, 1 if head else 0))
