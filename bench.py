@@ -227,6 +227,8 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--split", action="store_true")
+    ap.add_argument("--batch-members", type=int, default=32,
+                    help="also time this many sessions decoded together on the tensor cores (0: skip)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -307,6 +309,27 @@ def main():
                "sample": f"{n} decode tokens at {m.position - n} context from the GPU state "
                          f"(teacher-forced, {agree}/{n} argmax agree)"}
 
+    # ---- batched sessions on the tensor cores (extra measurement, not `value`) ----
+    batched = None
+    nb = args.batch_members if not split else 0
+    if nb > 0:
+        members = [m] + [q35.Model.load(model_dir, local, capacity=cap) for _ in range(nb - 1)]
+        for mb in members[1:]:
+            mb.copy_from(m)
+        bt = q35.Batch(members, tensor_cores=True)
+        bt.decode_timed(4)
+        barrier()
+        bms = bt.decode_timed(16)
+        barrier()
+        bt.close()
+        for mb in members[1:]:
+            mb.close()
+        bmax = reduce_max(bms, world, "cuda")
+        batched = {"route": "tcgen05 GEMM projections and head (q35_batch_create_ex, Q35_BATCH_TENSOR_CORES)",
+                   "members_per_gpu": nb, "context": m.position, "steps": 16,
+                   "us_per_step": 1e3 * bmax / 16, "tok_s": aggregate_tok_s(world * nb, 16, bmax / 1e3),
+                   "note": "members forked from this session's state (q35_session_copy); device-timed"}
+
     if rank == 0:
         out = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -336,6 +359,7 @@ def main():
                               "frac": step_bytes * (value / streams) / 1e9 / peak},
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
+            "batched": batched,
         }
         print(json.dumps(out), flush=True)
     if world > 1:
