@@ -21,16 +21,6 @@ __host__ __device__ inline uint32_t sw128_off(int r, int c) {
   return uint32_t((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
 }
 
-// Shared-memory matrix descriptor, K-major without swizzle: core matrices of
-// 8 rows x 16 bytes stored as 128 contiguous bytes; `lbo` is the byte stride
-// between the two 8-element halves of one 16-element K step, `sbo` the byte
-// stride between groups of 8 rows. Bits: start >> 4 [0,14), lbo >> 4
-// [16,30), sbo >> 4 [32,46), version 1 [46,48), layout 0 (none) [61,64).
-Q35_DEV uint64_t tc_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-  return uint64_t((saddr >> 4) & 0x3fffu) | (uint64_t((lbo >> 4) & 0x3fffu) << 16) |
-         (uint64_t((sbo >> 4) & 0x3fffu) << 32) | (uint64_t(1) << 46);
-}
-
 // Instruction descriptor of kind::f16 with bf16 A and B, f32 accumulator,
 // both operands K-major: c_format [4,6) = 1, a_format [7,10) = 1, b_format
 // [10,13) = 1, N >> 3 at [17,23), M >> 4 at [24,29).
