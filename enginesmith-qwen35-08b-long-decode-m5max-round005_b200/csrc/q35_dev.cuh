@@ -135,6 +135,9 @@ Q35_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+Q35_DEV void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 Q35_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(

@@ -7,18 +7,21 @@
 //
 // Swap-AB tiling: the 128 weight rows of a CTA are the MMA's M, the tokens
 // its N (16..256), K runs in blocks of 64 (one quantisation group, so one
-// scale/bias per row and block). Per block two threads dequantise one row's
-// 64 weights into shared memory in the 128-byte-swizzled K-major layout, the
-// tokens' activations are stored beside them in the same layout, and one
-// thread issues four 128 x Np x 16 MMAs accumulating in TMEM; two
-// shared-memory stages let the next block's dequantisation overlap the
-// running MMAs (tcgen05.commit to a per-stage mbarrier). A CTA's codes,
-// scales and biases arrive by bulk copy (the next work item's behind the
-// current epilogue); CTAs are persistent over (row tile, K split) items, and
-// the last CTA of a split tile sums the f32 partials in split order
-// (deterministic). The epilogue reads TMEM with tcgen05.ld (thread = row, 8
-// tokens per load).
+// scale/bias per row and block). A persistent CTA walks (row tile, K split)
+// work items with warp-specialised roles linked by mbarriers: a loader thread
+// brings each block's codes and the tokens' activations in by 2-D TMA (the
+// activations already in the 128-byte-swizzled K-major layout) and each item's
+// scales and biases by bulk copy; eight producer warps dequantise the block
+// (packed bf16) into the same swizzled layout; one thread issues four
+// 128 x Np x 16 MMAs per block into one of two TMEM accumulators
+// (tcgen05.commit frees the stage); four epilogue warps drain the other
+// accumulator with tcgen05.ld while the next item accumulates. A ring of 2-4
+// stages decouples the roles. Split partials (f32) are summed in split order
+// by a second kernel (deterministic).
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
+
+#include <mutex>
 
 #include "q35_kernels.h"
 #include "q35_launch.h"
@@ -30,46 +33,44 @@ namespace q35 {
 
 constexpr int kGemmRows = 128;
 constexpr int kGemmKb = 64;
-constexpr int kGemmThreads = 512;  // four per weight row
-constexpr int kGemmQuarters = kGemmThreads / 128;
+constexpr int kGemmThreads = 512;  // 16 warps: roles below
+constexpr int kGemmProducerWarps = 8;
+constexpr int kGemmMmaWarp = 8, kGemmLoadWarp = 9, kGemmEpiWarp0 = 12;
 constexpr int kGemmMaxTokens = 256;
-constexpr int kGemmMaxKb = 16;  // K blocks per work item (its codes are staged whole)
+constexpr int kGemmMaxKb = 16;  // K blocks per work item
 constexpr uint32_t kErrGemmWait = 8;
-// The workspace starts with the split counters (kGemmMaxTiles words, then the
-// error word) at a fixed offset, so GEMMs of different shapes can share one
-// workspace: every counter is zero between launches (the last CTA of a split
-// tile resets its own), whatever the other GEMMs left in the partials.
+// The workspace starts with a fixed header (kGemmMaxTiles words, then the
+// error word), then the split partials; GEMMs of different shapes share one
+// workspace.
 constexpr int kGemmMaxTiles = 4096;
 constexpr size_t kGemmCounterBytes = size_t(kGemmMaxTiles) * 4 + 256;
 
 __host__ __device__ inline int gemm_np(int T) { return ((T + 15) / 16) * 16; }
 __host__ __device__ inline size_t gemm_a_bytes() { return size_t(kGemmRows) * kGemmKb * 2; }
 __host__ __device__ inline size_t gemm_b_bytes(int Np) { return size_t(Np) * kGemmKb * 2; }
-// a row's staged codes: kblocks x 32 bytes plus 16 bytes of padding, so
-// consecutive rows fall on different banks
-__host__ __device__ inline int gemm_code_stride(int kblocks) { return kblocks * 32 + 16; }
+constexpr size_t kGemmCodeStage = size_t(kGemmRows) * 32;  // 128 rows x 8 words
 struct GemmLayout {
   size_t a, b, codes, scl, bia, bar, total;
 };
-__host__ __device__ inline GemmLayout gemm_layout(int Np, int kblocks, int K) {
+// Ring of `S` stages (A tile, B tile, the block's codes), then per item slot
+// (2) the tile's scales and biases, then the barriers.
+__host__ __device__ inline GemmLayout gemm_layout(int Np, int S, int K) {
   GemmLayout L;
   L.a = 0;
-  L.b = L.a + 2 * gemm_a_bytes();
-  L.codes = L.b + 2 * gemm_b_bytes(Np);
-  L.scl = L.codes + size_t(kGemmRows) * gemm_code_stride(kblocks);
-  L.bia = L.scl + size_t(kGemmRows) * (K / 64) * 2;
-  L.bar = (L.bia + size_t(kGemmRows) * (K / 64) * 2 + 15) & ~size_t(15);
-  L.total = L.bar + 64;
+  L.b = L.a + size_t(S) * gemm_a_bytes();
+  L.codes = L.b + size_t(S) * gemm_b_bytes(Np);
+  L.scl = L.codes + size_t(S) * kGemmCodeStage;
+  L.bia = L.scl + 2 * size_t(kGemmRows) * (K / 64) * 2;
+  L.bar = (L.bia + 2 * size_t(kGemmRows) * (K / 64) * 2 + 15) & ~size_t(15);
+  L.total = L.bar + 256;
   return L;
 }
 __host__ __device__ inline uint32_t gemm_tmem_cols(int Np) {
   uint32_t c = 32;
-  while (c < uint32_t(Np)) c <<= 1;
+  while (c < uint32_t(2 * Np)) c <<= 1;  // two accumulators
   return c;
 }
 
-// Persistent: CTA c takes work items c, c + gridDim.x, ... of the
-// (row tile, K split) grid `tiles x splits` (item = tile * splits + split).
 // The segment of global row tile `tile`, its first tile and its first row in
 // the concatenated row space.
 __device__ __forceinline__ int gemm_seg_of(const QGemmArgs& a, int tile, int* tile0, int* grow0) {
@@ -88,237 +89,263 @@ __device__ __forceinline__ int gemm_seg_of(const QGemmArgs& a, int tile, int* ti
   return 0;
 }
 
+Q35_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Warp roles (persistent CTA over work items blockIdx.x, + gridDim.x, ...):
+//   warps 0-7   producers: dequantise A of each K block into the ring
+//   warp 8      lane 0 issues the MMAs (two TMEM accumulators, by item parity)
+//   warp 9      lane 0 stages: per item the tile's scales/biases (bulk copy),
+//               per K block the codes and the activations (2-D TMA)
+//   warps 12-15 epilogue: TMEM -> outputs (or split partials + reduction)
+// Barriers: lfull[s] (loads landed), full[s] (A written, 8 producer warps),
+// empty[s] (MMAs of the stage done, tcgen05.commit), wfull/wempty[w] (item
+// scales), afull/aempty[a] (accumulator ready / drained). Every wait is
+// bounded; after a failure the roles leave their loops.
 __global__ void __launch_bounds__(kGemmThreads, 1) k_qgemm(const __grid_constant__ QGemmArgs a) {
-  const int tiles = a.tiles, splits = a.splits;
   extern __shared__ __align__(1024) uint8_t smem[];
-  __shared__ int last;
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int K = a.K, KW = K / 8, KG = K / 64, nkb = K / kGemmKb;
-  const int T = a.T, Np = a.Np;
-  const GemmLayout L = gemm_layout(Np, a.kblocks, K);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int K = a.K, KG = K / 64, nkb = K / kGemmKb;
+  const int T = a.T, Np = a.Np, S = a.stages;
+  const int tiles = a.tiles, splits = a.splits, nitems = tiles * splits;
+  const GemmLayout L = gemm_layout(Np, S, K);
   uint8_t* As = smem + L.a;
   uint8_t* Bs = smem + L.b;
-  uint8_t* codes = smem + L.codes;
-  const uint16_t* scl = reinterpret_cast<const uint16_t*>(smem + L.scl);
-  const uint16_t* bia = reinterpret_cast<const uint16_t*>(smem + L.bia);
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L.bar);  // [0,1] MMA stages, [2] weights
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 3);
-  int* bad = reinterpret_cast<int*>(tslot + 1);
+  uint8_t* Cs = smem + L.codes;
+  uint16_t* scl = reinterpret_cast<uint16_t*>(smem + L.scl);
+  uint16_t* bia = reinterpret_cast<uint16_t*>(smem + L.bia);
+  uint64_t* lfull = reinterpret_cast<uint64_t*>(smem + L.bar);
+  uint64_t* full = lfull + 4;
+  uint64_t* empty = full + 4;
+  uint64_t* wfull = empty + 4;
+  uint64_t* wempty = wfull + 2;
+  uint64_t* afull = wempty + 2;
+  uint64_t* aempty = afull + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(aempty + 2);
+  volatile int* bad = reinterpret_cast<volatile int*>(tslot + 1);
   const uint32_t cols = gemm_tmem_cols(Np);
-  const int nitems = tiles * splits;
-  const int r = tid & (kGemmRows - 1), qtr = tid >> 7;  // row, quarter of its 64 values
+  const size_t sgs = size_t(kGemmRows) * KG;  // scale/bias slot stride (elements)
 
   if (warp == 0) tc_alloc(tslot, cols);
   if (tid == 0) {
-    mbar_init(&bar[0], 1);
-    mbar_init(&bar[1], 1);
-    mbar_init(&bar[2], 1);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&lfull[s], 1);
+      mbar_init(&full[s], kGemmProducerWarps);
+      mbar_init(&empty[s], 1);
+    }
+    for (int w = 0; w < 2; ++w) {
+      mbar_init(&wfull[w], 1);
+      mbar_init(&wempty[w], kGemmProducerWarps);
+      mbar_init(&afull[w], 1);
+      mbar_init(&aempty[w], 4);
+    }
     fence_mbar_init();
     // the swizzled operand tiles need 1024-byte aligned bases
     *bad = (smem_u32(smem) & 1023u) != 0u;
     if (*bad && a.err) atomicCAS(a.err, 0u, kErrGemmWait);
   }
-  for (int i = tid; i < 2 * (Np - T) * 8; i += kGemmThreads) {  // padding tokens stay zero
-    const int s = i / ((Np - T) * 8), q = i % ((Np - T) * 8), t = T + q / 8, j = q % 8;
-    *reinterpret_cast<uint4*>(Bs + s * gemm_b_bytes(Np) + sw128_off(t, j)) = make_uint4(0u, 0u, 0u, 0u);
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
-
-  // stage an item's weights: the codes of its K blocks (one bulk copy per
-  // row) and its tile's scales and biases (one copy each)
-  auto stage = [&](int item) {
-    const int tile = item / splits, sp = item - tile * splits;
-    int stile0, sgrow0;
-    const QGemmSeg& sg = a.seg[gemm_seg_of(a, tile, &stile0, &sgrow0)];
-    const int row0 = (tile - stile0) * kGemmRows, nrows = min(kGemmRows, sg.rows - row0);
-    const int kb0 = sp * a.kblocks, nit = min(nkb, kb0 + a.kblocks) - kb0;
-    fence_proxy_async();  // earlier generic reads of these buffers before the copies
-    if (tid == 0) {
-      const uint32_t sb = uint32_t(nrows) * KG * 2;
-      mbar_expect_tx(&bar[2], uint32_t(nrows) * nit * 32 + 2 * sb);
-      bulk_g2s(smem + L.scl, sg.s + size_t(row0) * KG, sb, &bar[2]);
-      bulk_g2s(smem + L.bia, sg.b + size_t(row0) * KG, sb, &bar[2]);
+  pdl_launch();  // dependents may start staging their constants
+  // everything but the loader's first scale copies and the producers (shared
+  // memory only) follows the previous kernel
+  if (warp == kGemmMmaWarp || warp >= kGemmEpiWarp0) pdl_wait();
+  auto wait = [&](uint64_t* b, uint32_t parity) {
+    if (*bad) return false;
+    if (!mbar_wait_limit(b, parity, kWaitLimit, a.err, kErrGemmWait)) {
+      *bad = 1;
+      return false;
     }
-    __syncthreads();  // expect_tx is registered before any code copy lands
-    if (tid < nrows)
-      bulk_g2s(codes + tid * gemm_code_stride(a.kblocks), sg.w + size_t(row0 + tid) * KW + size_t(kb0) * 8,
-               uint32_t(nit) * 32, &bar[2]);
+    return true;
   };
-  if (int(blockIdx.x) < nitems) stage(blockIdx.x);
-  pdl_wait();
-  pdl_launch();
-
-  constexpr int kBRegs = kGemmMaxTokens * 8 / kGemmThreads;
-  uint4 breg[kBRegs];
-  // activations of block kb: element i = j * T + t (token fastest, so the
-  // shared-memory stores of 8 consecutive threads are one 128-byte row);
-  // each slot's source offset and tile offset are fixed for the kernel
-  size_t bsrc[kBRegs];
-  uint32_t bdst[kBRegs];
-#pragma unroll
-  for (int q = 0; q < kBRegs; ++q) {
-    const int i = tid + q * kGemmThreads, j = i / T, t = i - j * T;
-    bsrc[q] = size_t(t) * K + size_t(j) * 8;
-    bdst[q] = sw128_off(t, j);
-  }
-  auto load_b = [&](int kb) {
-#pragma unroll
-    for (int q = 0; q < kBRegs; ++q)
-      if (tid + q * kGemmThreads < T * 8)
-        breg[q] = __ldg(reinterpret_cast<const uint4*>(a.x + bsrc[q] + size_t(kb) * kGemmKb));
+  auto item_geom = [&](int item, int& tile, int& sp, int& seg, int& row0, int& nrows, int& grow0, int& kb0,
+                       int& nit) {
+    tile = item / splits;
+    sp = item - tile * splits;
+    int stile0;
+    seg = gemm_seg_of(a, tile, &stile0, &grow0);
+    row0 = (tile - stile0) * kGemmRows;
+    nrows = min(kGemmRows, a.seg[seg].rows - row0);
+    kb0 = sp * a.kblocks;
+    nit = min(nkb, kb0 + a.kblocks) - kb0;
   };
-  const uint32_t idesc = tc_idesc_bf16(kGemmRows, Np);
-  const uint32_t tbase = tmem + (uint32_t(32 * (warp & 3)) << 16);
-  uint32_t wphase = 0, mma_uses[2] = {0u, 0u};
 
-  for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
-    const int tile = item / splits, sp = item - tile * splits;
-    int stile0, sgrow0;
-    const QGemmSeg& sg = a.seg[gemm_seg_of(a, tile, &stile0, &sgrow0)];
-    const int row0 = (tile - stile0) * kGemmRows, nrows = min(kGemmRows, sg.rows - row0);
-    const int kb0 = sp * a.kblocks, nit = min(nkb, kb0 + a.kblocks) - kb0;
-    const bool rok = r < nrows;
-    const int row = row0 + r;              // row within the segment
-    const int grow = sgrow0 + row;         // row in the concatenated space (partials)
-    // CTAs walk their K blocks from different starting blocks, so they do
-    // not all read the same activation lines at the same moment
-    const int rot = nit > 0 ? int(blockIdx.x) % nit : 0;
-    load_b(kb0 + rot);
-    if (!mbar_wait_limit(&bar[2], wphase, kWaitLimit, a.err, kErrGemmWait)) *bad = 1;
-    wphase ^= 1u;
-    const uint8_t* crow = codes + r * gemm_code_stride(a.kblocks) + qtr * 8;
-    for (int it = 0; it < nit; ++it) {
-      const int ib = it + rot < nit ? it + rot : it + rot - nit;  // block within the item
-      const int kb = kb0 + ib, s = it & 1;
-      if (mma_uses[s] > 0 &&
-          !mbar_wait_limit(&bar[s], (mma_uses[s] - 1) & 1u, kWaitLimit, a.err, kErrGemmWait))
-        *bad = 1;
-      uint8_t* A = As + s * gemm_a_bytes();
-      uint8_t* B = Bs + s * gemm_b_bytes(Np);
-#pragma unroll
-      for (int q = 0; q < kBRegs; ++q)
-        if (tid + q * kGemmThreads < T * 8) *reinterpret_cast<uint4*>(B + bdst[q]) = breg[q];
-      if (it + 1 < nit) load_b(kb0 + (ib + 1 < nit ? ib + 1 : 0));
-      // this thread's 32 of its row's 64 values -> bf16(s q + b), 4 core matrices
-      uint2 c = make_uint2(0u, 0u);
-      float sc = 0.0f, bi = 0.0f;
-      if (rok) {
-        c = *reinterpret_cast<const uint2*>(crow + ib * 32);
-        sc = bf2f(scl[r * KG + kb]);
-        bi = bf2f(bia[r * KG + kb]);
+  if (warp == kGemmLoadWarp && lane == 0) {
+    // ---------------- loader ----------------
+    // scales are constants: the first item's may load before the dependency wait
+    int g = 0;
+    for (int item = blockIdx.x, j = 0; item < nitems && !*bad; item += gridDim.x, ++j) {
+      int tile, sp, seg, row0, nrows, grow0, kb0, nit;
+      item_geom(item, tile, sp, seg, row0, nrows, grow0, kb0, nit);
+      const int w = j & 1;
+      if (j >= 2 && !wait(&wempty[w], uint32_t((j >> 1) - 1) & 1u)) break;
+      const uint32_t sb = uint32_t(nrows) * KG * 2;
+      mbar_expect_tx(&wfull[w], 2 * sb);
+      bulk_g2s(scl + w * sgs, a.seg[seg].s + size_t(row0) * KG, sb, &wfull[w]);
+      bulk_g2s(bia + w * sgs, a.seg[seg].b + size_t(row0) * KG, sb, &wfull[w]);
+      if (j == 0) pdl_wait();  // the activations come from the previous kernel
+      for (int it = 0; it < nit; ++it, ++g) {
+        const int s = g % S, u = g / S;
+        if (u >= 1 && !wait(&empty[s], uint32_t(u - 1) & 1u)) break;
+        mbar_expect_tx(&lfull[s], uint32_t(kGemmCodeStage + gemm_b_bytes(Np)));
+        tma_load_2d(Cs + s * kGemmCodeStage, &a.cmap[seg], (kb0 + it) * 8, row0, &lfull[s]);
+        tma_load_2d(Bs + s * gemm_b_bytes(Np), &a.xmap, (kb0 + it) * kGemmKb, 0, &lfull[s]);
       }
-      const uint32_t words[2] = {c.x, c.y};
-      // packed bf16: the nibbles at word positions (e, e + 4) become the pair
-      // (128 + n_e, 128 + n_{e+4}) by one LOP3 with the bf16 bits of 128; an
-      // exact subtraction of 128 and one fma rounding to nearest even give
-      // bf16(s q + b) (s q is exact, so this is the correctly rounded value),
-      // and byte permutes restore the order (0,1) (2,3) (4,5) (6,7)
-      const __nv_bfloat162 s2 = __floats2bfloat162_rn(sc, sc), b2 = __floats2bfloat162_rn(bi, bi);
-      const __nv_bfloat162 m128 = __floats2bfloat162_rn(128.0f, 128.0f);
+    }
+  } else if (warp < kGemmProducerWarps) {
+    // ---------------- producers ----------------
+    const int r = tid & (kGemmRows - 1), half = tid >> 7;
+    int g = 0;
+    for (int item = blockIdx.x, j = 0; item < nitems && !*bad; item += gridDim.x, ++j) {
+      int tile, sp, seg, row0, nrows, grow0, kb0, nit;
+      item_geom(item, tile, sp, seg, row0, nrows, grow0, kb0, nit);
+      const int w = j & 1;
+      if (!wait(&wfull[w], uint32_t(j >> 1) & 1u)) break;
+      const bool rok = r < nrows;
+      for (int it = 0; it < nit; ++it, ++g) {
+        const int s = g % S, u = g / S, kb = kb0 + it;
+        if (!wait(&lfull[s], uint32_t(u) & 1u)) break;
+        const uint4 c = *reinterpret_cast<const uint4*>(Cs + s * kGemmCodeStage + r * 32 + half * 16);
+        const float sc = rok ? bf2f(scl[w * sgs + size_t(r) * KG + kb]) : 0.0f;
+        const float bi = rok ? bf2f(bia[w * sgs + size_t(r) * KG + kb]) : 0.0f;
+        const uint32_t words[4] = {c.x, c.y, c.z, c.w};
+        // packed bf16: the nibbles at word positions (e, e + 4) become the pair
+        // (128 + n_e, 128 + n_{e+4}) by one LOP3 with the bf16 bits of 128; an
+        // exact subtraction of 128 and one fma rounding to nearest even give
+        // bf16(s q + b) (s q is exact, so this is the correctly rounded value),
+        // and byte permutes restore the order (0,1) (2,3) (4,5) (6,7)
+        const __nv_bfloat162 s2 = __floats2bfloat162_rn(sc, sc), b2 = __floats2bfloat162_rn(bi, bi);
+        const __nv_bfloat162 m128 = __floats2bfloat162_rn(128.0f, 128.0f);
+        uint8_t* A = As + s * gemm_a_bytes();
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        uint32_t v[4];
+        for (int q = 0; q < 4; ++q) {
+          uint32_t v[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const uint32_t m = ((words[j] >> (4 * e)) & 0x000f000fu) | 0x43004300u;  // nibbles e, e + 4
-          const __nv_bfloat162 q2 = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&m), m128);
-          const __nv_bfloat162 w2 = __hfma2(s2, q2, b2);
-          v[e] = *reinterpret_cast<const uint32_t*>(&w2);  // lo: value e, hi: value e + 4
+          for (int e = 0; e < 4; ++e) {
+            const uint32_t m = ((words[q] >> (4 * e)) & 0x000f000fu) | 0x43004300u;
+            const __nv_bfloat162 q2 = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&m), m128);
+            const __nv_bfloat162 w2 = __hfma2(s2, q2, b2);
+            v[e] = *reinterpret_cast<const uint32_t*>(&w2);
+          }
+          const uint4 o = rok ? make_uint4(__byte_perm(v[0], v[1], 0x5410), __byte_perm(v[2], v[3], 0x5410),
+                                           __byte_perm(v[0], v[1], 0x7632), __byte_perm(v[2], v[3], 0x7632))
+                              : make_uint4(0u, 0u, 0u, 0u);
+          *reinterpret_cast<uint4*>(A + sw128_off(r, half * 4 + q)) = o;
         }
-        const uint4 o = rok ? make_uint4(__byte_perm(v[0], v[1], 0x5410), __byte_perm(v[2], v[3], 0x5410),
-                                         __byte_perm(v[0], v[1], 0x7632), __byte_perm(v[2], v[3], 0x7632))
-                            : make_uint4(0u, 0u, 0u, 0u);
-        *reinterpret_cast<uint4*>(A + sw128_off(r, qtr * 2 + j)) = o;
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full[s]);
       }
-      fence_proxy_async();
-      tc_fence_before();
-      __syncthreads();
-      if (tid == 0 && !*bad) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&wempty[w]);
+    }
+  } else if (warp == kGemmMmaWarp && lane == 0) {
+    // ---------------- MMA issuer ----------------
+    const uint32_t idesc = tc_idesc_bf16(kGemmRows, Np);
+    int g = 0;
+    for (int item = blockIdx.x, j = 0; item < nitems && !*bad; item += gridDim.x, ++j) {
+      int tile, sp, seg, row0, nrows, grow0, kb0, nit;
+      item_geom(item, tile, sp, seg, row0, nrows, grow0, kb0, nit);
+      const int acc = j & 1;
+      if (j >= 2 && !wait(&aempty[acc], uint32_t((j >> 1) - 1) & 1u)) break;
+      tc_fence_after();
+      const uint32_t d = tmem + uint32_t(acc * Np);
+      for (int it = 0; it < nit; ++it, ++g) {
+        const int s = g % S, u = g / S;
+        if (!wait(&full[s], uint32_t(u) & 1u)) break;
         tc_fence_after();
-        const uint32_t a0 = smem_u32(A), b0 = smem_u32(B);
+        const uint32_t a0 = smem_u32(As + s * gemm_a_bytes()), b0 = smem_u32(Bs + s * gemm_b_bytes(Np));
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          tc_mma_bf16(tmem, tc_desc_sw128(a0 + 32 * kk, 1024), tc_desc_sw128(b0 + 32 * kk, 1024), idesc,
+          tc_mma_bf16(d, tc_desc_sw128(a0 + 32 * kk, 1024), tc_desc_sw128(b0 + 32 * kk, 1024), idesc,
                       (it > 0 || kk > 0) ? 1u : 0u);
-        tc_commit(&bar[s]);
+        tc_commit(&empty[s]);
       }
-      ++mma_uses[s];
+      tc_commit(&afull[acc]);
     }
-    // every code of this item is read: stage the next item behind the epilogue
-    const int next = item + int(gridDim.x);
-    if (next < nitems) stage(next);
-    const int sl = (nit - 1) & 1;
-    if (nit > 0 && !mbar_wait_limit(&bar[sl], (mma_uses[sl] - 1) & 1u, kWaitLimit, a.err, kErrGemmWait))
-      *bad = 1;
-    tc_fence_after();
-    const bool ok = !*bad && nit > 0;
-    const bool splitk = splits > 1;
-    if (ok) {
-      // warp w reads TMEM lanes 32 (w % 4).. and token part w / 4 (8-token units)
-      const int tph = ((T + 8 * kGemmQuarters - 1) / (8 * kGemmQuarters)) * 8;
-      const int c0 = (warp >> 2) * tph, c1 = min(T, c0 + tph);
-      for (int cc = c0; cc < c1; cc += 8) {
+  } else if (warp >= kGemmEpiWarp0) {
+    // ---------------- epilogue ----------------
+    const int e = tid - kGemmEpiWarp0 * 32;  // 0..127 = TMEM lane = tile row
+    const uint32_t lane_base = uint32_t(32 * (warp & 3)) << 16;
+    for (int item = blockIdx.x, j = 0; item < nitems && !*bad; item += gridDim.x, ++j) {
+      int tile, sp, seg, row0, nrows, grow0, kb0, nit;
+      item_geom(item, tile, sp, seg, row0, nrows, grow0, kb0, nit);
+      const int acc = j & 1;
+      if (!wait(&afull[acc], uint32_t(j >> 1) & 1u)) break;
+      tc_fence_after();
+      const QGemmSeg& sg = a.seg[seg];
+      const bool rok = e < nrows;
+      const int row = row0 + e, grow = grow0 + row;
+      const bool splitk = splits > 1;
+      for (int c0 = 0; c0 < T; c0 += 8) {
         float v[8];
-        tc_ld8(tbase + uint32_t(cc), v);
+        tc_ld8(tmem + lane_base + uint32_t(acc * Np + c0), v);
         if (!rok) continue;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int t = cc + e;
-          if (t >= c1) break;
+        for (int q = 0; q < 8; ++q) {
+          const int t = c0 + q;
+          if (t >= T) break;
           if (splitk) {
-            a.part[(size_t(sp) * T + t) * a.rows_total + grow] = v[e];
+            a.part[(size_t(sp) * T + t) * a.rows_total + grow] = v[q];
           } else {
             uint16_t* y = sg.y + size_t(t) * sg.ystride + row;
             if (sg.res)
-              *y = f2bf(__fadd_rn(bf2f(sg.res[size_t(t) * sg.ystride + row]), bfr(v[e])));
+              *y = f2bf(__fadd_rn(bf2f(sg.res[size_t(t) * sg.ystride + row]), bfr(v[q])));
             else
-              *y = f2bf(v[e]);
+              *y = f2bf(v[q]);
           }
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if ((tid & 31) == 0) mbar_arrive(&aempty[acc]);
     }
-    tc_fence_before();
-    __syncthreads();  // TMEM reads done before the next item's first MMA
-    if (!splitk || !ok) continue;
-
-    // split K: the last CTA of this row tile sums the partials in split order
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) last = atomicAdd(&a.counters[tile], 1u) == uint32_t(splits - 1);
-    __syncthreads();
-    if (!last) continue;
-    __threadfence();
-    if (tid == 0) a.counters[tile] = 0;
-    if (rok) {
-      for (int t0 = qtr * 8; t0 < T; t0 += 8 * kGemmQuarters) {
-        float acc[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
-        for (int q = 0; q < splits; ++q) {
-#pragma unroll
-          for (int e = 0; e < 8; ++e)
-            if (t0 + e < T) acc[e] = __fadd_rn(acc[e], __ldcg(&a.part[(size_t(q) * T + t0 + e) * a.rows_total + grow]));
-        }
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int t = t0 + e;
-          if (t >= T) break;
-          uint16_t* y = sg.y + size_t(t) * sg.ystride + row;
-          if (sg.res)
-            *y = f2bf(__fadd_rn(bf2f(sg.res[size_t(t) * sg.ystride + row]), bfr(acc[e])));
-          else
-            *y = f2bf(acc[e]);
-        }
-      }
-    }
-    __syncthreads();
   }
+  __syncwarp();  // the loader and MMA lanes rejoin their warps before the barrier
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tc_dealloc(tmem, cols);
+}
+
+// Split K: y = bf16(sum over splits in split order) (+ residual), thread =
+// (row of the concatenated row space, block of 8 tokens), consecutive threads
+// on consecutive rows.
+__global__ void __launch_bounds__(256) k_qgemm_reduce(const __grid_constant__ QGemmArgs a) {
+  pdl_wait();
+  pdl_launch();
+  const int R = a.rows_total, T = a.T;
+  const int i = blockIdx.x * 256 + threadIdx.x;
+  if (i >= R * ((T + 7) / 8)) return;
+  const int grow = i % R, t0 = (i / R) * 8;
+  int seg = 0, r0 = 0;
+  while (seg + 1 < a.nseg && grow >= r0 + a.seg[seg].rows) r0 += a.seg[seg++].rows;
+  const QGemmSeg& sg = a.seg[seg];
+  const int row = grow - r0;
+  float s8[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) s8[q] = 0.0f;
+  for (int p = 0; p < a.splits; ++p) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      if (t0 + q < T) s8[q] = __fadd_rn(s8[q], __ldcg(&a.part[(size_t(p) * T + t0 + q) * R + grow]));
+  }
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const int t = t0 + q;
+    if (t >= T) break;
+    uint16_t* y = sg.y + size_t(t) * sg.ystride + row;
+    if (sg.res)
+      *y = f2bf(__fadd_rn(bf2f(sg.res[size_t(t) * sg.ystride + row]), bfr(s8[q])));
+    else
+      *y = f2bf(s8[q]);
+  }
 }
 
 // Host side ------------------------------------------------------------------
@@ -361,13 +388,41 @@ size_t qgemm_workspace_bytes(int N, int K, int T) {
   return qgemm_workspace_bytes(a);
 }
 
+constexpr size_t kGemmSmemMax = 220 * 1024;  // + the 1 KB of static shared memory
+
 cudaError_t qgemm_init() {
-  return cudaFuncSetAttribute(k_qgemm, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              int(gemm_layout(kGemmMaxTokens, kGemmMaxKb, 4096).total));
+  return cudaFuncSetAttribute(k_qgemm, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kGemmSmemMax));
 }
 
-// Validates, lays out the workspace (partials, counters, error word) and
-// launches. The counters must be zero; `zero_counters` clears them first.
+// cuTensorMapEncodeTiled through the runtime's driver entry point.
+static PFN_cuTensorMapEncodeTiled_v12000 tmap_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D tensor map: inner extent `d0` (contiguous), `d1` rows `pitch` bytes
+// apart, boxes b0 x b1.
+static bool tmap_2d(CUtensorMap* m, CUtensorMapDataType ty, const void* base, uint64_t d0, uint64_t d1,
+                    uint64_t pitch, uint32_t b0, uint32_t b1, CUtensorMapSwizzle sw) {
+  auto fn = tmap_encode();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {d0, d1}, strides[1] = {pitch};
+  const cuuint32_t box[2] = {b0, b1}, estr[2] = {1, 1};
+  return fn(m, ty, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Validates, lays out the workspace (header with the error word, partials),
+// encodes the TMA descriptors and launches (plus the split reduction).
+// `zero_counters` clears the header first.
 cudaError_t launch_qgemm(QGemmArgs a, void* ws, size_t ws_bytes, bool zero_counters, cudaStream_t st, bool pdl) {
   if (a.T < 1 || a.T > kGemmMaxTokens || a.K % 512 != 0 || a.K < 512 || a.K > 4096 || a.nseg < 1 ||
       a.nseg > kGemmSegs || !a.x)
@@ -390,13 +445,28 @@ cudaError_t launch_qgemm(QGemmArgs a, void* ws, size_t ws_bytes, bool zero_count
   a.part = reinterpret_cast<float*>(w + kGemmCounterBytes);
   if (!a.err) a.err = a.counters + kGemmMaxTiles;
   a.Np = gemm_np(a.T);
+  a.stages = 0;
+  for (int S = 4; S >= 2 && !a.stages; --S)
+    if (gemm_layout(a.Np, S, a.K).total <= kGemmSmemMax) a.stages = S;
+  if (!a.stages) return cudaErrorInvalidValue;
+  for (int i = 0; i < a.nseg; ++i)
+    if (!tmap_2d(&a.cmap[i], CU_TENSOR_MAP_DATA_TYPE_UINT32, a.seg[i].w, uint64_t(a.K / 8),
+                 uint64_t(a.seg[i].rows), uint64_t(a.K / 2), 8, kGemmRows, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return cudaErrorInvalidValue;
+  if (!tmap_2d(&a.xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a.x, uint64_t(a.K), uint64_t(a.T), uint64_t(a.K) * 2,
+               kGemmKb, uint32_t(a.Np), CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
   if (zero_counters) {
     cudaError_t e = cudaMemsetAsync(a.counters, 0, kGemmCounterBytes, st);
     if (e != cudaSuccess) return e;
   }
   const int items = tiles * splits;
   const int grid = items < 148 ? items : 148;
-  return launch_ex(k_qgemm, dim3(grid), dim3(kGemmThreads), gemm_layout(a.Np, kb, a.K).total, st, pdl, a);
+  cudaError_t e = launch_ex(k_qgemm, dim3(grid), dim3(kGemmThreads), gemm_layout(a.Np, a.stages, a.K).total, st,
+                            pdl, a);
+  if (e != cudaSuccess || splits == 1) return e;
+  const int work = a.rows_total * ((a.T + 7) / 8);
+  return launch_ex(k_qgemm_reduce, dim3((work + 255) / 256), dim3(256), 0, st, true, a);
 }
 
 }  // namespace q35

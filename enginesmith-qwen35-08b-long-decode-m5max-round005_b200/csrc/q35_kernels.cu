@@ -474,9 +474,6 @@ __device__ __forceinline__ void attn_time_end(Ctl* ctl) {
   }
 }
 
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
 
 // Warp roles, linked only by full/empty mbarrier pairs (every wait bounded):
 //   warps 0-7   score: keys 4w..4w+3 of each tile for the four query heads

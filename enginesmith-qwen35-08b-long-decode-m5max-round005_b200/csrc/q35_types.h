@@ -3,6 +3,7 @@
 // :41-78 hard-codes (hidden 1024, 24 layers with layer l%4==3 full attention,
 // MLP 3584, vocab 248,320, GDN 16 heads x 128, attention 8 q / 2 kv heads x 256).
 #pragma once
+#include <cuda.h>  // CUtensorMap (TMA descriptors in the GEMM arguments)
 #include <stdint.h>
 
 namespace q35 {
@@ -199,9 +200,15 @@ struct QGemmArgs {
   int kblocks;           // 64-wide K blocks per split
   int tiles, splits;     // 128-row tiles over all segments, K splits
   int rows_total;        // sum of the segments' rows (partials row index)
+  int stages;            // shared-memory ring depth
   float* part;           // split partials [splits][T][rows_total] f32 (splits > 1)
   uint32_t* counters;    // [tiles], zero between launches
   uint32_t* err;         // bounded-wait failure flag (optional)
+  // TMA descriptors (filled by launch_qgemm): each segment's codes as a
+  // [rows][K/8] u32 tensor, boxes of 128 rows x 8 words; x as a [T][K] bf16
+  // tensor, boxes of Np tokens x 64, landing in the 128-byte swizzle
+  alignas(64) CUtensorMap cmap[kGemmSegs];
+  alignas(64) CUtensorMap xmap;
 };
 
 // Per-token steps of the tensor-core batched-session route (q35_tokens.cu).
