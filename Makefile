@@ -24,7 +24,7 @@ $(BUILD)/q35_synth.o: $(CSRC)/q35_synth.cpp include/q35.h
 	@mkdir -p $(BUILD)
 	$(CXX) $(CXXFLAGS) -O3 -c $< -o $@
 
-$(LIB): $(BUILD)/q35_kernels.o $(BUILD)/q35_prefill.o $(BUILD)/q35_gemm.o $(BUILD)/q35_tokens.o $(BUILD)/q35_runtime.o $(BUILD)/q35_noalloc.o $(BUILD)/q35_synth.o
+$(LIB): $(BUILD)/q35_kernels.o $(BUILD)/q35_prefill.o $(BUILD)/q35_gemm.o $(BUILD)/q35_tokens.o $(BUILD)/q35_prompt.o $(BUILD)/q35_runtime.o $(BUILD)/q35_noalloc.o $(BUILD)/q35_synth.o
 	@mkdir -p $(LIBDIR)
 	$(NVCC) $(ARCH) -shared -o $@ $^ -lcudart -lpthread
 

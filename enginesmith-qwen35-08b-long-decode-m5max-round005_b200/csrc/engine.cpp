@@ -71,6 +71,7 @@ int main(int argc, char** argv) {
     if (a == "--model" && i + 1 < argc) model = argv[++i];
     else if (a == "--device" && i + 1 < argc) device = std::atoi(argv[++i]);
     else if (a == "--capacity" && i + 1 < argc) opts.capacity = uint32_t(std::strtoul(argv[++i], nullptr, 10));
+    else if (a == "--tensor-prompt") opts.flags |= Q35_FLAG_TENSOR_PROMPT;  // prompts on the tensor cores
     else {
       std::fprintf(stderr, "engine: unknown argument %s\n", a.c_str());
       return 1;

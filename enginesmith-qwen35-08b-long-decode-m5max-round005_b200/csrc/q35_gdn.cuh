@@ -1,6 +1,7 @@
-// Gated delta net arithmetic shared by the decode step and the chunked
-// prompt path, so both evaluate exactly the same operations in the same
-// order (the oracle's restatement of gdn_input.metal / gdn.metal).
+// Gated delta net and attention-prologue arithmetic shared by the decode
+// step and the prompt paths, so all evaluate exactly the same operations in
+// the same order (the oracle's restatement of gdn_input.metal / gdn.metal /
+// attention.metal).
 #pragma once
 #include "q35_qmv.cuh"
 
@@ -101,6 +102,67 @@ Q35_DEV void rope_pair(uint32_t position, int pair, float* cs) {
   const float angle = __fmul_rn(float(position), inv_freq);
   cs[2 * pair] = (float)cos((double)angle);
   cs[2 * pair + 1] = (float)sin((double)angle);
+}
+
+// Per-head RMSNorm (attention.metal:37-53: two 32-thread partials of 128
+// values) followed by partial RoPE (attention.metal:55-70). One warp, one
+// head; out[d] gets the bf16 value as f32.
+Q35_DEV void head_norm_rope(const uint16_t* x, const uint16_t* gain,
+                                               const float* cs, float* nrm, float* out, int lane) {
+  // Lane l owns dims 4l..4l+3 and 128+4l..128+4l+3 (the reference's two
+  // partial sums); every global load is issued up front. x, gain 8-byte
+  // aligned, cs 16-byte aligned.
+  const uint2 xa = *reinterpret_cast<const uint2*>(x + 4 * lane);
+  const uint2 xb = *reinterpret_cast<const uint2*>(x + 128 + 4 * lane);
+  const uint2 ga = *reinterpret_cast<const uint2*>(gain + 4 * lane);
+  const uint2 gb = *reinterpret_cast<const uint2*>(gain + 128 + 4 * lane);
+  float4 c0 = make_float4(0.f, 0.f, 0.f, 0.f), c1 = c0;  // (cos, sin) of pairs 4(l&7)..+3
+  if (lane < 16) {
+    c0 = reinterpret_cast<const float4*>(cs)[2 * (lane & 7)];
+    c1 = reinterpret_cast<const float4*>(cs)[2 * (lane & 7) + 1];
+  }
+  const float va[4] = {bf_lo(xa.x), bf_hi(xa.x), bf_lo(xa.y), bf_hi(xa.y)};
+  const float vb[4] = {bf_lo(xb.x), bf_hi(xb.x), bf_lo(xb.y), bf_hi(xb.y)};
+  const float gA[4] = {bf_lo(ga.x), bf_hi(ga.x), bf_lo(ga.y), bf_hi(ga.y)};
+  const float gB[4] = {bf_lo(gb.x), bf_hi(gb.x), bf_lo(gb.y), bf_hi(gb.y)};
+  float pa = 0.0f, pb = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    pa = __fadd_rn(pa, __fmul_rn(va[i], va[i]));
+    pb = __fadd_rn(pb, __fmul_rn(vb[i], vb[i]));
+  }
+  const float s0 = warp_sum(pa), s1 = warp_sum(pb);
+  const float inv = drsqrtf(__fadd_rn(__fmul_rn(__fadd_rn(s0, s1), 0.00390625f), 1e-6f));
+  float na[4], nb[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    na[i] = bfr(__fmul_rn(bfr(__fmul_rn(va[i], inv)), gA[i]));
+    nb[i] = bfr(__fmul_rn(bfr(__fmul_rn(vb[i], inv)), gB[i]));
+  }
+  *reinterpret_cast<float4*>(nrm + 4 * lane) = make_float4(na[0], na[1], na[2], na[3]);
+  __syncwarp();
+  if (lane < 16) {  // partial RoPE on dims 0..63: pair p = d & 31 rotates (p, p + 32)
+    const float c[4] = {c0.x, c0.z, c1.x, c1.z}, sn[4] = {c0.y, c0.w, c1.y, c1.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int pair = 4 * (lane & 7) + i;
+      const float lo = nrm[pair], hi = nrm[pair + 32];
+      na[i] = lane < 8 ? bfr(__fsub_rn(__fmul_rn(lo, c[i]), __fmul_rn(hi, sn[i])))
+                       : bfr(__fadd_rn(__fmul_rn(lo, sn[i]), __fmul_rn(hi, c[i])));
+    }
+  }
+  *reinterpret_cast<float4*>(out + 4 * lane) = make_float4(na[0], na[1], na[2], na[3]);
+  *reinterpret_cast<float4*>(out + 128 + 4 * lane) = make_float4(nb[0], nb[1], nb[2], nb[3]);
+  __syncwarp();
+}
+
+// attention.metal:140-150: the attention output gate, sigmoid with BF16
+// steps after exp, add and reciprocal (mirrored by sign).
+Q35_DEV float attn_gate_bf(float x) {
+  const float e = bfr(dexpf(fabsf(x)));
+  const float denom = bfr(__fadd_rn(1.0f, e));
+  const float inverse = bfr(__fdiv_rn(1.0f, denom));
+  return bfr(x < 0.0f ? inverse : __fsub_rn(1.0f, inverse));
 }
 
 }  // namespace q35

@@ -5,10 +5,10 @@
 // qmm_q4_nax). Unlike the exact matvec this changes the summation order, so it
 // matches a float32 reference within tolerance, not bit for bit.
 //
-// Swap-AB tiling: the 128 weight rows of a CTA are the MMA's M, the tokens
-// its N (16..256), K runs in blocks of 64 (one quantisation group, so one
-// scale/bias per row and block). A persistent CTA walks (row tile, K split)
-// work items with warp-specialised roles linked by mbarriers: a loader thread
+// Swap-AB tiling: the 128 weight rows of a CTA are the MMA's M, a tile of up
+// to 256 tokens its N (16..256), K runs in blocks of 64 (one quantisation
+// group, so one scale/bias per row and block). A persistent CTA walks (row
+// tile, token tile, K split) work items with warp-specialised roles linked by mbarriers: a loader thread
 // brings each block's codes and the tokens' activations in by 2-D TMA (the
 // activations already in the 128-byte-swizzled K-major layout) and each item's
 // scales and biases by bulk copy; eight producer warps dequantise the block
@@ -36,7 +36,8 @@ constexpr int kGemmKb = 64;
 constexpr int kGemmThreads = 512;  // 16 warps: roles below
 constexpr int kGemmProducerWarps = 8;
 constexpr int kGemmMmaWarp = 8, kGemmLoadWarp = 9, kGemmEpiWarp0 = 12;
-constexpr int kGemmMaxTokens = 256;
+constexpr int kGemmTokTile = 256;  // tokens per work item (the MMA's largest N)
+constexpr int kGemmMaxTokens = 4096;
 constexpr int kGemmMaxKb = 16;  // K blocks per work item
 constexpr uint32_t kErrGemmWait = 8;
 // The workspace starts with a fixed header (kGemmMaxTiles words, then the
@@ -46,6 +47,7 @@ constexpr int kGemmMaxTiles = 4096;
 constexpr size_t kGemmCounterBytes = size_t(kGemmMaxTiles) * 4 + 256;
 
 __host__ __device__ inline int gemm_np(int T) { return ((T + 15) / 16) * 16; }
+inline int gemm_ttiles(int T) { return (T + kGemmTokTile - 1) / kGemmTokTile; }
 __host__ __device__ inline size_t gemm_a_bytes() { return size_t(kGemmRows) * kGemmKb * 2; }
 __host__ __device__ inline size_t gemm_b_bytes(int Np) { return size_t(Np) * kGemmKb * 2; }
 constexpr size_t kGemmCodeStage = size_t(kGemmRows) * 32;  // 128 rows x 8 words
@@ -112,7 +114,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_qgemm(const __grid_constant
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int K = a.K, KG = K / 64, nkb = K / kGemmKb;
   const int T = a.T, Np = a.Np, S = a.stages;
-  const int tiles = a.tiles, splits = a.splits, nitems = tiles * splits;
+  const int tiles = a.tiles, splits = a.splits, ttiles = a.ttiles, nitems = tiles * ttiles * splits;
   const GemmLayout L = gemm_layout(Np, S, K);
   uint8_t* As = smem + L.a;
   uint8_t* Bs = smem + L.b;
@@ -165,10 +167,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_qgemm(const __grid_constant
     }
     return true;
   };
+  // item = (row tile, token tile, split), splits innermost and then the token
+  // tiles, so CTAs running side by side share a weight tile in L2
   auto item_geom = [&](int item, int& tile, int& sp, int& seg, int& row0, int& nrows, int& grow0, int& kb0,
-                       int& nit) {
-    tile = item / splits;
-    sp = item - tile * splits;
+                       int& nit, int& tt) {
+    sp = item % splits;
+    const int rest = item / splits;
+    tt = rest % ttiles;
+    tile = rest / ttiles;
     int stile0;
     seg = gemm_seg_of(a, tile, &stile0, &grow0);
     row0 = (tile - stile0) * kGemmRows;
@@ -182,8 +188,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_qgemm(const __grid_constant
     // scales are constants: the first item's may load before the dependency wait
     int g = 0;
     for (int item = blockIdx.x, j = 0; item < nitems && !*bad; item += gridDim.x, ++j) {
-      int tile, sp, seg, row0, nrows, grow0, kb0, nit;
-      item_geom(item, tile, sp, seg, row0, nrows, grow0, kb0, nit);
+      int tile, sp, seg, row0, nrows, grow0, kb0, nit, tt;
+      item_geom(item, tile, sp, seg, row0, nrows, grow0, kb0, nit, tt);
       const int w = j & 1;
       if (j >= 2 && !wait(&wempty[w], uint32_t((j >> 1) - 1) & 1u)) break;
       const uint32_t sb = uint32_t(nrows) * KG * 2;
@@ -196,7 +202,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_qgemm(const __grid_constant
         if (u >= 1 && !wait(&empty[s], uint32_t(u - 1) & 1u)) break;
         mbar_expect_tx(&lfull[s], uint32_t(kGemmCodeStage + gemm_b_bytes(Np)));
         tma_load_2d(Cs + s * kGemmCodeStage, &a.cmap[seg], (kb0 + it) * 8, row0, &lfull[s]);
-        tma_load_2d(Bs + s * gemm_b_bytes(Np), &a.xmap, (kb0 + it) * kGemmKb, 0, &lfull[s]);
+        tma_load_2d(Bs + s * gemm_b_bytes(Np), &a.xmap, (kb0 + it) * kGemmKb, tt * Np, &lfull[s]);
       }
     }
   } else if (warp < kGemmProducerWarps) {
@@ -204,8 +210,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_qgemm(const __grid_constant
     const int r = tid & (kGemmRows - 1), half = tid >> 7;
     int g = 0;
     for (int item = blockIdx.x, j = 0; item < nitems && !*bad; item += gridDim.x, ++j) {
-      int tile, sp, seg, row0, nrows, grow0, kb0, nit;
-      item_geom(item, tile, sp, seg, row0, nrows, grow0, kb0, nit);
+      int tile, sp, seg, row0, nrows, grow0, kb0, nit, tt;
+      item_geom(item, tile, sp, seg, row0, nrows, grow0, kb0, nit, tt);
       const int w = j & 1;
       if (!wait(&wfull[w], uint32_t(j >> 1) & 1u)) break;
       const bool rok = r < nrows;
@@ -251,8 +257,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_qgemm(const __grid_constant
     const uint32_t idesc = tc_idesc_bf16(kGemmRows, Np);
     int g = 0;
     for (int item = blockIdx.x, j = 0; item < nitems && !*bad; item += gridDim.x, ++j) {
-      int tile, sp, seg, row0, nrows, grow0, kb0, nit;
-      item_geom(item, tile, sp, seg, row0, nrows, grow0, kb0, nit);
+      int tile, sp, seg, row0, nrows, grow0, kb0, nit, tt;
+      item_geom(item, tile, sp, seg, row0, nrows, grow0, kb0, nit, tt);
       const int acc = j & 1;
       if (j >= 2 && !wait(&aempty[acc], uint32_t((j >> 1) - 1) & 1u)) break;
       tc_fence_after();
@@ -275,8 +281,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_qgemm(const __grid_constant
     const int e = tid - kGemmEpiWarp0 * 32;  // 0..127 = TMEM lane = tile row
     const uint32_t lane_base = uint32_t(32 * (warp & 3)) << 16;
     for (int item = blockIdx.x, j = 0; item < nitems && !*bad; item += gridDim.x, ++j) {
-      int tile, sp, seg, row0, nrows, grow0, kb0, nit;
-      item_geom(item, tile, sp, seg, row0, nrows, grow0, kb0, nit);
+      int tile, sp, seg, row0, nrows, grow0, kb0, nit, tt;
+      item_geom(item, tile, sp, seg, row0, nrows, grow0, kb0, nit, tt);
       const int acc = j & 1;
       if (!wait(&afull[acc], uint32_t(j >> 1) & 1u)) break;
       tc_fence_after();
@@ -284,14 +290,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_qgemm(const __grid_constant
       const bool rok = e < nrows;
       const int row = row0 + e, grow = grow0 + row;
       const bool splitk = splits > 1;
-      for (int c0 = 0; c0 < T; c0 += 8) {
+      const int tb = tt * Np, tn = min(Np, T - tb);
+      for (int c0 = 0; c0 < tn; c0 += 8) {
         float v[8];
         tc_ld8(tmem + lane_base + uint32_t(acc * Np + c0), v);
         if (!rok) continue;
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-          const int t = c0 + q;
-          if (t >= T) break;
+          if (c0 + q >= tn) break;
+          const int t = tb + c0 + q;
           if (splitk) {
             a.part[(size_t(sp) * T + t) * a.rows_total + grow] = v[q];
           } else {
@@ -374,7 +381,7 @@ void qgemm_plan(int tiles, int K, int* splits, int* kblocks) {
 size_t qgemm_workspace_bytes(const QGemmArgs& a) {
   const int tiles = gemm_tiles(a);
   int splits, kb;
-  qgemm_plan(tiles, a.K, &splits, &kb);
+  qgemm_plan(tiles * gemm_ttiles(a.T), a.K, &splits, &kb);
   const size_t part = splits > 1 ? size_t(splits) * a.T * gemm_rows(a) * 4 : 0;
   return kGemmCounterBytes + part;
 }
@@ -408,15 +415,23 @@ static PFN_cuTensorMapEncodeTiled_v12000 tmap_encode() {
   return fn;
 }
 
-// 2-D tensor map: inner extent `d0` (contiguous), `d1` rows `pitch` bytes
-// apart, boxes b0 x b1.
-static bool tmap_2d(CUtensorMap* m, CUtensorMapDataType ty, const void* base, uint64_t d0, uint64_t d1,
+bool tmap_2d(CUtensorMap* m, CUtensorMapDataType ty, const void* base, uint64_t d0, uint64_t d1,
                     uint64_t pitch, uint32_t b0, uint32_t b1, CUtensorMapSwizzle sw) {
   auto fn = tmap_encode();
   if (!fn) return false;
   const cuuint64_t dims[2] = {d0, d1}, strides[1] = {pitch};
   const cuuint32_t box[2] = {b0, b1}, estr[2] = {1, 1};
   return fn(m, ty, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool tmap_3d(CUtensorMap* m, CUtensorMapDataType ty, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+             uint64_t p1, uint64_t p2, uint32_t b0, uint32_t b1, uint32_t b2, CUtensorMapSwizzle sw) {
+  auto fn = tmap_encode();
+  if (!fn) return false;
+  const cuuint64_t dims[3] = {d0, d1, d2}, strides[2] = {p1, p2};
+  const cuuint32_t box[3] = {b0, b1, b2}, estr[3] = {1, 1, 1};
+  return fn(m, ty, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
             CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -435,7 +450,8 @@ cudaError_t launch_qgemm(QGemmArgs a, void* ws, size_t ws_bytes, bool zero_count
   const int tiles = gemm_tiles(a);
   if (tiles > kGemmMaxTiles) return cudaErrorInvalidValue;
   int splits, kb;
-  qgemm_plan(tiles, a.K, &splits, &kb);
+  a.ttiles = gemm_ttiles(a.T);
+  qgemm_plan(tiles * a.ttiles, a.K, &splits, &kb);
   a.tiles = tiles;
   a.splits = splits;
   a.kblocks = kb;
@@ -444,7 +460,7 @@ cudaError_t launch_qgemm(QGemmArgs a, void* ws, size_t ws_bytes, bool zero_count
   a.counters = reinterpret_cast<uint32_t*>(w);
   a.part = reinterpret_cast<float*>(w + kGemmCounterBytes);
   if (!a.err) a.err = a.counters + kGemmMaxTiles;
-  a.Np = gemm_np(a.T);
+  a.Np = gemm_np(a.T < kGemmTokTile ? a.T : kGemmTokTile);
   a.stages = 0;
   for (int S = 4; S >= 2 && !a.stages; --S)
     if (gemm_layout(a.Np, S, a.K).total <= kGemmSmemMax) a.stages = S;
@@ -460,7 +476,7 @@ cudaError_t launch_qgemm(QGemmArgs a, void* ws, size_t ws_bytes, bool zero_count
     cudaError_t e = cudaMemsetAsync(a.counters, 0, kGemmCounterBytes, st);
     if (e != cudaSuccess) return e;
   }
-  const int items = tiles * splits;
+  const int items = tiles * a.ttiles * splits;
   const int grid = items < 148 ? items : 148;
   cudaError_t e = launch_ex(k_qgemm, dim3(grid), dim3(kGemmThreads), gemm_layout(a.Np, a.stages, a.K).total, st,
                             pdl, a);

@@ -35,10 +35,27 @@ cudaError_t launch_tok_swiglu(const TokArgs& a, cudaStream_t st, bool pdl);
 
 // Q4 GEMM on the tensor cores (q35_gemm.cu)
 cudaError_t qgemm_init();
+// TMA descriptors: 2-D (inner extent d0 contiguous, d1 rows `pitch` bytes
+// apart) and 3-D (pitches p1, p2 of dims 1 and 2), boxes b0 x b1 (x b2)
+bool tmap_2d(CUtensorMap* m, CUtensorMapDataType ty, const void* base, uint64_t d0, uint64_t d1,
+             uint64_t pitch, uint32_t b0, uint32_t b1, CUtensorMapSwizzle sw);
+bool tmap_3d(CUtensorMap* m, CUtensorMapDataType ty, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
+             uint64_t p1, uint64_t p2, uint32_t b0, uint32_t b1, uint32_t b2, CUtensorMapSwizzle sw);
 size_t qgemm_workspace_bytes(int N, int K, int T);
 size_t qgemm_workspace_bytes(const QGemmArgs& a);
 cudaError_t launch_qgemm(QGemmArgs a, void* ws, size_t ws_bytes, bool zero_counters, cudaStream_t st,
                          bool pdl);
+
+// prompt chunks on the tensor cores (q35_prompt.cu)
+cudaError_t prompt_kernels_init();
+size_t prompt_attn_items_max(int tmax, uint32_t capacity);
+void prompt_attn_plan(PromptArgs& a);  // query blocks and key splits of the chunk
+cudaError_t launch_prompt_rope(uint32_t p0, int T, float* rope, cudaStream_t st, bool pdl);
+cudaError_t launch_prompt_conv(const PromptArgs& a, cudaStream_t st, bool pdl);
+cudaError_t launch_prompt_gdn_prep(const PromptArgs& a, cudaStream_t st, bool pdl);
+cudaError_t launch_prompt_recur(const PromptArgs& a, cudaStream_t st, bool pdl);
+cudaError_t launch_prompt_attn_prep(const PromptArgs& a, cudaStream_t st, bool pdl);
+cudaError_t launch_prompt_attn(PromptArgs a, cudaStream_t st, bool pdl);
 
 // prompt chunks (q35_prefill.cu)
 cudaError_t chunk_kernels_init();

@@ -312,6 +312,7 @@ cudaError_t ensure_kernels_init() {
   e = kernels_init();
   if (e == cudaSuccess) e = chunk_kernels_init();
   if (e == cudaSuccess) e = qgemm_init();
+  if (e == cudaSuccess) e = prompt_kernels_init();
   if (e == cudaSuccess && dev < 64) g_init_mask |= uint64_t(1) << dev;
   return e;
 }
@@ -349,6 +350,18 @@ struct q35_session {
   uint16_t *c_q = nullptr, *c_k = nullptr, *c_v = nullptr, *c_gated = nullptr, *c_act = nullptr;
   float* c_rope = nullptr;
   float* c_zs = nullptr;  // z * sigmoid(z) of the chunk's tokens [16][2048]
+  // prompts on the tensor cores (Q35_FLAG_TENSOR_PROMPT): chunks of up to
+  // prompt_chunk tokens; buffers allocated on first use
+  bool tensor_prompt = false;
+  int prompt_chunk = kPromptChunk;
+  uint8_t* pbuf = nullptr;
+  uint16_t *p_h = nullptr, *p_xn = nullptr, *p_raw = nullptr, *p_z = nullptr, *p_ab = nullptr, *p_conv = nullptr;
+  uint16_t *p_y = nullptr, *p_gated = nullptr, *p_q = nullptr, *p_k = nullptr, *p_v = nullptr, *p_gu = nullptr;
+  uint16_t *p_act = nullptr, *p_qn = nullptr;
+  float *p_zs = nullptr, *p_rope = nullptr, *p_kq = nullptr, *p_gb = nullptr, *p_vv = nullptr;
+  float *p_opart = nullptr, *p_oml = nullptr, *p_omax = nullptr;
+  uint8_t* p_gws = nullptr;
+  size_t p_gws_bytes = 0;
   uint32_t position = 0;
   bool has_pending = false;
   uint32_t pending = 0;
@@ -727,6 +740,182 @@ cudaError_t capture_chunk(q35_session* s, cudaGraphExec_t* out) {
   return e;
 }
 
+// Buffers of the tensor-core prompt route, sized for prompt_chunk tokens (the
+// attention partials for the session's capacity); allocated on first use.
+cudaError_t ensure_prompt_buffers(q35_session* s) {
+  if (s->pbuf) return cudaSuccess;
+  const size_t N = size_t(s->prompt_chunk);
+  const size_t items = prompt_attn_items_max(s->prompt_chunk, s->capacity);
+  auto ws = [&](std::initializer_list<int> rows, int K) {
+    QGemmArgs g = {};
+    for (int r : rows) g.seg[g.nseg++].rows = r;
+    g.K = K;
+    g.T = int(N);
+    return qgemm_workspace_bytes(g);
+  };
+  s->p_gws_bytes = 0;
+  for (size_t w : {ws({kGdnConv, 2048, 16, 16}, kHidden), ws({kHidden}, 2048), ws({kMlp, kMlp}, kHidden),
+                   ws({kHidden}, kMlp), ws({kQProj, 512, 512}, kHidden)})
+    s->p_gws_bytes = std::max(s->p_gws_bytes, w);
+  struct Part {
+    void** p;
+    size_t bytes;
+  } parts[] = {
+      {(void**)&s->p_h, N * kHidden * 2},          {(void**)&s->p_xn, N * kHidden * 2},
+      {(void**)&s->p_raw, N * kGdnConv * 2},       {(void**)&s->p_z, N * 2048 * 2},
+      {(void**)&s->p_ab, N * 32 * 2},              {(void**)&s->p_conv, N * kGdnConv * 2},
+      {(void**)&s->p_y, N * 2048 * 2},             {(void**)&s->p_gated, N * 2048 * 2},
+      {(void**)&s->p_q, N * kQProj * 2},           {(void**)&s->p_k, N * 512 * 2},
+      {(void**)&s->p_v, N * 512 * 2},              {(void**)&s->p_gu, 2 * N * kMlp * 2},
+      {(void**)&s->p_act, N * kMlp * 2},           {(void**)&s->p_qn, 8 * N * 256 * 2},
+      {(void**)&s->p_zs, N * 2048 * 4},            {(void**)&s->p_rope, N * 64 * 4},
+      {(void**)&s->p_kq, 16 * N * 256 * 4},        {(void**)&s->p_gb, 16 * N * 2 * 4},
+      {(void**)&s->p_vv, 16 * 8 * N * 16 * 4},     {(void**)&s->p_opart, items * 128 * 256 * 4},
+      {(void**)&s->p_oml, items * 128 * 2 * 4},    {(void**)&s->p_gws, s->p_gws_bytes},
+      {(void**)&s->p_omax, items * 128 * 4},
+  };
+  size_t total = 0;
+  for (auto& pt : parts) total += (pt.bytes + 255) & ~size_t(255);
+  cudaError_t e = cudaMalloc(&s->pbuf, total);
+  if (e == cudaSuccess) e = cudaMemset(s->pbuf, 0, total);
+  if (e != cudaSuccess) {
+    if (s->pbuf) cudaFree(s->pbuf);
+    s->pbuf = nullptr;
+    return e;
+  }
+  size_t off = 0;
+  for (auto& pt : parts) {
+    *pt.p = s->pbuf + off;
+    off += (pt.bytes + 255) & ~size_t(255);
+  }
+  return cudaSuccess;
+}
+
+// One prompt chunk on the tensor cores: tokens p0 .. p0 + T - 1 (seq on the
+// device) through all 24 layers without the head, in the order of the
+// reference's prefill layer body (model.rs:233-289): per layer the input norm,
+// the fused projections as one GEMM over the chunk, the GDN conv, preparation
+// and recurrence (or the attention preparation, flash attention and gate),
+// the output projection with the residual, then the MLP.
+cudaError_t enqueue_prompt_chunk(q35_session* s, uint32_t p0, int T) {
+  const ModelW& M = s->M;
+  cudaStream_t st = s->stream;
+  bool pdl = false;
+  cudaError_t e = cudaSuccess;
+#define Q35_P(x)                    \
+  do {                              \
+    e = (x);                        \
+    if (e != cudaSuccess) return e; \
+    pdl = true;                     \
+  } while (0)
+  auto gemm = [&](const uint16_t* x, int K, std::initializer_list<QGemmSeg> segs) {
+    QGemmArgs g = {};
+    int i = 0;
+    for (const QGemmSeg& sg : segs) g.seg[i++] = sg;
+    g.nseg = i;
+    g.x = x;
+    g.K = K;
+    g.T = T;
+    g.err = &s->ctl->err;
+    return launch_qgemm(g, s->p_gws, s->p_gws_bytes, false, st, pdl);
+  };
+  auto rms = [&](const uint16_t* gain, bool embed) {
+    TokArgs t = {};
+    t.n = T;
+    t.h_in = s->p_h;
+    t.gain = gain;
+    t.xn = s->p_xn;
+    if (embed) {
+      t.ew = M.embed.w;
+      t.es = M.embed.s;
+      t.eb = M.embed.b;
+      t.h_out = s->p_h;
+      t.seq = s->seq;
+      t.p0 = p0;
+      t.ctl = s->ctl;
+      t.rope = s->p_rope;
+    }
+    return launch_tok_rms(t, st, pdl);
+  };
+  PromptArgs pa = {};
+  pa.T = T;
+  pa.p0 = p0;
+  pa.tmax = s->prompt_chunk;
+  pa.ctl = s->ctl;
+  pa.raw = s->p_raw;
+  pa.conv = s->p_conv;
+  pa.ab = s->p_ab;
+  pa.z = s->p_z;
+  pa.zs = s->p_zs;
+  pa.kq = s->p_kq;
+  pa.gb = s->p_gb;
+  pa.vv = s->p_vv;
+  pa.y = s->p_y;
+  pa.q_raw = s->p_q;
+  pa.k_raw = s->p_k;
+  pa.v_raw = s->p_v;
+  pa.rope = s->p_rope;
+  pa.qn = s->p_qn;
+  pa.capacity = s->capacity;
+  pa.opart = s->p_opart;
+  pa.oml = s->p_oml;
+  pa.omax = s->p_omax;
+  pa.gated = s->p_gated;
+  prompt_attn_plan(pa);
+  int gi = 0, ai = 0;
+  for (int l = 0; l < kLayers; ++l) {
+    const LayerW& L = M.L[l];
+    Q35_P(rms(L.in_norm, l == 0));
+    if (!L.attn) {
+      Q35_P(gemm(s->p_xn, kHidden, {{L.qkv.w, L.qkv.s, L.qkv.b, s->p_raw, nullptr, kGdnConv, kGdnConv},
+                                    {L.z.w, L.z.s, L.z.b, s->p_z, nullptr, 2048, 2048},
+                                    {L.a.w, L.a.s, L.a.b, s->p_ab, nullptr, 16, 32},
+                                    {L.bproj.w, L.bproj.s, L.bproj.b, s->p_ab + 16, nullptr, 16, 32}}));
+      pa.hist = s->hist + size_t(gi) * 3 * kGdnConv;
+      pa.convw = L.conv;
+      pa.a_log = L.alog;
+      pa.dt_bias = L.dt;
+      pa.state = s->state + size_t(gi) * kGdnHeads * 128 * 128;
+      Q35_P(launch_prompt_conv(pa, st, pdl));
+      Q35_P(launch_prompt_gdn_prep(pa, st, pdl));
+      Q35_P(launch_prompt_recur(pa, st, pdl));
+      TokArgs g = {};
+      g.n = T;
+      g.y = s->p_y;
+      g.zs = s->p_zs;
+      g.gw = L.gnorm;
+      g.gated = s->p_gated;
+      Q35_P(launch_tok_normgate(g, st, pdl));
+      Q35_P(gemm(s->p_gated, 2048, {{L.out.w, L.out.s, L.out.b, s->p_h, s->p_h, kHidden, kHidden}}));
+      ++gi;
+    } else {
+      Q35_P(gemm(s->p_xn, kHidden, {{L.q.w, L.q.s, L.q.b, s->p_q, nullptr, kQProj, kQProj},
+                                    {L.k.w, L.k.s, L.k.b, s->p_k, nullptr, 512, 512},
+                                    {L.v.w, L.v.s, L.v.b, s->p_v, nullptr, 512, 512}}));
+      pa.q_gain = L.qnorm;
+      pa.k_gain = L.knorm;
+      pa.kcache = s->kcache(ai);
+      pa.vcache = s->vcache(ai);
+      Q35_P(launch_prompt_attn_prep(pa, st, pdl));
+      Q35_P(launch_prompt_attn(pa, st, pdl));
+      Q35_P(gemm(s->p_gated, 2048, {{L.o.w, L.o.s, L.o.b, s->p_h, s->p_h, kHidden, kHidden}}));
+      ++ai;
+    }
+    Q35_P(rms(L.post_norm, false));
+    Q35_P(gemm(s->p_xn, kHidden, {{L.gate.w, L.gate.s, L.gate.b, s->p_gu, nullptr, kMlp, kMlp},
+                                  {L.up.w, L.up.s, L.up.b, s->p_gu + size_t(T) * kMlp, nullptr, kMlp, kMlp}}));
+    TokArgs sw = {};
+    sw.n = T;
+    sw.g = s->p_gu;
+    sw.u = s->p_gu + size_t(T) * kMlp;
+    sw.act = s->p_act;
+    Q35_P(launch_tok_swiglu(sw, st, pdl));
+    Q35_P(gemm(s->p_act, kMlp, {{L.down.w, L.down.s, L.down.b, s->p_h, s->p_h, kHidden, kHidden}}));
+  }
+#undef Q35_P
+  return e;
+}
+
 cudaError_t capture(q35_session* s, int steps, bool head, cudaGraphExec_t* out) {
   cudaGraph_t g = nullptr;
   cudaError_t e = cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal);
@@ -754,6 +943,7 @@ void free_session(q35_session* s) {
   if (s->xtab) cudaFree(s->xtab);
   if (s->xbuf) cudaFree(s->xbuf);
   if (s->buf) cudaFree(s->buf);
+  if (s->pbuf) cudaFree(s->pbuf);
   if (s->M.arena) cudaFree(s->M.arena);
   if (s->stream) cudaStreamDestroy(s->stream);
   delete s;
@@ -810,6 +1000,28 @@ int run_steps(q35_session* s, size_t n, bool head, cudaError_t* ce) {
         return Q35_ECUDA;
       }
     }
+  }
+  return Q35_OK;
+}
+
+// The prompt (positions 0 .. n - 1, already in seq) through tensor-core
+// chunks of up to prompt_chunk tokens, enqueued directly (each chunk's shapes
+// are known here); the host waits every few chunks so a cancel is observed.
+int run_prompt_tensor(q35_session* s, size_t n, cudaError_t* ce) {
+  cudaError_t e = ensure_prompt_buffers(s);
+  uint32_t p0 = 0;
+  int queued = 0;
+  while (e == cudaSuccess && n > 0) {
+    if (s->cancelled.load(std::memory_order_relaxed)) return Q35_ECANCEL;
+    const int T = int(std::min(n, size_t(s->prompt_chunk)));
+    e = enqueue_prompt_chunk(s, p0, T);
+    p0 += uint32_t(T);
+    n -= size_t(T);
+    if (e == cudaSuccess && (++queued % 4 == 0 || n == 0)) e = cudaStreamSynchronize(s->stream);
+  }
+  if (e != cudaSuccess) {
+    *ce = e;
+    return Q35_ECUDA;
   }
   return Q35_OK;
 }
@@ -1548,6 +1760,8 @@ int q35_open(const char* model_dir, int device, const q35_opts* opts, q35_sessio
     if (opts->decode_batch) s->dbatch = int(opts->decode_batch);
     if (opts->prefill_batch) s->pbatch = int(opts->prefill_batch);
     if (opts->flags & Q35_FLAG_TOKEN_BY_TOKEN_PROMPT) s->chunked = false;
+    if (opts->flags & Q35_FLAG_TENSOR_PROMPT) s->tensor_prompt = true;
+    if (opts->prompt_chunk) s->prompt_chunk = int(opts->prompt_chunk);
   }
   auto fail = [&](int code, const std::string& m) {
     copy_err(errbuf, err_len, m);
@@ -1556,6 +1770,8 @@ int q35_open(const char* model_dir, int device, const q35_opts* opts, q35_sessio
   };
   if (s->capacity % kAttnChains != 0 || s->capacity < kAttnChains || s->capacity > (1u << 30))
     return fail(Q35_EINVAL, "capacity must be a positive multiple of 64");
+  if (s->prompt_chunk < 32 || s->prompt_chunk > kPromptChunk || s->prompt_chunk % 32 != 0)
+    return fail(Q35_EINVAL, "prompt_chunk must be a multiple of 32 in 32..2048");
   cudaError_t e = cudaSetDevice(device);
   if (e != cudaSuccess) return fail(Q35_ECUDA, std::string("cudaSetDevice: ") + cudaGetErrorString(e));
   e = ensure_kernels_init();
@@ -1674,7 +1890,9 @@ int q35_generate(q35_session* s, const uint32_t* prompt, size_t n_prompt, size_t
     if (e == cudaSuccess) e = cudaMemcpyAsync(s->ctl, &c, sizeof(Ctl), cudaMemcpyHostToDevice, s->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
     if (e != cudaSuccess) return device_failure(s, e, "reset");
-    int rc = run_steps(s, n_prompt - 1, false, &e);
+    // the tensor-core prompt route needs every K/V row on this device
+    int rc = s->tensor_prompt && s->xworld <= 1 ? run_prompt_tensor(s, n_prompt - 1, &e)
+                                                : run_steps(s, n_prompt - 1, false, &e);
     if (rc == Q35_ECANCEL) {
       cudaStreamSynchronize(s->stream);
       reset_state(s);
@@ -1888,14 +2106,14 @@ int q35_op_qmv_q4(const uint32_t* w, const uint16_t* scales, const uint16_t* bia
 }
 
 size_t q35_op_qgemm_workspace_bytes(uint32_t tokens, uint32_t n, uint32_t k) {
-  if (tokens == 0 || tokens > 256 || n == 0 || n > 524288 || k < 512 || k % 512 != 0 || k > 4096) return 0;
+  if (tokens == 0 || tokens > 4096 || n == 0 || n > 524288 || k < 512 || k % 512 != 0 || k > 4096) return 0;
   return qgemm_workspace_bytes(int(n), int(k), int(tokens));
 }
 
 int q35_op_qgemm_q4(const uint32_t* w, const uint16_t* scales, const uint16_t* biases, const uint16_t* x,
                     uint32_t tokens, uint32_t n, uint32_t k, const uint16_t* residual, uint16_t* y,
                     void* workspace, size_t workspace_bytes, void* stream) {
-  if (!w || !scales || !biases || !x || !y || !workspace || tokens < 1 || tokens > 256 || n < 1 ||
+  if (!w || !scales || !biases || !x || !y || !workspace || tokens < 1 || tokens > 4096 || n < 1 ||
       n > 524288 || k < 512 || k % 512 != 0 || k > 4096)
     return Q35_EINVAL;
   for (const void* p : {static_cast<const void*>(scales), static_cast<const void*>(biases)})
@@ -2011,6 +2229,136 @@ int q35_op_attn_decode(const uint16_t* q_raw, const uint16_t* k_raw, const uint1
   at.gated = gated;
   at.ctl = ctl;
   if (e == cudaSuccess) e = launch_attn(at, st, false);
+  return op_status(e);
+}
+
+// Scratch of the prompt-chunk ops for `tokens` rows (rounded up to 32) and
+// the attention partials of a cache of `capacity` positions, after a control
+// block.
+namespace {
+struct PromptOpWs {
+  Ctl* ctl;
+  uint16_t *conv, *y, *qn;
+  float *zs, *kq, *gb, *vv, *rope, *opart, *oml, *omax;
+  size_t total;
+};
+PromptOpWs prompt_op_ws(uint8_t* base, uint32_t tokens, uint32_t capacity) {
+  const size_t N = (size_t(tokens) + 31) / 32 * 32;
+  const size_t items = prompt_attn_items_max(int(N), capacity);
+  PromptOpWs w = {};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    uint8_t* p = base ? base + off : nullptr;
+    off += (bytes + 255) & ~size_t(255);
+    return p;
+  };
+  w.ctl = (Ctl*)take(ctl_bytes());
+  w.conv = (uint16_t*)take(N * kGdnConv * 2);
+  w.y = (uint16_t*)take(N * 2048 * 2);
+  w.qn = (uint16_t*)take(8 * N * 256 * 2);
+  w.zs = (float*)take(N * 2048 * 4);
+  w.kq = (float*)take(16 * N * 256 * 4);
+  w.gb = (float*)take(16 * N * 2 * 4);
+  w.vv = (float*)take(16 * 8 * N * 16 * 4);
+  w.rope = (float*)take(N * 64 * 4);
+  w.opart = (float*)take(items * 128 * 256 * 4);
+  w.oml = (float*)take(items * 128 * 2 * 4);
+  w.omax = (float*)take(items * 128 * 4);
+  w.total = off;
+  return w;
+}
+bool aligned16(std::initializer_list<const void*> ps) {
+  for (const void* p : ps)
+    if (reinterpret_cast<uintptr_t>(p) % 16 != 0) return false;
+  return true;
+}
+}  // namespace
+
+size_t q35_op_prompt_workspace_bytes(uint32_t tokens, uint32_t capacity) {
+  if (tokens == 0 || tokens > uint32_t(kPromptChunk) || capacity % kAttnChains != 0) return 0;
+  return prompt_op_ws(nullptr, tokens, capacity).total;
+}
+
+int q35_op_prompt_gdn(const uint16_t* raw_qkv, const uint16_t* z, const uint16_t* ab, uint16_t* history,
+                      const uint16_t* conv_w, const float* a_log, const uint16_t* dt_bias, float* state,
+                      const uint16_t* norm_w, uint32_t tokens, uint16_t* gated, void* workspace,
+                      size_t workspace_bytes, void* stream) {
+  if (!raw_qkv || !z || !ab || !history || !conv_w || !a_log || !dt_bias || !state || !norm_w || !gated ||
+      !workspace || tokens == 0 || tokens > uint32_t(kPromptChunk) ||
+      workspace_bytes < q35_op_prompt_workspace_bytes(tokens, 0))
+    return Q35_EINVAL;
+  if (!aligned16({raw_qkv, z, state, gated, workspace, norm_w})) return Q35_EINVAL;
+  if (ensure_kernels_init() != cudaSuccess) return Q35_ECUDA;
+  cudaStream_t st = (cudaStream_t)stream;
+  const PromptOpWs w = prompt_op_ws((uint8_t*)workspace, tokens, 0);
+  PromptArgs pa = {};
+  pa.T = int(tokens);
+  pa.tmax = int((tokens + 31) / 32 * 32);
+  pa.ctl = w.ctl;
+  pa.raw = raw_qkv;
+  pa.hist = history;
+  pa.convw = conv_w;
+  pa.conv = w.conv;
+  pa.ab = ab;
+  pa.z = z;
+  pa.zs = w.zs;
+  pa.a_log = a_log;
+  pa.dt_bias = dt_bias;
+  pa.kq = w.kq;
+  pa.gb = w.gb;
+  pa.vv = w.vv;
+  pa.state = state;
+  pa.y = w.y;
+  cudaError_t e = launch_ctl_position(w.ctl, 0, st);
+  if (e == cudaSuccess) e = launch_prompt_conv(pa, st, false);
+  if (e == cudaSuccess) e = launch_prompt_gdn_prep(pa, st, true);
+  if (e == cudaSuccess) e = launch_prompt_recur(pa, st, true);
+  TokArgs g = {};
+  g.n = int(tokens);
+  g.y = w.y;
+  g.zs = w.zs;
+  g.gw = norm_w;
+  g.gated = gated;
+  if (e == cudaSuccess) e = launch_tok_normgate(g, st, true);
+  return op_status(e);
+}
+
+int q35_op_prompt_attention(const uint16_t* q_raw, const uint16_t* k_raw, const uint16_t* v_raw,
+                            const uint16_t* q_gain, const uint16_t* k_gain, uint16_t* kcache, uint16_t* vcache,
+                            uint32_t capacity, uint32_t p0, uint32_t tokens, uint16_t* gated, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  if (!q_raw || !k_raw || !v_raw || !q_gain || !k_gain || !kcache || !vcache || !gated || !workspace ||
+      tokens == 0 || tokens > uint32_t(kPromptChunk) || capacity == 0 || capacity % kAttnChains != 0 ||
+      uint64_t(p0) + tokens > capacity || workspace_bytes < q35_op_prompt_workspace_bytes(tokens, capacity))
+    return Q35_EINVAL;
+  if (!aligned16({q_raw, k_raw, v_raw, q_gain, k_gain, kcache, vcache, gated, workspace})) return Q35_EINVAL;
+  if (ensure_kernels_init() != cudaSuccess) return Q35_ECUDA;
+  cudaStream_t st = (cudaStream_t)stream;
+  const PromptOpWs w = prompt_op_ws((uint8_t*)workspace, tokens, capacity);
+  PromptArgs pa = {};
+  pa.T = int(tokens);
+  pa.p0 = p0;
+  pa.tmax = int((tokens + 31) / 32 * 32);
+  pa.ctl = w.ctl;
+  pa.q_raw = q_raw;
+  pa.k_raw = k_raw;
+  pa.v_raw = v_raw;
+  pa.q_gain = q_gain;
+  pa.k_gain = k_gain;
+  pa.rope = w.rope;
+  pa.qn = w.qn;
+  pa.kcache = kcache;
+  pa.vcache = vcache;
+  pa.capacity = capacity;
+  pa.opart = w.opart;
+  pa.oml = w.oml;
+  pa.omax = w.omax;
+  pa.gated = gated;
+  prompt_attn_plan(pa);
+  cudaError_t e = launch_ctl_position(w.ctl, p0, st);
+  if (e == cudaSuccess) e = launch_prompt_rope(p0, int(tokens), w.rope, st, false);
+  if (e == cudaSuccess) e = launch_prompt_attn_prep(pa, st, true);
+  if (e == cudaSuccess) e = launch_prompt_attn(pa, st, true);
   return op_status(e);
 }
 

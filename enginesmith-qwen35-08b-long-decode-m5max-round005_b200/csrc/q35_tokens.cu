@@ -1,10 +1,11 @@
-// Per-token steps of the tensor-core batched-session route: the operations
-// between the GEMMs (q35_gemm.cu) for n sessions at once, token t = session t.
-// Each is the decode step's arithmetic for that operation (the same device
-// functions as the matvec prologues and epilogues), applied per token:
+// Per-token steps of the tensor-core routes: the operations between the GEMMs
+// (q35_gemm.cu) for n tokens at once, token t = session t of a batched step
+// or token t of a prompt chunk (q35_prompt.cu). Each is the decode step's
+// arithmetic for that operation (the same device functions as the matvec
+// prologues and epilogues), applied per token:
 //   k_tok_rms      input RMSNorm (linear_input_norm.metal) of h[t]; in the
-//                  first layer the session's token is embedded first
-//                  (linear.metal:11-24) and its position and RoPE row recorded
+//                  first layer the token is embedded first (linear.metal:11-24)
+//                  and its position and RoPE row recorded
 //   k_tok_conv     GDN causal conv + SiLU and history shift (gdn_input.metal:163-177)
 //   k_tok_normgate GDN gated RMS output (gdn.metal:238-254)
 //   k_tok_swiglu   SwiGLU (linear_norm.metal:95-103)
@@ -25,11 +26,23 @@ __global__ void __launch_bounds__(32) k_tok_rms(const __grid_constant__ TokArgs 
   const int t = blockIdx.x, lane = threadIdx.x;
   float v[8][4];
   if (a.ew) {
-    Ctl* c = a.ctls[t];
-    const uint32_t p = ld_cg_u32(&c->pos);
-    if (lane == 0) c->pos_step = p;
+    // batched sessions: session t's pending token at its position; prompt
+    // chunk: token t of the session at p0 + t (token 0 moves the position past
+    // the chunk; nothing in the chunk reads it)
+    Ctl* c = a.seq ? a.ctl : a.ctls[t];
+    uint32_t p;
+    if (a.seq) {
+      p = a.p0 + uint32_t(t);
+      if (t == 0 && lane == 0) {
+        c->pos_step = a.p0;
+        c->pos = a.p0 + uint32_t(a.n);
+      }
+    } else {
+      p = ld_cg_u32(&c->pos);
+      if (lane == 0) c->pos_step = p;
+    }
     rope_pair(p, lane, a.rope + 64 * t);
-    uint32_t token = ld_cg_u32(&a.seqs[t][p]);
+    uint32_t token = ld_cg_u32(a.seq ? &a.seq[p] : &a.seqs[t][p]);
     if (token >= uint32_t(kVocab)) {
       if (lane == 0) atomicCAS(&c->err, 0u, kErrToken);
       token = 0;

@@ -196,9 +196,10 @@ struct QGemmArgs {
   QGemmSeg seg[kGemmSegs];
   int nseg;
   const uint16_t* x;     // [T][K] bf16 activations
-  int K, T, Np;          // Np: T rounded up to a multiple of 16 (the MMA N)
+  int K, T, Np;          // Np: min(T, 256) rounded up to a multiple of 16 (the MMA N)
   int kblocks;           // 64-wide K blocks per split
   int tiles, splits;     // 128-row tiles over all segments, K splits
+  int ttiles;            // token tiles of up to 256 (Np tokens each, the last one partial)
   int rows_total;        // sum of the segments' rows (partials row index)
   int stages;            // shared-memory ring depth
   float* part;           // split partials [splits][T][rows_total] f32 (splits > 1)
@@ -237,6 +238,10 @@ struct TokArgs {
   const uint16_t* g;           // swiglu: [n][3584] gate
   const uint16_t* u;           // [n][3584] up
   uint16_t* act;               // [n][3584]
+  // prompt chunks (one session, n tokens): token t at position p0 + t of seq
+  const uint32_t* seq;
+  uint32_t p0;
+  Ctl* ctl;
 };
 
 // Sequence-split exchange buffers of one rank: records [slot][source][cta]
@@ -291,6 +296,58 @@ struct HeadBatchArgs {
   const uint16_t* gain;
   int n;                  // sessions, <= kMaxSessions
   HeadOut out[kMaxSessions];
+};
+
+// Prompt chunks on the tensor cores (q35_prompt.cu): T consecutive prompt
+// tokens of one session at positions p0 .. p0 + T - 1, with the projections as
+// tcgen05 GEMMs over the chunk, the conv and GDN preparation per token, the
+// recurrence walking the chunk, and causal flash attention on the tensor cores
+// over 128-row blocks (4 query heads x 32 tokens) against 64-key tiles.
+constexpr int kPromptChunk = 2048;        // default and largest tokens per chunk
+constexpr int kPromptRecSub = 32;         // recurrence staging block (tokens)
+constexpr uint32_t kErrPromptWait = 9;    // a bounded wait of the prompt kernels expired
+struct PromptArgs {
+  int T;                  // tokens in this chunk
+  uint32_t p0;            // position of its first token
+  int tmax;               // rows of the per-token buffers (a multiple of 32)
+  Ctl* ctl;
+  // GDN layer
+  const uint16_t* raw;    // [T][6144] q | k | v projections
+  uint16_t* hist;         // the layer's conv history [3][6144]
+  const uint16_t* convw;  // [6144][4]
+  uint16_t* conv;         // [T][6144] conv outputs
+  const uint16_t* ab;     // [T][32] a (0..15) | b (16..31) projections
+  const uint16_t* z;      // [T][2048]
+  float* zs;              // [T][2048] z * sigmoid(z)
+  const float* a_log;     // [16]
+  const uint16_t* dt_bias;// [16]
+  float* kq;              // [16][tmax][256] normalised k (0..127) | q (128..255)
+  float* gb;              // [16][tmax][2] decay gate, beta
+  float* vv;              // [16][8][tmax][16] values by head and 16-row block
+  float* state;           // the layer's state [16][128][128]
+  uint16_t* y;            // [T][2048] recurrence outputs
+  // attention layer
+  const uint16_t* q_raw;  // [T][4096] query | gate per head
+  const uint16_t* k_raw;  // [T][512]
+  const uint16_t* v_raw;  // [T][512]
+  const uint16_t* q_gain;
+  const uint16_t* k_gain;
+  const float* rope;      // [T][64] RoPE rows of the chunk's positions
+  uint16_t* qn;           // [8][tmax][256] normalised, rotated queries
+  uint16_t* kcache;       // the layer's caches, chain layout of `capacity` positions
+  uint16_t* vcache;
+  uint32_t capacity;
+  int nqb, nsplit;        // 32-token query blocks; key splits per block
+  float* opart;           // [2][nqb][nsplit][128][256] unnormalised outputs
+  float* oml;             // [2][nqb][nsplit][128][2] (max score, sum of weights)
+  float* omax;            // [2][nqb][nsplit][128] each split's row maxima (first pass)
+  uint16_t* gated;        // [T][2048]
+  // TMA descriptors: queries as [8 heads][T][256] (boxes 4 heads x 32 tokens
+  // x 64 dims), keys and values as [128 = 2 heads x 64 chains][capacity / 64
+  // slots][256] (boxes 64 chains x 1 slot x 64 dims = 64 consecutive positions)
+  alignas(64) CUtensorMap qmap;
+  alignas(64) CUtensorMap kmap;
+  alignas(64) CUtensorMap vmap;
 };
 
 }  // namespace q35

@@ -27,6 +27,7 @@ BATCH_TENSOR_CORES = 1
 
 OK, EINVAL, ECUDA, ECANCEL, EIO, ENOMEM, ETIMEOUT, ENCCL = 0, -1, -2, -3, -4, -5, -6, -7
 FLAG_TOKEN_BY_TOKEN_PROMPT = 1
+FLAG_TENSOR_PROMPT = 2
 
 
 class Q35Error(RuntimeError):
@@ -37,7 +38,7 @@ class Q35Error(RuntimeError):
 
 class _Opts(ctypes.Structure):
     _fields_ = [("capacity", c_uint32), ("decode_batch", c_uint32),
-                ("prefill_batch", c_uint32), ("flags", c_uint32)]
+                ("prefill_batch", c_uint32), ("flags", c_uint32), ("prompt_chunk", c_uint32)]
 
 
 def _load() -> ctypes.CDLL:
@@ -65,6 +66,9 @@ def _load() -> ctypes.CDLL:
         "q35_op_gdn_step": (c_int, [P] * 17),
         "q35_op_attn_workspace_bytes": (c_size_t, []),
         "q35_op_attn_decode": (c_int, [P, P, P, P, P, P, P, c_uint32, c_uint32, P, P, P]),
+        "q35_op_prompt_workspace_bytes": (c_size_t, [c_uint32, c_uint32]),
+        "q35_op_prompt_gdn": (c_int, [P, P, P, P, P, P, P, P, P, c_uint32, P, P, c_size_t, P]),
+        "q35_op_prompt_attention": (c_int, [P, P, P, P, P, P, P, c_uint32, c_uint32, c_uint32, P, P, c_size_t, P]),
         "q35_op_head_workspace_bytes": (c_size_t, []),
         "q35_op_head_argmax": (c_int, [P, P, P, P, P, P, P, P, P, P]),
         "q35_op_greedy": (c_int, [P, P, P, P, P]),
@@ -121,8 +125,12 @@ class Model:
 
     @classmethod
     def load(cls, path: str, device: int = 0, capacity: int = 0, decode_batch: int = 0,
-             prefill_batch: int = 0, token_by_token_prompt: bool = False) -> "Model":
-        opts = _Opts(capacity, decode_batch, prefill_batch, FLAG_TOKEN_BY_TOKEN_PROMPT if token_by_token_prompt else 0)
+             prefill_batch: int = 0, token_by_token_prompt: bool = False, tensor_prompt: bool = False,
+             prompt_chunk: int = 0) -> "Model":
+        """tensor_prompt: prompts on the tensor cores (Q35_FLAG_TENSOR_PROMPT) in
+        chunks of prompt_chunk tokens (0 = 2048)."""
+        flags = (FLAG_TOKEN_BY_TOKEN_PROMPT if token_by_token_prompt else 0) | (FLAG_TENSOR_PROMPT if tensor_prompt else 0)
+        opts = _Opts(capacity, decode_batch, prefill_batch, flags, prompt_chunk)
         h = c_void_p()
         err = ctypes.create_string_buffer(2048)
         rc = lib().q35_open(path.encode(), device, ctypes.byref(opts), ctypes.byref(h), err, len(err))
@@ -312,7 +320,7 @@ def qmv_q4(w, scales, biases, x, residual=None, out=None):
 
 def qgemm_q4(w, scales, biases, x, residual=None, out=None, ws=None):
     """y[T][N] = bf16(x W^T) (+ residual) on the tensor cores (tcgen05), W the
-    Q4 matrix dequantised as bf16(s q + b); x [T][K] bf16 with T <= 256."""
+    Q4 matrix dequantised as bf16(s q + b); x [T][K] bf16 with T <= 4096."""
     import torch
     n, kw = w.shape
     t = x.shape[0]
@@ -366,6 +374,42 @@ def attn_decode(q_raw, k_raw, v_raw, q_gain, k_gain, kcache, vcache, capacity: i
     _op(lib().q35_op_attn_decode(_ptr(q_raw), _ptr(k_raw), _ptr(v_raw), _ptr(q_gain), _ptr(k_gain),
                                  _ptr(kcache), _ptr(vcache), capacity, pos, _ptr(gated), _ptr(ws),
                                  _stream()), "attn_decode")
+    return gated
+
+
+def _prompt_ws(tokens: int, capacity: int, device):
+    import torch
+    n = lib().q35_op_prompt_workspace_bytes(tokens, capacity)
+    if n == 0:
+        raise Q35Error(EINVAL, "prompt op: invalid shape")
+    return torch.empty(n, dtype=torch.uint8, device=device), n
+
+
+def prompt_gdn(raw_qkv, z, ab, history, conv_w, a_log, dt_bias, state, norm_w):
+    """One GDN layer's prompt-chunk steps over T tokens (q35_op_prompt_gdn):
+    raw_qkv [T][6144], z [T][2048], ab [T][32]; history and state updated in
+    place; returns gated [T][2048] (bf16 bits)."""
+    import torch
+    t = raw_qkv.shape[0]
+    gated = torch.empty((t, 2048), dtype=torch.uint16, device=raw_qkv.device)
+    ws, n = _prompt_ws(t, 0, raw_qkv.device)
+    _op(lib().q35_op_prompt_gdn(_ptr(raw_qkv), _ptr(z), _ptr(ab), _ptr(history), _ptr(conv_w), _ptr(a_log),
+                                _ptr(dt_bias), _ptr(state), _ptr(norm_w), t, _ptr(gated), _ptr(ws), n,
+                                _stream()), "prompt_gdn")
+    return gated
+
+
+def prompt_attention(q_raw, k_raw, v_raw, q_gain, k_gain, kcache, vcache, capacity: int, p0: int):
+    """One attention layer's prompt-chunk steps for tokens at p0 .. p0 + T - 1
+    (q35_op_prompt_attention): appends their K/V to the chain-layout caches and
+    returns gated [T][2048] (bf16 bits)."""
+    import torch
+    t = q_raw.shape[0]
+    gated = torch.empty((t, 2048), dtype=torch.uint16, device=q_raw.device)
+    ws, n = _prompt_ws(t, capacity, q_raw.device)
+    _op(lib().q35_op_prompt_attention(_ptr(q_raw), _ptr(k_raw), _ptr(v_raw), _ptr(q_gain), _ptr(k_gain),
+                                      _ptr(kcache), _ptr(vcache), capacity, p0, t, _ptr(gated), _ptr(ws), n,
+                                      _stream()), "prompt_attention")
     return gated
 
 

@@ -45,12 +45,23 @@ typedef struct q35_opts {
   uint32_t decode_batch; /* decode steps per CUDA-graph launch (0 -> 8) */
   uint32_t prefill_batch;/* prompt steps per CUDA-graph launch (0 -> 16) */
   uint32_t flags;        /* Q35_FLAG_* bits, 0 by default */
+  uint32_t prompt_chunk; /* tokens per tensor-core prompt chunk (0 -> 2048); a
+                            multiple of 32 in 32..2048 */
 } q35_opts;
 
 /* Consume prompts one token per step (the decode step without the head)
  * instead of in chunks of 16 tokens. Both give bit-identical state; the
  * chunked route reads each weight once per chunk. */
 #define Q35_FLAG_TOKEN_BY_TOKEN_PROMPT 1u
+
+/* Consume prompts on the tensor cores, as the reference's prefill does
+ * (model.rs:100-110, :189-198): chunks of prompt_chunk tokens with every
+ * projection a tcgen05 GEMM over the chunk and causal flash attention on the
+ * tensor cores (bf16 attention weights). The state after the prompt then
+ * differs from the decode route's within the GEMM/flash-attention tolerance
+ * rather than bit for bit; decoding is unchanged. Ignored under a sequence
+ * split (those prompts take the decode route). */
+#define Q35_FLAG_TENSOR_PROMPT 2u
 
 /* ---------------------------------------------------------------------- */
 /* Session API                                                             */
@@ -189,12 +200,42 @@ int q35_op_qmv_q4(const uint32_t* w, const uint16_t* scales, const uint16_t* bia
  * in the place of the reference's quantised matmul qmm_q4_nax,
  * kernels/linear_nax.metal:1096-1139): y[t][n] = bf16(sum_k W[n][k] x[t][k]),
  * or bf16(residual[t][n] + bf16(.)) when residual is non-NULL (may alias y),
- * for t < tokens (1..256), with W dequantised as bf16(s*q + b). x [tokens][k]
+ * for t < tokens (1..4096), with W dequantised as bf16(s*q + b). x [tokens][k]
  * bf16, y [tokens][n]; n up to 524,288; k a multiple of 512 up to 4096; w, x, scales, biases and
  * workspace 16-byte aligned. The float32 accumulation runs in
  * the tensor core's order, so results match a float32 reference within
  * tolerance rather than the matvec bit for bit. workspace: at least
  * q35_op_qgemm_workspace_bytes(tokens, n, k) bytes (0 = invalid shape). */
+/* Prompt chunks on the tensor cores, one layer's steps over `tokens` (1..2048)
+ * consecutive prompt tokens, for tests and other hosts. Workspace: at least
+ * q35_op_prompt_workspace_bytes(tokens, capacity) bytes (capacity 0 for the
+ * GDN op; 0 = invalid shape), 16-byte aligned.
+ *
+ * q35_op_prompt_gdn: the GDN conv, preparation, recurrence and gated norm of
+ * the prefill (gdn.metal gdn_conv :33-52, gdn_history :56-71, gdn_prepare
+ * :75-114, the multi-row gdn_recur loop :176-228, gdn_norm_gate :230-255):
+ * raw_qkv [T][6144], z [T][2048], ab [T][32] (a | b projections), history
+ * [3][6144] and state [16][128][128] f32 updated in place, conv_w [6144][4],
+ * a_log [16] f32, dt_bias [16], norm_w [128]; gated [T][2048]. Each token's
+ * arithmetic is the decode step's, so results equal T decode steps bit for bit.
+ *
+ * q35_op_prompt_attention: per-head q/k norm, partial RoPE and the K/V append
+ * of positions p0 .. p0 + T - 1 (attention.metal:72-131), causal flash
+ * attention on the tensor cores (attention_prefill.metal:1830-2258) and the
+ * output gate (attention.metal:140-150): q_raw [T][4096] (query | gate per
+ * head), k_raw and v_raw [T][512], caches in the chain layout of `capacity`
+ * positions (as q35_op_attn_decode), gated [T][2048]. Attention weights are
+ * bf16 and sums run in the tensor core's order (tolerance, not bit-exact). */
+size_t q35_op_prompt_workspace_bytes(uint32_t tokens, uint32_t capacity);
+int q35_op_prompt_gdn(const uint16_t* raw_qkv, const uint16_t* z, const uint16_t* ab, uint16_t* history,
+                      const uint16_t* conv_w, const float* a_log, const uint16_t* dt_bias, float* state,
+                      const uint16_t* norm_w, uint32_t tokens, uint16_t* gated, void* workspace,
+                      size_t workspace_bytes, void* stream);
+int q35_op_prompt_attention(const uint16_t* q_raw, const uint16_t* k_raw, const uint16_t* v_raw,
+                            const uint16_t* q_gain, const uint16_t* k_gain, uint16_t* kcache, uint16_t* vcache,
+                            uint32_t capacity, uint32_t p0, uint32_t tokens, uint16_t* gated, void* workspace,
+                            size_t workspace_bytes, void* stream);
+
 size_t q35_op_qgemm_workspace_bytes(uint32_t tokens, uint32_t n, uint32_t k);
 int q35_op_qgemm_q4(const uint32_t* w, const uint16_t* scales, const uint16_t* biases, const uint16_t* x,
                     uint32_t tokens, uint32_t n, uint32_t k, const uint16_t* residual, uint16_t* y,

@@ -430,6 +430,44 @@ void attn_f32(const uint16_t* query, const uint16_t* kcache, const uint16_t* vca
   }
 }
 
+/* The tensor-core prompt route's attention (the engine's k_pr_attn, in the
+ * place of the reference's prefill flash attention, attention_prefill.metal
+ * :1830-2258, rather than its decode kernels): raw scores s_i = q . k_i with
+ * the products summed in double and rounded to f32 once (the value the tensor
+ * core's f32 sum approximates), the row maximum m, weights
+ * p_i = bf16(2^(f32(f32(s_i - m) * log2(e) / 16))) (the 1/16 score scale
+ * folded in), out = sum p_i v_i / sum p_i with both sums in double. The
+ * engine splits long key ranges into parts whose weights are relative to the
+ * part's maximum and rescales them when merging; that rounding is not
+ * restated. */
+void attn_f32_flash(const uint16_t* query, const uint16_t* kcache, const uint16_t* vcache, uint32_t len,
+                    uint32_t capacity, float* out /*[8*256]*/) {
+  pool().run(8, [&](long h0, long h1) {
+    for (long qh = h0; qh < h1; ++qh) {
+      const int kh = int(qh) / 4;
+      const uint16_t* kc = kcache + size_t(kh) * capacity * 256;
+      const uint16_t* vc = vcache + size_t(kh) * capacity * 256;
+      std::vector<float> sc(len);
+      float m = -INFINITY;
+      for (uint32_t i = 0; i < len; ++i) {
+        double acc = 0.0;
+        for (int d = 0; d < 256; ++d) acc += double(bf2f(query[qh * 256 + d])) * double(bf2f(kc[size_t(i) * 256 + d]));
+        sc[i] = float(acc);
+        m = std::max(m, sc[i]);
+      }
+      double l = 0.0;
+      std::vector<double> o(256, 0.0);
+      for (uint32_t i = 0; i < len; ++i) {
+        const float arg = (sc[i] - m) * 0.0901684400555602f;
+        const double p = double(bfr(std::exp2(arg)));
+        l += p;
+        for (int d = 0; d < 256; ++d) o[d] += p * double(bf2f(vc[size_t(i) * 256 + d]));
+      }
+      for (int d = 0; d < 256; ++d) out[qh * 256 + d] = float(o[d] / l);
+    }
+  });
+}
+
 /* Sequence split over `world` ranks (the engine's config-5 path; the
  * reference runs on one device, so this has no reference counterpart). Rank
  * r holds positions r, r + world, ...; on each rank 64 chains walk its keys
@@ -911,6 +949,21 @@ void orc_attn_prepare(const uint16_t* q_raw, const uint16_t* k_raw, const uint16
   }
 }
 
+void orc_attn_flash_f32(const uint16_t* query, const uint16_t* kcache, const uint16_t* vcache,
+                        uint32_t len, uint32_t capacity, float* o) {
+  attn_f32_flash(query, kcache, vcache, len, capacity, o);
+}
+
+/* attention.metal:140-150 on the prompt route's attention output */
+void orc_attn_flash_gate(const uint16_t* query, const uint16_t* kcache, const uint16_t* vcache, uint32_t len,
+                         uint32_t capacity, const uint16_t* q_raw, uint16_t* gated) {
+  std::vector<float> o(2048);
+  attn_f32_flash(query, kcache, vcache, len, capacity, o.data());
+  for (int head = 0; head < 8; ++head)
+    for (int d = 0; d < 256; ++d)
+      gated[head * 256 + d] = f2bf(bfr(o[head * 256 + d]) * gate_sigmoid_bf(bf2f(q_raw[head * 512 + 256 + d])));
+}
+
 void orc_attn_decode_f32(const uint16_t* query, const uint16_t* kcache, const uint16_t* vcache,
                          uint32_t len, uint32_t capacity, float* o) {
   attn_f32(query, kcache, vcache, len, capacity, o);
@@ -1021,6 +1074,7 @@ struct orc_session {
   uint16_t lse = 0;
   int split_world = 1;  // attention as a sequence split over this many ranks
   bool gemm = false;     // projections and head with the tensor-core route's numerics
+  bool flash = false;    // attention as the tensor-core prompt route's (attn_f32_flash)
 };
 
 extern "C" {
@@ -1158,8 +1212,26 @@ void orc_session_import(orc_session* s, uint32_t pos, uint32_t cap_src,
   }
 }
 
+/* The session's state at its position: kv [6][K|V][2][pos][256] u16, state
+ * [18][16][128][128] f32, hist [18][3][6144] u16 (import_state's layout). */
+void orc_session_export(const orc_session* s, uint16_t* kv, float* state, uint16_t* hist) {
+  const size_t pos = s->position;
+  for (int a = 0; a < 6; ++a)
+    for (int kvi = 0; kvi < 2; ++kvi)
+      for (int h = 0; h < 2; ++h) {
+        const auto& src = kvi == 0 ? s->kc[a] : s->vc[a];
+        std::memcpy(kv + ((size_t(a) * 2 + kvi) * 2 + h) * pos * 256, &src[size_t(h) * s->capacity * 256],
+                    pos * 512);
+      }
+  for (int g = 0; g < 18; ++g) {
+    std::memcpy(state + size_t(g) * s->state[g].size(), s->state[g].data(), s->state[g].size() * 4);
+    std::memcpy(hist + size_t(g) * s->hist[g].size(), s->hist[g].data(), s->hist[g].size() * 2);
+  }
+}
+
 void orc_session_set_split(orc_session* s, int world) { s->split_world = world > 1 ? world : 1; }
 void orc_session_set_gemm(orc_session* s, int on) { s->gemm = on != 0; }
+void orc_session_set_flash(orc_session* s, int on) { s->flash = on != 0; }
 
 /* model.rs:228-307 with rows=1 */
 uint32_t orc_session_step(orc_session* S, uint32_t token, int want_head) {
@@ -1194,8 +1266,13 @@ uint32_t orc_session_step(orc_session* S, uint32_t token, int want_head) {
       orc_qmv_q4(L.v.w, L.v.s, L.v.b, u.data(), nullptr, 512, 1024, v.data());
       orc_attn_prepare(q.data(), k.data(), v.data(), L.qnorm, L.knorm, S->position, S->capacity,
                        query.data(), S->kc[ai].data(), S->vc[ai].data());
-      orc_attn_decode_gate_split(query.data(), S->kc[ai].data(), S->vc[ai].data(), S->position + 1,
-                                 S->capacity, S->split_world, q.data(), gated.data());
+      if (S->flash) {
+        orc_attn_flash_gate(query.data(), S->kc[ai].data(), S->vc[ai].data(), S->position + 1, S->capacity,
+                            q.data(), gated.data());
+      } else {
+        orc_attn_decode_gate_split(query.data(), S->kc[ai].data(), S->vc[ai].data(), S->position + 1,
+                                   S->capacity, S->split_world, q.data(), gated.data());
+      }
       orc_qmv_q4(L.o.w, L.o.s, L.o.b, gated.data(), h.data(), 1024, 2048, h.data());
       ++ai;
     }

@@ -90,6 +90,12 @@ void orc_attn_decode_gate_split(const uint16_t* query, const uint16_t* kcache, c
                                 uint32_t len, uint32_t capacity, int world, const uint16_t* q_raw,
                                 uint16_t* gated);
 /* f32 attention output before rounding (for tolerance tests), o[8*256] */
+/* the tensor-core prompt route's attention (f32, before the gate) */
+void orc_attn_flash_f32(const uint16_t* query, const uint16_t* kcache, const uint16_t* vcache,
+                        uint32_t len, uint32_t capacity, float* o);
+/* the prompt route's attention followed by the output gate */
+void orc_attn_flash_gate(const uint16_t* query, const uint16_t* kcache, const uint16_t* vcache, uint32_t len,
+                         uint32_t capacity, const uint16_t* q_raw, uint16_t* gated);
 void orc_attn_decode_f32(const uint16_t* query, const uint16_t* kcache, const uint16_t* vcache,
                          uint32_t len, uint32_t capacity, float* o);
 
@@ -119,6 +125,8 @@ uint32_t orc_session_position(const orc_session* s);
 /* projections and head of later steps with the engine's tensor-core route's
  * numerics (weights dequantised to bf16, dot products exact then rounded) */
 void orc_session_set_gemm(orc_session* s, int on);
+/* attention of later steps as the tensor-core prompt route's (attn_f32_flash) */
+void orc_session_set_flash(orc_session* s, int on);
 /* attention of later steps as the engine's sequence split over `world` ranks */
 void orc_session_set_split(orc_session* s, int world);
 uint32_t orc_session_step(orc_session* s, uint32_t token, int want_head);
@@ -130,6 +138,7 @@ void orc_session_final_hidden(const orc_session* s, uint16_t* out);
  * (li=0..5) K and V caches [2][cap_src][256] of which `pos` positions are
  * copied; per GDN layer (gi=0..17) state f32[16*128*128] and history
  * bf16[3*6144]. */
+void orc_session_export(const orc_session* s, uint16_t* kv, float* state, uint16_t* hist);
 void orc_session_import(orc_session* s, uint32_t pos, uint32_t cap_src,
                         const uint16_t* const* kcaches, const uint16_t* const* vcaches,
                         const float* const* states, const uint16_t* const* histories);

@@ -69,10 +69,14 @@ def lib() -> ctypes.CDLL:
             "orc_session_step": (c_uint32, [P, c_uint32, c_int]),
             "orc_session_set_split": (None, [P, c_int]),
             "orc_session_set_gemm": (None, [P, c_int]),
+            "orc_session_set_flash": (None, [P, c_int]),
             "orc_session_logits": (None, [P, P]),
             "orc_session_lse": (c_uint16, [P]),
             "orc_session_final_hidden": (None, [P, P]),
             "orc_session_import": (None, [P, c_uint32, c_uint32, P, P, P, P]),
+            "orc_session_export": (None, [P, P, P, P]),
+            "orc_attn_flash_f32": (None, [P, P, P, c_uint32, c_uint32, P]),
+            "orc_attn_flash_gate": (None, [P, P, P, c_uint32, c_uint32, P, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -187,6 +191,20 @@ def attn_decode_f32(query, kcache, vcache, length: int, capacity: int) -> np.nda
     return o
 
 
+def attn_flash_f32(query, kcache, vcache, length: int, capacity: int) -> np.ndarray:
+    """The tensor-core prompt route's attention output (f32 [8*256])."""
+    out = np.zeros(2048, np.float32)
+    lib().orc_attn_flash_f32(_p(query), _p(kcache), _p(vcache), length, capacity, _p(out))
+    return out
+
+
+def attn_flash_gate(query, kcache, vcache, length: int, capacity: int, q_raw) -> np.ndarray:
+    """The prompt route's attention with the output gate (bf16 [8*256])."""
+    gated = np.zeros(2048, np.uint16)
+    lib().orc_attn_flash_gate(_p(query), _p(kcache), _p(vcache), length, capacity, _p(q_raw), _p(gated))
+    return gated
+
+
 def head(w, s, b, x):
     """Returns (token, logits u16[N], lse u16)."""
     n, kw = w.shape
@@ -255,6 +273,11 @@ class OracleSession:
         route's numerics (bf16-dequantised weights, exact dot products)."""
         lib().orc_session_set_gemm(self.s, 1 if on else 0)
 
+    def set_flash(self, on: bool) -> None:
+        """Attention of later steps with the engine's tensor-core prompt
+        route's numerics (flash attention: bf16 weights, exact sums)."""
+        lib().orc_session_set_flash(self.s, 1 if on else 0)
+
     def step(self, token: int, head: bool = True) -> int:
         return int(lib().orc_session_step(self.s, token, 1 if head else 0))
 
@@ -277,6 +300,15 @@ class OracleSession:
             tok = self.step(tok, head=True)
             out.append(tok)
         return out
+
+    def export_state(self):
+        """(kv [6,2,2,pos,256] u16, state [18,16,128,128] f32, hist [18,3,6144] u16)."""
+        pos = self.position
+        kv = np.zeros((6, 2, 2, pos, 256), np.uint16)
+        st = np.zeros((18, 16, 128, 128), np.float32)
+        hi = np.zeros((18, 3, 6144), np.uint16)
+        lib().orc_session_export(self.s, _p(kv), _p(st), _p(hi))
+        return kv, st, hi
 
     def import_state(self, pos: int, kv: np.ndarray, state: np.ndarray, hist: np.ndarray):
         """kv [6,2,2,pos,256] u16 (layer, K|V, head, pos, d); state [18,...]; hist [18,...]."""

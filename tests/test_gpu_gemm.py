@@ -5,8 +5,8 @@ accumulated in float32 (TF32 off), output rounded to bf16. The tensor core's
 accumulation order differs from the reference's, so the bar is the north
 star's tolerance (norm-wise relative error <= 1e-2), and per output at most
 one bf16 ulp plus 1e-4 of the largest output (float32 accumulation order). Shapes cover every projection of the model,
-the vocabulary head, token counts 1..256 (the MMA's N: padding and the
-256-column limit), K splits (K = 2048, 3584) and partial row tiles."""
+the vocabulary head, token counts 1..256 (the MMA's N: padding) and above
+(token tiles of 256, the last one partial, as a prompt chunk uses), K splits (K = 2048, 3584) and partial row tiles."""
 import numpy as np
 import pytest
 
@@ -39,6 +39,7 @@ def reference(w, scales, biases, x):
 @pytest.mark.parametrize("t,n,k", [
     (1, 3584, 1024), (8, 8224, 1024), (16, 1024, 3584), (17, 1024, 2048), (64, 7168, 1024),
     (100, 5120, 1024), (256, 4096, 1024), (48, 248320, 1024), (200, 1000, 2048),
+    (300, 8224, 1024), (2048, 1024, 3584), (1000, 3584, 1024),
 ])
 def test_qgemm_matches_f32(cuda, t, n, k):
     import torch
@@ -74,6 +75,6 @@ def test_qgemm_rejects_bad_arguments(cuda):
     w, s, b, x = make(256, 1024, 4, 1)
     W, S, B, X = w.cuda(), s.cuda().view(torch.uint16), b.cuda().view(torch.uint16), x.cuda().view(torch.uint16)
     with pytest.raises(q35.Q35Error):
-        q35.qgemm_q4(W, S, B, torch.zeros((257, 1024), dtype=torch.uint16, device="cuda"))
+        q35.qgemm_q4(W, S, B, torch.zeros((4097, 1024), dtype=torch.uint16, device="cuda"))
     with pytest.raises(q35.Q35Error):
         q35.qgemm_q4(W[:, :4], S, B, X)  # k = 32, not a multiple of 512

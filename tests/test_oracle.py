@@ -161,6 +161,35 @@ def test_attention_matches_float64(O, length):
     assert np.linalg.norm(o - ref) <= tol * np.linalg.norm(ref)
 
 
+def attention_flash_f64(query, kc, vc, length):
+    """The tensor-core prompt route's attention: exact scores rounded to f32,
+    weights bf16(2^((s - max) log2(e) / 16)), exact weighted sums."""
+    q = I.bf2f(query).astype(np.float64).reshape(8, 256)
+    out = np.zeros((8, 256))
+    for h in range(8):
+        k = I.bf2f(kc[h // 4, :length]).astype(np.float64)
+        v = I.bf2f(vc[h // 4, :length]).astype(np.float64)
+        s = (k @ q[h]).astype(np.float32)
+        arg = ((s - s.max()).astype(np.float32) * np.float32(0.0901684400555602)).astype(np.float32)
+        p = I.bf2f(I.f2bf(np.exp2(arg.astype(np.float64)).astype(np.float32))).astype(np.float64)
+        out[h] = p @ v / p.sum()
+    return out.reshape(-1)
+
+
+@pytest.mark.parametrize("length", [1, 31, 64, 1025])
+def test_flash_attention_restatement(O, length):
+    """The oracle's restatement of the prompt route's attention follows its
+    formula, and stays within the bf16 weights' error of exact attention."""
+    c = I.config3(2, length)
+    kc, vc = c["kc"].copy(), c["vc"].copy()
+    q = O.attn_prepare(c["q_raw"], c["k_raw"], c["v_raw"], c["q_gain"], c["k_gain"], c["pos"], c["cap"], kc, vc)
+    o = O.attn_flash_f32(q, kc, vc, length, c["cap"]).astype(np.float64)
+    ref = attention_flash_f64(q, kc, vc, length)
+    assert np.linalg.norm(o - ref) <= 1e-6 * np.linalg.norm(ref)
+    exact = attention_f64(q, kc, vc, length)
+    assert np.linalg.norm(o - exact) <= 1e-2 * np.linalg.norm(exact)
+
+
 def test_rope_and_qk_norm(O):
     """Per-head RMSNorm, then RoPE on dims < 64 with pairs (i, i+32), theta 1e7."""
     c = I.config3(2, 100)
