@@ -8,6 +8,11 @@ step is one decode token of one session; every GPU runs its own session
 (independent sessions, weak scaling). Inputs are synthetic and seeded.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--context C] [--impl q35|reference] [--split]
+                  [--prompt-route tensor|decode]
+
+The prompt is consumed on the tensor cores by default (as the reference's
+prefill: GEMM projections and flash attention over 2048-token chunks); its
+wall time is reported in the "prefill" field, beside the decode metric.
 
 --split (N > 1, config 5's second part): ONE session whose attention K/V is
 sequence-split over the N GPUs (rank r keeps positions p % N == r, the ranks
@@ -227,6 +232,9 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--split", action="store_true")
+    ap.add_argument("--prompt-route", default="tensor", choices=["tensor", "decode"],
+                    help="prompt on the tensor cores (the reference's GEMM/flash-attention prefill) "
+                         "or through the decode step's kernels")
     ap.add_argument("--batch-members", type=int, default=32,
                     help="also time this many sessions decoded together on the tensor cores (0: skip)")
     args = ap.parse_args()
@@ -249,8 +257,9 @@ def main():
                                 device_id=torch.device("cuda", local))
     model_dir = ensure_model(world, rank)
     cap = ((args.context + args.warmup + 2 * args.steps + args.cpu_tokens + 64) // 32) * 32
-    m = q35.Model.load(model_dir, local, capacity=cap)
     split = args.split and world > 1
+    tensor_prompt = args.prompt_route == "tensor" and not split  # a split session takes the decode route
+    m = q35.Model.load(model_dir, local, capacity=cap, tensor_prompt=tensor_prompt)
     if split:
         q35.split_connect_dist(m)  # one stream over all ranks: the same prompt everywhere
     streams = 1 if split else world
@@ -346,6 +355,10 @@ def main():
                        "parallelism": f"sequence split x{world}" if split else f"sessions x{world}",
                        "l2": "inputs larger than L2 (each step streams ~%.2f GB)" % (step_bytes / 1e9),
                        "prefill_s": round(prefill_s, 2)},
+            "prefill": {"route": ("tensor cores: tcgen05 GEMM projections, causal flash attention, "
+                                  "2048-token chunks" if tensor_prompt else "decode step kernels, 16-token chunks"),
+                        "tokens": args.context, "seconds": prefill_s, "tok_s": args.context / prefill_s,
+                        "note": "wall clock of q35_generate(prompt, 1) (the prompt, then its last token decoded)"},
             "gpu_launches": args.steps * (18 * 3 + 6 * 4 + 24 * 2 + 1),
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 4},
             "roofline": {"bound": "hbm", "kernel": "k_attn (split GQA decode attention)",

@@ -179,14 +179,18 @@ def test_tensor_prompt_chunk_sizes_agree(models):
     p = prompt(5, 1100)
     outs = []
     for m in models:
-        toks = m.generate(p, 4, True)
+        # the state after the prompt and its last token (both runs see the same
+        # inputs; a generated continuation could differ at a near-tie)
+        toks = m.generate(p, 1, True)
         outs.append((toks, f32(m.last_logits()[0]), m.dump_state()))
     (ta, la, (ka, sa, ha)), (tb, lb, (kb, sb, hb)) = outs
+    assert not np.isnan(sa).any() and not np.isnan(f32(ka)).any()
     ek, es, el = rel(f32(ka), f32(kb)), rel(sa, sb), rel(la, lb)
     print(f"chunks 2048 vs 64 at 1100 tokens: kv {ek:.4f} state {es:.4f} logits {el:.4f}")
-    # the chunk size changes the GEMMs' K-split plan and the attention's key
-    # splits (summation orders), which this model amplifies like the oracle
-    # comparison above (measured K/V 7.9 %)
+    # 2048-token chunks run the GEMMs over token tiles, with another K-split
+    # plan (summation order), which this model amplifies like the oracle
+    # comparison above (measured: K/V 1.4 % after the first attention layer,
+    # 7.8 % at the last; GDN state up to 10.5 %)
     assert ek <= 0.15 and es <= 0.25 and el <= 0.25, (ek, es, el)
     assert ta[0] == tb[0] or float(la.max() - la[tb[0]]) <= 5e-2 * float(np.abs(la).max())
 
