@@ -94,6 +94,51 @@ Q35_DEV float gdn_row_step(float (&s)[32], const float* kk, const float* qq, flo
   return out;
 }
 
+// gdn_row_step with 8 lanes per value row, in pieces: lane octant r8 owns
+// keys 16 r8 .. 16 r8 + 15, i.e. partials 4 (r8 & 1) .. 4 (r8 & 1) + 3 of lane
+// quarter r8 / 2. Each lane sums its four partials as that quarter's half of
+// the tree ((p0 + p1) + (p2 + p3)), shuffle-xor 1 joins the halves, and xor 2
+// and 4 take the quarters' xor 1 and 2: the same additions in the same
+// association (a + b = b + a exactly), so memory (gdn_decay_dot8 reduced by
+// gdn_reduce8), delta = (v - memory) * beta, and out (gdn_update_dot8
+// reduced) equal gdn_row_step's results bit for bit.
+Q35_DEV float gdn_decay_dot8(float (&s)[16], const float* kk, float gt) {  // S *= g; this lane's part of S k
+  float part[4];
+#pragma unroll
+  for (int pb = 0; pb < 4; ++pb) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int e = pb * 4 + i;
+      s[e] = __fmul_rn(s[e], gt);
+      acc = __fadd_rn(acc, __fmul_rn(s[e], kk[e]));
+    }
+    part[pb] = acc;
+  }
+  return __fadd_rn(__fadd_rn(part[0], part[1]), __fadd_rn(part[2], part[3]));
+}
+Q35_DEV float gdn_update_dot8(float (&s)[16], const float* kk, const float* qq, float delta) {  // S += k delta; part of S q
+  float part[4];
+#pragma unroll
+  for (int pb = 0; pb < 4; ++pb) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int e = pb * 4 + i;
+      s[e] = __fadd_rn(s[e], __fmul_rn(kk[e], delta));
+      acc = __fadd_rn(acc, __fmul_rn(s[e], qq[e]));
+    }
+    part[pb] = acc;
+  }
+  return __fadd_rn(__fadd_rn(part[0], part[1]), __fadd_rn(part[2], part[3]));
+}
+// the row reduction: shuffle-xor 1, 2, 4
+Q35_DEV float gdn_reduce8(float x) {
+#pragma unroll
+  for (int m = 1; m <= 4; m <<= 1) x = __fadd_rn(x, __shfl_xor_sync(0xffffffffu, x, m));
+  return x;
+}
+
 // attention.metal:55-70 / the RoPE table: cos/sin of position * inv_freq for
 // the 32 rotary pairs, evaluated in double from the f32 angle.
 Q35_DEV void rope_pair(uint32_t position, int pair, float* cs) {

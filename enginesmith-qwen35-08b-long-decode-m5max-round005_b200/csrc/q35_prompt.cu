@@ -40,25 +40,34 @@ namespace q35 {
 // GDN layer
 // ---------------------------------------------------------------------------
 
-// grid (6144 / 256, ceil(T / 64)): channel c for 64 consecutive tokens; the
-// window starts with the three raw rows before the block (the history for the
-// chunk's first tokens).
+// grid (6144 / 512, ceil(T / 16)): thread = channel pair (2c, 2c + 1) for 16
+// consecutive tokens; the 19 raw rows it needs (the three before the block
+// from the history at the chunk's start) are loaded first as 32-bit pairs.
+constexpr int kPrConvTokens = 16;
 __global__ void __launch_bounds__(256) k_pr_conv(const __grid_constant__ PromptArgs a) {
   pdl_wait();
   pdl_launch();
+  constexpr int P = kGdnConv / 2;  // channel pairs per row
   const int c = blockIdx.x * 256 + threadIdx.x;
-  const int t0 = blockIdx.y * 64, t1 = min(a.T, t0 + 64);
-  auto x = [&](int t) -> uint16_t {
-    return t >= 0 ? a.raw[size_t(t) * kGdnConv + c] : a.hist[(3 + t) * kGdnConv + c];
-  };
-  uint16_t w0 = x(t0 - 3), w1 = x(t0 - 2), w2 = x(t0 - 1);
-  const uint16_t w4[4] = {a.convw[4 * c], a.convw[4 * c + 1], a.convw[4 * c + 2], a.convw[4 * c + 3]};
-  for (int t = t0; t < t1; ++t) {
-    const uint16_t r = a.raw[size_t(t) * kGdnConv + c];
-    a.conv[size_t(t) * kGdnConv + c] = gdn_conv_value(w0, w1, w2, r, w4);
-    w0 = w1;
-    w1 = w2;
-    w2 = r;
+  const int t0 = blockIdx.y * kPrConvTokens, t1 = min(a.T, t0 + kPrConvTokens);
+  const uint32_t* raw = reinterpret_cast<const uint32_t*>(a.raw);
+  const uint32_t* hist = reinterpret_cast<const uint32_t*>(a.hist);
+  uint32_t r[kPrConvTokens + 3];
+#pragma unroll
+  for (int i = 0; i < kPrConvTokens + 3; ++i) {
+    const int t = t0 - 3 + i;
+    r[i] = t < 0 ? hist[(3 + t) * P + c] : t < t1 ? raw[size_t(t) * P + c] : 0u;
+  }
+  const uint16_t wa[4] = {a.convw[8 * c], a.convw[8 * c + 1], a.convw[8 * c + 2], a.convw[8 * c + 3]};
+  const uint16_t wb[4] = {a.convw[8 * c + 4], a.convw[8 * c + 5], a.convw[8 * c + 6], a.convw[8 * c + 7]};
+  uint32_t* conv = reinterpret_cast<uint32_t*>(a.conv);
+#pragma unroll
+  for (int i = 0; i < kPrConvTokens; ++i) {
+    if (t0 + i >= t1) break;
+    const uint16_t lo = gdn_conv_value(uint16_t(r[i]), uint16_t(r[i + 1]), uint16_t(r[i + 2]), uint16_t(r[i + 3]), wa);
+    const uint16_t hi = gdn_conv_value(uint16_t(r[i] >> 16), uint16_t(r[i + 1] >> 16), uint16_t(r[i + 2] >> 16),
+                                       uint16_t(r[i + 3] >> 16), wb);
+    conv[size_t(t0 + i) * P + c] = uint32_t(lo) | (uint32_t(hi) << 16);
   }
 }
 
@@ -98,10 +107,11 @@ __global__ void __launch_bounds__(512) k_pr_gdn_prep(const __grid_constant__ Pro
   }
 }
 
-// Recurrence: grid (8 row blocks, 16 heads) x 64 threads as the decode step's
-// k_gdn_recur (4 lanes per value row, 32 state values each), walking the
-// chunk's tokens in order. Thread 0 streams blocks of kPromptRecSub tokens'
-// k|q rows, gates and values through a ring of kPrRecStages stages.
+// Recurrence: grid (8 row blocks, 16 heads) x 128 threads, 8 lanes per value
+// row with 16 state values each (gdn_decay_dot8 / gdn_update_dot8: the decode
+// step's sums in its order, half the work per lane), walking the chunk's tokens in
+// order. Thread 0 streams blocks of kPromptRecSub tokens' k|q rows, gates and
+// values through a ring of kPrRecStages stages.
 constexpr int kPrRecStages = 3;
 struct PrRecStage {
   float kq[kPromptRecSub][256];
@@ -110,13 +120,13 @@ struct PrRecStage {
 };
 constexpr size_t kPrRecSmem = sizeof(PrRecStage) * kPrRecStages;
 
-__global__ void __launch_bounds__(64) k_pr_recur(const __grid_constant__ PromptArgs a) {
+__global__ void __launch_bounds__(128) k_pr_recur(const __grid_constant__ PromptArgs a) {
   extern __shared__ __align__(128) uint8_t dsm[];
   PrRecStage* stg = reinterpret_cast<PrRecStage*>(dsm);
   __shared__ __align__(8) uint64_t full[kPrRecStages];
   const int tid = threadIdx.x, rb = blockIdx.x, h = blockIdx.y;
   const int T = a.T, nsub = (T + kPromptRecSub - 1) / kPromptRecSub;
-  const int row = tid >> 2, r = tid & 3, vrow = rb * 16 + row;
+  const int row = tid >> 3, r = tid & 7, vrow = rb * 16 + row;
   if (tid == 0) {
     for (int s = 0; s < kPrRecStages; ++s) mbar_init(&full[s], 1);
     fence_mbar_init();
@@ -135,10 +145,10 @@ __global__ void __launch_bounds__(64) k_pr_recur(const __grid_constant__ PromptA
   };
   if (tid == 0)
     for (int b = 0; b < kPrRecStages && b < nsub; ++b) issue(b);
-  float* gstate = a.state + (size_t(h) * 128 + vrow) * 128 + r * 32;
-  float s[32];
+  float* gstate = a.state + (size_t(h) * 128 + vrow) * 128 + r * 16;
+  float s[16];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
+  for (int i = 0; i < 4; ++i) {
     const float4 v = reinterpret_cast<const float4*>(gstate)[i];
     s[4 * i] = v.x;
     s[4 * i + 1] = v.y;
@@ -157,8 +167,9 @@ __global__ void __launch_bounds__(64) k_pr_recur(const __grid_constant__ PromptA
     const int n = min(kPromptRecSub, T - b * kPromptRecSub);
     uint16_t* y = a.y + size_t(b) * kPromptRecSub * 2048 + h * 128 + vrow;
     for (int i = 0; i < n; ++i) {
-      const float out = gdn_row_step(s, &S.kq[i][r * 32], &S.kq[i][128 + r * 32], S.gb[i][0], S.gb[i][1],
-                                     S.vv[i][row]);
+      const float memory = gdn_reduce8(gdn_decay_dot8(s, &S.kq[i][r * 16], S.gb[i][0]));
+      const float delta = __fmul_rn(__fsub_rn(S.vv[i][row], memory), S.gb[i][1]);
+      const float out = gdn_reduce8(gdn_update_dot8(s, &S.kq[i][r * 16], &S.kq[i][128 + r * 16], delta));
       if (r == 0) y[size_t(i) * 2048] = f2bf(out);
     }
     __syncthreads();  // stage b is free again
@@ -166,7 +177,7 @@ __global__ void __launch_bounds__(64) k_pr_recur(const __grid_constant__ PromptA
   }
   if (!ok) return;
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
+  for (int i = 0; i < 4; ++i)
     reinterpret_cast<float4*>(gstate)[i] = make_float4(s[4 * i], s[4 * i + 1], s[4 * i + 2], s[4 * i + 3]);
 }
 
@@ -224,6 +235,15 @@ constexpr size_t kPaSmem = 1024 + kPaQBytes + kPaStages * kPaTileBytes + 2 * kPa
 // exp(x / 16) = 2^(x log2(e) / 16): the 1/sqrt(256) score scale folded in
 constexpr float kPaExp2Scale = 0.0901684400555602f;
 
+// 2^x by the PTX ex2.approx.ftz.f32 instruction (relative error below 2^-22;
+// results below 2^-126 flush to zero): the attention weights are rounded to
+// bf16 right after, so this matches an exact 2^x but for rare roundings.
+Q35_DEV float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 Q35_DEV void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
@@ -253,8 +273,12 @@ __global__ void __launch_bounds__(256, 1) k_pr_attn(const __grid_constant__ Prom
   volatile int* bad = reinterpret_cast<volatile int*>(tslot + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int item = blockIdx.x;
-  const int sp = item % a.nsplit, pair = item / a.nsplit, qb = pair % a.nqb, kvh = pair / a.nqb;
+  // CTAs in launch order walk the query blocks innermost, so the CTAs resident
+  // together read the same key range (served from L2); partials are indexed
+  // by (KV head, query block, split)
+  const int qb = blockIdx.x % a.nqb, rest = blockIdx.x / a.nqb;
+  const int sp = rest % a.nsplit, kvh = rest / a.nsplit;
+  const int pair = kvh * a.nqb + qb, item = pair * a.nsplit + sp;
   const int qlast = min(a.T, qb * 32 + 32) - 1;
   const int ntile = int((a.p0 + uint32_t(qlast)) / 64u) + 1;  // key tiles the block reaches
   const int tb = int(int64_t(ntile) * sp / a.nsplit), te = int(int64_t(ntile) * (sp + 1) / a.nsplit);
@@ -400,29 +424,47 @@ __global__ void __launch_bounds__(256, 1) k_pr_attn(const __grid_constant__ Prom
     };
     bool ok = true;
     if (PASS == 0) {
+      float mp[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mp[i] = -INFINITY;
       for (int j = 0; j < n && ok; ++j) {
         if (!(ok = load_s())) break;
         const int64_t k0 = int64_t(tb + j) * 64;
+        if (k0 + 63 <= rowpos) {
 #pragma unroll
-        for (int c = 0; c < 64; ++c)
-          if (k0 + c <= rowpos) m = fmaxf(m, sv[c]);
+          for (int c = 0; c < 64; ++c) mp[c & 7] = fmaxf(mp[c & 7], sv[c]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 64; ++c)
+            if (k0 + c <= rowpos) mp[c & 7] = fmaxf(mp[c & 7], sv[c]);
+        }
       }
+      m = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
       if (ok) a.omax[size_t(item) * 128 + e] = m;  // -inf for an empty split
     } else {
       const float* om = a.omax + size_t(pair) * a.nsplit * 128 + e;
       for (int s2 = 0; s2 < a.nsplit; ++s2) m = fmaxf(m, __ldcg(om + size_t(s2) * 128));
     }
+    float lp[8];  // partial sums of the bf16 weights
+#pragma unroll
+    for (int i = 0; i < 8; ++i) lp[i] = 0.0f;
     for (int j = 0; j < n && ok && PASS == 1; ++j) {
       if (!(ok = load_s())) break;
       const int64_t k0 = int64_t(tb + j) * 64;
+      const bool diag = k0 + 63 > rowpos;  // only tiles reaching past the row's position are masked
       uint32_t pk[32];
 #pragma unroll
       for (int c = 0; c < 64; c += 2) {
-        const float p0 = k0 + c <= rowpos ? bfr(exp2f(__fmul_rn(__fsub_rn(sv[c], m), kPaExp2Scale))) : 0.0f;
-        const float p1 =
-            k0 + c + 1 <= rowpos ? bfr(exp2f(__fmul_rn(__fsub_rn(sv[c + 1], m), kPaExp2Scale))) : 0.0f;
-        l = __fadd_rn(__fadd_rn(l, p0), p1);
-        pk[c >> 1] = pack_bf2(p0, p1);
+        float x0 = ex2_approx(__fmul_rn(__fsub_rn(sv[c], m), kPaExp2Scale));
+        float x1 = ex2_approx(__fmul_rn(__fsub_rn(sv[c + 1], m), kPaExp2Scale));
+        if (diag) {
+          if (k0 + c > rowpos) x0 = 0.0f;
+          if (k0 + c + 1 > rowpos) x1 = 0.0f;
+        }
+        const __nv_bfloat162 p2 = __floats2bfloat162_rn(x0, x1);
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(&p2);
+        pk[c >> 1] = w;
+        lp[(c >> 1) & 7] = __fadd_rn(lp[(c >> 1) & 7], __fadd_rn(bf_lo(w), bf_hi(w)));
       }
       if (j >= 2 && !(ok = wait(&pfree[j & 1], uint32_t((j >> 1) - 1) & 1u))) break;
       uint8_t* P = Ps + (j & 1) * kPaPBytes;
@@ -438,6 +480,8 @@ __global__ void __launch_bounds__(256, 1) k_pr_attn(const __grid_constant__ Prom
       oml[e * 2] = -INFINITY;  // an empty split: no weight in the combine
       oml[e * 2 + 1] = 0.0f;
     } else if (ok && wait(ofull, 0)) {
+      l = __fadd_rn(__fadd_rn(__fadd_rn(lp[0], lp[1]), __fadd_rn(lp[2], lp[3])),
+                    __fadd_rn(__fadd_rn(lp[4], lp[5]), __fadd_rn(lp[6], lp[7])));
       tc_fence_after();
       float* orow = opart + size_t(e) * 256;
       for (int c0 = 0; c0 < 256; c0 += 32) {
@@ -528,13 +572,14 @@ cudaError_t launch_prompt_rope(uint32_t p0, int T, float* rope, cudaStream_t st,
   return launch_ex(k_pr_rope, dim3(T), dim3(32), 0, st, pdl, p0, rope);
 }
 cudaError_t launch_prompt_conv(const PromptArgs& a, cudaStream_t st, bool pdl) {
-  return launch_ex(k_pr_conv, dim3(kGdnConv / 256, (a.T + 63) / 64), dim3(256), 0, st, pdl, a);
+  return launch_ex(k_pr_conv, dim3(kGdnConv / 512, (a.T + kPrConvTokens - 1) / kPrConvTokens), dim3(256), 0, st,
+                   pdl, a);
 }
 cudaError_t launch_prompt_gdn_prep(const PromptArgs& a, cudaStream_t st, bool pdl) {
   return launch_ex(k_pr_gdn_prep, dim3(a.T), dim3(512), 0, st, pdl, a);
 }
 cudaError_t launch_prompt_recur(const PromptArgs& a, cudaStream_t st, bool pdl) {
-  return launch_ex(k_pr_recur, dim3(8, kGdnHeads), dim3(64), kPrRecSmem, st, pdl, a);
+  return launch_ex(k_pr_recur, dim3(8, kGdnHeads), dim3(128), kPrRecSmem, st, pdl, a);
 }
 cudaError_t launch_prompt_attn_prep(const PromptArgs& a, cudaStream_t st, bool pdl) {
   return launch_ex(k_pr_attn_prep, dim3(a.T), dim3(320), 0, st, pdl, a);

@@ -399,14 +399,19 @@ def prompt_gdn(raw_qkv, z, ab, history, conv_w, a_log, dt_bias, state, norm_w):
     return gated
 
 
-def prompt_attention(q_raw, k_raw, v_raw, q_gain, k_gain, kcache, vcache, capacity: int, p0: int):
+def prompt_attention(q_raw, k_raw, v_raw, q_gain, k_gain, kcache, vcache, capacity: int, p0: int, ws=None,
+                     out=None):
     """One attention layer's prompt-chunk steps for tokens at p0 .. p0 + T - 1
     (q35_op_prompt_attention): appends their K/V to the chain-layout caches and
-    returns gated [T][2048] (bf16 bits)."""
+    returns gated [T][2048] (bf16 bits). ws: a workspace of
+    q35_op_prompt_workspace_bytes(T, capacity) bytes (allocated if None)."""
     import torch
     t = q_raw.shape[0]
-    gated = torch.empty((t, 2048), dtype=torch.uint16, device=q_raw.device)
-    ws, n = _prompt_ws(t, capacity, q_raw.device)
+    gated = out if out is not None else torch.empty((t, 2048), dtype=torch.uint16, device=q_raw.device)
+    if ws is None:
+        ws, n = _prompt_ws(t, capacity, q_raw.device)
+    else:
+        n = ws.numel() * ws.element_size()
     _op(lib().q35_op_prompt_attention(_ptr(q_raw), _ptr(k_raw), _ptr(v_raw), _ptr(q_gain), _ptr(k_gain),
                                       _ptr(kcache), _ptr(vcache), capacity, p0, t, _ptr(gated), _ptr(ws), n,
                                       _stream()), "prompt_attention")

@@ -2,6 +2,10 @@
 
   python -m q35.opbench --op qmv|gdn|attn|head|qgemm [--len N] [--iters K] [--copies R]
                         [--tokens T --rows N --k K]   (qgemm: the tensor-core Q4 GEMM)
+  python -m q35.opbench --op pattn --len P0 --tokens T  (prompt-chunk flash attention of T
+                        tokens at positions P0.., tensor FLOP/s of its two GEMMs)
+  python -m q35.opbench --op prefill --len N            (an N-token prompt through the session
+                        API on the tensor cores: wall-clock tok/s)
 
 Each call works on a fresh copy of its big operands (weights, recurrent
 state, or K/V cache), rotating over enough copies that the working set is
@@ -30,7 +34,7 @@ def main():
     import inputs as I
 
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", choices=["qmv", "gdn", "attn", "head", "qgemm"], required=True)
+    ap.add_argument("--op", choices=["qmv", "gdn", "attn", "head", "qgemm", "pattn", "prefill"], required=True)
     ap.add_argument("--tokens", type=int, default=64)
     ap.add_argument("--rows", type=int, default=7168)
     ap.add_argument("--k", type=int, default=1024)
@@ -47,6 +51,23 @@ def main():
             a = a.view(np.int32)
         return torch.from_numpy(a).to(dev)
 
+    if args.op == "prefill":
+        import time
+        d = os.environ.get("Q35_SYNTH_DIR", "/tmp/q35_synth_3")
+        if not os.path.exists(os.path.join(d, "model.safetensors")):
+            q35.write_synthetic_model(d, 3)
+        m = q35.Model.load(d, 0, capacity=((args.len + 2048 + 63) // 64) * 64, tensor_prompt=True)
+        rng = np.random.default_rng(1)
+        m.generate([int(v) for v in rng.integers(0, q35.VOCAB, 2048)], 1, True)  # warm-up
+        prompt = [int(v) for v in rng.integers(0, q35.VOCAB, args.len)]
+        t0 = time.perf_counter()
+        m.generate(prompt, 1, True)
+        dt = time.perf_counter() - t0
+        m.close()
+        print(json.dumps({"op": "prefill", "len": args.len, "seconds": dt, "tok_s": args.len / dt,
+                          "note": "wall clock of generate(prompt, 1): the prompt on the tensor cores, then "
+                                  "its last token decoded"}))
+        return
     if args.op == "qmv":
         w, s, b, x = I.config1(0)
         copies = args.copies or 256
@@ -105,6 +126,31 @@ def main():
 
         def call(i):
             q35.qgemm_q4(W[i % copies], S, B, X, out=Y, ws=wsb)
+    elif args.op == "pattn":
+        p0, t = args.len, args.tokens
+        cap = ((p0 + t + 63) // 64) * 64
+        r = I.Rng(7, 5)
+        kc = np.zeros((2, cap, 256), np.uint16)
+        vc = np.zeros((2, cap, 256), np.uint16)
+        if p0:
+            kc[:, :p0] = I.f2bf(r.normal(2 * p0 * 256)).reshape(2, p0, 256)
+            vc[:, :p0] = I.f2bf(r.normal(2 * p0 * 256)).reshape(2, p0, 256)
+        copies = args.copies or 1
+        KC = [T(I.to_chain_major(kc)) for _ in range(copies)]
+        VC = [T(I.to_chain_major(vc)) for _ in range(copies)]
+        ins = {"q_raw": T(I.f2bf(r.normal(t * 4096)).reshape(t, 4096)),
+               "k_raw": T(I.f2bf(r.normal(t * 512)).reshape(t, 512)),
+               "v_raw": T(I.f2bf(r.normal(t * 512)).reshape(t, 512)),
+               "q_gain": T(I.f2bf(1.0 + r.normal(256, 0.02))), "k_gain": T(I.f2bf(1.0 + r.normal(256, 0.02)))}
+        ws, _ = q35._prompt_ws(t, cap, dev)
+        gated = torch.empty((t, 2048), dtype=torch.int16, device=dev)
+        keys = t * p0 + t * (t + 1) // 2  # (query token, key) pairs under the causal mask
+        flops = 2.0 * 2 * 256 * 8 * keys  # S = Q K^T and O = P V for 8 query heads
+        nbytes = 2 * 2 * (p0 + t) * 256 * 2 + t * (4096 + 2 * 512 + 2048) * 2
+
+        def call(i):
+            q35.prompt_attention(ins["q_raw"], ins["k_raw"], ins["v_raw"], ins["q_gain"], ins["k_gain"],
+                                 KC[i % copies], VC[i % copies], cap, p0, ws=ws, out=gated)
     else:
         d = I.config3(2, args.len)
         per = d["kc"].nbytes * 2
@@ -140,6 +186,8 @@ def main():
            "bytes_per_call": nbytes, "gbs": nbytes / us / 1e3, "copies": copies}
     if args.op == "qgemm":
         out.update({"tokens": args.tokens, "rows": args.rows, "k": args.k, "tflops": flops / us / 1e6})
+    if args.op == "pattn":
+        out.update({"len": args.len, "tokens": args.tokens, "flops_per_call": flops, "tflops": flops / us / 1e6})
     print(json.dumps(out))
 
 
