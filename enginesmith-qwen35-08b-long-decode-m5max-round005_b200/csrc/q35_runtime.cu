@@ -746,17 +746,20 @@ cudaError_t ensure_prompt_buffers(q35_session* s) {
   if (s->pbuf) return cudaSuccess;
   const size_t N = size_t(s->prompt_chunk);
   const size_t items = prompt_attn_items_max(s->prompt_chunk, s->capacity);
-  auto ws = [&](std::initializer_list<int> rows, int K) {
+  // the largest GEMM workspace over every chunk length (a shorter last chunk
+  // may split K further)
+  auto ws = [&](std::initializer_list<int> rows, int K, int T) {
     QGemmArgs g = {};
     for (int r : rows) g.seg[g.nseg++].rows = r;
     g.K = K;
-    g.T = int(N);
+    g.T = T;
     return qgemm_workspace_bytes(g);
   };
   s->p_gws_bytes = 0;
-  for (size_t w : {ws({kGdnConv, 2048, 16, 16}, kHidden), ws({kHidden}, 2048), ws({kMlp, kMlp}, kHidden),
-                   ws({kHidden}, kMlp), ws({kQProj, 512, 512}, kHidden)})
-    s->p_gws_bytes = std::max(s->p_gws_bytes, w);
+  for (int T = 1; T <= int(N); ++T)
+    for (size_t w : {ws({kGdnConv, 2048, 16, 16}, kHidden, T), ws({kHidden}, 2048, T), ws({kMlp, kMlp}, kHidden, T),
+                     ws({kHidden}, kMlp, T), ws({kQProj, 512, 512}, kHidden, T)})
+      s->p_gws_bytes = std::max(s->p_gws_bytes, w);
   struct Part {
     void** p;
     size_t bytes;

@@ -71,3 +71,26 @@ def test_open_reports_errors_without_crashing():
     opts = q35._Opts(96, 0, 0, 0)  # capacity not a multiple of 64
     rc = q35.lib().q35_open(b"/nonexistent", 0, ctypes.byref(opts), ctypes.byref(h), err, len(err))
     assert rc == q35.EINVAL and b"multiple of 64" in err.value and not h.value
+
+
+def test_open_rejects_bad_prompt_chunk():
+    import ctypes
+    h = ctypes.c_void_p()
+    err = ctypes.create_string_buffer(512)
+    for bad in (16, 48, 4096):
+        opts = q35._Opts(4096, 0, 0, q35.FLAG_TENSOR_PROMPT, bad)
+        rc = q35.lib().q35_open(b"/nonexistent", 0, ctypes.byref(opts), ctypes.byref(h), err, len(err))
+        assert rc == q35.EINVAL and b"prompt_chunk" in err.value and not h.value
+
+
+def test_op_workspace_queries():
+    """The ops' workspace sizes are host arithmetic: 0 marks an invalid shape."""
+    lib = q35.lib()
+    pw = lib.q35_op_prompt_workspace_bytes
+    assert pw(0, 0) == 0 and pw(2049, 4096) == 0 and pw(1, 100) == 0
+    sizes = [pw(t, 4096) for t in (1, 32, 33, 2048)]
+    assert all(s > 0 for s in sizes) and sizes == sorted(sizes)
+    assert pw(2048, 262144) > pw(2048, 4096)  # more key splits for a larger cache
+    qw = lib.q35_op_qgemm_workspace_bytes
+    assert qw(0, 1024, 1024) == 0 and qw(4097, 1024, 1024) == 0 and qw(8, 1024, 1000) == 0
+    assert qw(1, 1024, 1024) > 0 and qw(4096, 1024, 3584) > 0

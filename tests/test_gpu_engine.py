@@ -11,9 +11,9 @@ pytestmark = pytest.mark.gpu
 
 
 class Engine:
-    def __init__(self, model_dir):
+    def __init__(self, model_dir, *extra):
         import q35
-        self.p = subprocess.Popen([q35.ENGINE_PATH, "--model", model_dir, "--capacity", "4096"],
+        self.p = subprocess.Popen([q35.ENGINE_PATH, "--model", model_dir, "--capacity", "4096", *extra],
                                   stdin=subprocess.PIPE, stdout=subprocess.PIPE, text=True, bufsize=1)
 
     def ask(self, req):
@@ -47,6 +47,27 @@ def test_generate_matches_session_api(cuda, engine, synth_model_dir):
         m.close()
     assert r1 == {"id": 2, "ok": True, "tokens": a}
     assert r2 == {"id": 3, "ok": True, "tokens": b}
+
+
+def test_tensor_prompt_flag(cuda, synth_model_dir):
+    """engine --tensor-prompt consumes prompts on the tensor cores: the same
+    tokens as the session API with tensor_prompt=True."""
+    import q35
+    import inputs as I
+    prompt = [int(v) for v in I.Rng(31, 2).ints(300, 248320)]
+    e = Engine(synth_model_dir, "--tensor-prompt")
+    try:
+        assert e.ask({"id": 1, "op": "hello"})["ok"]
+        r = e.ask({"id": 2, "op": "generate", "prompt": prompt, "max_tokens": 5, "reset": True})
+    finally:
+        e.p.stdin.close()
+        e.p.wait(timeout=60)
+    m = q35.Model.load(synth_model_dir, 0, capacity=4096, tensor_prompt=True)
+    try:
+        want = m.generate(prompt, 5, True)
+    finally:
+        m.close()
+    assert r == {"id": 2, "ok": True, "tokens": want}
 
 
 def test_errors_keep_state(cuda, engine):
