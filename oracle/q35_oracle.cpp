@@ -770,6 +770,13 @@ void qmv_gemm_f32(const uint32_t* w, const uint16_t* s, const uint16_t* b, const
     }
   });
 }
+/* qmv_gemm_f32 for callers (the tensor-core routes' projections, before the
+ * bf16 output rounding). */
+void orc_qmv_gemm_f32(const uint32_t* w, const uint16_t* s, const uint16_t* b, const uint16_t* x, int N, int K,
+                      float* y) {
+  qmv_gemm_f32(w, s, b, x, N, K, y);
+}
+
 void orc_qmv_q4(const uint32_t* w, const uint16_t* s, const uint16_t* b, const uint16_t* x,
                 const uint16_t* residual, int N, int K, uint16_t* y) {
   std::vector<float> v(N);

@@ -45,6 +45,9 @@ float orc_fexp(float x);
 void orc_embedding_q4(const uint32_t* w, const uint16_t* s, const uint16_t* b,
                       uint32_t token, int K, uint16_t* out);
 /* qmv_q4 / qmv_add_q4, linear.metal:28-123. residual may be NULL. */
+/* the tensor-core routes' matvec: weights bf16(s q + b), exact dot products (f32 out) */
+void orc_qmv_gemm_f32(const uint32_t* w, const uint16_t* s, const uint16_t* b, const uint16_t* x, int N, int K,
+                      float* y);
 void orc_qmv_q4(const uint32_t* w, const uint16_t* s, const uint16_t* b,
                 const uint16_t* x, const uint16_t* residual, int N, int K, uint16_t* y);
 /* f32 value before the bf16 store (for tolerance tests) */

@@ -77,6 +77,7 @@ def lib() -> ctypes.CDLL:
             "orc_session_export": (None, [P, P, P, P]),
             "orc_attn_flash_f32": (None, [P, P, P, c_uint32, c_uint32, P]),
             "orc_attn_flash_gate": (None, [P, P, P, c_uint32, c_uint32, P, P]),
+            "orc_qmv_gemm_f32": (None, [P, P, P, P, c_int, c_int, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -127,6 +128,14 @@ def qmv_q4_f32(w, s, b, x) -> np.ndarray:
     n, kw = w.shape
     y = np.zeros(n, np.float32)
     lib().orc_qmv_q4_f32(_p(w), _p(s), _p(b), _p(x), n, kw * 8, _p(y))
+    return y
+
+
+def qmv_gemm_f32(w, s, b, x) -> np.ndarray:
+    """The tensor-core routes' matvec: weights bf16(s q + b), exact dot products, f32 out."""
+    n, k = w.shape[0], w.shape[1] * 8
+    y = np.zeros(n, np.float32)
+    lib().orc_qmv_gemm_f32(_p(w), _p(s), _p(b), _p(x), n, k, _p(y))
     return y
 
 

@@ -6,7 +6,8 @@ small. The GPU parity tests compare the CUDA path against these files and
 against the live oracle; the CPU tests check that the oracle still reproduces
 them bit for bit.
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py          (every fixture)
+    python tests/golden/make_golden.py tensor   (tensor_routes.npz only)
 """
 import os
 import sys
@@ -23,8 +24,28 @@ import inputs as I  # noqa: E402
 import q35_oracle as O  # noqa: E402
 
 
+def tensor_routes():
+    """The tensor-core routes' restatements: the GEMM-numerics matvec (config 1
+    shapes, f32 before the output rounding) and the prompt route's flash
+    attention with the gate (config 3, at a few lengths)."""
+    outs = {}
+    for n, k, seed in ((3584, 1024, 0), (1024, 3584, 11)):
+        w, s, b, x = I.config1(seed, n, k)
+        outs[f"gemm_{n}x{k}"] = O.qmv_gemm_f32(w, s, b, x)
+    for length in (1, 31, 1025, 4096):
+        c = I.config3(2, length)
+        kc, vc = c["kc"].copy(), c["vc"].copy()
+        q = O.attn_prepare(c["q_raw"], c["k_raw"], c["v_raw"], c["q_gain"], c["k_gain"], c["pos"], c["cap"], kc, vc)
+        outs[f"flash_{length}"] = O.attn_flash_gate(q, kc, vc, length, c["cap"], c["q_raw"])
+    np.savez_compressed(os.path.join(HERE, "tensor_routes.npz"), **outs)
+
+
 def main():
     O.set_threads(os.cpu_count() or 1)
+    if sys.argv[1:] == ["tensor"]:
+        tensor_routes()
+        return
+    tensor_routes()
     # config 1: Q4 matvec 3584 x 1024, seed 0 (and the residual form)
     w, s, b, x = I.config1(0)
     res = I.f2bf(I.Rng(5).normal(3584))

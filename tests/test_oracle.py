@@ -161,6 +161,22 @@ def test_attention_matches_float64(O, length):
     assert np.linalg.norm(o - ref) <= tol * np.linalg.norm(ref)
 
 
+@pytest.mark.parametrize("n,k,seed", [(3584, 1024, 0), (1024, 2048, 4), (77, 3584, 9)])
+def test_gemm_numerics_matvec(O, n, k, seed):
+    """The tensor-core routes' matvec restatement (weights bf16(s q + b) from
+    one fused multiply-add, dot products exact): against numpy float64, at
+    most one f32 ulp apart (the order of the float64 sums differs)."""
+    w, s, b, x = I.config1(seed, n, k)
+    q = I.unpack_q4(w).astype(np.float64)
+    sc = np.repeat(I.bf2f(s).astype(np.float64), 64, axis=1)
+    bi = np.repeat(I.bf2f(b).astype(np.float64), 64, axis=1)
+    wd = I.bf2f(I.f2bf((sc * q + bi).astype(np.float32))).astype(np.float64)
+    ref = (wd @ I.bf2f(x).astype(np.float64)).astype(np.float32)
+    got = O.qmv_gemm_f32(w, s, b, x)
+    ulp = np.spacing(np.abs(ref))
+    assert np.all(np.abs(got - ref) <= ulp), float(np.max(np.abs(got - ref) / ulp))
+
+
 def attention_flash_f64(query, kc, vc, length):
     """The tensor-core prompt route's attention: exact scores rounded to f32,
     weights bf16(2^((s - max) log2(e) / 16)), exact weighted sums."""
@@ -259,6 +275,19 @@ def test_golden_config3(O, length):
     q = O.attn_prepare(c["q_raw"], c["k_raw"], c["v_raw"], c["q_gain"], c["k_gain"], c["pos"], c["cap"], kc, vc)
     assert np.array_equal(O.attn_decode_gate(q, kc, vc, length, c["cap"], c["q_raw"]), g[f"gated_{length}"])
     assert np.array_equal(kc[:, c["pos"]], g[f"krow_{length}"])
+
+
+def test_golden_tensor_routes(O):
+    """The tensor-core routes' restatements reproduce their committed outputs."""
+    g = np.load(os.path.join(GOLD, "tensor_routes.npz"))
+    for n, k, seed in ((3584, 1024, 0), (1024, 3584, 11)):
+        w, s, b, x = I.config1(seed, n, k)
+        assert np.array_equal(O.qmv_gemm_f32(w, s, b, x), g[f"gemm_{n}x{k}"])
+    for length in (1, 31, 1025, 4096):
+        c = I.config3(2, length)
+        kc, vc = c["kc"].copy(), c["vc"].copy()
+        q = O.attn_prepare(c["q_raw"], c["k_raw"], c["v_raw"], c["q_gain"], c["k_gain"], c["pos"], c["cap"], kc, vc)
+        assert np.array_equal(O.attn_flash_gate(q, kc, vc, length, c["cap"], c["q_raw"]), g[f"flash_{length}"])
 
 
 def test_golden_greedy_audit(O):
