@@ -1838,6 +1838,10 @@ int q35_open(const char* model_dir, int device, const q35_opts* opts, q35_sessio
     *p.p = s->buf + off;
     off += (p.bytes + 255) & ~size_t(255);
   }
+  if (s->tensor_prompt) {  // the prompt route's chunk buffers, so a shortage shows here
+    e = ensure_prompt_buffers(s);
+    if (e != cudaSuccess) return fail(Q35_ENOMEM, std::string("prompt buffers: ") + cudaGetErrorString(e));
+  }
   Ctl c = {};
   c.capacity = s->capacity;
   c.attn_t0 = ~0ull;
