@@ -94,3 +94,22 @@ def test_op_workspace_queries():
     qw = lib.q35_op_qgemm_workspace_bytes
     assert qw(0, 1024, 1024) == 0 and qw(4097, 1024, 1024) == 0 and qw(8, 1024, 1000) == 0
     assert qw(1, 1024, 1024) > 0 and qw(4096, 1024, 3584) > 0
+
+
+def test_prompt_ops_reject_bad_arguments():
+    """The prompt-chunk ops validate their arguments before touching a device."""
+    import ctypes
+    lib = q35.lib()
+    buf = ctypes.create_string_buffer(64)
+    p = ctypes.cast(buf, ctypes.c_void_p)
+    gdn = lib.q35_op_prompt_gdn
+    # a null input, zero tokens, too many tokens, a workspace below the query
+    assert gdn(None, p, p, p, p, p, p, p, p, 4, p, p, 1 << 30, None) == q35.EINVAL
+    assert gdn(p, p, p, p, p, p, p, p, p, 0, p, p, 1 << 30, None) == q35.EINVAL
+    assert gdn(p, p, p, p, p, p, p, p, p, 2049, p, p, 1 << 30, None) == q35.EINVAL
+    assert gdn(p, p, p, p, p, p, p, p, p, 4, p, p, 16, None) == q35.EINVAL
+    att = lib.q35_op_prompt_attention
+    # capacity not a multiple of 64, the tokens past the capacity, a small workspace
+    assert att(p, p, p, p, p, p, p, 100, 0, 4, p, p, 1 << 30, None) == q35.EINVAL
+    assert att(p, p, p, p, p, p, p, 128, 126, 4, p, p, 1 << 30, None) == q35.EINVAL
+    assert att(p, p, p, p, p, p, p, 128, 0, 4, p, p, 16, None) == q35.EINVAL
