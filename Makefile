@@ -31,8 +31,10 @@ $(LIB): $(BUILD)/q35_kernels.o $(BUILD)/q35_prefill.o $(BUILD)/q35_gemm.o $(BUIL
 $(ENGINE): $(CSRC)/engine.cpp $(CSRC)/q35_json.h include/q35.h $(LIB)
 	$(CXX) $(CXXFLAGS) -o $@ $< -L$(LIBDIR) -lq35cuda -Wl,-rpath,'$$ORIGIN' -pthread
 
-$(ORACLE): oracle/q35_oracle.cpp oracle/q35_oracle.h
-	$(CXX) -std=c++17 -O2 -fPIC -shared -ffp-contract=off -pthread -Wall -o $@ $<
+# The oracle also carries the seeded synthetic-model writer (plain C++), so the
+# CPU reference arm can write the model without loading the CUDA library.
+$(ORACLE): oracle/q35_oracle.cpp oracle/q35_oracle.h $(CSRC)/q35_synth.cpp include/q35.h
+	$(CXX) -std=c++17 -O2 -fPIC -shared -ffp-contract=off -pthread -Wall -Iinclude -o $@ oracle/q35_oracle.cpp $(CSRC)/q35_synth.cpp
 
 clean:
 	rm -rf $(BUILD) $(LIB) $(ENGINE) $(ORACLE)

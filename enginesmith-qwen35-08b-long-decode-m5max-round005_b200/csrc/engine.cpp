@@ -66,12 +66,16 @@ int main(int argc, char** argv) {
   const char* model = nullptr;
   int device = 0;
   q35_opts opts = {};
+  // Prompts take the tensor-core route by default, as the reference's prefill
+  // takes its GEMM/flash-attention route (model.rs:100-110, :189-198).
+  opts.flags = Q35_FLAG_TENSOR_PROMPT;
   for (int i = 1; i < argc; ++i) {
     std::string a = argv[i];
     if (a == "--model" && i + 1 < argc) model = argv[++i];
     else if (a == "--device" && i + 1 < argc) device = std::atoi(argv[++i]);
     else if (a == "--capacity" && i + 1 < argc) opts.capacity = uint32_t(std::strtoul(argv[++i], nullptr, 10));
-    else if (a == "--tensor-prompt") opts.flags |= Q35_FLAG_TENSOR_PROMPT;  // prompts on the tensor cores
+    else if (a == "--tensor-prompt") opts.flags |= Q35_FLAG_TENSOR_PROMPT;  // the default, kept for old callers
+    else if (a == "--decode-prompt") opts.flags &= ~Q35_FLAG_TENSOR_PROMPT;  // prompts through the decode kernels
     else {
       std::fprintf(stderr, "engine: unknown argument %s\n", a.c_str());
       return 1;
@@ -144,10 +148,13 @@ int main(int argc, char** argv) {
         }
         if (bad.empty() && (!mt || !mt->as_u64(count))) bad = "missing max_tokens";
         if (bad.empty() && (!rs || rs->type != q35json::Value::Bool)) bad = "missing reset";
+        // model.rs:98: the output length is checked before anything is
+        // allocated for it
+        if (bad.empty() && (count == 0 || count > uint64_t(q35_capacity(s)))) bad = "invalid output length";
         if (!bad.empty()) {
           reply = error_reply(id, bad);
         } else {
-          tokens.assign(count ? size_t(count) : 1, 0);
+          tokens.assign(size_t(count), 0);
           int rc = q35_generate(s, prompt.data(), prompt.size(), size_t(count), rs->b ? 1 : 0,
                                 tokens.data());
           if (eof.load()) break;

@@ -438,6 +438,8 @@ bool tmap_3d(CUtensorMap* m, CUtensorMapDataType ty, const void* base, uint64_t 
 // Validates, lays out the workspace (header with the error word, partials),
 // encodes the TMA descriptors and launches (plus the split reduction).
 // `zero_counters` clears the header first.
+size_t qgemm_err_offset() { return size_t(kGemmMaxTiles) * 4; }
+
 cudaError_t launch_qgemm(QGemmArgs a, void* ws, size_t ws_bytes, bool zero_counters, cudaStream_t st, bool pdl) {
   if (a.T < 1 || a.T > kGemmMaxTokens || a.K % 512 != 0 || a.K < 512 || a.K > 4096 || a.nseg < 1 ||
       a.nseg > kGemmSegs || !a.x)

@@ -8,6 +8,11 @@
 namespace q35 {
 
 cudaError_t kernels_init();
+// Byte offset of the bounded-wait error word in a q35_op_qgemm_q4 workspace.
+size_t qgemm_err_offset();
+// Scratch base of the allocation-free attention op on device `dev` (NULL
+// before that op's first call there).
+unsigned char* noalloc_scratch(int dev);
 // Largest rows-per-CTA whose k_qmv shared-memory layout fits one CTA per SM.
 int qmv_max_rows(int K);
 size_t qmv_smem_bytes(const QmvArgs& a);

@@ -21,7 +21,8 @@
 // Set-up: the first call on a device (with that device current) looks up the
 // scratch's device address with cudaGetSymbolAddress and sets the kernels'
 // shared-memory limits. Make that first call before any stream capture on
-// the device.
+// the device. The address is cached per device number for the life of the
+// process, so calls after a cudaDeviceReset of that device are unsupported.
 #include <cstdint>
 #include <cstdio>
 #include <mutex>
@@ -34,9 +35,11 @@ namespace {
 
 using namespace q35;
 
-// Maximum scratch per device: 576 KiB. This call needs the control block plus
-// the per-chain partials of 2 kv heads x 64 chains x 4 query heads
-// (f32 [256] output + f32 (max, sum)): 528,640 bytes at any context length.
+// Maximum scratch per device: 576 KiB. This call needs the control block
+// (rounded up to 256 bytes: 512) plus the per-chain partials of 2 kv heads x
+// 64 chains x 4 query heads (f32 [256] output + f32 (max, sum)): 528,896
+// bytes at any context length; a static_assert below holds the layout to the
+// maximum.
 constexpr size_t kScratchBytes = 576 * 1024;
 
 __device__ __align__(256) unsigned char g_attn_scratch[kScratchBytes];
@@ -45,6 +48,8 @@ constexpr size_t kCtlBytes = (sizeof(Ctl) + 255) & ~size_t(255);
 constexpr size_t kPartOBytes = size_t(kKvHeads) * kAttnChains * 4 * kHeadDim * 4;
 constexpr size_t kPartMlBytes = size_t(kKvHeads) * kAttnChains * 4 * 2 * 4;
 constexpr size_t kNeedBytes = kCtlBytes + kPartOBytes + kPartMlBytes;
+static_assert(kNeedBytes <= kScratchBytes, "the attention op's scratch layout outgrew the static array");
+static_assert(kNeedBytes == 528896, "scratch need changed: update the documented figure");
 
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
@@ -55,6 +60,14 @@ void put_err(char* err, size_t n, const char* msg) {
 }
 
 }  // namespace
+
+namespace q35 {
+unsigned char* noalloc_scratch(int dev) {
+  if (dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lk(g_mu);
+  return g_ptr[dev];
+}
+}  // namespace q35
 
 extern "C" int q35_op_attn_decode_noalloc(const uint16_t* q_raw, const uint16_t* k_raw,
                                           const uint16_t* v_raw, const uint16_t* q_gain,
@@ -78,14 +91,6 @@ extern "C" int q35_op_attn_decode_noalloc(const uint16_t* q_raw, const uint16_t*
   }
   if (pos >= capacity) {
     put_err(err, err_len, "attn_decode_noalloc: pos must be below capacity");
-    return Q35_EINVAL;
-  }
-  if (kNeedBytes > kScratchBytes) {
-    char m[160];
-    std::snprintf(m, sizeof(m),
-                  "attn_decode_noalloc: needs %zu bytes of scratch, above the %zu-byte maximum",
-                  kNeedBytes, kScratchBytes);
-    put_err(err, err_len, m);
     return Q35_EINVAL;
   }
   int dev = 0;

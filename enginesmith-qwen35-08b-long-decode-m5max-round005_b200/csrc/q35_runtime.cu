@@ -317,6 +317,25 @@ cudaError_t ensure_kernels_init() {
   return e;
 }
 
+// The session options q35_open accepts (host arithmetic only).
+bool validate_opts(const q35_opts* o, std::string& m) {
+  const uint32_t cap = o && o->capacity ? o->capacity : kDefaultCapacity;
+  const uint32_t chunk = o && o->prompt_chunk ? o->prompt_chunk : uint32_t(kPromptChunk);
+  if (cap % kAttnChains != 0 || cap < kAttnChains || cap > (1u << 30)) {
+    m = "capacity must be a positive multiple of 64";
+    return false;
+  }
+  if (chunk < 32 || chunk > uint32_t(kPromptChunk) || chunk % 32 != 0) {
+    m = "prompt_chunk must be a multiple of 32 in 32..2048";
+    return false;
+  }
+  if (o && (o->decode_batch > 1024 || o->prefill_batch > 1024)) {
+    m = "decode_batch and prefill_batch must be at most 1024";
+    return false;
+  }
+  return true;
+}
+
 void copy_err(char* dst, size_t n, const std::string& m) {
   if (dst && n) std::snprintf(dst, n, "%s", m.c_str());
 }
@@ -343,6 +362,12 @@ struct q35_session {
   uint16_t* hist = nullptr;
   uint16_t* kv = nullptr;  // [6 layers][K|V][2][capacity][256]
   cudaGraphExec_t gdec1 = nullptr, gdecN = nullptr, gpre1 = nullptr, gpreN = nullptr;
+  // kernel launches in one replay of the decode graphs (counted at capture)
+  uint32_t kn_dec1 = 0, kn_decN = 0;
+  uint64_t launches = 0;  // decode-graph kernel launches since the last q35_launch_count reset
+  // in-flight window of the token loop: the host waits on the event of the
+  // launch kInflight places back before it queues the next one
+  cudaEvent_t inflight[kInflight] = {};
   // prompt chunks of kPrefillTokens tokens (per-token rows of each buffer)
   bool chunked = true;
   cudaGraphExec_t gchunk = nullptr;
@@ -919,7 +944,21 @@ cudaError_t enqueue_prompt_chunk(q35_session* s, uint32_t p0, int T) {
   return e;
 }
 
-cudaError_t capture(q35_session* s, int steps, bool head, cudaGraphExec_t* out) {
+// Kernel nodes of a captured graph: the launches one replay performs.
+uint32_t kernel_nodes(cudaGraph_t g) {
+  size_t n = 0;
+  if (cudaGraphGetNodes(g, nullptr, &n) != cudaSuccess || n == 0) return 0;
+  std::vector<cudaGraphNode_t> nodes(n);
+  if (cudaGraphGetNodes(g, nodes.data(), &n) != cudaSuccess) return 0;
+  uint32_t k = 0;
+  for (size_t i = 0; i < n; ++i) {
+    cudaGraphNodeType t;
+    if (cudaGraphNodeGetType(nodes[i], &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++k;
+  }
+  return k;
+}
+
+cudaError_t capture(q35_session* s, int steps, bool head, cudaGraphExec_t* out, uint32_t* knodes = nullptr) {
   cudaGraph_t g = nullptr;
   cudaError_t e = cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal);
   if (e != cudaSuccess) return e;
@@ -931,6 +970,7 @@ cudaError_t capture(q35_session* s, int steps, bool head, cudaGraphExec_t* out) 
     return le;
   }
   if (e != cudaSuccess) return e;
+  if (knodes) *knodes = kernel_nodes(g);
   e = cudaGraphInstantiate(out, g, 0);
   cudaGraphDestroy(g);
   return e;
@@ -941,6 +981,8 @@ void free_session(q35_session* s) {
   if (s->device >= 0) cudaSetDevice(s->device);
   for (cudaGraphExec_t g : {s->gdec1, s->gdecN, s->gpre1, s->gpreN, s->gchunk})
     if (g) cudaGraphExecDestroy(g);
+  for (cudaEvent_t ev : s->inflight)
+    if (ev) cudaEventDestroy(ev);
   for (void* p : s->xpeer)
     if (p) cudaIpcCloseMemHandle(p);
   if (s->xtab) cudaFree(s->xtab);
@@ -973,35 +1015,44 @@ int device_failure(q35_session* s, cudaError_t e, const char* what) {
 
 // Runs `n` steps from the current device state (graphs of the batch size
 // then single steps). Returns 0, Q35_ECANCEL or a CUDA error code.
+// Before the i-th launch of a loop: wait until launch i - kInflight has
+// finished, so at most kInflight graph launches (chunks) are queued and a
+// cancel waits for no more than that; after it: mark its end.
+cudaError_t inflight_wait(q35_session* s, size_t i) {
+  return i >= size_t(kInflight) ? cudaEventSynchronize(s->inflight[i % kInflight]) : cudaSuccess;
+}
+cudaError_t inflight_mark(q35_session* s, size_t i) {
+  return cudaEventRecord(s->inflight[i % kInflight], s->stream);
+}
+
 int run_steps(q35_session* s, size_t n, bool head, cudaError_t* ce) {
   cudaGraphExec_t g1 = head ? s->gdec1 : s->gpre1;
   cudaGraphExec_t gN = head ? s->gdecN : s->gpreN;
   const size_t B = size_t(head ? s->dbatch : s->pbatch);
   size_t launched = 0;
   while (n > 0) {
+    cudaError_t e = inflight_wait(s, launched);
+    if (e != cudaSuccess) {
+      *ce = e;
+      return Q35_ECUDA;
+    }
     if (s->cancelled.load(std::memory_order_relaxed)) return Q35_ECANCEL;
-    cudaError_t e;
     if (!head && s->gchunk && n >= size_t(kPrefillTokens)) {
       e = cudaGraphLaunch(s->gchunk, s->stream);
       n -= kPrefillTokens;
     } else if (n >= B && gN) {
       e = cudaGraphLaunch(gN, s->stream);
       n -= B;
+      if (head) s->launches += s->kn_decN;
     } else {
       e = cudaGraphLaunch(g1, s->stream);
       n -= 1;
+      if (head) s->launches += s->kn_dec1;
     }
+    if (e == cudaSuccess) e = inflight_mark(s, launched++);
     if (e != cudaSuccess) {
       *ce = e;
       return Q35_ECUDA;
-    }
-    // keep the queued work bounded so a cancel is observed promptly
-    if (++launched % 16 == 0) {
-      e = cudaStreamSynchronize(s->stream);
-      if (e != cudaSuccess) {
-        *ce = e;
-        return Q35_ECUDA;
-      }
     }
   }
   return Q35_OK;
@@ -1013,15 +1064,18 @@ int run_steps(q35_session* s, size_t n, bool head, cudaError_t* ce) {
 int run_prompt_tensor(q35_session* s, size_t n, cudaError_t* ce) {
   cudaError_t e = ensure_prompt_buffers(s);
   uint32_t p0 = 0;
-  int queued = 0;
+  size_t queued = 0;
   while (e == cudaSuccess && n > 0) {
+    e = inflight_wait(s, queued);
+    if (e != cudaSuccess) break;
     if (s->cancelled.load(std::memory_order_relaxed)) return Q35_ECANCEL;
     const int T = int(std::min(n, size_t(s->prompt_chunk)));
     e = enqueue_prompt_chunk(s, p0, T);
     p0 += uint32_t(T);
     n -= size_t(T);
-    if (e == cudaSuccess && (++queued % 4 == 0 || n == 0)) e = cudaStreamSynchronize(s->stream);
+    if (e == cudaSuccess) e = inflight_mark(s, queued++);
   }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
   if (e != cudaSuccess) {
     *ce = e;
     return Q35_ECUDA;
@@ -1075,6 +1129,8 @@ struct q35_batch {
   AttnSess* asess = nullptr;
   HeadOut* hout = nullptr;
   cudaGraphExec_t g1 = nullptr, gN = nullptr;
+  uint32_t kn_g1 = 0, kn_gN = 0;  // kernel launches per replay (counted at capture)
+  uint64_t launches = 0;          // since the last q35_batch_launch_count reset
   int nbatch = 8;
   std::string err;
 };
@@ -1386,7 +1442,7 @@ cudaError_t enqueue_batch_step_tensor(q35_batch* b, bool first) {
   return e;
 }
 
-cudaError_t capture_batch(q35_batch* b, int steps, cudaGraphExec_t* out) {
+cudaError_t capture_batch(q35_batch* b, int steps, cudaGraphExec_t* out, uint32_t* knodes) {
   cudaGraph_t g = nullptr;
   cudaError_t e = cudaStreamBeginCapture(b->stream, cudaStreamCaptureModeThreadLocal);
   if (e != cudaSuccess) return e;
@@ -1399,6 +1455,7 @@ cudaError_t capture_batch(q35_batch* b, int steps, cudaGraphExec_t* out) {
     return le;
   }
   if (e != cudaSuccess) return e;
+  *knodes = kernel_nodes(g);
   e = cudaGraphInstantiate(out, g, 0);
   cudaGraphDestroy(g);
   return e;
@@ -1446,9 +1503,11 @@ int batch_run(q35_batch* b, size_t steps, float* ms) {
     if (left >= size_t(b->nbatch) && b->gN) {
       e = cudaGraphLaunch(b->gN, b->stream);
       left -= size_t(b->nbatch);
+      b->launches += b->kn_gN;
     } else {
       e = cudaGraphLaunch(b->g1, b->stream);
       left -= 1;
+      b->launches += b->kn_g1;
     }
     if (!ms && e == cudaSuccess && ++launched % 16 == 0) e = cudaStreamSynchronize(b->stream);
   }
@@ -1599,8 +1658,8 @@ int q35_batch_create_ex(q35_session** sessions, int n, uint32_t flags, q35_batch
     e = cudaMemcpy(b->asess, as.data(), as.size() * sizeof(AttnSess), cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemcpy(b->hout, ho.data(), ho.size() * sizeof(HeadOut), cudaMemcpyHostToDevice);
   }
-  if (e == cudaSuccess) e = capture_batch(b, 1, &b->g1);
-  if (e == cudaSuccess) e = capture_batch(b, b->nbatch, &b->gN);
+  if (e == cudaSuccess) e = capture_batch(b, 1, &b->g1, &b->kn_g1);
+  if (e == cudaSuccess) e = capture_batch(b, b->nbatch, &b->gN, &b->kn_gN);
   if (e != cudaSuccess) {
     free_batch(b);
     return fail(Q35_ECUDA, std::string("batch graph capture: ") + cudaGetErrorString(e));
@@ -1639,6 +1698,13 @@ int q35_batch_decode_timed(q35_batch* b, size_t steps, float* ms) {
 }
 
 const char* q35_batch_last_error(const q35_batch* b) { return b ? b->err.c_str() : "no batch"; }
+
+int q35_batch_launch_count(q35_batch* b, int reset, uint64_t* launches) {
+  if (!b) return Q35_EINVAL;
+  if (launches) *launches = b->launches;
+  if (reset) b->launches = 0;
+  return Q35_OK;
+}
 
 void q35_batch_destroy(q35_batch* b) { free_batch(b); }
 
@@ -1710,8 +1776,8 @@ int q35_split_connect(q35_session* s, const void* handles) {
       cudaGraphExecDestroy(*g);
       *g = nullptr;
     }
-  e = capture(s, 1, true, &s->gdec1);
-  if (e == cudaSuccess && s->dbatch > 1) e = capture(s, s->dbatch, true, &s->gdecN);
+  e = capture(s, 1, true, &s->gdec1, &s->kn_dec1);
+  if (e == cudaSuccess && s->dbatch > 1) e = capture(s, s->dbatch, true, &s->gdecN, &s->kn_decN);
   if (e == cudaSuccess) e = capture(s, 1, false, &s->gpre1);
   if (e == cudaSuccess && s->pbatch > 1) e = capture(s, s->pbatch, false, &s->gpreN);
   if (e == cudaSuccess && s->chunked) e = capture_chunk(s, &s->gchunk);
@@ -1758,6 +1824,14 @@ int q35_open(const char* model_dir, int device, const q35_opts* opts, q35_sessio
     s->model_id = rp ? rp : model_dir;
     free(rp);
   }
+  {
+    std::string m;
+    if (!validate_opts(opts, m)) {
+      copy_err(errbuf, err_len, m);
+      delete s;
+      return Q35_EINVAL;
+    }
+  }
   if (opts) {
     if (opts->capacity) s->capacity = opts->capacity;
     if (opts->decode_batch) s->dbatch = int(opts->decode_batch);
@@ -1771,16 +1845,15 @@ int q35_open(const char* model_dir, int device, const q35_opts* opts, q35_sessio
     free_session(s);
     return code;
   };
-  if (s->capacity % kAttnChains != 0 || s->capacity < kAttnChains || s->capacity > (1u << 30))
-    return fail(Q35_EINVAL, "capacity must be a positive multiple of 64");
-  if (s->prompt_chunk < 32 || s->prompt_chunk > kPromptChunk || s->prompt_chunk % 32 != 0)
-    return fail(Q35_EINVAL, "prompt_chunk must be a multiple of 32 in 32..2048");
   cudaError_t e = cudaSetDevice(device);
   if (e != cudaSuccess) return fail(Q35_ECUDA, std::string("cudaSetDevice: ") + cudaGetErrorString(e));
   e = ensure_kernels_init();
   if (e != cudaSuccess) return fail(Q35_ECUDA, std::string("kernel setup: ") + cudaGetErrorString(e));
   e = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking);
   if (e != cudaSuccess) return fail(Q35_ECUDA, std::string("stream: ") + cudaGetErrorString(e));
+  for (cudaEvent_t& ev : s->inflight)
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+  if (e != cudaSuccess) return fail(Q35_ECUDA, std::string("event: ") + cudaGetErrorString(e));
   {
     Loader ld;
     if (!ld.open(model_dir) || !ld.upload(s->M) || !bind_model(ld, s->M))
@@ -1846,8 +1919,8 @@ int q35_open(const char* model_dir, int device, const q35_opts* opts, q35_sessio
   c.capacity = s->capacity;
   c.attn_t0 = ~0ull;
   e = cudaMemcpy(s->ctl, &c, sizeof(Ctl), cudaMemcpyHostToDevice);
-  if (e == cudaSuccess) e = capture(s, 1, true, &s->gdec1);
-  if (e == cudaSuccess && s->dbatch > 1) e = capture(s, s->dbatch, true, &s->gdecN);
+  if (e == cudaSuccess) e = capture(s, 1, true, &s->gdec1, &s->kn_dec1);
+  if (e == cudaSuccess && s->dbatch > 1) e = capture(s, s->dbatch, true, &s->gdecN, &s->kn_decN);
   if (e == cudaSuccess) e = capture(s, 1, false, &s->gpre1);
   if (e == cudaSuccess && s->pbatch > 1) e = capture(s, s->pbatch, false, &s->gpreN);
   if (e == cudaSuccess && s->chunked) e = capture_chunk(s, &s->gchunk);
@@ -1865,6 +1938,29 @@ void q35_cancel(q35_session* s) {
 const char* q35_last_error(const q35_session* s) { return s ? s->err.c_str() : "no session"; }
 
 uint32_t q35_position(const q35_session* s) { return s ? s->position : 0; }
+
+uint32_t q35_capacity(const q35_session* s) { return s ? s->capacity : 0; }
+
+int q35_pending(const q35_session* s, uint32_t* token) {
+  if (!s || !token) return Q35_EINVAL;
+  if (!s->has_pending) return Q35_EINVAL;
+  *token = s->pending;
+  return Q35_OK;
+}
+
+int q35_check_opts(const q35_opts* opts, char* errbuf, size_t err_len) {
+  std::string m;
+  if (validate_opts(opts, m)) return Q35_OK;
+  copy_err(errbuf, err_len, m);
+  return Q35_EINVAL;
+}
+
+int q35_launch_count(q35_session* s, int reset, uint64_t* launches) {
+  if (!s) return Q35_EINVAL;
+  if (launches) *launches = s->launches;
+  if (reset) s->launches = 0;
+  return Q35_OK;
+}
 
 // Model::generate + Model::decode (model.rs:97-180)
 int q35_generate(q35_session* s, const uint32_t* prompt, size_t n_prompt, size_t max_tokens,
@@ -1956,9 +2052,11 @@ int q35_decode_timed(q35_session* s, size_t steps, float* ms) {
       if (n >= size_t(s->dbatch) && gN) {
         e = cudaGraphLaunch(gN, s->stream);
         n -= size_t(s->dbatch);
+        s->launches += s->kn_decN;
       } else {
         e = cudaGraphLaunch(g1, s->stream);
         n -= 1;
+        s->launches += s->kn_dec1;
       }
     }
   }
@@ -2198,6 +2296,25 @@ int q35_op_gdn_step(const uint16_t* raw_qkv, const uint16_t* z, const uint16_t* 
   o.ctl = ctl;
   if (e == cudaSuccess) e = launch_qmv(o, st, false);
   return op_status(e);
+}
+
+int q35_op_status(const void* workspace, uint32_t kind, uint32_t* site, void* stream) {
+  if (kind > Q35_OPWS_QGEMM) return Q35_EINVAL;
+  const uint8_t* base = static_cast<const uint8_t*>(workspace);
+  if (!base) {
+    if (kind != Q35_OPWS_CTL) return Q35_EINVAL;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return Q35_ECUDA;
+    base = noalloc_scratch(dev);
+    if (!base) return Q35_EINVAL;  // no allocation-free call on this device yet
+  }
+  const uint8_t* word = base + (kind == Q35_OPWS_QGEMM ? qgemm_err_offset() : offsetof(Ctl, err));
+  uint32_t v = 0;
+  cudaError_t e = cudaStreamSynchronize((cudaStream_t)stream);
+  if (e == cudaSuccess) e = cudaMemcpy(&v, word, 4, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return Q35_ECUDA;
+  if (site) *site = v;
+  return v ? Q35_ETIMEOUT : Q35_OK;
 }
 
 size_t q35_op_attn_workspace_bytes(void) {

@@ -38,6 +38,10 @@ constexpr int kHeadRowsPerCta = kHeadRowsPerChunk * kHeadChunksPerCta;  // 1680
 constexpr int kHeadCtas = (kVocab + kHeadRowsPerCta - 1) / kHeadRowsPerCta;  // 148
 constexpr int kHeadStages = 4;
 constexpr int kPrefillTokens = 16;  // prompt tokens per chunk launch
+// graph launches (prompt chunks) the token loop keeps queued: with 8 decode
+// steps per graph at most 16 steps are in flight when a cancel arrives, as
+// the reference's bounded-ahead loop keeps (model.rs:127)
+constexpr int kInflight = 2;
 
 // Device-resident control block of one decode session (or one op call).
 struct Ctl {

@@ -53,6 +53,11 @@ def _load() -> ctypes.CDLL:
         "q35_last_error": (c_char_p, [P]),
         "q35_close": (None, [P]),
         "q35_position": (c_uint32, [P]),
+        "q35_capacity": (c_uint32, [P]),
+        "q35_pending": (c_int, [P, POINTER(c_uint32)]),
+        "q35_check_opts": (c_int, [POINTER(_Opts), c_char_p, c_size_t]),
+        "q35_launch_count": (c_int, [P, c_int, POINTER(c_uint64)]),
+        "q35_batch_launch_count": (c_int, [P, c_int, POINTER(c_uint64)]),
         "q35_dump_state": (c_int, [P, P, P, P]),
         "q35_last_logits": (c_int, [P, P, P]),
         "q35_decode_timed": (c_int, [P, c_size_t, POINTER(c_float)]),
@@ -105,6 +110,17 @@ def lib() -> ctypes.CDLL:
     return _lib
 
 
+def check_opts(capacity: int = 0, decode_batch: int = 0, prefill_batch: int = 0, flags: int = 0,
+               prompt_chunk: int = 0) -> None:
+    """Raise Q35Error when q35_open would reject these session options
+    (host arithmetic only; no device needed)."""
+    opts = _Opts(capacity, decode_batch, prefill_batch, flags, prompt_chunk)
+    err = ctypes.create_string_buffer(512)
+    rc = lib().q35_check_opts(ctypes.byref(opts), err, len(err))
+    if rc != OK:
+        raise Q35Error(rc, err.value.decode())
+
+
 def write_synthetic_model(path: str, seed: int) -> None:
     """Seeded random-init model in the MLX layout (config.json + model.safetensors)."""
     err = ctypes.create_string_buffer(1024)
@@ -155,6 +171,19 @@ class Model:
     @property
     def position(self) -> int:
         return int(lib().q35_position(self._h))
+
+    @property
+    def pending(self) -> int:
+        """The token the next continuation consumes first (last emitted id)."""
+        t = c_uint32()
+        self._check(lib().q35_pending(self._h, ctypes.byref(t)))
+        return int(t.value)
+
+    def launch_count(self, reset: bool = False) -> int:
+        """Kernel launches of the decode graphs replayed since the last reset."""
+        n = c_uint64()
+        self._check(lib().q35_launch_count(self._h, 1 if reset else 0, ctypes.byref(n)))
+        return int(n.value)
 
     def decode_timed(self, steps: int) -> float:
         ms = c_float()
@@ -278,6 +307,12 @@ class Batch:
         ms = c_float()
         self._check(lib().q35_batch_decode_timed(self._h, steps, ctypes.byref(ms)))
         return float(ms.value)
+
+    def launch_count(self, reset: bool = False) -> int:
+        """Kernel launches of the batch's decode graphs since the last reset."""
+        n = c_uint64()
+        self._check(lib().q35_batch_launch_count(self._h, 1 if reset else 0, ctypes.byref(n)))
+        return int(n.value)
 
     def close(self) -> None:
         if self._h:

@@ -97,6 +97,28 @@ void q35_close(q35_session* s);
 /* Tokens consumed so far (Model::position, model.rs:32). */
 uint32_t q35_position(const q35_session* s);
 
+/* Context capacity of the session in tokens (model.rs:8, CAPACITY): the
+ * bound of generate's "invalid output length" and "context capacity
+ * exceeded" checks (model.rs:98-113). */
+uint32_t q35_capacity(const q35_session* s);
+
+/* The pending token (Model::pending, model.rs:32): the last emitted id, which
+ * the next q35_generate(reset=0) consumes first. Q35_EINVAL when the session
+ * holds no continuation state. */
+int q35_pending(const q35_session* s, uint32_t* token);
+
+/* Validates session options as q35_open does, without a device or a model
+ * (host arithmetic only): Q35_OK, or Q35_EINVAL with the message q35_open
+ * would give (e.g. "capacity must be a positive multiple of 64"). No
+ * counterpart in the reference, whose capacity is a constant. */
+int q35_check_opts(const q35_opts* opts, char* err, size_t err_len);
+
+/* Kernel launches the session's decode steps have enqueued since the last
+ * reset (the kernel nodes of each replayed decode graph, counted when the
+ * graph was captured); reset != 0 clears the count after reading it.
+ * Benchmark aid, no counterpart in the reference. */
+int q35_launch_count(q35_session* s, int reset, uint64_t* launches);
+
 /* Copy the device state to host memory for checking: per attention layer
  * (6) K and V caches, converted to position order and truncated to the first
  * `pos` positions (layout [2][pos][256] each), per GDN layer (18) recurrent state
@@ -174,6 +196,9 @@ int q35_batch_decode(q35_batch* b, size_t steps, uint32_t* out_tokens);
 /* As q35_batch_decode, tokens left on the device; device time in ms. */
 int q35_batch_decode_timed(q35_batch* b, size_t steps, float* ms);
 const char* q35_batch_last_error(const q35_batch* b);
+/* Kernel launches of the batch's decode graphs since the last reset (as
+ * q35_launch_count). */
+int q35_batch_launch_count(q35_batch* b, int reset, uint64_t* launches);
 void q35_batch_destroy(q35_batch* b);
 
 /* Device-clock timing of the attention launches (benchmark aid, no
@@ -281,14 +306,32 @@ int q35_op_attn_decode(const uint16_t* q_raw, const uint16_t* k_raw, const uint1
                        uint16_t* vcache, uint32_t capacity, uint32_t pos, uint16_t* gated,
                        void* workspace, void* stream);
 
+/* Status of an op call's bounded device waits. Every op runs
+ * asynchronously; a wait inside it that gives up (after 2^24 polls) lets the
+ * kernel finish and records a site code in the op's workspace instead of
+ * hanging the stream. This waits for `stream`, then reads that word:
+ * Q35_OK, or Q35_ETIMEOUT with *site (may be NULL) set to the code; the word
+ * is cleared by the op's next call on the same workspace. kind:
+ * Q35_OPWS_CTL for the workspaces of q35_op_gdn_step, q35_op_attn_decode,
+ * q35_op_head_argmax, q35_op_greedy, q35_op_prompt_gdn and
+ * q35_op_prompt_attention (a control block first), with workspace NULL for
+ * q35_op_attn_decode_noalloc's scratch on the current device (after its
+ * first call there); Q35_OPWS_QGEMM for q35_op_qgemm_q4's workspace. No
+ * counterpart in the reference, whose Metal waits are unbounded. */
+#define Q35_OPWS_CTL 0u
+#define Q35_OPWS_QGEMM 1u
+int q35_op_status(const void* workspace, uint32_t kind, uint32_t* site, void* stream);
+
 /* Allocation-free form of q35_op_attn_decode, for callers that cannot call
  * cudaMalloc or hand out a workspace (no counterpart in the reference: its
  * Metal host allocates every buffer itself). Same arguments and results as
  * q35_op_attn_decode, minus the workspace: the scratch is a 576 KiB array in
  * the library's device image, held by every device that loads the library
- * until exit (this op needs 528,640 bytes of it at any context length; a
- * larger need is rejected). The first call on a device looks up the array's
- * address and sets kernel attributes, so make it before any stream capture.
+ * until exit (this op uses 528,896 bytes of it at any context length; the
+ * build fails if the layout outgrows the array). The first call on a device
+ * looks up the array's address and sets kernel attributes, so make it before
+ * any stream capture; the address is kept per device number, so calls after
+ * a cudaDeviceReset of that device are unsupported.
  * All calls on a device share the array: calls that overlap on the GPU race.
  * Rejected arguments return Q35_EINVAL with a message in err (may be NULL). */
 int q35_op_attn_decode_noalloc(const uint16_t* q_raw, const uint16_t* k_raw,

@@ -18,13 +18,19 @@ LIB_PATH = os.path.join(HERE, "libq35oracle.so")
 VOCAB = 248320
 
 
+ROOT = os.path.dirname(HERE)
+SYNTH_SRC = os.path.join(ROOT, "enginesmith-qwen35-08b-long-decode-m5max-round005_b200", "csrc", "q35_synth.cpp")
+
+
 def build() -> None:
-    """Compile the oracle with g++ (no GPU needed)."""
-    src = os.path.join(HERE, "q35_oracle.cpp")
-    if os.path.exists(LIB_PATH) and os.path.getmtime(LIB_PATH) >= os.path.getmtime(src):
+    """Compile the oracle (and the synthetic-model writer it carries) with
+    g++ (no GPU needed)."""
+    srcs = [os.path.join(HERE, "q35_oracle.cpp"), SYNTH_SRC]
+    if os.path.exists(LIB_PATH) and all(os.path.getmtime(LIB_PATH) >= os.path.getmtime(s) for s in srcs
+                                        if os.path.exists(s)):
         return
     subprocess.check_call(["g++", "-std=c++17", "-O2", "-fPIC", "-shared", "-ffp-contract=off",
-                           "-pthread", "-o", LIB_PATH, src])
+                           "-pthread", "-I", os.path.join(ROOT, "include"), "-o", LIB_PATH, *srcs])
 
 
 _lib = None
@@ -38,6 +44,7 @@ def lib() -> ctypes.CDLL:
         P = c_void_p
         sig = {
             "orc_set_threads": (None, [c_int]),
+            "q35_write_synthetic_model": (c_int, [c_char_p, ctypes.c_uint64, c_char_p, ctypes.c_size_t]),
             "orc_get_threads": (c_int, []),
             "orc_f2bf": (c_uint16, [c_float]),
             "orc_bf2f": (c_float, [c_uint16]),
@@ -89,6 +96,16 @@ def lib() -> ctypes.CDLL:
 
 def _p(a):
     return None if a is None else c_void_p(a.ctypes.data)
+
+
+def write_synthetic_model(path: str, seed: int) -> None:
+    """The seeded random-init model (config.json + model.safetensors in the
+    MLX layout), byte for byte what the CUDA library's writer produces: the
+    same C++ source is compiled into this library."""
+    err = ctypes.create_string_buffer(1024)
+    rc = lib().q35_write_synthetic_model(path.encode(), seed, err, len(err))
+    if rc != 0:
+        raise RuntimeError(f"synthetic model: {err.value.decode()}")
 
 
 def set_threads(n: int) -> None:

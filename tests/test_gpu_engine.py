@@ -35,11 +35,13 @@ def test_hello(engine):
 
 
 def test_generate_matches_session_api(cuda, engine, synth_model_dir):
+    """The engine's default prompt route is the tensor-core one (as the
+    reference prefills through its GEMM route with no flag)."""
     import q35
     prompt = [11, 2024, 77777, 248319, 5]
     r1 = engine.ask({"id": 2, "op": "generate", "prompt": prompt, "max_tokens": 4, "reset": True})
     r2 = engine.ask({"id": 3, "op": "generate", "prompt": [], "max_tokens": 3, "reset": False})
-    m = q35.Model.load(synth_model_dir, 0, capacity=4096)
+    m = q35.Model.load(synth_model_dir, 0, capacity=4096, tensor_prompt=True)
     try:
         a = m.generate(prompt, 4, True)
         b = m.generate([], 3, False)
@@ -70,6 +72,27 @@ def test_tensor_prompt_flag(cuda, synth_model_dir):
     assert r == {"id": 2, "ok": True, "tokens": want}
 
 
+def test_decode_prompt_flag(cuda, synth_model_dir):
+    """engine --decode-prompt consumes prompts through the decode kernels: the
+    same tokens as the session API's default (bit-exact) route."""
+    import q35
+    import inputs as I
+    prompt = [int(v) for v in I.Rng(32, 2).ints(40, 248320)]
+    e = Engine(synth_model_dir, "--decode-prompt")
+    try:
+        assert e.ask({"id": 1, "op": "hello"})["ok"]
+        r = e.ask({"id": 2, "op": "generate", "prompt": prompt, "max_tokens": 5, "reset": True})
+    finally:
+        e.p.stdin.close()
+        e.p.wait(timeout=60)
+    m = q35.Model.load(synth_model_dir, 0, capacity=4096)
+    try:
+        want = m.generate(prompt, 5, True)
+    finally:
+        m.close()
+    assert r == {"id": 2, "ok": True, "tokens": want}
+
+
 def test_errors_keep_state(cuda, engine):
     base = engine.ask({"id": 4, "op": "generate", "prompt": [7, 8, 9], "max_tokens": 2, "reset": True})
     assert base["ok"]
@@ -82,6 +105,11 @@ def test_errors_keep_state(cuda, engine):
          "context capacity exceeded"),
         ({"id": 12, "op": "generate", "prompt": [1], "max_tokens": 5000, "reset": True}, "invalid output length"),
         ({"id": 13, "op": "generate", "prompt": [1], "max_tokens": 0, "reset": True}, "invalid output length"),
+        # far beyond any buffer: rejected before anything is allocated (model.rs:98)
+        ({"id": 14, "op": "generate", "prompt": [1], "max_tokens": 10 ** 12, "reset": True},
+         "invalid output length"),
+        ({"id": 15, "op": "generate", "prompt": [], "max_tokens": 2 ** 63, "reset": False},
+         "invalid output length"),
     ]
     for req, msg in bad:
         r = engine.ask(req)
@@ -105,3 +133,56 @@ def test_unknown_op_and_bad_json(engine):
 def test_eof_exits_cleanly(engine):
     engine.p.stdin.close()
     assert engine.p.wait(timeout=60) == 0
+
+
+def test_long_prompt_lines(cuda, synth_model_dir):
+    """JSON lines as long as the protocol allows (docs/protocol.md: prompts up
+    to 524,288 ids): at the default capacity 262,144 a 262,144-id prompt with
+    max_tokens 1 fits exactly (prompt + count - 1 <= capacity, model.rs:101)
+    and a 524,288-id prompt is refused without losing the state."""
+    import inputs as I
+    import q35
+    e = subprocess.Popen([q35.ENGINE_PATH, "--model", synth_model_dir], stdin=subprocess.PIPE,
+                         stdout=subprocess.PIPE, text=True, bufsize=1 << 20)
+    ask = Engine.ask.__get__(type("E", (), {"p": e})())
+    try:
+        assert ask({"id": 1, "op": "hello"})["ok"]
+        ids = [int(v) for v in I.Rng(33, 2).ints(524288, 248320)]
+        r = ask({"id": 2, "op": "generate", "prompt": ids[:262144], "max_tokens": 1, "reset": True})
+        assert r["ok"] and len(r["tokens"]) == 1 and 0 <= r["tokens"][0] < 248320
+        r = ask({"id": 3, "op": "generate", "prompt": ids[:262144], "max_tokens": 2, "reset": True})
+        assert r == {"id": 3, "ok": False, "error": "context capacity exceeded"}
+        r = ask({"id": 4, "op": "generate", "prompt": ids, "max_tokens": 1, "reset": True})
+        assert r == {"id": 4, "ok": False, "error": "context capacity exceeded"}
+        # the 262,144-token state is full: a continuation of one more token is refused too
+        r = ask({"id": 5, "op": "generate", "prompt": [], "max_tokens": 1, "reset": False})
+        assert r == {"id": 5, "ok": False, "error": "context capacity exceeded"}
+        r = ask({"id": 6, "op": "generate", "prompt": ids[:7], "max_tokens": 3, "reset": True})
+        assert r["ok"] and len(r["tokens"]) == 3
+    finally:
+        e.stdin.close()
+        assert e.wait(timeout=120) == 0
+
+
+def test_eof_during_long_continuation(cuda, synth_model_dir):
+    """Closing stdin 50 ms into an 8,192-token continuation stops the engine
+    promptly with exit code 0 and no reply (source/src/main.rs:17-25; the
+    reference measured 22.6 ms from the close to the exit)."""
+    import time
+    import q35
+    e = subprocess.Popen([q35.ENGINE_PATH, "--model", synth_model_dir, "--capacity", "16384"],
+                         stdin=subprocess.PIPE, stdout=subprocess.PIPE, text=True, bufsize=1)
+    ask = Engine.ask.__get__(type("E", (), {"p": e})())
+    assert ask({"id": 1, "op": "hello"})["ok"]
+    assert ask({"id": 2, "op": "generate", "prompt": [5, 6, 7], "max_tokens": 1, "reset": True})["ok"]
+    e.stdin.write(json.dumps({"id": 3, "op": "generate", "prompt": [], "max_tokens": 8192, "reset": False}) + "\n")
+    e.stdin.flush()
+    time.sleep(0.05)
+    t0 = time.perf_counter()
+    e.stdin.close()
+    rc = e.wait(timeout=60)
+    dt = time.perf_counter() - t0
+    rest = e.stdout.read()
+    print(f"engine exit {dt * 1e3:.1f} ms after end of input")
+    assert rc == 0 and rest == ""
+    assert dt < 0.25, dt

@@ -56,3 +56,46 @@ def test_probe_rejects_bad_arguments(cuda):
     import torch
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     assert q35.diag_bounded_wait(0, err) == q35.EINVAL
+
+
+def test_op_status_reports_recorded_waits(cuda):
+    """q35_op_status reads the bounded-wait word an asynchronous op leaves in
+    its workspace: Q35_OK after a clean call; Q35_ETIMEOUT with the site code
+    once a site is recorded there (host-side injection, as an expired wait
+    would record it); the op's next call clears it."""
+    import ctypes
+    import q35
+    import torch
+    lib = q35.lib()
+    lib.q35_op_status.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.POINTER(ctypes.c_uint32),
+                                  ctypes.c_void_p]
+    lib.q35_op_status.restype = ctypes.c_int
+    site = ctypes.c_uint32(99)
+    st = torch.cuda.current_stream().cuda_stream
+    rng = I.Rng(41)
+    cap = 128
+    T = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).cuda()
+    q_raw, k_raw, v_raw = (T(I.f2bf(rng.normal(n))) for n in (4096, 512, 512))
+    qg, kg = T(I.f2bf(1 + 0.1 * rng.normal(256))), T(I.f2bf(1 + 0.1 * rng.normal(256)))
+    kc = torch.zeros(2 * cap * 256, dtype=torch.int16, device="cuda")
+    vc = torch.zeros_like(kc)
+    ws = q35.workspace("attn")
+    q35.attn_decode(q_raw, k_raw, v_raw, qg, kg, kc, vc, cap, 0, ws=ws)
+    assert lib.q35_op_status(ws.data_ptr(), 0, ctypes.byref(site), st) == q35.OK and site.value == 0
+    ws.view(torch.int32)[3] = 2  # Ctl::err sits after three 32-bit words
+    assert lib.q35_op_status(ws.data_ptr(), 0, ctypes.byref(site), st) == q35.ETIMEOUT and site.value == 2
+    q35.attn_decode(q_raw, k_raw, v_raw, qg, kg, kc, vc, cap, 1, ws=ws)
+    assert lib.q35_op_status(ws.data_ptr(), 0, ctypes.byref(site), st) == q35.OK
+    # the GEMM's word: after its tile counters
+    w, s, b, _ = I.config1(42)
+    x = T(I.f2bf(rng.normal(8 * 1024)))
+    Tw = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(
+        {np.uint16: np.int16, np.uint32: np.int32}[a.dtype.type])).cuda()
+    gws = torch.empty(int(lib.q35_op_qgemm_workspace_bytes(8, 3584, 1024)), dtype=torch.uint8, device="cuda")
+    q35.qgemm_q4(Tw(w), Tw(s), Tw(b), x.view(8, 1024), ws=gws)
+    assert lib.q35_op_status(gws.data_ptr(), 1, ctypes.byref(site), st) == q35.OK
+    gws.view(torch.int32)[4096] = 8
+    assert lib.q35_op_status(gws.data_ptr(), 1, ctypes.byref(site), st) == q35.ETIMEOUT and site.value == 8
+    q35.qgemm_q4(Tw(w), Tw(s), Tw(b), x.view(8, 1024), ws=gws)
+    assert lib.q35_op_status(gws.data_ptr(), 1, None, st) == q35.OK
+    assert lib.q35_op_status(ws.data_ptr(), 7, None, st) == q35.EINVAL

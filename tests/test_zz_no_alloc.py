@@ -2,8 +2,9 @@
 against the workspace entry point (q35_op_attn_decode), through the C ABI.
 
 Two calls in a row share the library's static scratch: a 1,500-key call on
-the split route (64 chains, bf16 partials) leaves its partials behind, then a
-700-key call on the short route (32 chains) must not see them. Each call's
+the split route (64 chains from 1,024 keys on, f32 partials) leaves its
+partials behind, then a 700-key call on the short route (32 chains below
+1,024 keys, f32 partials) must not see them. Each call's
 gated output and K/V append must equal the workspace entry point's bit for
 bit (the tolerance every attention test here uses), on identical copies of
 the inputs. Collected last so it also runs after every other test's kernels.
