@@ -10,6 +10,7 @@
 // input, cancels the running request (main.rs:17-25); replies go to stdout
 // only, diagnostics to stderr.
 #include <atomic>
+#include <chrono>
 #include <condition_variable>
 #include <cstdio>
 #include <cstdlib>
@@ -52,6 +53,23 @@ struct LineQueue {
     cv.notify_all();
   }
 };
+
+// Q35_ENGINE_TRACE=1: milliseconds from the end of input to each shutdown
+// step, on stderr (diagnostics only).
+std::atomic<int64_t> g_eof_ns{0};
+bool trace_on() {
+  static const bool on = std::getenv("Q35_ENGINE_TRACE") != nullptr;
+  return on;
+}
+int64_t now_ns() {
+  return std::chrono::duration_cast<std::chrono::nanoseconds>(
+             std::chrono::steady_clock::now().time_since_epoch())
+      .count();
+}
+void trace(const char* what) {
+  if (trace_on() && g_eof_ns.load())
+    std::fprintf(stderr, "engine: %s %.2f ms after end of input\n", what, (now_ns() - g_eof_ns.load()) * 1e-6);
+}
 
 std::string error_reply(const std::string& id, const std::string& msg) {
   std::string out = "{\"id\":" + id + ",\"ok\":false,\"error\":";
@@ -101,6 +119,7 @@ int main(int argc, char** argv) {
     // Disconnect stops inference after the currently queued GPU work. The
     // cancel is published before the flag, so main never frees the session
     // while the reader still uses it.
+    g_eof_ns.store(now_ns());
     q35_cancel(s);
     eof.store(true);
     lines.close();
@@ -157,7 +176,10 @@ int main(int argc, char** argv) {
           tokens.assign(size_t(count), 0);
           int rc = q35_generate(s, prompt.data(), prompt.size(), size_t(count), rs->b ? 1 : 0,
                                 tokens.data());
-          if (eof.load()) break;
+          if (eof.load()) {
+            trace("request stopped");
+            break;
+          }
           if (rc != Q35_OK) {
             reply = error_reply(id, q35_last_error(s));
           } else {
@@ -179,6 +201,8 @@ int main(int argc, char** argv) {
     std::fwrite(reply.data(), 1, reply.size(), stdout);
     std::fflush(stdout);
   }
+  trace("loop left");
   q35_close(s);
+  trace("session closed");
   return 0;
 }

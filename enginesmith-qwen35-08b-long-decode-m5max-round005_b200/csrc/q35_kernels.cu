@@ -59,15 +59,16 @@ __device__ __forceinline__ void gdn_conv_channel(int c, uint16_t raw, uint16_t* 
 }
 
 
-// 256 threads and <= 64 registers: up to four CTAs (of consecutive launches)
-// share an SM, so a launch's weight prefetch overlaps its predecessor.
 constexpr int kQmvThreads = 512;
+
+// Registers per thread of the two matvec launch classes (launch_qmv).
+constexpr int qmv_class_regs(int epi) { return epi == kEpiResAdd ? 72 : 56; }
 
 // Specialised per (prologue, epilogue) pair at compile time, so a launch runs
 // only its own code (smaller instruction footprint, no runtime branching on
 // the variant); PRO and EPI must equal PRO and EPI.
 template <int PRO, int EPI>
-__global__ void __launch_bounds__(kQmvThreads, 1) k_qmv(const __grid_constant__ QmvArgs a) {
+__global__ void __maxnreg__(qmv_class_regs(EPI)) k_qmv(const __grid_constant__ QmvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int kWarps = kQmvThreads / 32;
@@ -737,7 +738,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn(const __grid_constant_
 // rank order: M = max m_q, f_q = e^(m_q - M), o = sum f_q o_q / sum f_q l_q.
 // Every rank merges the same records in the same order, so all ranks get
 // the same bits. Returns the lane's normalised value.
-constexpr unsigned long long kXWaitNs = 10ull * 1000 * 1000 * 1000;  // 10 s
+constexpr unsigned long long kXWaitNs = 10ull * 1000 * 1000 * 1000;  // default bound: 10 s
 __device__ __noinline__ float x_exchange(const AttnArgs& a, float r, float m, float l, uint32_t pos) {
   constexpr float kMin = -3.4028234663852886e38f;
   __shared__ int xfail;
@@ -763,12 +764,13 @@ __device__ __noinline__ float x_exchange(const AttnArgs& a, float r, float m, fl
     // after any expired wait of this session (err set) the rest of the
     // queued work falls through instead of waiting again
     const unsigned long long t0 = globaltimer_ns();
+    const unsigned long long limit = a.xwait_ms ? a.xwait_ms * 1000000ull : kXWaitNs;
     while (ld_acquire_sys_u64(f) != tag) {
       if (ld_cg_u32(&a.ctl->err) != 0u) {
         xfail = 1;
         break;
       }
-      if (globaltimer_ns() - t0 > kXWaitNs) {
+      if (globaltimer_ns() - t0 > limit) {
         atomicCAS(&a.ctl->err, 0u, kErrXWait);
         xfail = 1;
         break;
@@ -1427,11 +1429,25 @@ int qmv_max_rows(int K) {
   return r;
 }
 
+// Two resource classes of matvec launches, so that each launch's CTAs fit on
+// the SMs beside its predecessor's (they start, and stream their weights into
+// shared memory, while the predecessor computes) but never beside a CTA of
+// their own launch or class (which made the block scheduler stack a launch's
+// CTAs onto a few SMs):
+//   class X (no residual: qkv/z/a/b, q/k/v, gate/up): >= 115 KB of shared
+//     memory (two never fit in 228 KB) and 512 x 56 registers;
+//   class Y (residual add: the output and down projections): the shared
+//     memory it needs (<= 111 KB at the model's shapes) and 512 x 72
+//     registers (two would need 73,728 of the SM's 65,536).
+// X + Y use exactly the 65,536 registers and fit the shared memory. The
+// model's chain alternates X and Y (qkv, [recurrence or attention], out,
+// gate/up, down, next qkv ...).
 cudaError_t launch_qmv(const QmvArgs& a, cudaStream_t st, bool pdl) {
   const int grid = (a.units + a.units_per_cta - 1) / a.units_per_cta;
   void (*kern)(QmvArgs) = qmv_kernel(a.pro, a.epi);
   if (!kern) return cudaErrorInvalidValue;
-  return launch_ex(kern, dim3(grid), dim3(kQmvThreads), spread(qmv_smem_bytes(a)), st, pdl, a);
+  const size_t need = qmv_smem_bytes(a);
+  return launch_ex(kern, dim3(grid), dim3(kQmvThreads), a.epi == kEpiResAdd ? need : spread(need), st, pdl, a);
 }
 cudaError_t launch_recur(const RecurArgs& a, cudaStream_t st, bool pdl) {
   return launch_ex(k_gdn_recur, dim3(8, kGdnHeads), dim3(64), kSpreadSmem, st, pdl, a);

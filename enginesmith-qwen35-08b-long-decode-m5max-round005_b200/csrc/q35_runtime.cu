@@ -397,6 +397,7 @@ struct q35_session {
   // sequence split (xworld > 1 once connected): this rank's exchange buffers
   // (records, then flags), the peers' mapped buffers and the device tables
   int xrank = 0, xworld = 1, xpend_world = 0;
+  uint32_t xwait_ms = 0;  // bound of the exchange wait (0: the kernel's 10 s)
   uint8_t* xbuf = nullptr;
   std::vector<void*> xpeer;
   void** xtab = nullptr;  // [xworld] record pointers, then [xworld] flag pointers
@@ -425,6 +426,7 @@ void split_attn_args(const q35_session* s, AttnArgs& at, int ai) {
   at.xrank = s->xrank;
   at.xworld = s->xworld;
   at.xlayer = ai;
+  at.xwait_ms = s->xwait_ms;
   at.xrecv = reinterpret_cast<float* const*>(s->xtab);
   at.xflag = reinterpret_cast<unsigned long long* const*>(s->xtab + s->xworld);
 }
@@ -1788,6 +1790,14 @@ int q35_split_connect(q35_session* s, const void* handles) {
 }
 
 int q35_split_world(const q35_session* s) { return s ? s->xworld : 0; }
+
+int q35_split_set_wait(q35_session* s, uint32_t ms) {
+  if (!s) return Q35_EINVAL;
+  if (ms < 1 || ms > 600000) return set_err(s, Q35_EINVAL, "split: wait bound must be 1..600000 ms");
+  if (s->xworld > 1) return set_err(s, Q35_EINVAL, "split: set the wait bound before connecting");
+  s->xwait_ms = ms;
+  return Q35_OK;
+}
 
 int q35_diag_bounded_wait(uint32_t polls, uint32_t* err_dev, void* stream) {
   if (!err_dev || polls == 0) return Q35_EINVAL;

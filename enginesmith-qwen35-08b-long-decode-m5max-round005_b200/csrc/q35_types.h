@@ -169,6 +169,7 @@ struct AttnArgs {
   // (m, l, o) records through every rank's receive buffer (xrecv, xflag:
   // device addresses of each rank's buffers, this rank's included).
   int xrank, xworld, xlayer;
+  uint32_t xwait_ms;  // bound of the wait for the peers' records (0: 10 s)
   float* const* xrecv;
   unsigned long long* const* xflag;
   // batched sessions (launch grid z = session): each session's cache and

@@ -86,6 +86,7 @@ def _load() -> ctypes.CDLL:
         "q35_split_prepare": (c_int, [P, c_int, c_int, P]),
         "q35_split_connect": (c_int, [P, P]),
         "q35_split_world": (c_int, [P]),
+        "q35_split_set_wait": (c_int, [P, c_uint32]),
         "q35_batch_create": (c_int, [POINTER(c_void_p), c_int, POINTER(c_void_p), c_char_p, c_size_t]),
         "q35_batch_create_ex": (c_int, [POINTER(c_void_p), c_int, c_uint32, POINTER(c_void_p), c_char_p, c_size_t]),
         "q35_batch_decode": (c_int, [P, c_size_t, POINTER(c_uint32)]),
@@ -228,6 +229,10 @@ class Model:
         buf = ctypes.create_string_buffer(blob, len(blob))
         self._check(lib().q35_split_connect(self._h, buf))
 
+    def split_set_wait(self, ms: int) -> None:
+        """Bound of the exchange wait for the peers' records (before connecting)."""
+        self._check(lib().q35_split_set_wait(self._h, ms))
+
     @property
     def split_world(self) -> int:
         return int(lib().q35_split_world(self._h))
@@ -257,13 +262,15 @@ class Model:
             pass
 
 
-def split_connect_dist(model, group=None) -> None:
+def split_connect_dist(model, group=None, wait_ms: int = 0) -> None:
     """Sequence-split set-up over torch.distributed, one process per GPU: each
     rank prepares its exchange buffer, the handles are all-gathered in rank
     order (any backend; the handles are plain bytes) and each rank connects.
     Every rank of `group` must call this with its own session."""
     import torch.distributed as dist
     rank, world = dist.get_rank(group), dist.get_world_size(group)
+    if wait_ms:
+        model.split_set_wait(wait_ms)
     mine = model.split_prepare(rank, world)
     handles = [None] * world
     dist.all_gather_object(handles, mine, group=group)

@@ -167,6 +167,12 @@ int q35_force_pending(q35_session* s, uint32_t token);
 int q35_split_prepare(q35_session* s, int rank, int world, void* handle);
 int q35_split_connect(q35_session* s, const void* handles);
 int q35_split_world(const q35_session* s);
+/* Bound, in milliseconds (1..600000), of each attention combine's wait for
+ * the peers' records; 10 s unless set. Call before q35_split_connect (the
+ * decode graphs are captured there). A wait that runs out makes the request
+ * fail with Q35_ETIMEOUT and resets the session; the peers' next exchanges
+ * (which wait for this rank) run out the same way. */
+int q35_split_set_wait(q35_session* s, uint32_t ms);
 
 /* Batched sessions (no counterpart in the reference, whose engine serves one
  * stream): 1..8 sessions of one device, each already holding a continuation

@@ -44,3 +44,26 @@ def test_split_two_gpus(cuda, synth_model_dir, tmp_path):
     assert all(v["logits_equal_b"]), v
     pos = v["position_b"]
     assert v["local_positions_b"] == [(pos + 1) // 2, pos // 2], v
+
+
+def test_split_silent_peer_times_out(cuda, synth_model_dir, tmp_path):
+    """A rank that skips a request: its peer's bounded exchange wait (300 ms
+    here) runs out, the request fails with Q35_ETIMEOUT and resets the
+    session, and a fresh request of both ranks then works and agrees bit for
+    bit. No GPU fault: the waiting kernel gives up and returns."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    out = tmp_path / "timeout.json"
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", Q35_SYNTH_DIR=synth_model_dir)
+    cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
+           os.path.join(HERE, "split_timeout_worker.py"), str(out)]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    v = json.loads(out.read_text())
+    print(json.dumps(v))
+    assert v["timed_out"] and "did not arrive" in v["message"], v
+    assert v["seconds"] < 5.0, v
+    assert v["position_after"] == 0 and v["state_reset"], v
+    assert v["recovered_same_tokens"] and v["recovered_ranks_identical"], v
