@@ -201,8 +201,10 @@ int main(int argc, char** argv) {
     std::fwrite(reply.data(), 1, reply.size(), stdout);
     std::fflush(stdout);
   }
+  // End of input: the running request has drained (q35_generate waits for
+  // its queued work). Leave at once rather than tearing the CUDA context down
+  // by hand, which took ~0.3 s; the driver reclaims the device memory.
   trace("loop left");
-  q35_close(s);
-  trace("session closed");
-  return 0;
+  std::fflush(stdout);
+  std::_Exit(0);
 }

@@ -61,14 +61,11 @@ __device__ __forceinline__ void gdn_conv_channel(int c, uint16_t raw, uint16_t* 
 
 constexpr int kQmvThreads = 512;
 
-// Registers per thread of the two matvec launch classes (launch_qmv).
-constexpr int qmv_class_regs(int epi) { return epi == kEpiResAdd ? 72 : 56; }
-
 // Specialised per (prologue, epilogue) pair at compile time, so a launch runs
 // only its own code (smaller instruction footprint, no runtime branching on
 // the variant); PRO and EPI must equal PRO and EPI.
 template <int PRO, int EPI>
-__global__ void __maxnreg__(qmv_class_regs(EPI)) k_qmv(const __grid_constant__ QmvArgs a) {
+__global__ void __launch_bounds__(kQmvThreads, 1) k_qmv(const __grid_constant__ QmvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int kWarps = kQmvThreads / 32;
@@ -247,16 +244,15 @@ __global__ void __maxnreg__(qmv_class_regs(EPI)) k_qmv(const __grid_constant__ Q
   const int ngroups = (nrows + 3) / 4;
   {
     // a warp's tasks usually share their chunk: its constants are loaded once
-    float4 xx[4], cc[4];
-    float xs = 0.0f;
+    XqPairs kc;
     int cur = -1;
     for (int task = warp; task < ngroups * nch; task += kWarps) {
       const int g = task / nch, c = task % nch;
       if (c != cur) {
-        load_xq(xq, xsum, c, lane, xx, cc, xs);
+        load_xq(xq, xsum, c, lane, kc);
         cur = c;
       }
-      qmv_chunk_core(codes, scl, bia, nrows, 4 * g, c, K, xx, cc, xs, pl, lane);
+      qmv_chunk_core(codes, scl, bia, nrows, 4 * g, c, K, kc, pl, lane);
     }
   }
   __syncthreads();
@@ -1061,10 +1057,9 @@ __global__ void __launch_bounds__(kHeadThreads, 1) k_head(const __grid_constant_
   build_xq(S.xf, kHidden, S.xq, S.xsum);
   __syncthreads();
   // the lane's constants of both 512-wide halves stay in registers
-  float4 xx0[4], cc0[4], xx1[4], cc1[4];
-  float xs0, xs1;
-  load_xq(S.xq, S.xsum, 0, lane, xx0, cc0, xs0);
-  load_xq(S.xq, S.xsum, 1, lane, xx1, cc1, xs1);
+  XqPairs k0, k1;
+  load_xq(S.xq, S.xsum, 0, lane, k0);
+  load_xq(S.xq, S.xsum, 1, lane, k1);
 
   // Warp w owns rows 4w..4w+3 of every chunk: both 512-wide halves,
   // the cross-lane finish and the logits, with no block barrier. The last
@@ -1077,8 +1072,8 @@ __global__ void __launch_bounds__(kHeadThreads, 1) k_head(const __grid_constant_
     mbar_wait(&S.bar[st], uint32_t(ch / kHeadStages) & 1u, a.ctl, kErrHeadWait);
     const int rows = min(kHeadRowsPerChunk, nrows - ch * kHeadRowsPerChunk);
     if (g0 < rows) {
-      qmv_chunk_core(S.codes[st], S.scl[st], S.bia[st], rows, g0, 0, kHidden, xx0, cc0, xs0, S.pl, lane);
-      qmv_chunk_core(S.codes[st], S.scl[st], S.bia[st], rows, g0, 1, kHidden, xx1, cc1, xs1, S.pl, lane);
+      qmv_chunk_core(S.codes[st], S.scl[st], S.bia[st], rows, g0, 0, kHidden, k0, S.pl, lane);
+      qmv_chunk_core(S.codes[st], S.scl[st], S.bia[st], rows, g0, 1, kHidden, k1, S.pl, lane);
     }
     __syncwarp();
     if (lane == 0) {
@@ -1429,25 +1424,11 @@ int qmv_max_rows(int K) {
   return r;
 }
 
-// Two resource classes of matvec launches, so that each launch's CTAs fit on
-// the SMs beside its predecessor's (they start, and stream their weights into
-// shared memory, while the predecessor computes) but never beside a CTA of
-// their own launch or class (which made the block scheduler stack a launch's
-// CTAs onto a few SMs):
-//   class X (no residual: qkv/z/a/b, q/k/v, gate/up): >= 115 KB of shared
-//     memory (two never fit in 228 KB) and 512 x 56 registers;
-//   class Y (residual add: the output and down projections): the shared
-//     memory it needs (<= 111 KB at the model's shapes) and 512 x 72
-//     registers (two would need 73,728 of the SM's 65,536).
-// X + Y use exactly the 65,536 registers and fit the shared memory. The
-// model's chain alternates X and Y (qkv, [recurrence or attention], out,
-// gate/up, down, next qkv ...).
 cudaError_t launch_qmv(const QmvArgs& a, cudaStream_t st, bool pdl) {
   const int grid = (a.units + a.units_per_cta - 1) / a.units_per_cta;
   void (*kern)(QmvArgs) = qmv_kernel(a.pro, a.epi);
   if (!kern) return cudaErrorInvalidValue;
-  const size_t need = qmv_smem_bytes(a);
-  return launch_ex(kern, dim3(grid), dim3(kQmvThreads), a.epi == kEpiResAdd ? need : spread(need), st, pdl, a);
+  return launch_ex(kern, dim3(grid), dim3(kQmvThreads), spread(qmv_smem_bytes(a)), st, pdl, a);
 }
 cudaError_t launch_recur(const RecurArgs& a, cudaStream_t st, bool pdl) {
   return launch_ex(k_gdn_recur, dim3(8, kGdnHeads), dim3(64), kSpreadSmem, st, pdl, a);

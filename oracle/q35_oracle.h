@@ -128,6 +128,15 @@ uint32_t orc_session_position(const orc_session* s);
 /* projections and head of later steps with the engine's tensor-core route's
  * numerics (weights dequantised to bf16, dot products exact then rounded) */
 void orc_session_set_gemm(orc_session* s, int on);
+/* Tokens per GEMM launch of the engine route being restated (batch members,
+ * prompt-chunk tokens): with the launch's row tiles it fixes the K split. */
+void orc_session_set_gemm_tokens(orc_session* s, int tokens);
+/* The engine's tensor-core GEMM on T tokens (x [T][K]): y [T][N] before the
+ * bf16 rounding, for a launch of `tiles` 128-row tiles (0: this matrix alone). */
+void orc_qgemm_tc(const uint32_t* w, const uint16_t* s, const uint16_t* b, const uint16_t* x, int T, int N,
+                  int K, int tiles, float* y);
+/* One 16-wide K step of the tensor core's bf16 MMA (f32 accumulator). */
+float tc_step(float acc, const float* p);
 /* attention of later steps as the tensor-core prompt route's (attn_f32_flash) */
 void orc_session_set_flash(orc_session* s, int on);
 /* attention of later steps as the engine's sequence split over `world` ranks */

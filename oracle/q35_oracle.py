@@ -76,6 +76,9 @@ def lib() -> ctypes.CDLL:
             "orc_session_step": (c_uint32, [P, c_uint32, c_int]),
             "orc_session_set_split": (None, [P, c_int]),
             "orc_session_set_gemm": (None, [P, c_int]),
+            "orc_session_set_gemm_tokens": (None, [P, c_int]),
+            "orc_qgemm_tc": (None, [P, P, P, P, c_int, c_int, c_int, c_int, P]),
+            "tc_step": (c_float, [c_float, P]),
             "orc_session_set_flash": (None, [P, c_int]),
             "orc_session_logits": (None, [P, P]),
             "orc_session_lse": (c_uint16, [P]),
@@ -154,6 +157,23 @@ def qmv_gemm_f32(w, s, b, x) -> np.ndarray:
     y = np.zeros(n, np.float32)
     lib().orc_qmv_gemm_f32(_p(w), _p(s), _p(b), _p(x), n, k, _p(y))
     return y
+
+
+def qgemm_tc(w, s, b, x, tiles: int = 0) -> np.ndarray:
+    """The engine's tensor-core GEMM (q35_op_qgemm_q4) restated: x [T][K]
+    bf16 -> y [T][N] f32 before the bf16 output rounding."""
+    T, K = x.shape
+    N = w.shape[0]
+    y = np.zeros((T, N), np.float32)
+    lib().orc_qgemm_tc(_p(w), _p(s), _p(b), _p(np.ascontiguousarray(x)), T, N, K, tiles, _p(y))
+    return y
+
+
+def tc_step(acc: float, p) -> float:
+    """One 16-wide MMA step of the tensor core (f32 accumulator)."""
+    p = np.ascontiguousarray(p, np.float32)
+    assert p.size == 16
+    return float(lib().tc_step(acc, _p(p)))
 
 
 def rms_norm(x, gain, eps=1e-6) -> np.ndarray:
@@ -298,6 +318,11 @@ class OracleSession:
         """Projections and head of later steps with the engine's tensor-core
         route's numerics (bf16-dequantised weights, exact dot products)."""
         lib().orc_session_set_gemm(self.s, 1 if on else 0)
+
+    def set_gemm_tokens(self, tokens: int) -> None:
+        """Tokens per GEMM launch of the engine route restated by set_gemm
+        (the batch's member count, or the prompt chunk's token count)."""
+        lib().orc_session_set_gemm_tokens(self.s, tokens)
 
     def set_flash(self, on: bool) -> None:
         """Attention of later steps with the engine's tensor-core prompt

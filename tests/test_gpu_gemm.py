@@ -78,3 +78,32 @@ def test_qgemm_rejects_bad_arguments(cuda):
         q35.qgemm_q4(W, S, B, torch.zeros((4097, 1024), dtype=torch.uint16, device="cuda"))
     with pytest.raises(q35.Q35Error):
         q35.qgemm_q4(W[:, :4], S, B, X)  # k = 32, not a multiple of 512
+
+
+@pytest.mark.parametrize("t,n,k", [
+    (1, 3584, 1024), (8, 1024, 3584), (17, 1024, 2048), (64, 7168, 1024), (300, 1000, 2048), (5, 512, 4096),
+])
+def test_qgemm_bitexact_with_oracle_restatement(cuda, oracle_threads, t, n, k):
+    """The GEMM equals the oracle's restatement of it bit for bit (weights
+    bf16(s q + b) rounded once; per K split, 16-wide MMA steps with the
+    tensor core's measured accumulation rule, tc_step; split partials summed
+    in order; bf16 output, and the residual form)."""
+    import torch
+    import q35
+    O = oracle_threads
+    w, s, b, x = make(n, k, t, seed=7 * n + k + t)
+    W, S, B, X = w.cuda(), s.cuda().view(torch.uint16), b.cuda().view(torch.uint16), x.cuda().view(torch.uint16)
+    y = q35.qgemm_q4(W, S, B, X).cpu().numpy().view(np.uint16)
+    torch.cuda.synchronize()
+    wn = w.numpy().view(np.uint32)
+    sn, bn, xn = (a.view(torch.int16).numpy().view(np.uint16) for a in (s, b, x))
+    f = O.qgemm_tc(wn, sn, bn, xn)
+    want = O.f2bf(f)
+    bad = int(np.count_nonzero(y != want))
+    assert bad == 0, f"{bad} of {y.size} outputs differ"
+    res = torch.randn((t, n)).to(torch.bfloat16)
+    y2 = res.clone().view(torch.uint16).cuda()
+    q35.qgemm_q4(W, S, B, X, residual=y2, out=y2)
+    rn = res.view(torch.int16).numpy().view(np.uint16)
+    want2 = O.f2bf(O.bf2f(rn) + O.bf2f(want))
+    assert np.array_equal(y2.cpu().numpy().view(np.uint16), want2)
