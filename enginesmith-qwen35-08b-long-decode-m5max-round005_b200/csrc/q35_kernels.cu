@@ -244,15 +244,16 @@ __global__ void __launch_bounds__(kQmvThreads, 1) k_qmv(const __grid_constant__ 
   const int ngroups = (nrows + 3) / 4;
   {
     // a warp's tasks usually share their chunk: its constants are loaded once
-    XqPairs kc;
+    float4 xx[4], cc[4];
+    float xs = 0.0f;
     int cur = -1;
     for (int task = warp; task < ngroups * nch; task += kWarps) {
       const int g = task / nch, c = task % nch;
       if (c != cur) {
-        load_xq(xq, xsum, c, lane, kc);
+        load_xq(xq, xsum, c, lane, xx, cc, xs);
         cur = c;
       }
-      qmv_chunk_core(codes, scl, bia, nrows, 4 * g, c, K, kc, pl, lane);
+      qmv_chunk_core(codes, scl, bia, nrows, 4 * g, c, K, xx, cc, xs, pl, lane);
     }
   }
   __syncthreads();
@@ -1057,9 +1058,10 @@ __global__ void __launch_bounds__(kHeadThreads, 1) k_head(const __grid_constant_
   build_xq(S.xf, kHidden, S.xq, S.xsum);
   __syncthreads();
   // the lane's constants of both 512-wide halves stay in registers
-  XqPairs k0, k1;
-  load_xq(S.xq, S.xsum, 0, lane, k0);
-  load_xq(S.xq, S.xsum, 1, lane, k1);
+  float4 xx0[4], cc0[4], xx1[4], cc1[4];
+  float xs0, xs1;
+  load_xq(S.xq, S.xsum, 0, lane, xx0, cc0, xs0);
+  load_xq(S.xq, S.xsum, 1, lane, xx1, cc1, xs1);
 
   // Warp w owns rows 4w..4w+3 of every chunk: both 512-wide halves,
   // the cross-lane finish and the logits, with no block barrier. The last
@@ -1072,8 +1074,8 @@ __global__ void __launch_bounds__(kHeadThreads, 1) k_head(const __grid_constant_
     mbar_wait(&S.bar[st], uint32_t(ch / kHeadStages) & 1u, a.ctl, kErrHeadWait);
     const int rows = min(kHeadRowsPerChunk, nrows - ch * kHeadRowsPerChunk);
     if (g0 < rows) {
-      qmv_chunk_core(S.codes[st], S.scl[st], S.bia[st], rows, g0, 0, kHidden, k0, S.pl, lane);
-      qmv_chunk_core(S.codes[st], S.scl[st], S.bia[st], rows, g0, 1, kHidden, k1, S.pl, lane);
+      qmv_chunk_core(S.codes[st], S.scl[st], S.bia[st], rows, g0, 0, kHidden, xx0, cc0, xs0, S.pl, lane);
+      qmv_chunk_core(S.codes[st], S.scl[st], S.bia[st], rows, g0, 1, kHidden, xx1, cc1, xs1, S.pl, lane);
     }
     __syncwarp();
     if (lane == 0) {

@@ -16,9 +16,8 @@
 // without converting integers: the masked half-word OR'd into 0x4B000000 is
 // the float 2^23 + m, and fmaf(2^23 + m, xx, -2^23 * xx) = round(m * xx) in
 // one instruction. Products and sums are otherwise separately rounded
-// (__fadd_rn / __fmul_rn, and the packed __ffma2_rn / __fadd2_rn that carry
-// two adjacent half-words' identical sequences side by side), so the result
-// equals the CPU restatement bit for bit.
+// (__fadd_rn / __fmul_rn), so the result equals the CPU restatement bit for
+// bit.
 #pragma once
 #include "q35_dev.cuh"
 
@@ -101,54 +100,21 @@ Q35_DEV float4 bf4(uint2 u) { return make_float4(bf_lo(u.x), bf_hi(u.x), bf_lo(u
 
 Q35_DEV float magic(uint32_t bits) { return __uint_as_float(bits | 0x4b000000u); }
 
-// The lane's chunk constants, paired for packed f32x2 arithmetic: x[p][j]
-// holds (xx_j of half 2p, xx_j of half 2p + 1) (the four activations of a
-// 16-bit half, scaled by 1, 1/16, 1/256, 1/4096), c[p][j] = -2^23 x[p][j]
-// (exact), xs the lane's activation sum.
-struct XqPairs {
-  float2 x[2][4], c[2][4];
-  float xs;
-};
-
-// The lane's constants of chunk c from the shared image built by build_xq.
-Q35_DEV void load_xq(const float4* xq, const float* xsum, int c, int lane, XqPairs& k) {
-  float4 xx[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) xx[i] = xq[(size_t(c) * 4 + i) * 32 + lane];
-#pragma unroll
-  for (int p = 0; p < 2; ++p) {
-    const float4 a = xx[2 * p], b = xx[2 * p + 1];
-    k.x[p][0] = make_float2(a.x, b.x);
-    k.x[p][1] = make_float2(a.y, b.y);
-    k.x[p][2] = make_float2(a.z, b.z);
-    k.x[p][3] = make_float2(a.w, b.w);
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-      k.c[p][j] = make_float2(__fmul_rn(-kTwo23, k.x[p][j].x), __fmul_rn(-kTwo23, k.x[p][j].y));
-  }
-  k.xs = xsum[c * 32 + lane];
-}
-
-// ((t0 + t1) + t2) + t3 of two 16-bit halves at once (low 16 bits of lo and
-// of hi), one per f32x2 component: each component is exactly the scalar
-// sequence t_j = fma(2^23 + m_j, xx_j, -2^23 xx_j) = round(m_j xx_j), then
-// the three adds, every operation rounded to nearest on its own (a packed
-// fma or add rounds each component as the scalar one does).
-Q35_DEV float2 pair_dot(uint32_t lo, uint32_t hi, const float2 (&x)[4], const float2 (&c)[4]) {
-  const float2 t0 = __ffma2_rn(make_float2(magic(lo & 0x000fu), magic(hi & 0x000fu)), x[0], c[0]);
-  const float2 t1 = __ffma2_rn(make_float2(magic(lo & 0x00f0u), magic(hi & 0x00f0u)), x[1], c[1]);
-  const float2 t2 = __ffma2_rn(make_float2(magic(lo & 0x0f00u), magic(hi & 0x0f00u)), x[2], c[2]);
-  const float2 t3 = __ffma2_rn(make_float2(magic(lo & 0xf000u), magic(hi & 0xf000u)), x[3], c[3]);
-  return __fadd2_rn(__fadd2_rn(__fadd2_rn(t0, t1), t2), t3);
+// ((t0 + t1) + t2) + t3 of one 16-bit half (low 16 bits of u).
+Q35_DEV float half_dot(uint32_t u, const float4& xx, const float4& cc) {
+  const float t0 = fmaf(magic(u & 0x000fu), xx.x, cc.x);
+  const float t1 = fmaf(magic(u & 0x00f0u), xx.y, cc.y);
+  const float t2 = fmaf(magic(u & 0x0f00u), xx.z, cc.z);
+  const float t3 = fmaf(magic(u & 0xf000u), xx.w, cc.w);
+  return __fadd_rn(__fadd_rn(__fadd_rn(t0, t1), t2), t3);
 }
 
 // The lane's chunk terms s*dotq + xs*b of rows [r0, r0+4) for chunk c (512
 // wide), with the lane's chunk constants in registers; rows at or beyond
-// nrows give 0. dotq sums the four half-word dots in order from +0, as the
-// reference's loop does (linear.metal:57-66).
+// nrows give 0.
 Q35_DEV void qmv_rows_terms(const uint32_t* codes, const uint16_t* scl, const uint16_t* bia,
-                            int nrows, int r0, int c, int K, const XqPairs& k, int lane,
-                            float (&term)[4]) {
+                            int nrows, int r0, int c, int K, const float4 (&xx)[4],
+                            const float4 (&cc)[4], float xs, int lane, float (&term)[4]) {
   const int KW = K / 8, KG = K / 64;
   const int w0 = 64 * c + 2 * lane;
   const int g = 8 * c + (lane >> 2);
@@ -163,13 +129,12 @@ Q35_DEV void qmv_rows_terms(const uint32_t* codes, const uint16_t* scl, const ui
   }
 #pragma unroll
   for (int r = 0; r < 4; ++r) {
-    const float2 s01 = pair_dot(q[r].x, q[r].x >> 16, k.x[0], k.c[0]);
-    const float2 s23 = pair_dot(q[r].y, q[r].y >> 16, k.x[1], k.c[1]);
-    float dotq = __fadd_rn(0.0f, s01.x);
-    dotq = __fadd_rn(dotq, s01.y);
-    dotq = __fadd_rn(dotq, s23.x);
-    dotq = __fadd_rn(dotq, s23.y);
-    const float t = __fadd_rn(__fmul_rn(sc[r], dotq), __fmul_rn(k.xs, bi[r]));
+    float dotq = 0.0f;
+    dotq = __fadd_rn(dotq, half_dot(q[r].x, xx[0], cc[0]));
+    dotq = __fadd_rn(dotq, half_dot(q[r].x >> 16, xx[1], cc[1]));
+    dotq = __fadd_rn(dotq, half_dot(q[r].y, xx[2], cc[2]));
+    dotq = __fadd_rn(dotq, half_dot(q[r].y >> 16, xx[3], cc[3]));
+    const float t = __fadd_rn(__fmul_rn(sc[r], dotq), __fmul_rn(xs, bi[r]));
     term[r] = r0 + r < nrows ? t : 0.0f;
   }
 }
@@ -178,13 +143,36 @@ Q35_DEV void qmv_rows_terms(const uint32_t* codes, const uint16_t* scl, const ui
 // [r0, r0+4) (those < nrows) of the CTA's smem image, chunk c (512 wide).
 // Writes each lane's chunk term s*dotq + xs*b to pl[(row * nch + c) * 32 + lane].
 Q35_DEV void qmv_chunk_core(const uint32_t* codes, const uint16_t* scl, const uint16_t* bia,
-                            int nrows, int r0, int c, int K, const XqPairs& k, float* pl, int lane) {
+                            int nrows, int r0, int c, int K, const float4 (&xx)[4],
+                            const float4 (&cc)[4], float xs, float* pl, int lane) {
   const int nch = K / 512;
   float term[4];
-  qmv_rows_terms(codes, scl, bia, nrows, r0, c, K, k, lane, term);
+  qmv_rows_terms(codes, scl, bia, nrows, r0, c, K, xx, cc, xs, lane, term);
 #pragma unroll
   for (int r = 0; r < 4; ++r)
     if (r0 + r < nrows) pl[(size_t(r0 + r) * nch + c) * 32 + lane] = term[r];
+}
+
+// The lane's constants of chunk c from the shared image built by build_xq.
+Q35_DEV void load_xq(const float4* xq, const float* xsum, int c, int lane, float4 (&xx)[4],
+                     float4 (&cc)[4], float& xs) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    xx[i] = xq[(size_t(c) * 4 + i) * 32 + lane];
+    cc[i] = make_float4(__fmul_rn(-kTwo23, xx[i].x), __fmul_rn(-kTwo23, xx[i].y),
+                        __fmul_rn(-kTwo23, xx[i].z), __fmul_rn(-kTwo23, xx[i].w));
+  }
+  xs = xsum[c * 32 + lane];
+}
+
+// One warp task reading the chunk constants from shared memory.
+Q35_DEV void qmv_chunk_task(const uint32_t* codes, const uint16_t* scl, const uint16_t* bia,
+                            int nrows, int r0, int c, int K, const float4* xq, const float* xsum,
+                            float* pl, int lane) {
+  float4 xx[4], cc[4];
+  float xs;
+  load_xq(xq, xsum, c, lane, xx, cc, xs);
+  qmv_chunk_core(codes, scl, bia, nrows, r0, c, K, xx, cc, xs, pl, lane);
 }
 
 // Tokens per warp task of the multi-token matvecs (prompt chunks, batched
