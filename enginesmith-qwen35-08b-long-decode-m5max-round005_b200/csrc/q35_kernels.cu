@@ -70,10 +70,35 @@ __global__ void __launch_bounds__(kQmvThreads, 1) k_qmv(const __grid_constant__ 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int kWarps = kQmvThreads / 32;
   const int K = a.K, KW = K / 8, KG = K / 64, nch = K / 512;
-  Piece pc[4];
-  const int np = qmv_pieces(a, blockIdx.x, pc);
-  int nrows = 0;
-  for (int i = 0; i < np; ++i) nrows += pc[i].count;
+  // This CTA's rows per segment (cnt[s] rows from row r0[s] of segment s), in
+  // registers: every loop over the four segments is unrolled with constant
+  // indices (a dynamically indexed array lands in local memory, and the
+  // parameter block read with a dynamic index; both cost a CTA that starts
+  // as its predecessor ends most of a microsecond before it reaches the
+  // dependency wait).
+  int cnt[4], r0[4];
+  {
+    const int u0 = blockIdx.x * a.units_per_cta;
+    const int u1 = min(u0 + a.units_per_cta, a.units);
+#pragma unroll
+    for (int sg = 0; sg < 4; ++sg) cnt[sg] = 0, r0[sg] = 0;
+    if (EPI == kEpiSwiglu) {  // the gate rows, then the up rows, of the same units
+      cnt[0] = cnt[1] = max(u1 - u0, 0);
+      r0[0] = r0[1] = u0;
+    } else {
+      int off = 0;
+#pragma unroll
+      for (int sg = 0; sg < 4; ++sg) {
+        if (sg < a.nseg) {
+          const int rows = a.seg[sg].rows;
+          const int lo = max(u0, off), hi = min(u1, off + rows);
+          if (lo < hi) cnt[sg] = hi - lo, r0[sg] = lo - off;
+          off += rows;
+        }
+      }
+    }
+  }
+  const int nrows = cnt[0] + cnt[1] + cnt[2] + cnt[3];
   const int rows_alloc = EPI == kEpiSwiglu ? 2 * a.units_per_cta : a.units_per_cta;
   const QmvLayout L = qmv_layout(K, rows_alloc);
   uint32_t* codes = reinterpret_cast<uint32_t*>(smem + L.codes);
@@ -94,55 +119,48 @@ __global__ void __launch_bounds__(kQmvThreads, 1) k_qmv(const __grid_constant__ 
   }
   __syncthreads();
   if (tid == 0 && nrows > 0) {
-    uint32_t bytes = 0;
-    for (int i = 0; i < np; ++i) bytes += uint32_t(pc[i].count) * (KW * 4 + KG * 4);
-    mbar_expect_tx(bar, bytes);
+    mbar_expect_tx(bar, uint32_t(nrows) * (KW * 4 + KG * 4));
     int srow = 0;
-    for (int i = 0; i < np; ++i) {
-      const QmvSeg& sg = a.seg[pc[i].seg];
-      const int n = pc[i].count;
-      bulk_g2s(codes + size_t(srow) * KW, sg.w + size_t(pc[i].row0) * KW, uint32_t(n) * KW * 4, bar);
-      bulk_g2s(scl + size_t(srow) * KG, sg.s + size_t(pc[i].row0) * KG, uint32_t(n) * KG * 2, bar);
-      bulk_g2s(bia + size_t(srow) * KG, sg.b + size_t(pc[i].row0) * KG, uint32_t(n) * KG * 2, bar);
-      srow += n;
+#pragma unroll
+    for (int sg = 0; sg < 4; ++sg) {
+      const int n = cnt[sg];
+      if (n > 0) {
+        bulk_g2s(codes + size_t(srow) * KW, a.seg[sg].w + size_t(r0[sg]) * KW, uint32_t(n) * KW * 4, bar);
+        bulk_g2s(scl + size_t(srow) * KG, a.seg[sg].s + size_t(r0[sg]) * KG, uint32_t(n) * KG * 2, bar);
+        bulk_g2s(bia + size_t(srow) * KG, a.seg[sg].b + size_t(r0[sg]) * KG, uint32_t(n) * KG * 2, bar);
+        srow += n;
+      }
     }
   }
-  // epilogue operands of the rows this thread finishes (thread i -> CTA row i)
+  // epilogue operands of the rows this thread finishes (thread i -> CTA row
+  // i), loaded now and converted after the wait, so the loads stay in flight
+  // meanwhile
   int e_seg = -1, e_row = 0;
   {
     int acc = 0;
-    for (int p = 0; p < np; ++p) {
-      if (tid >= acc && tid < acc + pc[p].count) {
-        e_seg = pc[p].seg;
-        e_row = pc[p].row0 + (tid - acc);
+#pragma unroll
+    for (int sg = 0; sg < 4; ++sg) {
+      if (tid >= acc && tid < acc + cnt[sg]) {
+        e_seg = sg;
+        e_row = r0[sg] + (tid - acc);
       }
-      acc += pc[p].count;
+      acc += cnt[sg];
     }
-    if (EPI == kEpiSwiglu && tid >= pc[0].count) e_seg = -1;
+    if (EPI == kEpiSwiglu && tid >= cnt[0]) e_seg = -1;
   }
   uint16_t pre_res = 0, pre_h[3] = {0, 0, 0};
-  float pre_w[4] = {0.f, 0.f, 0.f, 0.f};
+  uint2 pre_w4 = make_uint2(0u, 0u);
   if (e_seg >= 0) {
     if (EPI == kEpiResAdd) pre_res = a.res[e_row];
     if (EPI == kEpiGdnConv && e_seg == 0) {
       pre_h[0] = a.hist[e_row];
       pre_h[1] = a.hist[kGdnConv + e_row];
       pre_h[2] = a.hist[2 * kGdnConv + e_row];
-      const uint2 w4 = *reinterpret_cast<const uint2*>(a.convw + 4 * e_row);
-      pre_w[0] = bf_lo(w4.x);
-      pre_w[1] = bf_hi(w4.x);
-      pre_w[2] = bf_lo(w4.y);
-      pre_w[3] = bf_hi(w4.y);
+      pre_w4 = *reinterpret_cast<const uint2*>(a.convw + 4 * e_row);
     }
   }
-  float gain4[4] = {0.f, 0.f, 0.f, 0.f};
-  if ((PRO == kProRms || PRO == kProEmbedRms) && tid < 256) {
-    const uint2 g = *reinterpret_cast<const uint2*>(a.gain + 4 * tid);
-    gain4[0] = bf_lo(g.x);
-    gain4[1] = bf_hi(g.x);
-    gain4[2] = bf_lo(g.y);
-    gain4[3] = bf_hi(g.y);
-  }
+  uint2 gain_raw = make_uint2(0u, 0u);
+  if ((PRO == kProRms || PRO == kProEmbedRms) && tid < 256) gain_raw = *reinterpret_cast<const uint2*>(a.gain + 4 * tid);
 
   // Norm-gate prologue: z (written two launches back) and the norm weight are
   // ready, so the gate factor z * sigmoid(z) of head `warp` is formed before
@@ -150,15 +168,14 @@ __global__ void __launch_bounds__(kQmvThreads, 1) k_qmv(const __grid_constant__ 
   static_assert(kQmvThreads / 32 >= kGdnHeads, "one warp per GDN head");
   float ng_zs[4] = {0.f, 0.f, 0.f, 0.f}, ng_w[4] = {0.f, 0.f, 0.f, 0.f};
   if (PRO == kProNormGate && warp < kGdnHeads) {
-    const float4 z4 = bf4(*reinterpret_cast<const uint2*>(a.gz + warp * 128 + 4 * lane));
     const float4 w4 = bf4(*reinterpret_cast<const uint2*>(a.gw + 4 * lane));
-    const float z[4] = {z4.x, z4.y, z4.z, z4.w};
     ng_w[0] = w4.x, ng_w[1] = w4.y, ng_w[2] = w4.z, ng_w[3] = w4.w;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float sy = __fdiv_rn(1.0f, __fadd_rn(1.0f, dexpf(fabsf(z[i]))));
-      const float sig = z[i] < 0.0f ? sy : __fsub_rn(1.0f, sy);
-      ng_zs[i] = __fmul_rn(z[i], sig);
+    if (a.gzs) {  // formed by the input projection's epilogue
+      const float4 g4 = *reinterpret_cast<const float4*>(a.gzs + warp * 128 + 4 * lane);
+      ng_zs[0] = g4.x, ng_zs[1] = g4.y, ng_zs[2] = g4.z, ng_zs[3] = g4.w;
+    } else {
+      const float4 z4 = bf4(*reinterpret_cast<const uint2*>(a.gz + warp * 128 + 4 * lane));
+      ng_zs[0] = gdn_zgate(z4.x), ng_zs[1] = gdn_zgate(z4.y), ng_zs[2] = gdn_zgate(z4.z), ng_zs[3] = gdn_zgate(z4.w);
     }
   }
 
@@ -166,6 +183,7 @@ __global__ void __launch_bounds__(kQmvThreads, 1) k_qmv(const __grid_constant__ 
   //    activations k = 4t .. 4t+3 and emits its matvec constants.
   pdl_wait();
   pdl_launch();
+  const float gain4[4] = {bf_lo(gain_raw.x), bf_hi(gain_raw.x), bf_lo(gain_raw.y), bf_hi(gain_raw.y)};
   if (PRO == kProPlain) {
     const int ngroups = K / 4;
     uint2 raw[4];
@@ -263,8 +281,7 @@ __global__ void __launch_bounds__(kQmvThreads, 1) k_qmv(const __grid_constant__ 
   // 4. epilogue (thread i finishes CTA row i).
   if (e_seg < 0) return;
   if (EPI == kEpiSwiglu) {
-    const int n = pc[0].count;
-    a.seg[0].y[pc[0].row0 + tid] = swiglu_bf(bfr(vals[tid]), bfr(vals[n + tid]));
+    a.seg[0].y[r0[0] + tid] = swiglu_bf(bfr(vals[tid]), bfr(vals[cnt[0] + tid]));
     return;
   }
   const float v = vals[tid];
@@ -274,17 +291,19 @@ __global__ void __launch_bounds__(kQmvThreads, 1) k_qmv(const __grid_constant__ 
     // gdn_input.metal:419-431
     const uint16_t raw = f2bf(v);
     float acc = 0.0f;
-    acc = fmaf(bf2f(pre_h[0]), pre_w[0], acc);
-    acc = fmaf(bf2f(pre_h[1]), pre_w[1], acc);
-    acc = fmaf(bf2f(pre_h[2]), pre_w[2], acc);
-    acc = fmaf(bf2f(raw), pre_w[3], acc);
+    acc = fmaf(bf2f(pre_h[0]), bf_lo(pre_w4.x), acc);
+    acc = fmaf(bf2f(pre_h[1]), bf_hi(pre_w4.x), acc);
+    acc = fmaf(bf2f(pre_h[2]), bf_lo(pre_w4.y), acc);
+    acc = fmaf(bf2f(raw), bf_hi(pre_w4.y), acc);
     const float xq1 = bfr(acc);
     a.conv_out[e_row] = f2bf(__fmul_rn(xq1, sigmoid_bf(xq1)));
     a.hist[e_row] = pre_h[1];
     a.hist[kGdnConv + e_row] = pre_h[2];
     a.hist[2 * kGdnConv + e_row] = raw;
   } else {
-    a.seg[e_seg].y[e_row] = f2bf(v);
+    const uint16_t yb = f2bf(v);
+    a.seg[e_seg].y[e_row] = yb;
+    if (EPI == kEpiGdnConv && e_seg == 1 && a.zs_out) a.zs_out[e_row] = gdn_zgate(bf2f(yb));
   }
 }
 

@@ -357,6 +357,7 @@ struct q35_session {
   uint16_t *q = nullptr, *k = nullptr, *v = nullptr, *gated = nullptr, *act = nullptr;
   uint16_t *logits = nullptr, *lse = nullptr;
   float *attn_po = nullptr, *attn_pml = nullptr, *head_part = nullptr;
+  float* zs = nullptr;  // z * sigmoid(z) of the step's GDN layer [2048]
   uint32_t *seq = nullptr, *out_tokens = nullptr;
   float* state = nullptr;
   uint16_t* hist = nullptr;
@@ -468,6 +469,7 @@ cudaError_t enqueue_step(q35_session* s, bool head, bool first) {
       a.hist = s->hist + size_t(gi) * 3 * kGdnConv;
       a.convw = L.conv;
       a.conv_out = s->conv_out;
+      a.zs_out = s->zs;
       a.ctl = s->ctl;
       Q35_L(launch_qmv(a, st, pdl));
       RecurArgs r = {};
@@ -490,6 +492,7 @@ cudaError_t enqueue_step(q35_session* s, bool head, bool first) {
       o.pro = kProNormGate;
       o.gy = s->y;
       o.gz = s->z;
+      o.gzs = s->zs;
       o.gw = L.gnorm;
       o.epi = kEpiResAdd;
       o.res = s->h;
@@ -1892,6 +1895,7 @@ int q35_open(const char* model_dir, int device, const q35_opts* opts, q35_sessio
       {(void**)&s->attn_po, size_t(kKvHeads) * kAttnChains * 4 * kHeadDim * 4},
       {(void**)&s->attn_pml, size_t(kKvHeads) * kAttnChains * 4 * 2 * 4},
       {(void**)&s->head_part, size_t(kHeadCtas) * 2 * 4},
+      {(void**)&s->zs, 2048 * 4},
       {(void**)&s->seq, (cap + 1) * 4},
       {(void**)&s->out_tokens, cap * 4},
       {(void**)&s->state, size_t(18) * kGdnHeads * 128 * 128 * 4},

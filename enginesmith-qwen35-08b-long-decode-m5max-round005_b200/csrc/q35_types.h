@@ -104,7 +104,8 @@ struct QmvArgs {
   const uint16_t* gy;    // norm-gate prologue: recurrence output [2048]
   const uint16_t* gz;    // z projection [2048]
   const uint16_t* gw;    // norm weight [128]
-  const float* gzs;      // chunk norm-gate prologue: precomputed z * sigmoid(z) [rows][2048] (optional)
+  const float* gzs;      // norm-gate prologue: precomputed z * sigmoid(z) [rows][2048] (optional)
+  float* zs_out;         // GDN input projection: z * sigmoid(z) of the z rows, f32 [2048] (optional)
   uint16_t* res;         // residual (in/out) for kEpiResAdd
   uint16_t* hist;        // GDN conv history [3][6144]
   const uint16_t* convw; // [6144][4]
