@@ -113,12 +113,15 @@ __global__ void __launch_bounds__(kQmvThreads, 1) k_qmv(const __grid_constant__ 
 
   // 1. Before the dependency wait: weights by bulk copy, and everything else
   //    written two or more launches back (gains, the residual, conv history).
-  if (tid == 0) {
+  //    The last thread (which finishes no row at the model's shapes) sets up
+  //    the barrier and issues the copies while the others preload; nobody
+  //    waits on the barrier before the block barrier after the activations.
+  constexpr int kIssuer = kQmvThreads - 1;
+  if (tid == kIssuer) {
     mbar_init(bar, 1);
     fence_mbar_init();
   }
-  __syncthreads();
-  if (tid == 0 && nrows > 0) {
+  if (tid == kIssuer && nrows > 0) {
     mbar_expect_tx(bar, uint32_t(nrows) * (KW * 4 + KG * 4));
     int srow = 0;
 #pragma unroll
@@ -260,7 +263,30 @@ __global__ void __launch_bounds__(kQmvThreads, 1) k_qmv(const __grid_constant__ 
   // 3. dot products from shared memory.
   mbar_wait(bar, 0, a.ctl, kErrQmvWait);
   const int ngroups = (nrows + 3) / 4;
-  {
+  if (ngroups <= kWarps && nch <= (ngroups * nch + kWarps - 1) / kWarps) {
+    // Whole groups: warp g walks the chunks of rows 4g..4g+3 in order and
+    // keeps the lane's chunk sum in registers (the same additions, in chunk
+    // order, as the shared-memory finish below), then the butterfly; taken
+    // when the chunk tasks would need as many rounds anyway.
+    if (warp < ngroups) {
+      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      for (int c = 0; c < nch; ++c) {
+        float4 xx[4], cc[4];
+        float xs;
+        load_xq(xq, xsum, c, lane, xx, cc, xs);
+        float term[4];
+        qmv_rows_terms(codes, scl, bia, nrows, 4 * warp, c, K, xx, cc, xs, lane, term);
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[r] = __fadd_rn(acc[r], term[r]);
+      }
+      const float v = reduce4(acc[0], acc[1], acc[2], acc[3], lane);
+      if ((lane & 7) == 0) {
+        const int r = 4 * warp + (((lane >> 4) & 1) << 1) + ((lane >> 3) & 1);
+        if (r < nrows) vals[r] = v;
+      }
+    }
+    __syncthreads();
+  } else {
     // a warp's tasks usually share their chunk: its constants are loaded once
     float4 xx[4], cc[4];
     float xs = 0.0f;
@@ -273,10 +299,10 @@ __global__ void __launch_bounds__(kQmvThreads, 1) k_qmv(const __grid_constant__ 
       }
       qmv_chunk_core(codes, scl, bia, nrows, 4 * g, c, K, xx, cc, xs, pl, lane);
     }
+    __syncthreads();
+    for (int g = warp; g < ngroups; g += kWarps) qmv_finish_task(pl, nrows, 4 * g, nch, vals, lane);
+    __syncthreads();
   }
-  __syncthreads();
-  for (int g = warp; g < ngroups; g += kWarps) qmv_finish_task(pl, nrows, 4 * g, nch, vals, lane);
-  __syncthreads();
 
   // 4. epilogue (thread i finishes CTA row i).
   if (e_seg < 0) return;
