@@ -766,6 +766,9 @@ cudaError_t capture_chunk(q35_session* s, cudaGraphExec_t* out) {
   }
   if (e != cudaSuccess) return e;
   e = cudaGraphInstantiate(out, g, 0);
+  // upload now, so that the first replay (inside a request or a timed region)
+  // does not pay for it
+  if (e == cudaSuccess) e = cudaGraphUpload(*out, s->stream);
   cudaGraphDestroy(g);
   return e;
 }
@@ -977,6 +980,9 @@ cudaError_t capture(q35_session* s, int steps, bool head, cudaGraphExec_t* out, 
   if (e != cudaSuccess) return e;
   if (knodes) *knodes = kernel_nodes(g);
   e = cudaGraphInstantiate(out, g, 0);
+  // upload now, so that the first replay (inside a request or a timed region)
+  // does not pay for it
+  if (e == cudaSuccess) e = cudaGraphUpload(*out, s->stream);
   cudaGraphDestroy(g);
   return e;
 }
@@ -1462,6 +1468,9 @@ cudaError_t capture_batch(q35_batch* b, int steps, cudaGraphExec_t* out, uint32_
   if (e != cudaSuccess) return e;
   *knodes = kernel_nodes(g);
   e = cudaGraphInstantiate(out, g, 0);
+  // upload now, so that the first replay (inside a request or a timed region)
+  // does not pay for it
+  if (e == cudaSuccess) e = cudaGraphUpload(*out, b->stream);
   cudaGraphDestroy(g);
   return e;
 }
