@@ -56,11 +56,18 @@ def prompt(seed, n):
     return [int(v) for v in I.Rng(900 + seed, 7).ints(n, 248320)]
 
 
-def oracle_after_prompt(O, om, p):
+def oracle_after_prompt(O, om, p, chunk=2048):
+    """The oracle through the prompt route's numerics: every projection as the
+    tensor-core GEMM of its chunk (the chunk's token count fixes the GEMM's K
+    split), attention as the flash restatement; the last token by the decode
+    route."""
     s = O.OracleSession(om, CAP)
     s.set_gemm(True)
     s.set_flash(True)
-    for t in p[:-1]:
+    body = p[:-1]
+    for i, t in enumerate(body):
+        c0 = (i // chunk) * chunk
+        s.set_gemm_tokens(min(chunk, len(body) - c0))
         s.step(t, head=False)
     s.set_gemm(False)
     s.set_flash(False)
@@ -152,7 +159,7 @@ def test_tensor_prompt_matches_oracle(models, oracle_threads, omodel, n, which):
     tok = m.generate(p, 1, True)[0]
     lg = f32(m.last_logits()[0])
     kv, st, hi = m.dump_state()
-    s, otok = oracle_after_prompt(O, omodel, p)
+    s, otok = oracle_after_prompt(O, omodel, p, 2048 if which == 0 else 64)
     olg = f32(s.logits())
     okv, ost, ohi = s.export_state()
     assert kv.shape == okv.shape

@@ -163,18 +163,29 @@ def test_attention_matches_float64(O, length):
 
 @pytest.mark.parametrize("n,k,seed", [(3584, 1024, 0), (1024, 2048, 4), (77, 3584, 9)])
 def test_gemm_numerics_matvec(O, n, k, seed):
-    """The tensor-core routes' matvec restatement (weights bf16(s q + b) from
-    one fused multiply-add, dot products exact): against numpy float64, at
-    most one f32 ulp apart (the order of the float64 sums differs)."""
+    """The tensor-core routes' matvec restatement (weights bf16(s q + b)
+    rounded once; per 16-wide K step the tensor core's truncating
+    accumulation, tc_step; K splits summed in order): against the exact dot
+    product of the same weights in float64, within the accumulation's own
+    error bound. Each step truncates its 17 aligned terms 2 bits below the
+    f32 ulp of their largest and the sum once more, so its error is below
+    17/4 + 1 ulps of the largest magnitude it sees, which the sum of
+    |products| bounds; each split partial adds one rounding."""
     w, s, b, x = I.config1(seed, n, k)
     q = I.unpack_q4(w).astype(np.float64)
     sc = np.repeat(I.bf2f(s).astype(np.float64), 64, axis=1)
     bi = np.repeat(I.bf2f(b).astype(np.float64), 64, axis=1)
-    wd = I.bf2f(I.f2bf((sc * q + bi).astype(np.float32))).astype(np.float64)
-    ref = (wd @ I.bf2f(x).astype(np.float64)).astype(np.float32)
-    got = O.qmv_gemm_f32(w, s, b, x)
-    ulp = np.spacing(np.abs(ref))
-    assert np.all(np.abs(got - ref) <= ulp), float(np.max(np.abs(got - ref) / ulp))
+    m, e = np.frexp(sc * q + bi)  # exact in float64; one bf16 rounding, ties to even
+    wd = np.ldexp(np.rint(np.ldexp(m, 8)), e - 8)
+    xv = I.bf2f(x).astype(np.float64)
+    ref = wd @ xv
+    got = O.qmv_gemm_f32(w, s, b, x).astype(np.float64)
+    mag = np.abs(wd) @ np.abs(xv)
+    steps = k // 16
+    bound = (steps * (17 / 4 + 1) + 8) * 2.0 ** -23 * mag
+    assert np.all(np.abs(got - ref) <= bound), float(np.max(np.abs(got - ref) / bound))
+    # and the tensor core's rule is not the exact sum rounded once: some rows differ from it
+    assert np.any(got != ref.astype(np.float32))
 
 
 def attention_flash_f64(query, kc, vc, length):
