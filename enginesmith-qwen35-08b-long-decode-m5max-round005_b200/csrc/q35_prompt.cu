@@ -220,8 +220,8 @@ __global__ void __launch_bounds__(320) k_pr_attn_prep(const __grid_constant__ Pr
 // rows r = 32 hq + i (query head 4 kvh + hq, token 32 qb + i), keys in 64-key
 // tiles [tb, te) of the split. Two launches: PASS 0 computes S = Q K^T over
 // the split and each row's maximum; PASS 1 takes the row maximum M over all
-// splits, recomputes S and accumulates O += P V with P = bf16(2^((S - M)
-// log2(e) / 16)), so every split weighs its keys against the same maximum
+// splits, recomputes S and accumulates O += P V with P = bf16(e^((S - M) / 16))
+// (pa_weight), so every split weighs its keys against the same maximum
 // (the combine then only adds). Roles: warp 0 lane 0 loads Q once and the key
 // and value tiles through a ring (3-D TMA, 128-byte swizzle), warp 1 lane 0
 // issues the MMAs, warp 2 owns the TMEM allocation, warps 4-7 (thread = row =
@@ -233,16 +233,15 @@ constexpr uint32_t kPaTileBytes = 64 * 256 * 2;  // one key or value tile: 4 blo
 constexpr uint32_t kPaPBytes = 128 * 64 * 2;     // P: 128 rows x 64 keys
 constexpr size_t kPaSmem = 1024 + kPaQBytes + kPaStages * kPaTileBytes + 2 * kPaPBytes + 256;
 // exp(x / 16) = 2^(x log2(e) / 16): the 1/sqrt(256) score scale folded in
+// (the combine's split factors, which are all 1: every split carries the
+// row's maximum)
 constexpr float kPaExp2Scale = 0.0901684400555602f;
 
-// 2^x by the PTX ex2.approx.ftz.f32 instruction (relative error below 2^-22;
-// results below 2^-126 flush to zero): the attention weights are rounded to
-// bf16 right after, so this matches an exact 2^x but for rare roundings.
-Q35_DEV float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
+// The attention weight of a score s against the row maximum m:
+// e^((s - m) / 16) by the decode kernels' fexp (Cody-Waite reduction and a
+// polynomial of IEEE-exact operations, so the CPU oracle restates it bit for
+// bit), rounded to bf16 by the caller.
+Q35_DEV float pa_weight(float s, float m) { return fexp(__fmul_rn(__fsub_rn(s, m), 0.0625f)); }
 
 Q35_DEV void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
   asm volatile(
@@ -455,8 +454,8 @@ __global__ void __launch_bounds__(256, 1) k_pr_attn(const __grid_constant__ Prom
       uint32_t pk[32];
 #pragma unroll
       for (int c = 0; c < 64; c += 2) {
-        float x0 = ex2_approx(__fmul_rn(__fsub_rn(sv[c], m), kPaExp2Scale));
-        float x1 = ex2_approx(__fmul_rn(__fsub_rn(sv[c + 1], m), kPaExp2Scale));
+        float x0 = pa_weight(sv[c], m);
+        float x1 = pa_weight(sv[c + 1], m);
         if (diag) {
           if (k0 + c > rowpos) x0 = 0.0f;
           if (k0 + c + 1 > rowpos) x1 = 0.0f;

@@ -469,6 +469,91 @@ void attn_f32_flash(const uint16_t* query, const uint16_t* kcache, const uint16_
   });
 }
 
+/* The tensor-core prompt route's attention exactly (q35_prompt.cu k_pr_attn
+ * and k_pr_attn_combine) for the token at position `pos` of a prompt chunk
+ * of T tokens starting at p0c (the chunk fixes the key splits):
+ *  - scores s_i = q . k_i as 16 MMA steps over the head dimensions (tc_step);
+ *  - the row maximum m over the valid keys i <= pos;
+ *  - key splits as the kernel plans them (attn_splits): the token's 32-token
+ *    query block reaches ntile 64-key tiles, split sp takes tiles
+ *    [ntile sp / nsplit, ntile (sp + 1) / nsplit);
+ *  - per split: weights p_i = bf16(fexp((s_i - m) / 16)) (0 past pos), their
+ *    sum in eight partials (key pair c/2 into partial (c/2) % 8, pairs added
+ *    first) combined as ((l0 + l1) + (l2 + l3)) + ((l4 + l5) + (l6 + l7)),
+ *    and o = sum p_i v_i as MMA steps over 16 keys at a time from zero;
+ *  - the splits summed in order (every split's factor is e^0 = 1);
+ *  - out = (sum o) / (sum l), before the caller's bf16 rounding. */
+static int pa_splits(int nqb, int maxtiles) {
+  const int want = (444 + 2 * nqb - 1) / (2 * nqb);
+  int ns = (maxtiles + 127) / 128;
+  if (ns < want) ns = want;
+  if (ns > maxtiles) ns = maxtiles;
+  return ns < 1 ? 1 : ns;
+}
+
+void attn_flash_tc(const uint16_t* query, const uint16_t* kcache, const uint16_t* vcache, uint32_t pos,
+                   uint32_t capacity, uint32_t p0c, uint32_t T, float* out /*[8*256]*/) {
+  const uint32_t t = pos - p0c;
+  const int nqb = int((T + 31) / 32), qb = int(t / 32);
+  const int maxtiles = int((p0c + T - 1) / 64) + 1;
+  const int nsplit = pa_splits(nqb, maxtiles);
+  const uint32_t qlast = std::min<uint32_t>(T, uint32_t(qb) * 32 + 32) - 1;
+  const int ntile = int((p0c + qlast) / 64) + 1;
+  pool().run(8, [&](long h0, long h1) {
+    for (long qh = h0; qh < h1; ++qh) {
+      const int kh = int(qh) / 4;
+      const uint16_t* kc = kcache + size_t(kh) * capacity * 256;
+      const uint16_t* vc = vcache + size_t(kh) * capacity * 256;
+      float qf[256];
+      for (int d = 0; d < 256; ++d) qf[d] = bf2f(query[qh * 256 + d]);
+      std::vector<float> sc(size_t(ntile) * 64, 0.0f);
+      float m = -INFINITY;
+      for (uint32_t i = 0; i <= pos; ++i) {
+        float acc = 0.0f, p[16];
+        for (int st = 0; st < 16; ++st) {
+          for (int j = 0; j < 16; ++j) p[j] = qf[st * 16 + j] * bf2f(kc[size_t(i) * 256 + st * 16 + j]);
+          acc = tc_step(acc, p);
+        }
+        sc[i] = acc;
+        m = std::max(m, acc);
+      }
+      float L = 0.0f;
+      std::vector<float> O(256, 0.0f), os(256);
+      for (int sp = 0; sp < nsplit; ++sp) {
+        const int tb = int(int64_t(ntile) * sp / nsplit), te = int(int64_t(ntile) * (sp + 1) / nsplit);
+        if (te <= tb) continue;  // an empty split carries no weight
+        float lp[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        std::fill(os.begin(), os.end(), 0.0f);
+        for (int tile = tb; tile < te; ++tile) {
+          const uint32_t k0 = uint32_t(tile) * 64;
+          float pw[64];
+          for (int c = 0; c < 64; c += 2) {
+            const float x0 = k0 + c <= pos ? fexp((sc[k0 + c] - m) * 0.0625f) : 0.0f;
+            const float x1 = k0 + c + 1 <= pos ? fexp((sc[k0 + c + 1] - m) * 0.0625f) : 0.0f;
+            pw[c] = bfr(x0);
+            pw[c + 1] = bfr(x1);
+            lp[(c >> 1) & 7] = lp[(c >> 1) & 7] + (pw[c] + pw[c + 1]);
+          }
+          for (int d = 0; d < 256; ++d)
+            for (int kk = 0; kk < 4; ++kk) {
+              float p[16];
+              for (int j = 0; j < 16; ++j) {
+                const uint32_t key = k0 + kk * 16 + j;
+                // past the row's position the weight is 0 (the cache row's value is finite)
+                p[j] = pw[kk * 16 + j] == 0.0f ? 0.0f : pw[kk * 16 + j] * bf2f(vc[size_t(key) * 256 + d]);
+              }
+              os[d] = tc_step(os[d], p);
+            }
+        }
+        const float l = ((lp[0] + lp[1]) + (lp[2] + lp[3])) + ((lp[4] + lp[5]) + (lp[6] + lp[7]));
+        L = L + l;
+        for (int d = 0; d < 256; ++d) O[d] = O[d] + os[d];
+      }
+      for (int d = 0; d < 256; ++d) out[qh * 256 + d] = O[d] / L;
+    }
+  });
+}
+
 /* Sequence split over `world` ranks (the engine's config-5 path; the
  * reference runs on one device, so this has no reference counterpart). Rank
  * r holds positions r, r + world, ...; on each rank 64 chains walk its keys
@@ -1058,6 +1143,15 @@ void orc_attn_flash_f32(const uint16_t* query, const uint16_t* kcache, const uin
 }
 
 /* attention.metal:140-150 on the prompt route's attention output */
+void orc_attn_flash_tc_gate(const uint16_t* query, const uint16_t* kcache, const uint16_t* vcache, uint32_t pos,
+                            uint32_t capacity, uint32_t p0c, uint32_t T, const uint16_t* q_raw, uint16_t* gated) {
+  std::vector<float> o(2048);
+  attn_flash_tc(query, kcache, vcache, pos, capacity, p0c, T, o.data());
+  for (int head = 0; head < 8; ++head)
+    for (int d = 0; d < 256; ++d)
+      gated[head * 256 + d] = f2bf(bfr(o[head * 256 + d]) * gate_sigmoid_bf(bf2f(q_raw[head * 512 + 256 + d])));
+}
+
 void orc_attn_flash_gate(const uint16_t* query, const uint16_t* kcache, const uint16_t* vcache, uint32_t len,
                          uint32_t capacity, const uint16_t* q_raw, uint16_t* gated) {
   std::vector<float> o(2048);
@@ -1178,6 +1272,7 @@ struct orc_session {
   int split_world = 1;  // attention as a sequence split over this many ranks
   bool gemm = false;     // projections and head with the tensor-core route's numerics
   int gemm_tokens = 1;   // tokens of the engine's GEMM launches (sessions of a batch, prompt chunk)
+  uint32_t chunk_p0 = 0, chunk_T = 0;  // the prompt chunk of the next steps (flash mode; T 0: unset)
   bool flash = false;    // attention as the tensor-core prompt route's (attn_f32_flash)
 };
 
@@ -1336,6 +1431,11 @@ void orc_session_export(const orc_session* s, uint16_t* kv, float* state, uint16
 void orc_session_set_split(orc_session* s, int world) { s->split_world = world > 1 ? world : 1; }
 void orc_session_set_gemm(orc_session* s, int on) { s->gemm = on != 0; }
 void orc_session_set_gemm_tokens(orc_session* s, int tokens) { s->gemm_tokens = tokens > 0 ? tokens : 1; }
+void orc_session_set_chunk(orc_session* s, uint32_t p0, uint32_t tokens) {
+  s->chunk_p0 = p0;
+  s->chunk_T = tokens;
+  s->gemm_tokens = tokens > 0 ? int(tokens) : 1;
+}
 
 /* The engine's tensor-core GEMM (q35_op_qgemm_q4) on T tokens: y[t][n] before
  * the bf16 rounding, for a launch of `tiles` 128-row tiles (0: this matrix
@@ -1399,7 +1499,10 @@ uint32_t orc_session_step(orc_session* S, uint32_t token, int want_head) {
       orc_qmv_q4(L.v.w, L.v.s, L.v.b, u.data(), nullptr, 512, 1024, v.data());
       orc_attn_prepare(q.data(), k.data(), v.data(), L.qnorm, L.knorm, S->position, S->capacity,
                        query.data(), S->kc[ai].data(), S->vc[ai].data());
-      if (S->flash) {
+      if (S->flash && S->chunk_T > 0) {
+        orc_attn_flash_tc_gate(query.data(), S->kc[ai].data(), S->vc[ai].data(), S->position, S->capacity,
+                               S->chunk_p0, S->chunk_T, q.data(), gated.data());
+      } else if (S->flash) {
         orc_attn_flash_gate(query.data(), S->kc[ai].data(), S->vc[ai].data(), S->position + 1, S->capacity,
                             q.data(), gated.data());
       } else {

@@ -131,6 +131,14 @@ void orc_session_set_gemm(orc_session* s, int on);
 /* Tokens per GEMM launch of the engine route being restated (batch members,
  * prompt-chunk tokens): with the launch's row tiles it fixes the K split. */
 void orc_session_set_gemm_tokens(orc_session* s, int tokens);
+/* The prompt chunk (first position, token count) the next steps belong to:
+ * sets the GEMM token count, and in flash mode the attention restates the
+ * prompt route exactly (orc_attn_flash_tc_gate). */
+void orc_session_set_chunk(orc_session* s, uint32_t p0, uint32_t tokens);
+/* The prompt route's gated attention, exactly (the kernel's splits, fexp
+ * weights, MMA accumulation), for the token at `pos` of the chunk (p0c, T). */
+void orc_attn_flash_tc_gate(const uint16_t* query, const uint16_t* kcache, const uint16_t* vcache, uint32_t pos,
+                            uint32_t capacity, uint32_t p0c, uint32_t T, const uint16_t* q_raw, uint16_t* gated);
 /* The engine's tensor-core GEMM on T tokens (x [T][K]): y [T][N] before the
  * bf16 rounding, for a launch of `tiles` 128-row tiles (0: this matrix alone). */
 void orc_qgemm_tc(const uint32_t* w, const uint16_t* s, const uint16_t* b, const uint16_t* x, int T, int N,

@@ -77,6 +77,8 @@ def lib() -> ctypes.CDLL:
             "orc_session_set_split": (None, [P, c_int]),
             "orc_session_set_gemm": (None, [P, c_int]),
             "orc_session_set_gemm_tokens": (None, [P, c_int]),
+            "orc_session_set_chunk": (None, [P, c_uint32, c_uint32]),
+            "orc_attn_flash_tc_gate": (None, [P, P, P, c_uint32, c_uint32, c_uint32, c_uint32, P, P]),
             "orc_qgemm_tc": (None, [P, P, P, P, c_int, c_int, c_int, c_int, P]),
             "tc_step": (c_float, [c_float, P]),
             "orc_session_set_flash": (None, [P, c_int]),
@@ -244,6 +246,15 @@ def attn_flash_f32(query, kcache, vcache, length: int, capacity: int) -> np.ndar
     return out
 
 
+def attn_flash_tc_gate(query, kcache, vcache, pos: int, capacity: int, p0c: int, tokens: int, q_raw) -> np.ndarray:
+    """The prompt route's gated attention for the token at `pos` of the
+    chunk (p0c, tokens), exactly as the tensor-core kernels compute it."""
+    out = np.zeros(2048, np.uint16)
+    lib().orc_attn_flash_tc_gate(_p(np.ascontiguousarray(query)), _p(kcache), _p(vcache), pos, capacity, p0c,
+                                 tokens, _p(np.ascontiguousarray(q_raw)), _p(out))
+    return out
+
+
 def attn_flash_gate(query, kcache, vcache, length: int, capacity: int, q_raw) -> np.ndarray:
     """The prompt route's attention with the output gate (bf16 [8*256])."""
     gated = np.zeros(2048, np.uint16)
@@ -323,6 +334,11 @@ class OracleSession:
         """Tokens per GEMM launch of the engine route restated by set_gemm
         (the batch's member count, or the prompt chunk's token count)."""
         lib().orc_session_set_gemm_tokens(self.s, tokens)
+
+    def set_chunk(self, p0: int, tokens: int) -> None:
+        """The prompt chunk (first position, token count) of the next steps:
+        the GEMM token count, and the exact flash restatement in flash mode."""
+        lib().orc_session_set_chunk(self.s, p0, tokens)
 
     def set_flash(self, on: bool) -> None:
         """Attention of later steps with the engine's tensor-core prompt

@@ -349,3 +349,17 @@ def test_tc_step_against_device_golden(O):
             acc = O.tc_step(acc, x[s:s + 16])
         bad += np.float32(acc).view(np.uint32) != np.float32(g).view(np.uint32)
     assert bad == 0, f"{bad} of {len(d['gpu'])} sums differ"
+
+
+@pytest.mark.parametrize("length", [1, 31, 64, 1025])
+def test_flash_tc_restatement_close_to_flash_formula(O, length):
+    """The prompt route's exact restatement (attn_flash_tc_gate: the tensor
+    core's truncating MMA accumulation, fexp weights, the kernels' key splits)
+    stays within bf16 rounding of the flash formula with exact sums
+    (attn_flash_gate)."""
+    c = I.config3(2, length)
+    kc, vc = c["kc"].copy(), c["vc"].copy()
+    q = O.attn_prepare(c["q_raw"], c["k_raw"], c["v_raw"], c["q_gain"], c["k_gain"], c["pos"], c["cap"], kc, vc)
+    a = I.bf2f(O.attn_flash_tc_gate(q, kc, vc, length - 1, c["cap"], 0, length, c["q_raw"])).astype(np.float64)
+    b = I.bf2f(O.attn_flash_gate(q, kc, vc, length, c["cap"], c["q_raw"])).astype(np.float64)
+    assert np.linalg.norm(a - b) <= 1e-2 * np.linalg.norm(b)
