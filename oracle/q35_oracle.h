@@ -143,8 +143,9 @@ void orc_attn_flash_tc_gate(const uint16_t* query, const uint16_t* kcache, const
  * bf16 rounding, for a launch of `tiles` 128-row tiles (0: this matrix alone). */
 void orc_qgemm_tc(const uint32_t* w, const uint16_t* s, const uint16_t* b, const uint16_t* x, int T, int N,
                   int K, int tiles, float* y);
-/* One 16-wide K step of the tensor core's bf16 MMA (f32 accumulator). */
-float tc_step(float acc, const float* p);
+/* One 16-wide K step of the tensor core's bf16 MMA (f32 accumulator):
+ * acc + sum a[i] b[i] with the measured alignment and truncation. */
+float tc_step(float acc, const float* a, const float* b);
 /* attention of later steps as the tensor-core prompt route's (attn_f32_flash) */
 void orc_session_set_flash(orc_session* s, int on);
 /* attention of later steps as the engine's sequence split over `world` ranks */

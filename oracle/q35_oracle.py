@@ -80,7 +80,7 @@ def lib() -> ctypes.CDLL:
             "orc_session_set_chunk": (None, [P, c_uint32, c_uint32]),
             "orc_attn_flash_tc_gate": (None, [P, P, P, c_uint32, c_uint32, c_uint32, c_uint32, P, P]),
             "orc_qgemm_tc": (None, [P, P, P, P, c_int, c_int, c_int, c_int, P]),
-            "tc_step": (c_float, [c_float, P]),
+            "tc_step": (c_float, [c_float, P, P]),
             "orc_session_set_flash": (None, [P, c_int]),
             "orc_session_logits": (None, [P, P]),
             "orc_session_lse": (c_uint16, [P]),
@@ -171,11 +171,13 @@ def qgemm_tc(w, s, b, x, tiles: int = 0) -> np.ndarray:
     return y
 
 
-def tc_step(acc: float, p) -> float:
-    """One 16-wide MMA step of the tensor core (f32 accumulator)."""
-    p = np.ascontiguousarray(p, np.float32)
-    assert p.size == 16
-    return float(lib().tc_step(acc, _p(p)))
+def tc_step(acc: float, a, b=None) -> float:
+    """One 16-wide MMA step of the tensor core (f32 accumulator): acc + sum
+    a[i] b[i] (b defaults to ones, i.e. the products given as a)."""
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ones(16, np.float32) if b is None else np.ascontiguousarray(b, np.float32)
+    assert a.size == 16 and b.size == 16
+    return float(lib().tc_step(acc, _p(a), _p(b)))
 
 
 def rms_norm(x, gain, eps=1e-6) -> np.ndarray:

@@ -363,3 +363,23 @@ def test_flash_tc_restatement_close_to_flash_formula(O, length):
     a = I.bf2f(O.attn_flash_tc_gate(q, kc, vc, length - 1, c["cap"], 0, length, c["q_raw"])).astype(np.float64)
     b = I.bf2f(O.attn_flash_gate(q, kc, vc, length, c["cap"], c["q_raw"])).astype(np.float64)
     assert np.linalg.norm(a - b) <= 1e-2 * np.linalg.norm(b)
+
+
+def test_tc_step_against_device_chains(O):
+    """tc_step over chains of 1, 2, 4 and 64 MMA steps measured on a B200
+    with products of widely different exponents (weights from Q4 scales and
+    biases over 14 binades, activations over 13; tests/golden/make_mma_golden.py):
+    bit for bit. These pin the alignment by the factors' exponent sum."""
+    path = os.path.join(GOLD, "tc_mma_chains.npz")
+    if not os.path.exists(path):
+        pytest.skip("tc_mma_chains.npz not generated yet (needs a GPU)")
+    d = np.load(path)
+    for n in (1, 2, 4, 64):
+        a, b, g = I.bf2f(d[f"a{n}"]), I.bf2f(d[f"b{n}"]), d[f"gpu{n}"]
+        bad = 0
+        for ai, bi, gi in zip(a, b, g):
+            acc = 0.0
+            for s in range(0, 16 * n, 16):
+                acc = O.tc_step(acc, ai[s:s + 16], bi[s:s + 16])
+            bad += np.float32(acc).view(np.uint32) != np.float32(gi).view(np.uint32)
+        assert bad == 0, f"{n} steps: {bad} of {len(g)} differ"
