@@ -335,10 +335,14 @@ __global__ void __launch_bounds__(kQmvThreads, 1) k_qmv(const __grid_constant__ 
 
 // ---------------------------------------------------------------------------
 // GDN recurrence (gdn.metal:176-228, T = 1) with the Q/K normalisation and
-// gates of gdn_input.metal:433-460. Grid (8 row blocks, 16 heads) x 64
-// threads; thread = (value row, quarter of the key axis), 32 f32 of state.
+// gates of gdn_input.metal:433-460. Grid (8 row blocks, 16 heads) x 128
+// threads: 8 lanes per value row, 16 f32 of state each, the reference's row
+// reduction restated piecewise (gdn_decay_dot8 / gdn_reduce8 /
+// gdn_update_dot8, bit-identical to gdn_row_step). After the dependency wait
+// warps 0-3 form the q norm, the k norm, the decay gate and beta in parallel;
+// exp(A_log), a weight, is formed before the wait.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(64) k_gdn_recur(const __grid_constant__ RecurArgs a) {
+__global__ void __launch_bounds__(128) k_gdn_recur(const __grid_constant__ RecurArgs a) {
   __shared__ __align__(16) float st[16 * 128];
   __shared__ float qn[128], kn[128], gb[2];
   __shared__ __align__(8) uint64_t bar;
@@ -350,37 +354,38 @@ __global__ void __launch_bounds__(64) k_gdn_recur(const __grid_constant__ RecurA
     mbar_expect_tx(&bar, 16 * 128 * 4);
     bulk_g2s(st, a.state + (size_t(h) * 128 + rb * 16) * 128, 16 * 128 * 4, &bar);
   }
+  const float e1 = warp == 2 && lane == 0 ? dexpf(a.a_log[h]) : 0.0f;
   pdl_wait();
   pdl_launch();
   if (a.advance_pos && rb == 0 && h == 0 && tid == 0) a.ctl->pos = a.ctl->pos_step + 1;
-  // warp 0 -> q, warp 1 -> k (gdn_input.metal:433-441); g on thread 0, beta on
-  // thread 32, in parallel (gdn_input.metal:454-459)
-  gdn_qk_norm(a.conv, h, warp == 0, lane, warp == 0 ? qn : kn);
-  if (tid == 0) {
-    gb[0] = gdn_gate(a.a_raw[h], a.dt_bias[h], dexpf(a.a_log[h]));
-  } else if (tid == 32) {
-    gb[1] = gdn_beta(a.b_raw[h]);
+  // gdn_input.metal:433-441 (q, k) and :454-459 (g, beta)
+  if (warp < 2) {
+    gdn_qk_norm(a.conv, h, warp == 0, lane, warp == 0 ? qn : kn);
+  } else if (lane == 0) {
+    if (warp == 2) gb[0] = gdn_gate(a.a_raw[h], a.dt_bias[h], e1);
+    else gb[1] = gdn_beta(a.b_raw[h]);
   }
   __syncthreads();
   mbar_wait(&bar, 0, a.ctl, kErrRecurWait);
-  const int row = tid >> 2, r = tid & 3;
+  const int row = tid >> 3, r8 = tid & 7;
   const int vrow = rb * 16 + row;
   const float gt = gb[0], beta = gb[1];
-  float s[32];
+  float s[16];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float4 t = *reinterpret_cast<const float4*>(&st[row * 128 + r * 32 + i * 4]);
+  for (int i = 0; i < 4; ++i) {
+    const float4 t = *reinterpret_cast<const float4*>(&st[row * 128 + r8 * 16 + i * 4]);
     s[i * 4 + 0] = t.x;
     s[i * 4 + 1] = t.y;
     s[i * 4 + 2] = t.z;
     s[i * 4 + 3] = t.w;
   }
-  const float out =
-      gdn_row_step(s, kn + r * 32, qn + r * 32, gt, beta, bf2f(a.conv[4096 + h * 128 + vrow]));
-  if (r == 0) a.y[h * 128 + vrow] = f2bf(out);
-  float4* dst = reinterpret_cast<float4*>(a.state + (size_t(h) * 128 + vrow) * 128 + r * 32);
+  const float memory = gdn_reduce8(gdn_decay_dot8(s, kn + r8 * 16, gt));
+  const float delta = __fmul_rn(__fsub_rn(bf2f(a.conv[4096 + h * 128 + vrow]), memory), beta);
+  const float out = gdn_reduce8(gdn_update_dot8(s, kn + r8 * 16, qn + r8 * 16, delta));
+  if (r8 == 0) a.y[h * 128 + vrow] = f2bf(out);
+  float4* dst = reinterpret_cast<float4*>(a.state + (size_t(h) * 128 + vrow) * 128 + r8 * 16);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) dst[i] = make_float4(s[4 * i], s[4 * i + 1], s[4 * i + 2], s[4 * i + 3]);
+  for (int i = 0; i < 4; ++i) dst[i] = make_float4(s[4 * i], s[4 * i + 1], s[4 * i + 2], s[4 * i + 3]);
 }
 
 // Standalone conv/history step (the op-level GDN entry point; the decode
@@ -1478,7 +1483,7 @@ cudaError_t launch_qmv(const QmvArgs& a, cudaStream_t st, bool pdl) {
   return launch_ex(kern, dim3(grid), dim3(kQmvThreads), spread(qmv_smem_bytes(a)), st, pdl, a);
 }
 cudaError_t launch_recur(const RecurArgs& a, cudaStream_t st, bool pdl) {
-  return launch_ex(k_gdn_recur, dim3(8, kGdnHeads), dim3(64), kSpreadSmem, st, pdl, a);
+  return launch_ex(k_gdn_recur, dim3(8, kGdnHeads), dim3(128), kSpreadSmem, st, pdl, a);
 }
 cudaError_t launch_attn(const AttnArgs& a, cudaStream_t st, bool pdl) {
   cudaError_t e = launch_ex(k_attn<false>, dim3(kAttnChains, kKvHeads), dim3(kAttnThreads),
