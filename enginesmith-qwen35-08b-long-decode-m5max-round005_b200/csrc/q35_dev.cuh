@@ -24,6 +24,12 @@ Q35_DEV float bfr(float f) { return bf2f(f2bf(f)); }
 Q35_DEV uint32_t pack_bf2(float lo, float hi) { return uint32_t(f2bf(lo)) | (uint32_t(f2bf(hi)) << 16); }
 Q35_DEV float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
 Q35_DEV float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+// round(a * b) per component, as a packed fused multiply-add with a -0
+// addend (a * b + (-0) is a * b exactly, signed zeros included). The caller
+// passes the -0 from a kernel parameter: with a literal -0 ptxas turns the
+// instruction back into a multiply and fuses that into the add consuming it
+// (measured), which it cannot do for an addend it does not know.
+Q35_DEV float2 prod2(float2 a, float2 b, float2 nz) { return __ffma2_rn(a, b, nz); }
 
 Q35_DEV float dexpf(float x) { return (float)exp((double)x); }
 Q35_DEV float dlogf(float x) { return (float)log((double)x); }

@@ -607,12 +607,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn(const __grid_constant_
   if (warp < kAttnScoreWarps) {
     // ---------------- score warps ----------------
     // lane l owns dims 8l..8l+7 of every head (as the reference).
-    // Heads (0,1) and (2,3) share packed f32x2 adds (__fadd2_rn rounds each
-    // component as __fadd_rn). Every product is a scalar __fmul_rn, which is
-    // never contracted into a fused multiply-add, so each score keeps the
-    // scalar sequence. A packed multiply feeding a packed add is not used:
-    // ptxas (CUDA 12.9, sm_100a) fuses that pair into one packed fused
-    // multiply-add even with explicit .rn on both and -fmad=false (measured).
+    // Heads (0,1) and (2,3) share packed f32x2 products and adds, so each
+    // score keeps the scalar sequence of rounded products and sums: the adds
+    // are __fadd2_rn (each component as __fadd_rn), the products prod2 (each
+    // component exactly the rounded product). A packed multiply is not used:
+    // ptxas (CUDA 12.9, sm_100a) fuses it into the packed add that consumes
+    // it, even with explicit .rn on both and under -fmad=false (measured).
+    const float2 nzs = make_float2(a.nzero, a.nzero);
     float2 qp[2][8];
 #pragma unroll
     for (int p = 0; p < 2; ++p)
@@ -633,8 +634,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn(const __grid_constant_
         for (int p = 0; p < 2; ++p) {
           float2 sc = make_float2(0.0f, 0.0f);
 #pragma unroll
-          for (int e = 0; e < 8; ++e)
-            sc = __fadd2_rn(sc, make_float2(__fmul_rn(qp[p][e].x, k8[e]), __fmul_rn(qp[p][e].y, k8[e])));
+          for (int e = 0; e < 8; ++e) sc = __fadd2_rn(sc, prod2(qp[p][e], make_float2(k8[e], k8[e]), nzs));
           v[(2 * p) * 4 + jj] = sc.x;
           v[(2 * p + 1) * 4 + jj] = sc.y;
         }
@@ -684,9 +684,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn(const __grid_constant_
     // ---------------- recurrence warps ----------------
     const int wr = warp - kAttnRecWarp0, d = 64 * wr + 2 * lane, hs = lane & 3;
     // o2[i][p] = (o of head 2p, o of head 2p+1) at dim d + i. Products are
-    // scalar __fmul_rn (never contracted); the adds are packed __fadd2_rn.
+    // packed prod2 (the rounded products, never fused with the add); the adds
+    // are packed __fadd2_rn.
     float2 o2[2][2] = {{{0.0f, 0.0f}, {0.0f, 0.0f}}, {{0.0f, 0.0f}, {0.0f, 0.0f}}};
     float ssum = 0.0f;  // running sum of head lane & 3
+    const float2 nz2 = make_float2(a.nzero, a.nzero);
     for (int t = 0; t < ntiles; ++t) {
       const int st = t % kAttnStages, b = t % kAttnBufs;
       const int nk = min(kAttnTile, nkeys - t * kAttnTile);
@@ -702,19 +704,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn(const __grid_constant_
     const float v0 = bf_lo(VV), v1 = bf_hi(VV);                                \
     const float2 e01 = make_float2(e4.x, e4.y), e23 = make_float2(e4.z, e4.w); \
     ssum = __fadd_rn(ssum, es);                                                \
-    o2[0][0] = __fadd2_rn(o2[0][0], make_float2(__fmul_rn(e01.x, v0), __fmul_rn(e01.y, v0))); \
-    o2[0][1] = __fadd2_rn(o2[0][1], make_float2(__fmul_rn(e23.x, v0), __fmul_rn(e23.y, v0))); \
-    o2[1][0] = __fadd2_rn(o2[1][0], make_float2(__fmul_rn(e01.x, v1), __fmul_rn(e01.y, v1))); \
-    o2[1][1] = __fadd2_rn(o2[1][1], make_float2(__fmul_rn(e23.x, v1), __fmul_rn(e23.y, v1))); \
+    o2[0][0] = __fadd2_rn(o2[0][0], prod2(e01, make_float2(v0, v0), nz2)); \
+    o2[0][1] = __fadd2_rn(o2[0][1], prod2(e23, make_float2(v0, v0), nz2)); \
+    o2[1][0] = __fadd2_rn(o2[1][0], prod2(e01, make_float2(v1, v1), nz2)); \
+    o2[1][1] = __fadd2_rn(o2[1][1], prod2(e23, make_float2(v1, v1), nz2)); \
   }
 #define Q35_ATTN_RESCALE(J)                                                    \
   {                                                                            \
     const float4 f4 = S.f[b][J];                                               \
     ssum = __fmul_rn(ssum, reinterpret_cast<const float*>(&S.f[b][J])[hs]);    \
-    o2[0][0] = make_float2(__fmul_rn(o2[0][0].x, f4.x), __fmul_rn(o2[0][0].y, f4.y)); \
-    o2[0][1] = make_float2(__fmul_rn(o2[0][1].x, f4.z), __fmul_rn(o2[0][1].y, f4.w)); \
-    o2[1][0] = make_float2(__fmul_rn(o2[1][0].x, f4.x), __fmul_rn(o2[1][0].y, f4.y)); \
-    o2[1][1] = make_float2(__fmul_rn(o2[1][1].x, f4.z), __fmul_rn(o2[1][1].y, f4.w)); \
+    o2[0][0] = prod2(o2[0][0], make_float2(f4.x, f4.y), nz2); \
+    o2[0][1] = prod2(o2[0][1], make_float2(f4.z, f4.w), nz2); \
+    o2[1][0] = prod2(o2[1][0], make_float2(f4.x, f4.y), nz2); \
+    o2[1][1] = prod2(o2[1][1], make_float2(f4.z, f4.w), nz2); \
   }
       if (split && t != own_t) {
         if (fm == 0) {
@@ -1486,13 +1488,17 @@ cudaError_t launch_qmv(const QmvArgs& a, cudaStream_t st, bool pdl) {
 cudaError_t launch_recur(const RecurArgs& a, cudaStream_t st, bool pdl) {
   return launch_ex(k_gdn_recur, dim3(8, kGdnHeads), dim3(128), kSpreadSmem, st, pdl, a);
 }
-cudaError_t launch_attn(const AttnArgs& a, cudaStream_t st, bool pdl) {
+cudaError_t launch_attn(const AttnArgs& a_in, cudaStream_t st, bool pdl) {
+  AttnArgs a = a_in;
+  a.nzero = -0.0f;
   cudaError_t e = launch_ex(k_attn<false>, dim3(kAttnChains, kKvHeads), dim3(kAttnThreads),
                             spread(attn_smem_bytes()), st, pdl, a);
   if (e != cudaSuccess) return e;
   return launch_ex(k_attn_combine<false>, dim3(kQHeads, kHeadDim / 32), dim3(128), kSpreadSmem, st, true, a);
 }
-cudaError_t launch_attn_sessions(const AttnArgs& a, int n, cudaStream_t st, bool pdl) {
+cudaError_t launch_attn_sessions(const AttnArgs& a_in, int n, cudaStream_t st, bool pdl) {
+  AttnArgs a = a_in;
+  a.nzero = -0.0f;
   if (n < 1 || !a.sess || a.xworld > 1 || !a.rope) return cudaErrorInvalidValue;
   cudaError_t e = launch_ex(k_attn<true>, dim3(kAttnChains, kKvHeads, n), dim3(kAttnThreads),
                             spread(attn_smem_bytes()), st, pdl, a);

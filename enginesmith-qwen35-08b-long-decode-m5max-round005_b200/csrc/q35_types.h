@@ -177,6 +177,7 @@ struct AttnArgs {
   // control block; its q/k/v, gated, RoPE and partial rows sit at z times the
   // row size from the pointers above
   const struct AttnSess* sess;
+  float nzero;  // -0.0f, set by launch_attn*: the run-time addend of the packed products (prod2)
 };
 
 struct AttnSess {
