@@ -100,13 +100,16 @@ Q35_DEV float4 bf4(uint2 u) { return make_float4(bf_lo(u.x), bf_hi(u.x), bf_lo(u
 
 Q35_DEV float magic(uint32_t bits) { return __uint_as_float(bits | 0x4b000000u); }
 
-// ((t0 + t1) + t2) + t3 of one 16-bit half (low 16 bits of u).
+// ((t0 + t1) + t2) + t3 of one 16-bit half (low 16 bits of u). The four
+// products are two packed fused multiply-adds (each component exactly the
+// scalar fmaf) over consecutive k, whose xx and -2^23 xx already sit in
+// register pairs.
 Q35_DEV float half_dot(uint32_t u, const float4& xx, const float4& cc) {
-  const float t0 = fmaf(magic(u & 0x000fu), xx.x, cc.x);
-  const float t1 = fmaf(magic(u & 0x00f0u), xx.y, cc.y);
-  const float t2 = fmaf(magic(u & 0x0f00u), xx.z, cc.z);
-  const float t3 = fmaf(magic(u & 0xf000u), xx.w, cc.w);
-  return __fadd_rn(__fadd_rn(__fadd_rn(t0, t1), t2), t3);
+  const float2 t01 = __ffma2_rn(make_float2(magic(u & 0x000fu), magic(u & 0x00f0u)), make_float2(xx.x, xx.y),
+                                make_float2(cc.x, cc.y));
+  const float2 t23 = __ffma2_rn(make_float2(magic(u & 0x0f00u), magic(u & 0xf000u)), make_float2(xx.z, xx.w),
+                                make_float2(cc.z, cc.w));
+  return __fadd_rn(__fadd_rn(__fadd_rn(t01.x, t01.y), t23.x), t23.y);
 }
 
 // The lane's chunk terms s*dotq + xs*b of rows [r0, r0+4) for chunk c (512
