@@ -6,6 +6,12 @@
                         tokens at positions P0.., tensor FLOP/s of its two GEMMs)
   python -m q35.opbench --op prefill --len N            (an N-token prompt through the session
                         API on the tensor cores: wall-clock tok/s)
+  python -m q35.opbench --op batch --len N --members B [--route exact|tensor|single]
+                        (B sessions at context N decoded as one batch: one session
+                        consumes a seeded N-token prompt (tensor cores), B - 1 copies
+                        of it join,
+                        4 warm-up steps, --iters timed steps; aggregate tok/s by
+                        CUDA events on the batch stream)
 
 Each call works on a fresh copy of its big operands (weights, recurrent
 state, or K/V cache), rotating over enough copies that the working set is
@@ -34,7 +40,10 @@ def main():
     import inputs as I
 
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", choices=["qmv", "gdn", "attn", "head", "qgemm", "pattn", "prefill"], required=True)
+    ap.add_argument("--op", choices=["qmv", "gdn", "attn", "head", "qgemm", "pattn", "prefill", "batch"],
+                    required=True)
+    ap.add_argument("--members", type=int, default=8)
+    ap.add_argument("--route", choices=["exact", "tensor", "single"], default="tensor")
     ap.add_argument("--tokens", type=int, default=64)
     ap.add_argument("--rows", type=int, default=7168)
     ap.add_argument("--k", type=int, default=1024)
@@ -67,6 +76,32 @@ def main():
         print(json.dumps({"op": "prefill", "len": args.len, "seconds": dt, "tok_s": args.len / dt,
                           "note": "wall clock of generate(prompt, 1): the prompt on the tensor cores, then "
                                   "its last token decoded"}))
+        return
+    if args.op == "batch":
+        d = os.environ.get("Q35_SYNTH_DIR", "/tmp/q35_synth_3")
+        if not os.path.exists(os.path.join(d, "model.safetensors")):
+            q35.write_synthetic_model(d, 3)
+        n = 1 if args.route == "single" else args.members
+        steps = args.iters
+        cap = ((args.len + 1 + 4 + steps + 64 + 63) // 64) * 64
+        ms = [q35.Model.load(d, 0, capacity=cap, tensor_prompt=True) for _ in range(n)]
+        rng = np.random.default_rng(2)
+        ms[0].generate([int(v) for v in rng.integers(0, q35.VOCAB, args.len)], 1, True)
+        for m in ms[1:]:
+            m.copy_from(ms[0])
+        if args.route == "single":
+            ms[0].decode_timed(4)
+            t_ms = ms[0].decode_timed(steps)
+        else:
+            bt = q35.Batch(ms, tensor_cores=args.route == "tensor")
+            bt.decode_timed(4)
+            t_ms = bt.decode_timed(steps)
+            bt.close()
+        for m in ms:
+            m.close()
+        us = 1000.0 * t_ms / steps
+        print(json.dumps({"op": "batch", "len": args.len, "route": args.route, "members": n, "steps": steps,
+                          "us_per_step": us, "tok_s": n * steps / (t_ms / 1000.0)}))
         return
     if args.op == "qmv":
         w, s, b, x = I.config1(0)
