@@ -21,7 +21,11 @@ JSON line carries:
   e2e         the drop-in `engine` executable timed as the harness times it: a
               continuation request generate([], K, reset=false) from writing the
               JSON line to reading the reply
-  roofline    the attention launch (device clock, live) against the measured HBM peak
+  roofline    the kernel with the larger share of the step (the attention launches
+              or the Q4 matvec launches; both in roofline_kernels): its bytes per
+              launch over its device-clock launch time, from a 32-step pass with
+              the in-kernel timers on right after the timed region (the timed
+              region itself runs with them off), against the measured HBM peak
   cpu_baseline the oracle decoding from this GPU session's own state
               (teacher-forced, with its argmax agreement), on the host cores
   prefill     the prompt's wall time (tensor-core route by default)
@@ -55,6 +59,9 @@ for p in (PKG, os.path.join(ROOT, "tests")):
 METRIC = "decode tok/s at 32K/64K/128K ctx per GPU & 8-GPU aggregate; % HBM roofline"
 SYNTH_DIR = os.environ.get("Q35_SYNTH_DIR", "/tmp/q35_synth_3")
 MODEL_SEED = 3
+# decode steps of the instrumented pass after each timed region (the kernels'
+# device-clock timers on, for the roofline fields; not part of the timed region)
+INSTRUMENTED_STEPS = 32
 # bytes streamed per decode token (weights incl. tied head, GDN state R+W,
 # conv history + weights) plus 12,288 bytes of K/V per context token
 BYTES_FIXED = 422_940_672 + 37_748_736 + 2_211_840
@@ -90,7 +97,7 @@ def plan(args, world: int) -> dict:
     c5 = (not split) and args.config5 and C5_SESSIONS % world == 0
     # the longest context a session reaches: prompt, first token, warm-up,
     # timed steps, the CPU sample's GPU tokens, a margin
-    need = max(ctxs) + 1 + args.warmup + args.steps + args.cpu_tokens + 64
+    need = max(ctxs) + 1 + args.warmup + args.steps + INSTRUMENTED_STEPS + args.cpu_tokens + 64
     if c5:
         need = max(need, C5_CONTEXT + 1 + args.warmup + args.steps + 64)
     return {"split": split, "contexts": ctxs, "config5": c5, "capacity": capacity_for(need),
@@ -392,7 +399,7 @@ def main():
         m.generate(prompt, 1, True)
         prefill_s = time.perf_counter() - t0
         m.decode_timed(args.warmup)
-        m.attn_timing(reset=1)
+        m.attn_timing(reset=0)  # the kernels' device-clock timers stay off in the timed region
         m.launch_count(reset=True)
         start_pos = m.position
         barrier()
@@ -401,11 +408,18 @@ def main():
         barrier()
         clk.mark(w0, time.time())
         launches = m.launch_count(reset=True)
+        # instrumented pass right after it (same session and graphs): the timers
+        # on, INSTRUMENTED_STEPS steps, for the kernels' launch times
+        m.attn_timing(reset=1)
+        inst_ms = m.decode_timed(INSTRUMENTED_STEPS)
+        qmv_us, qmv_launches, qmv_bytes = m.qmv_timing()  # before attn_timing's reset clears it
         attn_us, attn_launches = m.attn_timing(reset=0)
+        barrier()
         ms_max = reduce_max(ms, world, "cuda")
         tok_s = aggregate_tok_s(streams, timed_steps, ms_max / 1e3)
-        avg_len = start_pos + (timed_steps + 1) / 2.0
-        local_len = avg_len / world if split else avg_len  # K/V rows this rank's attention reads
+        # K/V rows the attention launches of the instrumented pass read (per rank)
+        avg_len = start_pos + timed_steps + (INSTRUMENTED_STEPS + 1) / 2.0
+        local_len = avg_len / world if split else avg_len
         attn_bytes = 2 * 2 * 256 * 2 * local_len + 4096 * 2 + 2 * 512 * 2 + 2048 * 2
         attn_avg_s = attn_us / max(attn_launches, 1) * 1e-6
         step_bytes = BYTES_FIXED + BYTES_PER_CTX * (start_pos + timed_steps / 2.0) / (world if split else 1)
@@ -413,6 +427,8 @@ def main():
                 "prefill_s": reduce_max(prefill_s, world, "cuda"), "launches": launches,
                 "attn_bytes": attn_bytes, "attn_avg_s": attn_avg_s, "attn_launches": attn_launches,
                 "local_len": local_len, "step_bytes": step_bytes,
+                "qmv_us": qmv_us, "qmv_launches": qmv_launches, "qmv_bytes": qmv_bytes, "attn_us": attn_us,
+                "inst_ms_per_step": inst_ms / INSTRUMENTED_STEPS,
                 "step_frac": step_bytes * (tok_s / streams) / 1e9 / peak}
 
     # ---- headline: decode at --context (config 4) ----
@@ -437,7 +453,8 @@ def main():
         by_context[str(ctx)] = round(r["tok_s"], 2)
         extra[str(ctx)] = {"tok_s": r["tok_s"], "ms_per_step": r["ms_per_step"], "prefill_s": r["prefill_s"],
                            "step_roofline_frac": r["step_frac"],
-                           "attn_frac": (r["attn_bytes"] / r["attn_avg_s"] / 1e9 / peak) if r["attn_launches"] else None}
+                           "attn_frac": (r["attn_bytes"] / r["attn_avg_s"] / 1e9 / peak) if r["attn_launches"] else None,
+                           "qmv_frac": (r["qmv_bytes"] / (r["qmv_us"] * 1e-6) / 1e9 / peak) if r["qmv_launches"] else None}
 
     # ---- config 5: 8 sessions at 131,072 context over N GPUs, batched per GPU ----
     config5 = None
@@ -517,6 +534,35 @@ def main():
                 traffic = json.load(f)["dram_bytes_per_ctx_token"] * head["local_len"]
         except Exception:
             pass
+        inst_note = (f"device-clock launch times from the {INSTRUMENTED_STEPS}-step instrumented pass right after "
+                     f"the timed region ({head['inst_ms_per_step']:.4f} ms per step with the timers on, "
+                     f"{head['ms_per_step']:.4f} without)")
+        attn_roof = {"bound": "hbm", "kernel": "k_attn (split GQA decode attention, live device clock)",
+                     "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": (achieved / peak) if achieved else None,
+                     "traffic": traffic, "peak_kind": peak_kind,
+                     "algorithmic_bytes_per_launch": head["attn_bytes"],
+                     "avg_launch_us": head["attn_avg_s"] * 1e6, "launches": head["attn_launches"],
+                     "us_total": head["attn_us"], "measured": inst_note}
+        qmv_roof = None
+        if head["qmv_launches"]:
+            qb = head["qmv_bytes"] / head["qmv_launches"]
+            qs = head["qmv_us"] / head["qmv_launches"] * 1e-6
+            qtraffic = None
+            try:
+                with open(os.path.join(ROOT, "profiles", "qmv_traffic.json")) as f:
+                    qtraffic = json.load(f)["dram_bytes_per_algorithmic_byte"] * qb
+            except Exception:
+                pass
+            qmv_roof = {"bound": "hbm", "kernel": "k_qmv (the decode step's Q4 matvec launches, live device clock)",
+                        "achieved": qb / qs / 1e9, "peak": peak, "unit": "GB/s", "frac": qb / qs / 1e9 / peak,
+                        "traffic": qtraffic, "peak_kind": peak_kind, "algorithmic_bytes_per_launch": qb,
+                        "avg_launch_us": qs * 1e6, "launches": head["qmv_launches"],
+                        "us_total": head["qmv_us"], "measured": inst_note}
+        # the headline roofline is the kernel with the larger share of the step
+        roofline = attn_roof
+        if qmv_roof and head["qmv_us"] > head["attn_us"]:
+            roofline = qmv_roof
         out = {
             "metric": METRIC, "value": head["tok_s"], "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True,
@@ -542,12 +588,8 @@ def main():
             "gpu_launches": head["launches"],
             "gpu_launches_note": "kernel nodes of the decode graphs replayed in the timed region (this rank)",
             "e2e": e2e,
-            "roofline": {"bound": "hbm", "kernel": "k_attn (split GQA decode attention, live device clock)",
-                         "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": (achieved / peak) if achieved else None,
-                         "traffic": traffic, "peak_kind": peak_kind,
-                         "algorithmic_bytes_per_launch": head["attn_bytes"],
-                         "avg_launch_us": head["attn_avg_s"] * 1e6, "launches": head["attn_launches"]},
+            "roofline": roofline,
+            "roofline_kernels": {"k_attn": attn_roof, "k_qmv": qmv_roof},
             "step_roofline": {"bytes_per_token": head["step_bytes"],
                               "achieved_gbs": head["step_bytes"] * (head["tok_s"] / streams) / 1e9,
                               "frac": head["step_frac"], "peak_kind": peak_kind},

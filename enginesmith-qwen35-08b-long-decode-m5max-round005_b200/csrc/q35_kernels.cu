@@ -59,6 +59,12 @@ __device__ __forceinline__ void gdn_conv_channel(int c, uint16_t raw, uint16_t* 
 }
 
 
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
 constexpr int kQmvThreads = 512;
 
 // Specialised per (prologue, epilogue) pair at compile time, so a launch runs
@@ -184,8 +190,12 @@ __global__ void __launch_bounds__(kQmvThreads, 1) k_qmv(const __grid_constant__ 
 
   // 2. Activations: every prologue leaves thread t with the group of four
   //    activations k = 4t .. 4t+3 and emits its matvec constants.
+  // launch timing (the session's switch, written only by the host and by
+  // launches that complete before this one starts): read before the wait
+  const bool timing = a.ctl && ld_cg_u32(&a.ctl->timing_on);
   pdl_wait();
   pdl_launch();
+  if (timing && tid == 0) atomicMin(&a.ctl->qmv_t0, globaltimer_ns());
   const float gain4[4] = {bf_lo(gain_raw.x), bf_hi(gain_raw.x), bf_lo(gain_raw.y), bf_hi(gain_raw.y)};
   if (PRO == kProPlain) {
     const int ngroups = K / 4;
@@ -305,31 +315,51 @@ __global__ void __launch_bounds__(kQmvThreads, 1) k_qmv(const __grid_constant__ 
   }
 
   // 4. epilogue (thread i finishes CTA row i).
-  if (e_seg < 0) return;
-  if (EPI == kEpiSwiglu) {
-    a.seg[0].y[r0[0] + tid] = swiglu_bf(bfr(vals[tid]), bfr(vals[cnt[0] + tid]));
-    return;
+  if (e_seg >= 0) {
+    if (EPI == kEpiSwiglu) {
+      a.seg[0].y[r0[0] + tid] = swiglu_bf(bfr(vals[tid]), bfr(vals[cnt[0] + tid]));
+    } else {
+      const float v = vals[tid];
+      if (EPI == kEpiResAdd) {
+        a.res[e_row] = f2bf(__fadd_rn(bf2f(pre_res), bfr(v)));
+      } else if (EPI == kEpiGdnConv && e_seg == 0) {
+        // gdn_input.metal:419-431
+        const uint16_t raw = f2bf(v);
+        float acc = 0.0f;
+        acc = fmaf(bf2f(pre_h[0]), bf_lo(pre_w4.x), acc);
+        acc = fmaf(bf2f(pre_h[1]), bf_hi(pre_w4.x), acc);
+        acc = fmaf(bf2f(pre_h[2]), bf_lo(pre_w4.y), acc);
+        acc = fmaf(bf2f(raw), bf_hi(pre_w4.y), acc);
+        const float xq1 = bfr(acc);
+        a.conv_out[e_row] = f2bf(__fmul_rn(xq1, sigmoid_bf(xq1)));
+        a.hist[e_row] = pre_h[1];
+        a.hist[kGdnConv + e_row] = pre_h[2];
+        a.hist[2 * kGdnConv + e_row] = raw;
+      } else {
+        const uint16_t yb = f2bf(v);
+        a.seg[e_seg].y[e_row] = yb;
+        if (EPI == kEpiGdnConv && e_seg == 1 && a.zs_out) a.zs_out[e_row] = gdn_zgate(bf2f(yb));
+      }
+    }
   }
-  const float v = vals[tid];
-  if (EPI == kEpiResAdd) {
-    a.res[e_row] = f2bf(__fadd_rn(bf2f(pre_res), bfr(v)));
-  } else if (EPI == kEpiGdnConv && e_seg == 0) {
-    // gdn_input.metal:419-431
-    const uint16_t raw = f2bf(v);
-    float acc = 0.0f;
-    acc = fmaf(bf2f(pre_h[0]), bf_lo(pre_w4.x), acc);
-    acc = fmaf(bf2f(pre_h[1]), bf_hi(pre_w4.x), acc);
-    acc = fmaf(bf2f(pre_h[2]), bf_lo(pre_w4.y), acc);
-    acc = fmaf(bf2f(raw), bf_hi(pre_w4.y), acc);
-    const float xq1 = bfr(acc);
-    a.conv_out[e_row] = f2bf(__fmul_rn(xq1, sigmoid_bf(xq1)));
-    a.hist[e_row] = pre_h[1];
-    a.hist[kGdnConv + e_row] = pre_h[2];
-    a.hist[2 * kGdnConv + e_row] = raw;
-  } else {
-    const uint16_t yb = f2bf(v);
-    a.seg[e_seg].y[e_row] = yb;
-    if (EPI == kEpiGdnConv && e_seg == 1 && a.zs_out) a.zs_out[e_row] = gdn_zgate(bf2f(yb));
+  // launch timing: the last CTA to finish closes the launch's interval and
+  // adds its algorithmic bytes (rows x (K/2 code bytes + K/16 scale and bias bytes))
+  if (timing) {
+    __syncthreads();
+    if (tid == 0) {
+      atomicMax(&a.ctl->qmv_tend, globaltimer_ns());  // this CTA's end, before the accounting
+      __threadfence();
+      if (atomicAdd(&a.ctl->qmv_done, 1u) == gridDim.x - 1) {
+        const unsigned long long t0 = atomicExch(&a.ctl->qmv_t0, ~0ull);
+        const unsigned long long t1 = atomicExch(&a.ctl->qmv_tend, 0ull);
+        atomicAdd(&a.ctl->qmv_ns, t1 - t0);
+        unsigned long long rows = 0;
+        for (int sg = 0; sg < a.nseg; ++sg) rows += unsigned(a.seg[sg].rows);
+        atomicAdd(&a.ctl->qmv_bytes, rows * unsigned(K / 2 + K / 16));
+        atomicAdd(&a.ctl->qmv_launches, 1u);
+        atomicExch(&a.ctl->qmv_done, 0u);
+      }
+    }
   }
 }
 
@@ -448,23 +478,20 @@ __device__ __forceinline__ float reduce16(float* v, int lane) {
   return __fadd_rn(v[0], __shfl_xor_sync(0xffffffffu, v[0], 1));
 }
 
-__device__ __forceinline__ unsigned long long globaltimer_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
+// Launch timing: the earliest post-dependency start over CTAs to the latest
+// CTA end (taken before the accounting atomics, whose round trips are not
+// part of the launch's work), accumulated in the control block when enabled.
+__device__ __forceinline__ void attn_time_start(Ctl* ctl, bool timing) {
+  if (timing) atomicMin(&ctl->attn_t0, globaltimer_ns());
 }
-
-// Launch timing: the earliest post-dependency start over CTAs to the moment
-// the last CTA finishes, accumulated in the control block when enabled.
-__device__ __forceinline__ void attn_time_start(Ctl* ctl) {
-  if (ctl->timing_on) atomicMin(&ctl->attn_t0, globaltimer_ns());
-}
-__device__ __forceinline__ void attn_time_end(Ctl* ctl) {
-  if (!ctl->timing_on) return;
+__device__ __forceinline__ void attn_time_end(Ctl* ctl, bool timing) {
+  if (!timing) return;
+  atomicMax(&ctl->attn_tend, globaltimer_ns());  // this CTA's end, before the accounting
   __threadfence();
   if (atomicAdd(&ctl->attn_done, 1u) == gridDim.x * gridDim.y - 1) {
     const unsigned long long t0 = atomicExch(&ctl->attn_t0, ~0ull);
-    atomicAdd(&ctl->attn_ns, globaltimer_ns() - t0);
+    const unsigned long long t1 = atomicExch(&ctl->attn_tend, 0ull);
+    atomicAdd(&ctl->attn_ns, t1 - t0);
     atomicAdd(&ctl->attn_launches, 1u);
     atomicExch(&ctl->attn_done, 0u);
   }
@@ -576,9 +603,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn(const __grid_constant_
     for (int t = 0; t < kAttnStages && t < ntiles; ++t) issue(kbase, S.kt[t], &S.kfull[t], t);
   if (vprod)
     for (int t = 0; t < kAttnStages && t < ntiles; ++t) issue(vbase, S.vt[t], &S.vfull[t], t);
+  const bool timing = ld_cg_u32(&a.ctl->timing_on);  // read before the wait (host-set switch)
   pdl_wait();
   pdl_launch();
-  if (tid == 0) attn_time_start(a.ctl);
+  if (tid == 0) attn_time_start(a.ctl, timing);
 
   // Query heads 4kh..4kh+3 (warps 0-3) scaled by 1/16 (attention_decode.metal:289);
   // warp 4 prepares the current token's key (attention.metal:295-311).
@@ -778,7 +806,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1) k_attn(const __grid_constant_
   }
   __syncwarp();  // producer warps: lane 0 rejoins its warp before the barrier
   __syncthreads();
-  if (tid == 0) attn_time_end(a.ctl);
+  if (tid == 0) attn_time_end(a.ctl, timing);
 }
 
 // Sequence split, inside the combine: this rank's record (lanes 0-7 of warp

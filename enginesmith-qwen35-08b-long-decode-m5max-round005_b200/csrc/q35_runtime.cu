@@ -1941,6 +1941,7 @@ int q35_open(const char* model_dir, int device, const q35_opts* opts, q35_sessio
   Ctl c = {};
   c.capacity = s->capacity;
   c.attn_t0 = ~0ull;
+  c.qmv_t0 = ~0ull;
   e = cudaMemcpy(s->ctl, &c, sizeof(Ctl), cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = capture(s, 1, true, &s->gdec1, &s->kn_dec1);
   if (e == cudaSuccess && s->dbatch > 1) e = capture(s, s->dbatch, true, &s->gdecN, &s->kn_decN);
@@ -2012,6 +2013,7 @@ int q35_generate(q35_session* s, const uint32_t* prompt, size_t n_prompt, size_t
     Ctl c = {};
     c.capacity = s->capacity;
     c.attn_t0 = ~0ull;
+    c.qmv_t0 = ~0ull;
     c.epoch = ++s->epoch;  // ranks of a sequence split reset in step, so epochs agree
     if (e == cudaSuccess) e = cudaMemcpyAsync(s->ctl, &c, sizeof(Ctl), cudaMemcpyHostToDevice, s->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
@@ -2114,9 +2116,29 @@ int q35_attn_timing(q35_session* s, int reset, double* total_us, uint32_t* launc
     c.attn_launches = 0;
     c.attn_t0 = ~0ull;
     c.attn_ns = 0;
+    c.qmv_done = 0;
+    c.qmv_launches = 0;
+    c.qmv_t0 = ~0ull;
+    c.qmv_ns = 0;
+    c.qmv_bytes = 0;
+    c.attn_tend = 0;
+    c.qmv_tend = 0;
     e = cudaMemcpy(s->ctl, &c, sizeof(Ctl), cudaMemcpyHostToDevice);
     if (e != cudaSuccess) return set_err(s, Q35_ECUDA, std::string("timing: ") + cudaGetErrorString(e));
   }
+  return Q35_OK;
+}
+
+int q35_qmv_timing(q35_session* s, double* total_us, uint32_t* launches, double* weight_bytes) {
+  if (!s) return Q35_EINVAL;
+  cudaSetDevice(s->device);
+  cudaError_t e = cudaStreamSynchronize(s->stream);
+  Ctl c;
+  if (e == cudaSuccess) e = cudaMemcpy(&c, s->ctl, sizeof(Ctl), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return set_err(s, Q35_ECUDA, std::string("timing: ") + cudaGetErrorString(e));
+  if (total_us) *total_us = double(c.qmv_ns) * 1e-3;
+  if (launches) *launches = c.qmv_launches;
+  if (weight_bytes) *weight_bytes = double(c.qmv_bytes);
   return Q35_OK;
 }
 

@@ -61,7 +61,14 @@ struct Ctl {
   unsigned long long attn_t0;    // earliest post-dependency start of the running launch
   unsigned long long attn_ns;    // summed launch durations
   uint32_t epoch;      // reset generation (sequence-split exchange tags)
-  uint32_t pad[3];
+  // in-kernel timing of the matvec launches (same switch, same clock)
+  uint32_t qmv_done;             // CTAs finished in the running launch
+  uint32_t qmv_launches;         // launches accounted
+  unsigned long long qmv_t0;     // earliest post-dependency start of the running launch
+  unsigned long long qmv_ns;     // summed launch durations
+  unsigned long long qmv_bytes;  // summed algorithmic bytes (codes, scales, biases)
+  unsigned long long attn_tend;  // latest CTA end of the running attention launch
+  unsigned long long qmv_tend;   // latest CTA end of the running matvec launch
 };
 
 // Error site codes written to Ctl::err.

@@ -62,6 +62,7 @@ def _load() -> ctypes.CDLL:
         "q35_last_logits": (c_int, [P, P, P]),
         "q35_decode_timed": (c_int, [P, c_size_t, POINTER(c_float)]),
         "q35_attn_timing": (c_int, [P, c_int, POINTER(ctypes.c_double), POINTER(c_uint32)]),
+        "q35_qmv_timing": (c_int, [P, POINTER(ctypes.c_double), POINTER(c_uint32), POINTER(ctypes.c_double)]),
         "q35_op_qmv_q4": (c_int, [P, P, P, P, P, P, c_int, c_int, P]),
         "q35_op_embedding_q4": (c_int, [P, P, P, c_uint32, c_int, P, P]),
         "q35_op_qgemm_workspace_bytes": (c_size_t, [c_uint32, c_uint32, c_uint32]),
@@ -198,6 +199,14 @@ class Model:
         n = c_uint32()
         self._check(lib().q35_attn_timing(self._h, reset, ctypes.byref(us), ctypes.byref(n)))
         return float(us.value), int(n.value)
+
+    def qmv_timing(self):
+        """(total_us, launches, weight_bytes) of the matvec launches since the
+        last attn_timing reset (the same device-clock switch)."""
+        us, nb = ctypes.c_double(), ctypes.c_double()
+        n = c_uint32()
+        self._check(lib().q35_qmv_timing(self._h, ctypes.byref(us), ctypes.byref(n), ctypes.byref(nb)))
+        return float(us.value), int(n.value), float(nb.value)
 
     def dump_state(self):
         """Return (kv [6,2,2,pos,256] u16, state [18,16,128,128] f32, hist [18,3,6144] u16)."""

@@ -215,6 +215,13 @@ void q35_batch_destroy(q35_batch* b);
  * its last CTA. */
 int q35_attn_timing(q35_session* s, int reset, double* total_us, uint32_t* launches);
 
+/* Device-clock timing of the matvec launches, on the same switch as
+ * q35_attn_timing (whose reset clears both): the summed launch time in
+ * microseconds, the launch count and the launches' summed algorithmic bytes
+ * (rows x (K/2 code bytes + K/16 scale and bias bytes)) since the last reset.
+ * Benchmark aid, no counterpart in the reference. */
+int q35_qmv_timing(q35_session* s, double* total_us, uint32_t* launches, double* weight_bytes);
+
 /* ---------------------------------------------------------------------- */
 /* Op API (device pointers, caller-owned, nothing allocated)               */
 /* ---------------------------------------------------------------------- */
