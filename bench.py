@@ -376,7 +376,7 @@ def main():
     model_dir = ensure_model(world, rank)
     cap = pl["capacity"]
     split = pl["split"]
-    tensor_prompt = args.prompt_route == "tensor" and not split  # a split session takes the decode route
+    tensor_prompt = args.prompt_route == "tensor"  # a split rank runs the whole prompt, then keeps its share
     m = q35.Model.load(model_dir, local, capacity=cap, tensor_prompt=tensor_prompt)
     if split:
         q35.split_connect_dist(m)  # one stream over all ranks: the same prompt everywhere

@@ -400,6 +400,7 @@ struct q35_session {
   int xrank = 0, xworld = 1, xpend_world = 0;
   uint32_t xwait_ms = 0;  // bound of the exchange wait (0: the kernel's 10 s)
   uint8_t* xbuf = nullptr;
+  uint16_t* xkv = nullptr;  // one layer's K/V at full capacity: the tensor-core prompt's rows before the split keeps its share
   std::vector<void*> xpeer;
   void** xtab = nullptr;  // [xworld] record pointers, then [xworld] flag pointers
 
@@ -998,6 +999,7 @@ void free_session(q35_session* s) {
     if (p) cudaIpcCloseMemHandle(p);
   if (s->xtab) cudaFree(s->xtab);
   if (s->xbuf) cudaFree(s->xbuf);
+  if (s->xkv) cudaFree(s->xkv);
   if (s->buf) cudaFree(s->buf);
   if (s->pbuf) cudaFree(s->pbuf);
   if (s->M.arena) cudaFree(s->M.arena);
@@ -1092,6 +1094,44 @@ int run_prompt_tensor(q35_session* s, size_t n, cudaError_t* ce) {
     return Q35_ECUDA;
   }
   return Q35_OK;
+}
+
+// A sequence-split session's prompt on the tensor cores: every rank runs the
+// whole prompt route over all n rows in the full-capacity layout (so the GDN
+// state and conv history come out identical on every rank), then keeps only
+// its own positions p = l G + rank, moved to the local layout the split's
+// attention reads (local index l at chain l % 64, slot l / 64, heads at the
+// local capacity's stride). One layer at a time goes through a full-capacity
+// copy, since both layouts share the cache buffer. For local chain c the
+// source positions sit on one global chain, (c G + rank) % 64, every G-th
+// slot from (c G + rank) / 64: one strided 2-D copy per (layer, K/V, head,
+// chain).
+cudaError_t split_keep_local_rows(q35_session* s, size_t n) {
+  const size_t G = size_t(s->xworld), R = size_t(s->xrank);
+  const size_t cap = s->capacity, cps = cap / kAttnChains;
+  const size_t lcap = s->kv_capacity(), lcps = lcap / kAttnChains;
+  const size_t nloc = n > R ? (n - R + G - 1) / G : 0;
+  const size_t layer_elems = size_t(2) * kKvHeads * cap * kHeadDim;  // K then V, as kcache/vcache lie
+  const size_t row = size_t(kHeadDim) * 2;
+  cudaError_t e = cudaSuccess;
+  if (!s->xkv) e = cudaMalloc(&s->xkv, layer_elems * 2);
+  for (int ai = 0; ai < 6 && e == cudaSuccess; ++ai) {
+    e = cudaMemcpyAsync(s->xkv, s->kcache(ai), layer_elems * 2, cudaMemcpyDeviceToDevice, s->stream);
+    for (int which = 0; which < 2 && e == cudaSuccess; ++which)
+      for (int h = 0; h < kKvHeads && e == cudaSuccess; ++h) {
+        const uint16_t* src = s->xkv + (size_t(which) * kKvHeads + h) * cap * kHeadDim;
+        uint16_t* dst = (which ? s->vcache(ai) : s->kcache(ai)) + size_t(h) * lcap * kHeadDim;
+        for (size_t c = 0; c < size_t(kAttnChains) && e == cudaSuccess; ++c) {
+          const size_t rows = nloc > c ? (nloc - c + kAttnChains - 1) / kAttnChains : 0;
+          if (rows == 0) continue;
+          const size_t gc = (c * G + R) % kAttnChains, k0 = (c * G + R) / kAttnChains;
+          e = cudaMemcpy2DAsync(dst + c * lcps * kHeadDim, row, src + (gc * cps + k0) * kHeadDim, G * row, row,
+                                rows, cudaMemcpyDeviceToDevice, s->stream);
+        }
+      }
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
+  return e;
 }
 
 int check_device_ctl(q35_session* s) {
@@ -2018,9 +2058,13 @@ int q35_generate(q35_session* s, const uint32_t* prompt, size_t n_prompt, size_t
     if (e == cudaSuccess) e = cudaMemcpyAsync(s->ctl, &c, sizeof(Ctl), cudaMemcpyHostToDevice, s->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s->stream);
     if (e != cudaSuccess) return device_failure(s, e, "reset");
-    // the tensor-core prompt route needs every K/V row on this device
-    int rc = s->tensor_prompt && s->xworld <= 1 ? run_prompt_tensor(s, n_prompt - 1, &e)
-                                                : run_steps(s, n_prompt - 1, false, &e);
+    // the tensor-core prompt route computes every K/V row on this device; a
+    // sequence-split rank then keeps its own share
+    int rc = s->tensor_prompt ? run_prompt_tensor(s, n_prompt - 1, &e) : run_steps(s, n_prompt - 1, false, &e);
+    if (rc == Q35_OK && s->tensor_prompt && s->xworld > 1) {
+      e = split_keep_local_rows(s, n_prompt - 1);
+      if (e != cudaSuccess) rc = Q35_ECUDA;
+    }
     if (rc == Q35_ECANCEL) {
       cudaStreamSynchronize(s->stream);
       reset_state(s);

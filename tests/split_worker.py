@@ -6,7 +6,12 @@ attn_f32_split):
   (a) a short prompt decoded from scratch by both: same tokens, same logits;
   (b) a long prompt consumed on the GPUs, the ranks' state dumps gathered
       (each rank holds positions p % world == rank) and imported into the
-      oracle, which continues teacher-forced: same logits each step.
+      oracle, which continues teacher-forced: same logits each step;
+  (c) the same long prompt on the tensor-core prompt route (every rank runs
+      the whole prompt, then keeps its share of the K/V rows): the gathered
+      rows equal a single-GPU tensor-route session's bit for bit, the ranks'
+      replicated state agrees, and the oracle continues from the gathered
+      state with the same logits.
 It also records the distance to a single-GPU session (information only: the
 split merges in another order, and this random-init model's nearly flat
 logits amplify last-bit differences). Writes a JSON verdict.
@@ -132,9 +137,49 @@ def main():
             prev = gpu_toks[i]
         verdict["logits_equal_b"] = eq
     dist.barrier()
+
+    # (c) the long prompt on the tensor-core route
+    mt = q35.Model.load(model_dir, local, capacity=cap, tensor_prompt=True)
+    q35.split_connect_dist(mt)
+    first_c = mt.generate(p_long, 1, True)
+    kv_c, st_c, hi_c = mt.dump_state()
+    parts = [None] * world
+    dist.all_gather_object(parts, (kv_c, hashlib.sha256(st_c.tobytes()).hexdigest(),
+                                   hashlib.sha256(hi_c.tobytes()).hexdigest()))
+    gpu_toks, gpu_log = [], []
+    for _ in range(s_long):
+        gpu_toks += mt.generate([], 1, False)
+        gpu_log.append(mt.last_logits()[0])
+    digest = [hashlib.sha256(lg.tobytes()).hexdigest() for lg in gpu_log]
+    all_d = [None] * world
+    dist.all_gather_object(all_d, digest)
+    dist.barrier()
+    if rank == 0:
+        verdict["ranks_identical_c"] = all(d == all_d[0] for d in all_d)
+        verdict["replicated_state_c"] = all(p[1:] == parts[0][1:] for p in parts)
+        full = np.zeros_like(parts[0][0])
+        for p in parts:
+            full += p[0]
+        # rows the prompt route wrote (the last prompt token is the split decode step's)
+        single = q35.Model.load(model_dir, local, capacity=cap, tensor_prompt=True)
+        single.generate(p_long, 1, True)
+        kv_s, _, _ = single.dump_state()
+        single.close()
+        verdict["rows_equal_single_c"] = bool(np.array_equal(full[..., :n_long - 1, :], kv_s[..., :n_long - 1, :]))
+        s = O.OracleSession(om, cap)
+        s.set_split(world)
+        s.import_state(n_long, full, st_c, hi_c)
+        prev, eq = first_c[0], []
+        for i in range(s_long):
+            tok = s.step(prev)
+            eq.append(bool(np.array_equal(s.logits(), gpu_log[i])) and tok == gpu_toks[i])
+            prev = gpu_toks[i]
+        verdict["logits_equal_c"] = eq
+    dist.barrier()
     if rank == 0:
         with open(out_path, "w") as f:
             json.dump(verdict, f)
+    mt.close()
     m.close()
     dist.barrier()
     dist.destroy_process_group()

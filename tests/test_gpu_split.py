@@ -4,6 +4,9 @@ attn_f32_split): all ranks produce the same logits, bit for bit; a short
 prompt decoded from scratch gives the oracle's tokens and logits; after a
 1,500-token prompt the ranks' gathered state, imported into the oracle,
 continues with the same logits; each rank holds its share of the positions.
+The same prompt on the tensor-core route (every rank runs the whole prompt,
+then keeps its share of the K/V rows) gives rows identical to a single-GPU
+tensor-route session's and a gathered state the oracle continues exactly.
 The distance to a single-GPU session is recorded, not asserted (another
 merge order; on this random-init model last-bit differences grow to a few
 percent of the logits). Needs two GPUs (skipped otherwise)."""
@@ -44,6 +47,9 @@ def test_split_two_gpus(cuda, synth_model_dir, tmp_path):
     assert all(v["logits_equal_b"]), v
     pos = v["position_b"]
     assert v["local_positions_b"] == [(pos + 1) // 2, pos // 2], v
+    assert v["ranks_identical_c"] and v["replicated_state_c"], v
+    assert v["rows_equal_single_c"], v
+    assert all(v["logits_equal_c"]), v
 
 
 def test_split_silent_peer_times_out(cuda, synth_model_dir, tmp_path):
