@@ -1076,8 +1076,6 @@ struct HeadSmem {
   float4 xq[2 * 4 * 32];
   float xsum[2 * 32];
   float xf[kHidden];
-  float pl[kHeadRowsPerChunk * 2 * 32];
-  float vals[kHeadRowsPerChunk];
   float red[64];
   float wm[kHeadThreads / 32], ws[kHeadThreads / 32];
   uint64_t bar[kHeadStages];
@@ -1154,9 +1152,10 @@ __global__ void __launch_bounds__(kHeadThreads, 1) k_head(const __grid_constant_
     const int st = ch % kHeadStages;
     mbar_wait(&S.bar[st], uint32_t(ch / kHeadStages) & 1u, a.ctl, kErrHeadWait);
     const int rows = min(kHeadRowsPerChunk, nrows - ch * kHeadRowsPerChunk);
+    float t0[4] = {0.f, 0.f, 0.f, 0.f}, t1[4] = {0.f, 0.f, 0.f, 0.f};
     if (g0 < rows) {
-      qmv_chunk_core(S.codes[st], S.scl[st], S.bia[st], rows, g0, 0, kHidden, xx0, cc0, xs0, S.pl, lane);
-      qmv_chunk_core(S.codes[st], S.scl[st], S.bia[st], rows, g0, 1, kHidden, xx1, cc1, xs1, S.pl, lane);
+      qmv_rows_terms(S.codes[st], S.scl[st], S.bia[st], rows, g0, 0, kHidden, xx0, cc0, xs0, lane, t0);
+      qmv_rows_terms(S.codes[st], S.scl[st], S.bia[st], rows, g0, 1, kHidden, xx1, cc1, xs1, lane, t1);
     }
     __syncwarp();
     if (lane == 0) {
@@ -1170,10 +1169,15 @@ __global__ void __launch_bounds__(kHeadThreads, 1) k_head(const __grid_constant_
       }
     }
     if (g0 < rows) {
-      qmv_finish_task(S.pl, rows, g0, 2, S.vals, lane);
-      __syncwarp();
+      // the lane's two chunk terms summed from 0 in chunk order (the finish of
+      // qmv_finish_task, kept in registers), then the rows' butterflies:
+      // row j ends on lane 16 (j >> 1) + 8 (j & 1)
+      const float v = reduce4(__fadd_rn(__fadd_rn(0.0f, t0[0]), t1[0]), __fadd_rn(__fadd_rn(0.0f, t0[1]), t1[1]),
+                              __fadd_rn(__fadd_rn(0.0f, t0[2]), t1[2]), __fadd_rn(__fadd_rn(0.0f, t0[3]), t1[3]),
+                              lane);
+      const float vr = __shfl_sync(0xffffffffu, v, ((lane & 2) << 3) | ((lane & 1) << 3));
       if (lane < 4 && g0 + lane < rows) {
-        const uint16_t lb = f2bf(S.vals[g0 + lane]);
+        const uint16_t lb = f2bf(vr);
         a.logits[r0 + ch * kHeadRowsPerChunk + g0 + lane] = lb;
         lse_push(run_m, run_s, bf2f(lb));
       }
