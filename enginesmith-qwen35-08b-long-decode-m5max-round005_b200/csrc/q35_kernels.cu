@@ -883,12 +883,16 @@ __global__ void __launch_bounds__(128) k_attn_combine(const __grid_constant__ At
   if constexpr (SESS) sv = attn_session_view(a_in, blockIdx.z);
   const AttnArgs& a = SESS ? sv : a_in;
   constexpr float kMin = -3.4028234663852886e38f;
-  pdl_wait();
-  pdl_launch();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int qh = blockIdx.x, kh = qh >> 2, h = qh & 3;
   const int stripe = blockIdx.y * 4 + warp;  // 8 dims
+  // Before the wait: the step's position (written by its first launch) and
+  // the output gate (its input written by the q/k/v projection, two launches
+  // back), so neither load sits after the dependency wait.
   const uint32_t len = ld_cg_u32(&a.ctl->pos_step) + uint32_t(a.pos_add) + 1;
+  const float gate = lane < 8 ? attn_gate_bf(bf2f(a.q_raw[qh * 512 + 256 + stripe * 8 + lane])) : 0.0f;
+  pdl_wait();
+  pdl_launch();
   const bool xs = a.xworld > 1;
   const bool split = xs || len >= 1024;
   const size_t base = size_t(kh) * kAttnChains * 4 + h;  // + chain * 4
@@ -940,7 +944,7 @@ __global__ void __launch_bounds__(128) k_attn_combine(const __grid_constant__ At
   if (lane < 8) {
     const int d = stripe * 8 + lane;
     const float attention = bfr(r);
-    a.gated[qh * kHeadDim + d] = f2bf(__fmul_rn(attention, attn_gate_bf(bf2f(a.q_raw[qh * 512 + 256 + d]))));
+    a.gated[qh * kHeadDim + d] = f2bf(__fmul_rn(attention, gate));
   }
 }
 
