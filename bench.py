@@ -23,9 +23,10 @@ JSON line carries:
               JSON line to reading the reply
   roofline    the kernel with the larger share of the step (the attention launches
               or the Q4 matvec launches; both in roofline_kernels): its bytes per
-              launch over its device-clock launch time, from a 32-step pass with
-              the in-kernel timers on right after the timed region (the timed
-              region itself runs with them off), against the measured HBM peak
+              launch over its device-clock launch time, from the faster of two
+              32-step passes with the in-kernel timers on right after the timed
+              region (the timed region itself runs with them off), against the
+              measured HBM peak
   cpu_baseline the oracle decoding from this GPU session's own state
               (teacher-forced, with its argmax agreement), on the host cores
   prefill     the prompt's wall time (tensor-core route by default)
@@ -62,6 +63,7 @@ MODEL_SEED = 3
 # decode steps of the instrumented pass after each timed region (the kernels'
 # device-clock timers on, for the roofline fields; not part of the timed region)
 INSTRUMENTED_STEPS = 32
+INSTRUMENTED_PASSES = 2
 # bytes streamed per decode token (weights incl. tied head, GDN state R+W,
 # conv history + weights) plus 12,288 bytes of K/V per context token
 BYTES_FIXED = 422_940_672 + 37_748_736 + 2_211_840
@@ -97,7 +99,7 @@ def plan(args, world: int) -> dict:
     c5 = (not split) and args.config5 and C5_SESSIONS % world == 0
     # the longest context a session reaches: prompt, first token, warm-up,
     # timed steps, the CPU sample's GPU tokens, a margin
-    need = max(ctxs) + 1 + args.warmup + args.steps + INSTRUMENTED_STEPS + args.cpu_tokens + 64
+    need = max(ctxs) + 1 + args.warmup + args.steps + INSTRUMENTED_PASSES * INSTRUMENTED_STEPS + args.cpu_tokens + 64
     if c5:
         need = max(need, C5_CONTEXT + 1 + args.warmup + args.steps + 64)
     return {"split": split, "contexts": ctxs, "config5": c5, "capacity": capacity_for(need),
@@ -408,17 +410,24 @@ def main():
         barrier()
         clk.mark(w0, time.time())
         launches = m.launch_count(reset=True)
-        # instrumented pass right after it (same session and graphs): the timers
-        # on, INSTRUMENTED_STEPS steps, for the kernels' launch times
-        m.attn_timing(reset=1)
-        inst_ms = m.decode_timed(INSTRUMENTED_STEPS)
-        qmv_us, qmv_launches, qmv_bytes = m.qmv_timing()  # before attn_timing's reset clears it
-        attn_us, attn_launches = m.attn_timing(reset=0)
+        # instrumented passes right after it (same session and graphs): the
+        # timers on, INSTRUMENTED_STEPS steps each, for the kernels' launch
+        # times; of INSTRUMENTED_PASSES passes the one with the shorter step is
+        # kept (a short pass can catch a transient slowdown of the box)
+        best = None
+        for _ in range(INSTRUMENTED_PASSES):
+            m.attn_timing(reset=1)
+            pass_ms = m.decode_timed(INSTRUMENTED_STEPS)
+            q = m.qmv_timing()  # before attn_timing's reset clears it
+            at = m.attn_timing(reset=0)
+            if best is None or pass_ms < best[0]:
+                best = (pass_ms, q, at)
+        inst_ms, (qmv_us, qmv_launches, qmv_bytes), (attn_us, attn_launches) = best
         barrier()
         ms_max = reduce_max(ms, world, "cuda")
         tok_s = aggregate_tok_s(streams, timed_steps, ms_max / 1e3)
-        # K/V rows the attention launches of the instrumented pass read (per rank)
-        avg_len = start_pos + timed_steps + (INSTRUMENTED_STEPS + 1) / 2.0
+        # K/V rows the attention launches of the instrumented passes read (per rank)
+        avg_len = start_pos + timed_steps + (INSTRUMENTED_PASSES * INSTRUMENTED_STEPS + 1) / 2.0
         local_len = avg_len / world if split else avg_len
         attn_bytes = 2 * 2 * 256 * 2 * local_len + 4096 * 2 + 2 * 512 * 2 + 2048 * 2
         attn_avg_s = attn_us / max(attn_launches, 1) * 1e-6
@@ -534,9 +543,9 @@ def main():
                 traffic = json.load(f)["dram_bytes_per_ctx_token"] * head["local_len"]
         except Exception:
             pass
-        inst_note = (f"device-clock launch times from the {INSTRUMENTED_STEPS}-step instrumented pass right after "
-                     f"the timed region ({head['inst_ms_per_step']:.4f} ms per step with the timers on, "
-                     f"{head['ms_per_step']:.4f} without)")
+        inst_note = (f"device-clock launch times from the faster of {INSTRUMENTED_PASSES} {INSTRUMENTED_STEPS}-step "
+                     f"instrumented passes right after the timed region ({head['inst_ms_per_step']:.4f} ms per "
+                     f"step with the timers on, {head['ms_per_step']:.4f} without)")
         attn_roof = {"bound": "hbm", "kernel": "k_attn (split GQA decode attention, live device clock)",
                      "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": (achieved / peak) if achieved else None,

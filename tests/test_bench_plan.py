@@ -45,7 +45,7 @@ def test_capacities_accepted_and_sufficient(kw, world):
     for cap in (pl["capacity"], pl["engine_capacity"]):
         assert cap % 64 == 0
         q35.check_opts(capacity=cap, flags=q35.FLAG_TENSOR_PROMPT)  # raises when q35_open would refuse
-    longest = max(pl["contexts"]) + 1 + a.warmup + a.steps + bench.INSTRUMENTED_STEPS + a.cpu_tokens
+    longest = max(pl["contexts"]) + 1 + a.warmup + a.steps + bench.INSTRUMENTED_PASSES * bench.INSTRUMENTED_STEPS + a.cpu_tokens
     assert pl["capacity"] >= longest
     if pl["config5"]:
         assert pl["capacity"] >= bench.C5_CONTEXT + 1 + a.warmup + a.steps
